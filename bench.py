@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token sampler (BASELINE metric: sampled rows/s at
+B=256, V=128256 fp32; HBM GB/s vs peak; p50 us at B=1).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+One step = one nls_sample_batch call over one batch of the heterogeneous
+configuration (B=256 rows per GPU, V=128256, per-row
+temperature/top-k/top-p/min-p, penalties over a 256-token history, 16 bias
+entries per row). Inputs are seeded synthetic data of that shape. With N GPUs
+(torchrun) each rank samples its own 256-row batch (batch-sharded, no
+collective; weak scaling); rows are generated from (seed, global row).
+
+`value` is whole-job rows/s with every input already in HBM, timed with CUDA
+events on the launch stream, L2 flushed between steps. `e2e` is the same
+metric through the public host API (pinned host logits, host params/history/
+bias/uniforms, host outputs): H2D and D2H are inside its timed region.
+`--impl reference` times the reference sampler's CPU restatement (oracle/) on
+this host's cores over the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sampled rows/s at B=256,V=128256 fp32; HBM GB/s vs peak; p50 us at B=1"
+WORKLOAD = "c3_batched_hetero"
+SEED = 1234
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback (6.65 TB/s, earlier pool measurement)"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of each kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def row_is_full(params, V):
+    """The library's row split (nls_common.cuh row_mode): greedy and top-k
+    rows with k <= 256 go to the streaming kernel, the rest to the full-sort
+    kernel."""
+    k = np.where(params["top_k"] > 0, np.minimum(params["top_k"], V), V)
+    samp = params["temperature"] > 0
+    return samp & ~((k < V) & (k <= 256))
+
+
+def row_bytes(w):
+    per = np.full(w.B, w.V * 4 + 64 + 8 + 12, dtype=np.int64)
+    if w.hist_ids is not None:
+        per += np.diff(w.hist_off) * 8 + 8
+    if w.bias_ids is not None:
+        per += np.diff(w.bias_off) * 16 + 8
+    return per
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local, dist
+
+
+def reduce_max(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_sample(oracle, w, rows: int, threads: int):
+    """Time the oracle (reference sampler restatement) on `rows` rows."""
+    sel = slice(0, rows)
+    hoff = w.hist_off[: rows + 1] if w.hist_off is not None else None
+    boff = w.bias_off[: rows + 1] if w.bias_off is not None else None
+    t0 = time.perf_counter()
+    ids = oracle.sample_batch(w.logits[sel], w.params[sel], w.hist_ids, hoff, w.bias_ids,
+                              w.bias_vals, boff, w.uniforms[sel], threads=threads)
+    return time.perf_counter() - t0, ids
+
+
+def run_reference(args, world, rank, dist):
+    """--impl reference: the reference sampler's CPU restatement on host cores."""
+    if rank != 0:
+        return 0
+    from oracle import oracle
+    import __graft_entry__ as g
+    pkg = g.load_package()
+    oracle.build()
+    threads = os.cpu_count() or 1
+    w = pkg.workloads.make(WORKLOAD, seed=SEED)
+    for _ in range(args.warmup):
+        cpu_sample(oracle, w, w.B, threads)
+    times = []
+    for _ in range(args.steps):
+        dt, _ = cpu_sample(oracle, w, w.B, threads)
+        times.append(dt)
+    ms = 1e3 * statistics.mean(times)
+    value = w.B / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE config 3 shapes and distributions)",
+        "config": config_dict(world),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": f"the full {w.B}-row batch per step, rows spread over "
+                                   f"{threads} threads (C restatement of sampler.nim)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(world):
+    return {"workload": f"{WORKLOAD}: B=256 rows per GPU, V=128256 fp32, per-row T~U[0.5,1.2], "
+                        "top-k in {0,20,50,100}, top-p~U[0.8,1], min-p in {0,0.05}, "
+                        "rep/freq/pres 1.1/0.2/0.2 over 256 ids, 16 bias entries",
+            "rows_per_gpu": 256, "vocab": 128256,
+            "parallelism": f"batch-sharded x{world} (no collective)",
+            "l2": "flushed between steps (256 MiB write, outside the step events)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--latency-iters", type=int, default=200)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world, rank, local, dist = dist_setup(args)
+    if args.impl == "reference":
+        rc = run_reference(args, world, rank, dist)
+        if dist is not None:
+            dist.destroy_process_group()
+        return rc
+
+    import torch
+    import __graft_entry__ as g
+    pkg = g.load_package()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    B = 256
+    rows = np.arange(rank * B, (rank + 1) * B, dtype=np.int64)
+    w = pkg.workloads.make(WORKLOAD, seed=SEED, rows=rows)
+    eng = pkg.Engine(local, max_rows=B, max_vocab=w.V)
+
+    def t(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    d = dict(logits=t(w.logits), params=torch.from_numpy(w.params.view(np.uint8).copy()).to(dev),
+             hist_ids=t(w.hist_ids), hist_off=t(w.hist_off), bias_ids=t(w.bias_ids),
+             bias_vals=t(w.bias_vals), bias_off=t(w.bias_off), uniforms=t(w.uniforms))
+    out_ids = torch.empty(B, dtype=torch.int64, device=dev)
+    out_probs = torch.empty(B, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        eng.sample_batch(d["logits"], d["params"], d["hist_ids"], d["hist_off"], d["bias_ids"],
+                         d["bias_vals"], d["bias_off"], d["uniforms"], out_ids=out_ids,
+                         out_probs=out_probs, stream=sptr, check=False)
+
+    eng.set_profiling(True)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    st = eng._lib.nls_stream_status(eng._h, None)
+    if st != 0:
+        raise RuntimeError(f"warm-up status {st}")
+
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    step_ms, k_light, k_full = [], [], []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        kl, kf = eng.last_kernel_ms()
+        e1.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+        k_light.append(kl)
+        k_full.append(kf)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    st = eng._lib.nls_stream_status(eng._h, None)
+    if st != 0:
+        raise RuntimeError(f"timed-run status {st}")
+
+    ms = reduce_max(dist, statistics.mean(step_ms), dev)
+    value = B * world / (ms / 1e3)
+
+    # roofline of each kernel: algorithmic bytes of the rows it serves / its time
+    peak, peak_src = peaks()
+    full_rows = row_is_full(w.params, w.V)
+    rb = row_bytes(w)
+    traffic = ncu_traffic()
+    kern = {
+        "light_kernel": (int(rb[~full_rows].sum()), statistics.mean(k_light), int((~full_rows).sum())),
+        "full_kernel": (int(rb[full_rows].sum()), statistics.mean(k_full), int(full_rows.sum())),
+    }
+    roof = {}
+    for name, (nbytes, kms, nrows) in kern.items():
+        ach = nbytes / (kms / 1e3) / 1e9 if kms > 0 else 0.0
+        tr = traffic.get(name)
+        roof[name] = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                      "frac": ach / peak, "traffic": tr, "rows": nrows, "ms": kms,
+                      "algorithmic_bytes": nbytes, "peak_source": peak_src}
+    dominant = max(roof, key=lambda n: roof[n]["ms"])
+    step_bytes = int(rb.sum())
+    step_roof = {"achieved": step_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                 "frac": step_bytes / (ms / 1e3) / 1e9 / peak, "algorithmic_bytes": step_bytes}
+
+    # e2e through the host API: pinned host logits, host outputs, synchronous call
+    pinned = torch.empty((B, w.V), dtype=torch.float32, pin_memory=True)
+    pinned.numpy()[:] = w.logits
+    host_logits = pinned.numpy()
+    e2e_times = []
+    for i in range(args.e2e_steps + 1):
+        t0 = time.perf_counter()
+        ids_h, probs_h, st = eng.sample_batch(host_logits, w.params, w.hist_ids, w.hist_off,
+                                              w.bias_ids, w.bias_vals, w.bias_off, w.uniforms,
+                                              want_probs=True)
+        dt = time.perf_counter() - t0
+        if i > 0:
+            e2e_times.append(dt)
+    e2e_s = reduce_max(dist, statistics.mean(e2e_times), dev)
+    h2d = w.logits.nbytes + w.params.nbytes + w.uniforms.nbytes + \
+        (w.hist_ids.nbytes + w.hist_off.nbytes if w.hist_ids is not None else 0) + \
+        (w.bias_ids.nbytes + w.bias_vals.nbytes + w.bias_off.nbytes if w.bias_ids is not None else 0)
+    d2h = ids_h.nbytes + probs_h.nbytes + 4
+    # device and host paths must agree
+    assert np.array_equal(ids_h, out_ids.cpu().numpy()), "host and device paths differ"
+
+    # B=1 latency (BASELINE config 2 shape: one row, V=128256), device inputs
+    w1 = pkg.workloads.make("c2_llama3_b1", seed=SEED)
+    d1 = dict(logits=t(w1.logits), params=torch.from_numpy(w1.params.view(np.uint8).copy()).to(dev),
+              hist_ids=t(w1.hist_ids), hist_off=t(w1.hist_off), uniforms=t(w1.uniforms))
+    o1 = torch.empty(1, dtype=torch.int64, device=dev)
+    p1 = torch.empty(1, dtype=torch.float32, device=dev)
+    eng.set_profiling(False)
+    lat = []
+    for i in range(args.latency_iters + 10):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        eng.sample_batch(d1["logits"], d1["params"], d1["hist_ids"], d1["hist_off"], None, None,
+                         None, d1["uniforms"], out_ids=o1, out_probs=p1, stream=sptr, check=False)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= 10:
+            lat.append(e0.elapsed_time(e1) * 1e3)
+    lat.sort()
+    latency = {"p50_us": lat[len(lat) // 2], "p99_us": lat[int(len(lat) * 0.99) - 1],
+               "config": "c2_llama3_b1: B=1, V=128256, top-k 40, device inputs, CUDA events"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.build()
+        threads = os.cpu_count() or 1
+        cpu_sample(oracle, w, 32, threads)  # warm
+        dt, ref_ids = cpu_sample(oracle, w, B, threads)
+        cpu = {"value": B / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+               "sample": f"the same {B}-row batch once, rows spread over {threads} threads "
+                         "(C restatement of sampler.nim, oracle/)"}
+        cpu["matches_gpu_rows"] = int((ref_ids == ids_h).sum())
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, BASELINE config 3 shapes and distributions)",
+            "config": config_dict(world),
+            "roofline": dict(roof[dominant], kernel=dominant),
+            "roofline_kernels": roof,
+            "step_roofline": step_roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": B * world / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
+            "gpu_launches": 2 * args.steps,
+            "latency_b1": latency,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

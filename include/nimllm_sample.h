@@ -1,0 +1,151 @@
+/*
+ * nimllm_sample.h -- C ABI of libnimllm_sample.so, the B200 (sm_100a) token
+ * sampler for nimllm.
+ *
+ * The library replaces the logits->token path of nimllm's Nim sampler
+ * (src/nimllm/sampler.nim in the reference repository). Nim reaches it through
+ * {.importc, dynlib: "libnimllm_sample.so".}; the Nim `Sampler` object keeps
+ * its params, its history and its RNG on the host and passes one uniform per
+ * sampled row. Every entry point below cites the reference interface it
+ * replaces.
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes and status codes; no exceptions cross the ABI.
+ *  - The caller owns every buffer; inputs are never written.
+ *  - Token ids are Nim `int` (int64). Ids outside [0, vocab) in histories and
+ *    bias lists are ignored, as in sampler.nim:70,76.
+ *  - Rows are independent. Row r reads params[r], the history
+ *    hist_ids[hist_off[r] .. hist_off[r+1]), the bias entries
+ *    bias_ids/bias_vals[bias_off[r] .. bias_off[r+1]), logits + r*ld and
+ *    uniforms[r].
+ *  - Without NLS_DEVICE_INPUTS every input pointer is host memory; with it,
+ *    every input pointer (logits, params, histories, bias, uniforms) is device
+ *    memory of the handle's device. Likewise NLS_DEVICE_OUTPUTS for outputs.
+ *  - A call whose outputs are host memory returns after the results are
+ *    written (it synchronises `stream`). A call with device outputs is
+ *    stream-ordered and returns at once; its kernel-side status (NaN rows,
+ *    capacity) is read with nls_stream_status().
+ *  - One handle per host thread / stream; calls on one handle must not
+ *    overlap in time on the host.
+ */
+#ifndef NIMLLM_SAMPLE_H
+#define NIMLLM_SAMPLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NLS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define NLS_API __attribute__((visibility("default")))
+#else
+#define NLS_API
+#endif
+
+typedef int32_t nls_status;
+enum {
+  NLS_OK = 0,
+  NLS_ERR_INVALID_ARG = 1, /* bad pointer/size/flag, duplicate bias id in a row */
+  NLS_ERR_CUDA = 2,        /* a CUDA runtime call failed; see nls_last_error() */
+  NLS_ERR_NCCL = 3,        /* a collective failed (vocab-sharded mode) */
+  NLS_ERR_TIMEOUT = 4,     /* a bounded wait ran out */
+  NLS_ERR_NAN_LOGITS = 5,  /* a sampling row holds NaN after penalties/bias/temperature;
+                              its out id is -1 (the reference's comparisons are
+                              inconsistent on NaN, so no result can match it) */
+  NLS_ERR_CAPACITY = 6,    /* rows/vocab beyond the handle's limits, or a row whose
+                              penalty window holds more distinct ids than supported */
+  NLS_ERR_NO_DEVICE = 7    /* no usable CUDA device */
+};
+
+/* flags */
+#define NLS_DEVICE_INPUTS 1u  /* all input pointers are device memory */
+#define NLS_DEVICE_OUTPUTS 2u /* out_ids / out_probs are device memory (async call) */
+
+/* Per-row generation parameters: SamplerParams (sampler.nim:11-21) without
+ * `seed` (the RNG stays in the Nim Sampler, sampler.nim:25,39) and without
+ * `logitBias` (passed as the CSR bias lists). 64 bytes, no padding. */
+typedef struct nls_row_params {
+  double temperature;       /* sampler.nim:12  <= 0: greedy argmax                */
+  double top_p;             /* sampler.nim:14  active iff 0 < top_p < 1           */
+  double min_p;             /* sampler.nim:15  active iff min_p > 0               */
+  double repeat_penalty;    /* sampler.nim:16  1.0 = off                          */
+  double presence_penalty;  /* sampler.nim:18                                     */
+  double frequency_penalty; /* sampler.nim:19                                     */
+  int64_t top_k;            /* sampler.nim:13  <= 0 or >= vocab: full sort        */
+  int64_t repeat_last_n;    /* sampler.nim:17  <= 0: the whole history            */
+} nls_row_params;
+
+typedef struct nls_handle nls_handle;
+
+/* Create a handle bound to CUDA `device`, sized for up to max_rows rows of up
+ * to max_vocab logits (1 <= max_vocab <= 262144). Replaces newSampler
+ * (sampler.nim:37-39) as the owner of per-stream state: the handle owns the
+ * device staging buffers and scratch; params/RNG/history stay with the
+ * caller. */
+NLS_API nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_t max_vocab);
+
+/* Release a handle and its device memory. NULL is accepted. */
+NLS_API void nls_destroy(nls_handle* h);
+
+/* Sample one token per row: Sampler.sample (sampler.nim:59-121) for a batch of
+ * independent samplers. Per row, in the reference's order: repeat/frequency/
+ * presence penalties over the last repeat_last_n history ids (:63-74), logit
+ * bias (:75-76), greedy argmax when temperature <= 0 (:77-78, no uniform
+ * consumed), temperature (:80-81), top-k by the reference's heap rule or the
+ * full stable sort (:83-97), softmax over the candidates (:98-100), top-p
+ * (:102-108), min-p (:109-114) and the inverse-CDF draw with
+ * uniforms[r] = rng.rand(1.0) (:115-121).
+ *
+ *  logits     [rows x ld] fp32, row-major, ld >= vocab
+ *  params     [rows]
+ *  hist_ids   history ids, CSR by hist_off[rows+1]; NULL = no history
+ *  bias_ids, bias_vals, bias_off  logit bias, CSR; NULL = no bias.
+ *             Ids must be unique within a row (a Nim Table); bias_vals are
+ *             Nim floats and are rounded to float32 like `b.float32`.
+ *  uniforms   [rows] in [0, 1); NULL only if every row is greedy
+ *  out_ids    [rows] sampled token ids (-1 for a failed row)
+ *  out_probs  [rows] softmax probability of the sampled token among the
+ *             candidates (probs[i] in sampler.nim:100,120); NULL = not wanted.
+ *             Greedy rows report 1.0.
+ *  stream     cudaStream_t (NULL = legacy default stream) */
+NLS_API nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                            int32_t vocab, const nls_row_params* params,
+                            const int64_t* hist_ids, const int64_t* hist_off,
+                            const int64_t* bias_ids, const double* bias_vals,
+                            const int64_t* bias_off, const double* uniforms,
+                            int64_t* out_ids, float* out_probs, uint32_t flags, void* stream);
+
+/* argmax (sampler.nim:45-49) per row: first index of the maximum with the
+ * reference's strict `>` (a NaN never wins unless it sits at index 0). */
+NLS_API nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                            int32_t vocab, int64_t* out_ids, uint32_t flags, void* stream);
+
+/* Kernel-side status of the last asynchronous call on this handle: waits for
+ * `stream` and returns the first error the kernels recorded (NLS_OK if none). */
+NLS_API nls_status nls_stream_status(nls_handle* h, void* stream);
+
+/* Per-kernel timing of later calls on this handle (tracing; no counterpart
+ * in the reference, which only times whole generations with epochTime,
+ * chat.nim:191,246-247). With `on` set, every sampling call records CUDA
+ * events around each of its kernels on the call's stream. */
+NLS_API nls_status nls_set_profiling(nls_handle* h, int32_t on);
+
+/* Device time in milliseconds of each kernel of the last profiled call:
+ * out_ms[0] = streaming kernel (greedy and small top-k rows), out_ms[1] =
+ * full-sort kernel. Waits for those events. `n` is the capacity of out_ms. */
+NLS_API nls_status nls_last_kernel_ms(nls_handle* h, float* out_ms, int32_t n);
+
+/* Human-readable text of a status code / of the handle's last CUDA error. */
+NLS_API const char* nls_status_str(nls_status s);
+NLS_API const char* nls_last_error(const nls_handle* h);
+
+/* Library version string, e.g. "nimllm-sample-b200 0.1.0 (sm_100a)". */
+NLS_API const char* nls_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NIMLLM_SAMPLE_H */

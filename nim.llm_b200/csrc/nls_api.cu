@@ -1,0 +1,387 @@
+// nls_api.cu -- the C ABI of libnimllm_sample.so (include/nimllm_sample.h).
+//
+// Host glue only: argument checks, staging of host inputs into device
+// buffers owned by the handle, the two kernel launches, and the read-back of
+// results and status. No sampling arithmetic happens on the host, and there
+// is no CPU fallback: without a usable CUDA device every call fails with
+// NLS_ERR_NO_DEVICE or NLS_ERR_CUDA.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "nls_kernels.h"
+#include "nimllm_sample.h"
+
+struct nls_handle {
+  int device = 0;
+  int max_rows = 0;
+  int max_vocab = 0;
+  int sm_count = 0;
+  // staging for host inputs (grown on demand)
+  float* d_logits = nullptr;
+  size_t logits_cap = 0;
+  nls_row_params* d_params = nullptr;
+  double* d_uniforms = nullptr;
+  int64_t* d_hist_off = nullptr;
+  int64_t* d_bias_off = nullptr;
+  int64_t* d_hist = nullptr;
+  size_t hist_cap = 0;
+  int64_t* d_bias_ids = nullptr;
+  double* d_bias_vals = nullptr;
+  size_t bias_cap = 0;
+  size_t bias_vals_cap = 0;
+  // outputs for host-output calls
+  int64_t* d_out_ids = nullptr;
+  float* d_out_probs = nullptr;
+  // [0] status, [1] full_count, [2 ..] full_list
+  int* d_work = nullptr;
+  // full-sort scratch: slots x 3 x vpad words
+  uint32_t* d_scratch = nullptr;
+  int vpad = 0;
+  int slots = 0;
+  int* h_status = nullptr;  // pinned
+  // profiling: events around the two kernels of the last call
+  int profiling = 0;
+  int profiled = 0;
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  char last_err[256] = {0};
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+nls_status cuda_fail(nls_handle* h, cudaError_t e, const char* what) {
+  if (h) snprintf(h->last_err, sizeof h->last_err, "%s: %s", what, cudaGetErrorString(e));
+  return NLS_ERR_CUDA;
+}
+
+#define NLS_CUDA(h, call)                                   \
+  do {                                                      \
+    cudaError_t e_ = (call);                                \
+    if (e_ != cudaSuccess) return cuda_fail((h), e_, #call); \
+  } while (0)
+
+template <class T>
+nls_status grow(nls_handle* h, T** p, size_t* cap, size_t n) {
+  if (n <= *cap && *p) return NLS_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  size_t want = n < 1024 ? 1024 : n;
+  NLS_CUDA(h, cudaMalloc((void**)p, want * sizeof(T)));
+  *cap = want;
+  return NLS_OK;
+}
+
+bool csr_ok(const int64_t* off, int rows) {
+  if (off[0] < 0) return false;
+  for (int r = 0; r < rows; ++r)
+    if (off[r + 1] < off[r]) return false;
+  return true;
+}
+
+int pick_cluster(const nls_handle* h, int rows, int vocab) {
+  const char* env = getenv("NLS_CLUSTER");
+  int C = 1;
+  if (env && *env) {
+    C = atoi(env);
+  } else if (vocab >= 8192) {
+    int want = (2 * h->sm_count + rows - 1) / (rows > 0 ? rows : 1);
+    C = want;
+  }
+  int maxc = vocab / 2048;
+  if (C > maxc) C = maxc;
+  if (C > 8) C = 8;
+  if (C < 1) C = 1;
+  return C;
+}
+
+nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st) {
+  nls::BatchArgs a = a_in;
+  a.status = h->d_work;
+  a.full_count = h->d_work + 1;
+  a.full_list = h->d_work + 2;
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, 2 * sizeof(int), st));
+  const int C = pick_cluster(h, a.rows, a.V);
+  int chunk = (a.V + C - 1) / C;
+  chunk = (chunk + 3) & ~3;
+  const bool prof = h->profiling != 0;
+  if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[0], st));
+  NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
+  if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
+  if (!a.argmax_only) NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st));
+  if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
+  h->profiled = prof ? 1 : 0;
+  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
+  (void)flags;
+  return NLS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* nls_version(void) { return "nimllm-sample-b200 0.1.0 (sm_100a)"; }
+
+const char* nls_status_str(nls_status s) {
+  switch (s) {
+    case NLS_OK: return "ok";
+    case NLS_ERR_INVALID_ARG: return "invalid argument";
+    case NLS_ERR_CUDA: return "CUDA error";
+    case NLS_ERR_NCCL: return "NCCL error";
+    case NLS_ERR_TIMEOUT: return "timeout";
+    case NLS_ERR_NAN_LOGITS: return "NaN logits in a sampling row";
+    case NLS_ERR_CAPACITY: return "capacity exceeded";
+    case NLS_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+const char* nls_last_error(const nls_handle* h) { return h ? h->last_err : "null handle"; }
+
+void nls_destroy(nls_handle* h) {
+  if (!h) return;
+  {
+    DeviceGuard g(h->device);
+    cudaFree(h->d_logits);
+    cudaFree(h->d_params);
+    cudaFree(h->d_uniforms);
+    cudaFree(h->d_hist_off);
+    cudaFree(h->d_bias_off);
+    cudaFree(h->d_hist);
+    cudaFree(h->d_bias_ids);
+    cudaFree(h->d_bias_vals);
+    cudaFree(h->d_out_ids);
+    cudaFree(h->d_out_probs);
+    cudaFree(h->d_work);
+    cudaFree(h->d_scratch);
+    if (h->h_status) cudaFreeHost(h->h_status);
+    for (cudaEvent_t e : h->ev)
+      if (e) cudaEventDestroy(e);
+  }
+  delete h;
+}
+
+nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_t max_vocab) {
+  if (!out) return NLS_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (max_rows < 1 || max_vocab < 1 || max_vocab > nls::kMaxVocab) return NLS_ERR_INVALID_ARG;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return NLS_ERR_NO_DEVICE;
+  if (device < 0 || device >= ndev) return NLS_ERR_INVALID_ARG;
+  nls_handle* h = new (std::nothrow) nls_handle();
+  if (!h) return NLS_ERR_CAPACITY;
+  h->device = device;
+  h->max_rows = max_rows;
+  h->max_vocab = max_vocab;
+  DeviceGuard g(device);
+  nls_status st = NLS_OK;
+  auto fail = [&](cudaError_t e, const char* what) {
+    st = cuda_fail(h, e, what);
+    return st;
+  };
+  cudaError_t e;
+  if ((e = cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) {
+    fail(e, "cudaDeviceGetAttribute");
+  } else if ((e = cudaMalloc(&h->d_params, sizeof(nls_row_params) * max_rows)) != cudaSuccess) {
+    fail(e, "cudaMalloc(params)");
+  } else if ((e = cudaMalloc(&h->d_uniforms, sizeof(double) * max_rows)) != cudaSuccess) {
+    fail(e, "cudaMalloc(uniforms)");
+  } else if ((e = cudaMalloc(&h->d_hist_off, sizeof(int64_t) * (max_rows + 1))) != cudaSuccess) {
+    fail(e, "cudaMalloc(hist_off)");
+  } else if ((e = cudaMalloc(&h->d_bias_off, sizeof(int64_t) * (max_rows + 1))) != cudaSuccess) {
+    fail(e, "cudaMalloc(bias_off)");
+  } else if ((e = cudaMalloc(&h->d_out_ids, sizeof(int64_t) * max_rows)) != cudaSuccess) {
+    fail(e, "cudaMalloc(out_ids)");
+  } else if ((e = cudaMalloc(&h->d_out_probs, sizeof(float) * max_rows)) != cudaSuccess) {
+    fail(e, "cudaMalloc(out_probs)");
+  } else if ((e = cudaMalloc(&h->d_work, sizeof(int) * (2 + max_rows))) != cudaSuccess) {
+    fail(e, "cudaMalloc(work)");
+  } else if ((e = cudaMallocHost(&h->h_status, sizeof(int))) != cudaSuccess) {
+    fail(e, "cudaMallocHost(status)");
+  }
+  if (st == NLS_OK) {
+    h->vpad = (max_vocab + 31) & ~31;
+    h->slots = h->sm_count;
+    size_t words = (size_t)h->slots * 3 * (size_t)h->vpad;
+    if ((e = cudaMalloc(&h->d_scratch, words * sizeof(uint32_t))) != cudaSuccess)
+      fail(e, "cudaMalloc(scratch)");
+  }
+  if (st != NLS_OK) {
+    nls_destroy(h);
+    return st;
+  }
+  *h->h_status = 0;
+  *out = h;
+  return NLS_OK;
+}
+
+nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                            int32_t vocab, const nls_row_params* params,
+                            const int64_t* hist_ids, const int64_t* hist_off,
+                            const int64_t* bias_ids, const double* bias_vals,
+                            const int64_t* bias_off, const double* uniforms, int64_t* out_ids,
+                            float* out_probs, uint32_t flags, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0 || vocab < 1 || ld < vocab) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !params || !out_ids) return NLS_ERR_INVALID_ARG;
+  if ((hist_ids == nullptr) != (hist_off == nullptr)) return NLS_ERR_INVALID_ARG;
+  if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
+    return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool dev_in = (flags & NLS_DEVICE_INPUTS) != 0;
+  const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
+
+  nls::BatchArgs a{};
+  a.rows = rows;
+  a.V = vocab;
+  a.argmax_only = 0;
+  if (dev_in) {
+    a.logits = logits;
+    a.ld = ld;
+    a.params = params;
+    a.hist_ids = hist_ids;
+    a.hist_off = hist_off;
+    a.bias_ids = bias_ids;
+    a.bias_vals = bias_vals;
+    a.bias_off = bias_off;
+    a.uniforms = uniforms;
+  } else {
+    nls_status s;
+    if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
+                                  (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
+                                  cudaMemcpyHostToDevice, st));
+    NLS_CUDA(h, cudaMemcpyAsync(h->d_params, params, sizeof(nls_row_params) * rows,
+                                cudaMemcpyHostToDevice, st));
+    a.logits = h->d_logits;
+    a.ld = vocab;
+    a.params = h->d_params;
+    if (uniforms) {
+      NLS_CUDA(h, cudaMemcpyAsync(h->d_uniforms, uniforms, sizeof(double) * rows,
+                                  cudaMemcpyHostToDevice, st));
+      a.uniforms = h->d_uniforms;
+    }
+    if (hist_ids) {
+      if (!csr_ok(hist_off, rows)) return NLS_ERR_INVALID_ARG;
+      const size_t n = (size_t)hist_off[rows];
+      if ((s = grow(h, &h->d_hist, &h->hist_cap, n)) != NLS_OK) return s;
+      if (n) NLS_CUDA(h, cudaMemcpyAsync(h->d_hist, hist_ids, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+      NLS_CUDA(h, cudaMemcpyAsync(h->d_hist_off, hist_off, sizeof(int64_t) * (rows + 1),
+                                  cudaMemcpyHostToDevice, st));
+      a.hist_ids = h->d_hist;
+      a.hist_off = h->d_hist_off;
+    }
+    if (bias_ids) {
+      if (!csr_ok(bias_off, rows)) return NLS_ERR_INVALID_ARG;
+      const size_t n = (size_t)bias_off[rows];
+      if ((s = grow(h, &h->d_bias_ids, &h->bias_cap, n)) != NLS_OK) return s;
+      if ((s = grow(h, &h->d_bias_vals, &h->bias_vals_cap, n)) != NLS_OK) return s;
+      if (n) {
+        NLS_CUDA(h, cudaMemcpyAsync(h->d_bias_ids, bias_ids, n * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+        NLS_CUDA(h, cudaMemcpyAsync(h->d_bias_vals, bias_vals, n * sizeof(double), cudaMemcpyHostToDevice, st));
+      }
+      NLS_CUDA(h, cudaMemcpyAsync(h->d_bias_off, bias_off, sizeof(int64_t) * (rows + 1),
+                                  cudaMemcpyHostToDevice, st));
+      a.bias_ids = h->d_bias_ids;
+      a.bias_vals = h->d_bias_vals;
+      a.bias_off = h->d_bias_off;
+    }
+  }
+  a.out_ids = dev_out ? out_ids : h->d_out_ids;
+  a.out_probs = dev_out ? out_probs : (out_probs ? h->d_out_probs : nullptr);
+  nls_status s = run_batch(h, a, flags, st);
+  if (s != NLS_OK) return s;
+  if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(out_ids, h->d_out_ids, sizeof(int64_t) * rows, cudaMemcpyDeviceToHost, st));
+  if (out_probs)
+    NLS_CUDA(h, cudaMemcpyAsync(out_probs, h->d_out_probs, sizeof(float) * rows, cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  return (nls_status)*h->h_status;
+}
+
+nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                            int32_t vocab, int64_t* out_ids, uint32_t flags, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0 || vocab < 1 || ld < vocab) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !out_ids) return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  nls::BatchArgs a{};
+  a.rows = rows;
+  a.V = vocab;
+  a.argmax_only = 1;
+  if (flags & NLS_DEVICE_INPUTS) {
+    a.logits = logits;
+    a.ld = ld;
+  } else {
+    nls_status s;
+    if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
+                                  (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
+                                  cudaMemcpyHostToDevice, st));
+    a.logits = h->d_logits;
+    a.ld = vocab;
+  }
+  const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
+  a.out_ids = dev_out ? out_ids : h->d_out_ids;
+  nls_status s = run_batch(h, a, flags, st);
+  if (s != NLS_OK) return s;
+  if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(out_ids, h->d_out_ids, sizeof(int64_t) * rows, cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  return (nls_status)*h->h_status;
+}
+
+nls_status nls_set_profiling(nls_handle* h, int32_t on) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  if (on && !h->ev[0]) {
+    for (cudaEvent_t& e : h->ev) NLS_CUDA(h, cudaEventCreate(&e));
+  }
+  h->profiling = on ? 1 : 0;
+  return NLS_OK;
+}
+
+nls_status nls_last_kernel_ms(nls_handle* h, float* out_ms, int32_t n) {
+  if (!h || !out_ms || n < 1) return NLS_ERR_INVALID_ARG;
+  if (!h->profiled) return NLS_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  NLS_CUDA(h, cudaEventSynchronize(h->ev[2]));
+  float ms = 0.0f;
+  NLS_CUDA(h, cudaEventElapsedTime(&ms, h->ev[0], h->ev[1]));
+  out_ms[0] = ms;
+  if (n > 1) {
+    NLS_CUDA(h, cudaEventElapsedTime(&ms, h->ev[1], h->ev[2]));
+    out_ms[1] = ms;
+  }
+  return NLS_OK;
+}
+
+nls_status nls_stream_status(nls_handle* h, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  NLS_CUDA(h, cudaStreamSynchronize((cudaStream_t)stream));
+  return (nls_status)*h->h_status;
+}
+
+}  // extern "C"

@@ -1,0 +1,271 @@
+// nls_common.cuh -- device helpers shared by the sampler kernels (sm_100a).
+//
+// Numerics follow src/nimllm/sampler.nim (reference repository) exactly:
+// every parity-relevant float op uses an explicit round-to-nearest intrinsic
+// (__fadd_rn, __fmul_rn, __fdiv_rn, __dmul_rn, ...) and the library is built
+// with -fmad=false, so nothing is contracted into an FMA.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "nimllm_sample.h"
+
+namespace nls {
+
+constexpr int kMaxVocab = 1 << 18;   // token ids fit in 18 bits (composite sort keys)
+constexpr int kLightKMax = 256;      // top-k rows with k <= this take the streaming path
+
+enum RowMode : int { kModeGreedy = 0, kModeTopK = 1, kModeFull = 2 };
+
+// Per-call arguments, passed by value to every kernel.
+struct BatchArgs {
+  const float* logits;
+  int64_t ld;
+  int rows;
+  int V;
+  const nls_row_params* params;
+  const int64_t* hist_ids;   // may be null
+  const int64_t* hist_off;
+  const int64_t* bias_ids;   // may be null
+  const double* bias_vals;
+  const int64_t* bias_off;
+  const double* uniforms;    // may be null when every row is greedy
+  int64_t* out_ids;
+  float* out_probs;          // may be null
+  int* full_list;            // rows handed to the full-sort kernel
+  int* full_count;
+  int* status;               // first error code recorded by any kernel
+  int argmax_only;           // nls_argmax_batch: plain argmax, no params
+};
+
+__device__ __forceinline__ void record_status(int* st, int code) { atomicCAS(st, 0, code); }
+
+// Order-preserving map of an fp32 value onto uint32 (ascending key ==
+// ascending value). -0.0 maps to the key of +0.0: Nim's cmp and tuple `<`
+// treat the two zeros as equal, so they must tie here too.
+__device__ __forceinline__ uint32_t fkey(float y) {
+  uint32_t u = __float_as_uint(y);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// expf as the reference computes it (C expf, correctly rounded in practice):
+// the double-precision exponential rounded once to float.
+__device__ __forceinline__ float ref_expf(float x) { return __double2float_rn(exp((double)x)); }
+
+// Row classification (sampler.nim:77-78, 85-86).
+__device__ __forceinline__ int row_mode(const nls_row_params& p, int V, int64_t* k_out) {
+  int64_t k = (p.top_k > 0) ? (p.top_k < V ? p.top_k : (int64_t)V) : (int64_t)V;
+  *k_out = k;
+  if (p.temperature <= 0.0) return kModeGreedy;
+  if (k < V && k <= kLightKMax) return kModeTopK;
+  return kModeFull;
+}
+
+// Penalty condition of sampler.nim:64-65.
+__device__ __forceinline__ bool penalties_active(const nls_row_params& p, int64_t hist_len) {
+  return hist_len > 0 &&
+         (p.repeat_penalty != 1.0 || p.presence_penalty != 0.0 || p.frequency_penalty != 0.0);
+}
+
+// ---------------------------------------------------------------------------
+// Patch table: the positions of one row (or chunk of a row) that penalties
+// or bias modify, with the count of each id in the penalty window and its
+// bias. A shared-memory open-addressing hash (keys = token id, -1 = empty)
+// plus a bitmap over the chunk so the streaming loop tests one bit per
+// element and probes the hash only on a hit.
+// ---------------------------------------------------------------------------
+struct PatchTable {
+  int* key;
+  int* cnt;
+  float* bias;
+  int* flag;       // bit 0: has bias
+  uint32_t* bits;  // bitmap over [lo, hi), bit (pos - lo)
+  int log2size;
+  int lo, hi;
+};
+
+__device__ __forceinline__ uint32_t patch_hash(int tok, int log2size) {
+  return ((uint32_t)tok * 0x9E3779B1u) >> (32 - log2size);
+}
+
+// Returns false when the table is full.
+__device__ __forceinline__ bool patch_insert(PatchTable& T, int tok, int cnt_add,
+                                             bool has_bias, float b, int* dup_flag) {
+  const uint32_t mask = (1u << T.log2size) - 1u;
+  uint32_t h = patch_hash(tok, T.log2size);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    int prev = atomicCAS(&T.key[h], -1, tok);
+    if (prev == -1 || prev == tok) {
+      if (cnt_add) atomicAdd(&T.cnt[h], cnt_add);
+      if (has_bias) {
+        int old = atomicOr(&T.flag[h], 1);
+        if (old & 1) atomicExch(dup_flag, 1);
+        T.bias[h] = b;
+      }
+      return true;
+    }
+    h = (h + 1u) & mask;
+  }
+  return false;
+}
+
+__device__ __forceinline__ int patch_find(const PatchTable& T, int tok) {
+  const uint32_t mask = (1u << T.log2size) - 1u;
+  uint32_t h = patch_hash(tok, T.log2size);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    if (T.key[h] == tok) return (int)h;
+    h = (h + 1u) & mask;
+  }
+  return -1;
+}
+
+// Penalties then bias for one logit (sampler.nim:71-76). `cnt` > 0 only when
+// the penalty block is active for the row.
+__device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int slot,
+                                             const nls_row_params& p) {
+  int cnt = T.cnt[slot];
+  if (cnt > 0) {
+    if (p.repeat_penalty != 1.0) {
+      float rp = __double2float_rn(p.repeat_penalty);
+      x = (x > 0.0f) ? __fdiv_rn(x, rp) : __fmul_rn(x, rp);
+    }
+    double d = __dadd_rn(__dmul_rn((double)cnt, p.frequency_penalty), p.presence_penalty);
+    x = __fsub_rn(x, __double2float_rn(d));
+  }
+  if (T.flag[slot] & 1) x = __fadd_rn(x, T.bias[slot]);
+  return x;
+}
+
+// Block-wide construction of the patch table for positions [lo, hi) of `row`.
+// Returns the number of patched positions (block-uniform). Sets *overflow /
+// *dup (shared ints) on a full table / a duplicate bias id.
+__device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_params& p,
+                             PatchTable& T, int* s_counter, int* s_overflow, int* s_dup) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int hs = 1 << T.log2size;
+  for (int i = tid; i < hs; i += nt) { T.key[i] = -1; T.cnt[i] = 0; T.flag[i] = 0; }
+  const int nwords = (T.hi - T.lo + 31) >> 5;
+  for (int i = tid; i < nwords; i += nt) T.bits[i] = 0u;
+  if (tid == 0) { *s_counter = 0; *s_overflow = 0; *s_dup = 0; }
+  __syncthreads();
+  if (a.hist_ids != nullptr) {
+    int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+    if (penalties_active(p, h1 - h0)) {
+      int64_t start = h0;
+      if (p.repeat_last_n > 0 && h1 - h0 > p.repeat_last_n) start = h1 - p.repeat_last_n;  // :67
+      for (int64_t i = start + tid; i < h1; i += nt) {
+        int64_t tok = a.hist_ids[i];
+        if (tok >= T.lo && tok < T.hi) {
+          if (!patch_insert(T, (int)tok, 1, false, 0.0f, s_dup)) atomicExch(s_overflow, 1);
+        }
+      }
+    }
+  }
+  if (a.bias_ids != nullptr) {
+    int64_t b0 = a.bias_off[row], b1 = a.bias_off[row + 1];
+    for (int64_t i = b0 + tid; i < b1; i += nt) {
+      int64_t tok = a.bias_ids[i];
+      if (tok >= T.lo && tok < T.hi) {
+        float b = __double2float_rn(a.bias_vals[i]);  // b.float32 (:76)
+        if (!patch_insert(T, (int)tok, 0, true, b, s_dup)) atomicExch(s_overflow, 1);
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < hs; i += nt) {
+    int k = T.key[i];
+    if (k >= 0) {
+      int off = k - T.lo;
+      atomicOr(&T.bits[off >> 5], 1u << (off & 31));
+      atomicAdd(s_counter, 1);
+    }
+  }
+  __syncthreads();
+  return *s_counter;
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide radix select: the K-th largest key (1-based) among the entries i
+// in [0, n) for which get(i, &key) returns true. 8-bit digits, 4 rounds.
+// `hist` is 256 shared words, `sh` at least 4 shared words. All threads call.
+// ---------------------------------------------------------------------------
+template <class Get>
+__device__ uint32_t block_select_kth_largest(int n, uint32_t K, Get get, uint32_t* hist,
+                                             uint32_t* sh) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  uint32_t prefix = 0, pmask = 0;
+  if (tid == 0) sh[1] = K;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += nt) hist[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
+      uint32_t k;
+      if (get(i, &k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const int lane = tid;
+      uint32_t rem = sh[1];
+      // lane l owns bins 255-8l .. 248-8l (descending)
+      uint32_t c = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) c += hist[255 - 8 * lane - b];
+      uint32_t incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      uint32_t ball = __ballot_sync(0xffffffffu, incl >= rem);
+      int L = __ffs(ball) - 1;
+      if (lane == L) {
+        uint32_t above = incl - c;
+        int d = 0;
+        for (int b = 0; b < 8; ++b) {
+          int bin = 255 - 8 * lane - b;
+          uint32_t hc = hist[bin];
+          if (above + hc >= rem) { d = bin; break; }
+          above += hc;
+        }
+        sh[0] = (uint32_t)d;
+        sh[1] = rem - above;
+      }
+    }
+    __syncthreads();
+    prefix |= sh[0] << shift;
+    pmask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Block-wide bitonic sort of n64 (power of two) uint64 keys, descending.
+__device__ inline void block_bitonic_desc(unsigned long long* v, int n64) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int size = 2; size <= n64; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n64 / 2; i += nt) {
+        int lo = 2 * i - (i & (stride - 1));
+        int hi = lo + stride;
+        bool desc = ((lo & size) == 0);
+        unsigned long long x = v[lo], y = v[hi];
+        if ((x < y) == desc) { v[lo] = y; v[hi] = x; }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+}  // namespace nls

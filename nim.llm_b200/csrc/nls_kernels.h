@@ -1,0 +1,22 @@
+// nls_kernels.h -- host-side launchers of the sampler kernels.
+#pragma once
+
+#include <cstddef>
+#include <cuda_runtime.h>
+
+#include "nls_common.cuh"
+
+namespace nls {
+
+// Streaming kernel (greedy rows and top-k rows with k <= kLightKMax): one
+// cluster of C CTAs per row, CTA c owning positions [c*chunk, (c+1)*chunk).
+size_t light_smem_bytes(int C, int chunk);
+cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream);
+
+// Full-sort kernel over the rows listed in a.full_list (count in a.full_count):
+// `slots` persistent CTAs, each with 3*vpad words of `scratch`.
+size_t full_smem_bytes(int V);
+cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
+                        cudaStream_t stream);
+
+}  // namespace nls

@@ -1,0 +1,221 @@
+// nls_scan.cuh -- exact parallel replay of a sequential fp32 accumulation.
+//
+// The reference accumulates softmax denominators, top-p running sums, draw
+// totals and the draw itself one element at a time in fp32
+// (src/nimllm/sampler.nim:54-56, 104-108, 115-120). A tree reduction rounds
+// differently, and for long candidate lists (the full-sort path) the
+// difference reaches 1e-4 relative (small terms are absorbed by the running
+// sum). This file reproduces the sequential result bit for bit with a block
+// scan.
+//
+// Method. While the running value v stays inside one binade [2^E, 2^(E+1))
+// every representable result is a multiple of u = 2^(E-23). Adding a term a
+// and rounding to nearest-even is then integer arithmetic on S = v/u:
+//     S' = S + rne(a/u)              when frac(a/u) != 1/2   ("A" step)
+//     S' = the even one of S+k, S+k+1 when a/u = k + 1/2       ("B" step)
+// The maps {S -> S + c} and {S -> 2*ceil((S + c)/2) + d} are closed under
+// composition (worked out below), so a block can scan them in parallel. A
+// result that leaves the binade (the grid changes) is detected exactly on the
+// u-grid and that one element is recomputed with a real fp32 add; the scan
+// restarts from there with the new grid. Subtraction (the draw, r -= p) is the
+// same with S = -r/u. Everything else -- the sums themselves -- is exact
+// integer arithmetic.
+#pragma once
+
+#include <climits>
+#include <cstdint>
+
+namespace nls {
+
+// f(S) = isB ? (S + a) + ((S + a) & 1) + b : S + a
+struct Fn {
+  long long a, b;
+  int isB;
+};
+
+__device__ __forceinline__ Fn fn_identity() { return Fn{0, 0, 0}; }
+
+// "f then g"
+__device__ __forceinline__ Fn fn_compose(const Fn& f, const Fn& g) {
+  if (!f.isB) {
+    if (!g.isB) return Fn{f.a + g.a, 0, 0};
+    return Fn{f.a + g.a, g.b, 1};
+  }
+  if (!g.isB) return Fn{f.a, f.b + g.a, 1};
+  long long c = f.b + g.a;
+  return Fn{f.a, c + (c & 1LL) + g.b, 1};
+}
+
+__device__ __forceinline__ long long fn_apply(const Fn& f, long long S) {
+  long long t = S + f.a;
+  return f.isB ? t + (t & 1LL) + f.b : t;
+}
+
+// The step for adding a >= 0 on the grid 2^ue. Values of a/u at or above
+// 2^40 only ever occur at a binade change (they are clamped; the element is
+// then recomputed exactly).
+__device__ __forceinline__ Fn fn_of(float a, int ue) {
+  double q = ldexp((double)a, -ue);  // exact: a power-of-two scaling
+  const double kBig = 1099511627776.0;  // 2^40
+  if (q >= kBig) return Fn{1LL << 40, 0, 0};
+  double kf = floor(q);
+  double f = q - kf;
+  long long k = (long long)kf;
+  if (f < 0.5) return Fn{k, 0, 0};
+  if (f > 0.5) return Fn{k + 1, 0, 0};
+  return Fn{k, 0, 1};
+}
+
+// exact float value of S * 2^ue (|S| < 2^25 here)
+__device__ __forceinline__ float grid_value(long long S, int ue) {
+  return __double2float_rn(ldexp((double)S, ue));
+}
+
+__device__ __forceinline__ int binade_exp(float v) {
+  // exponent of |v| for normals; denormals and zero share the grid of
+  // [2^-126, 2^-125), i.e. E = -126.
+  uint32_t u = __float_as_uint(v) & 0x7fffffffu;
+  int e = (int)(u >> 23) - 127;
+  return e < -126 ? -126 : e;
+}
+
+struct ScanShared {
+  Fn warp_tot[32];
+  long long S_end;
+  float v;
+  int trig;
+  int stopped;
+};
+
+template <int NT>
+__device__ __forceinline__ Fn block_exclusive_scan_fn(Fn x, ScanShared& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Fn incl = x;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    Fn o;
+    o.a = __shfl_up_sync(0xffffffffu, incl.a, off);
+    o.b = __shfl_up_sync(0xffffffffu, incl.b, off);
+    o.isB = __shfl_up_sync(0xffffffffu, incl.isB, off);
+    if (lane >= off) incl = fn_compose(o, incl);
+  }
+  Fn excl;
+  excl.a = __shfl_up_sync(0xffffffffu, incl.a, 1);
+  excl.b = __shfl_up_sync(0xffffffffu, incl.b, 1);
+  excl.isB = __shfl_up_sync(0xffffffffu, incl.isB, 1);
+  if (lane == 0) excl = fn_identity();
+  if (lane == 31) sm.warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    constexpr int NW = NT / 32;
+    Fn w = (lane < NW) ? sm.warp_tot[lane] : fn_identity();
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      Fn o;
+      o.a = __shfl_up_sync(0xffffffffu, w.a, off);
+      o.b = __shfl_up_sync(0xffffffffu, w.b, off);
+      o.isB = __shfl_up_sync(0xffffffffu, w.isB, off);
+      if (lane >= off) w = fn_compose(o, w);
+    }
+    // exclusive per warp
+    Fn e;
+    e.a = __shfl_up_sync(0xffffffffu, w.a, 1);
+    e.b = __shfl_up_sync(0xffffffffu, w.b, 1);
+    e.isB = __shfl_up_sync(0xffffffffu, w.isB, 1);
+    if (lane == 0) e = fn_identity();
+    if (lane < NW) sm.warp_tot[lane] = e;
+  }
+  __syncthreads();
+  Fn wp = sm.warp_tot[warp];
+  __syncthreads();
+  return fn_compose(wp, excl);
+}
+
+struct ScanResult {
+  float v;     // final (or stopping) value
+  int stop_j;  // element at which `stop` fired, or -1
+};
+
+// Replays v <- fl(v + a_j) (DEC: v <- fl(v - a_j)) for j in [j0, j1), with
+// a_j = elem(j) >= 0 and finite. Stops at the first j whose new value makes
+// stop(value) true (the value after that element is returned). When `absorb`
+// is set (increasing sums over non-increasing terms only) the scan ends as
+// soon as the next term is below half a grid step: every later term then
+// rounds away. All threads of the block must call; NT = blockDim.x.
+template <int NT, int EPT, bool DEC, class Elem, class Stop>
+__device__ ScanResult exact_scan(int j0, int j1, float v0, Elem elem, Stop stop, bool has_stop,
+                                 bool absorb, ScanShared& sm) {
+  const int tid = threadIdx.x;
+  constexpr int CH = NT * EPT;
+  float v = v0;
+  int j = j0;
+  while (j < j1) {
+    const int E = binade_exp(v);
+    const int ue = E - 23;
+    long long S0 = (long long)ldexp((double)v, -ue);
+    if (DEC) S0 = -S0;
+    if (!DEC && absorb) {
+      float a0 = elem(j);
+      if ((double)a0 < ldexp(1.0, ue - 1)) break;
+    }
+    const int cend = (j1 - j > CH) ? j + CH : j1;
+    Fn fe[EPT];
+    Fn F = fn_identity();
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      int jj = j + tid * EPT + e;
+      fe[e] = fn_identity();
+      if (jj < cend) {
+        fe[e] = fn_of(elem(jj), ue);
+        F = fn_compose(F, fe[e]);
+      }
+    }
+    Fn P = block_exclusive_scan_fn<NT>(F, sm);
+    long long S = fn_apply(P, S0);
+    int trig = INT_MAX;
+    long long Strig = 0;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      int jj = j + tid * EPT + e;
+      if (jj < cend && trig == INT_MAX) {
+        long long Sn = fn_apply(fe[e], S);
+        bool t;
+        if (!DEC) t = (Sn >= (1LL << 24));
+        else t = (Sn >= 0) || (E > -126 && Sn >= -(1LL << 23));
+        if (!t && has_stop) t = stop(grid_value(DEC ? -Sn : Sn, ue));
+        if (t) { trig = jj; Strig = S; }
+        S = Sn;
+      }
+    }
+    if (tid == 0) sm.trig = INT_MAX;
+    __syncthreads();
+    if (trig != INT_MAX) atomicMin(&sm.trig, trig);
+    int last_owner = (cend - 1 - j) / EPT;
+    if (tid == last_owner) sm.S_end = S;
+    __syncthreads();
+    const int tmin = sm.trig;
+    if (tmin == INT_MAX) {
+      long long Se = sm.S_end;
+      v = grid_value(DEC ? -Se : Se, ue);
+      j = cend;
+      __syncthreads();
+      continue;
+    }
+    if (trig == tmin) {
+      float vprev = grid_value(DEC ? -Strig : Strig, ue);
+      float a = elem(tmin);
+      float vn = DEC ? __fsub_rn(vprev, a) : __fadd_rn(vprev, a);
+      sm.v = vn;
+      sm.stopped = has_stop ? (stop(vn) ? 1 : 0) : 0;
+    }
+    __syncthreads();
+    v = sm.v;
+    int st = sm.stopped;
+    __syncthreads();
+    if (st) return ScanResult{v, tmin};
+    j = tmin + 1;
+  }
+  return ScanResult{v, -1};
+}
+
+}  // namespace nls

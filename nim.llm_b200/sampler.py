@@ -1,0 +1,260 @@
+"""Host-side mirror of nimllm's sampler API over the C ABI.
+
+Mirrors src/nimllm/sampler.nim (reference repository): the same names,
+argument meaning and state -- `SamplerParams` (:11-21), `Sampler` with
+`params`, `rng` and `history` (:23-26), `defaultSampling` (:28-31),
+`greedySampling` (:33-35), `newSampler` (:37-39), `accept` (:41-43),
+`argmax` (:45-49) and `sample` (:59-121). Every sampling decision is made by
+libnimllm_sample.so on the GPU; this module only keeps the host state the
+Nim `Sampler` keeps (params, history, RNG) and marshals one call.
+
+`Engine` is the batched entry (one call samples B independent rows), used
+by the bench and the parity tests; it accepts numpy arrays (host memory) or
+torch CUDA tensors (device memory, NLS_DEVICE_INPUTS).
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+from typing import Optional
+
+import numpy as np
+
+from . import _abi
+from ._abi import NlsError, ROW_PARAMS_DTYPE
+
+
+# ---------------------------------------------------------------------------
+# SamplerParams and presets (sampler.nim:11-35)
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class SamplerParams:
+    temperature: float = 0.0
+    topK: int = 0
+    topP: float = 0.0
+    minP: float = 0.0
+    repeatPenalty: float = 0.0
+    repeatLastN: int = 0
+    presencePenalty: float = 0.0
+    frequencyPenalty: float = 0.0
+    seed: int = 0
+    logitBias: dict = dataclasses.field(default_factory=dict)
+
+
+def defaultSampling() -> SamplerParams:
+    return SamplerParams(temperature=0.7, topK=40, topP=0.95, minP=0.05,
+                         repeatPenalty=1.1, repeatLastN=64, seed=-1)
+
+
+def greedySampling() -> SamplerParams:
+    return SamplerParams(temperature=0.0, topK=0, topP=1.0, repeatPenalty=1.0, seed=0)
+
+
+def params_record(p: SamplerParams) -> np.void:
+    """The 64-byte nls_row_params record of a SamplerParams."""
+    rec = np.zeros(1, ROW_PARAMS_DTYPE)
+    rec[0] = (p.temperature, p.topP, p.minP, p.repeatPenalty, p.presencePenalty,
+              p.frequencyPenalty, p.topK, p.repeatLastN)
+    return rec[0]
+
+
+class Rand:
+    """Uniform source for `Sampler.rng`: `rand(1.0)` returns a float in [0, 1).
+
+    The reference draws with Nim's std/random; its stream cannot be produced
+    without Nim, so this default is numpy's PCG64 seeded from `seed` (seed < 0:
+    OS entropy). Any object with a `rand(max)` method can replace it, e.g. one
+    replaying uniforms recorded from a Nim program."""
+
+    def __init__(self, seed: int | None = None):
+        self._g = np.random.default_rng(None if seed is None or seed < 0 else seed)
+
+    def rand(self, maxv: float = 1.0) -> float:
+        return float(self._g.random()) * maxv
+
+
+# ---------------------------------------------------------------------------
+# Engine: one handle of the C library
+# ---------------------------------------------------------------------------
+def _host_ptr(a: Optional[np.ndarray]):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+class Engine:
+    """Owns one nls_handle (device staging and scratch) on `device`."""
+
+    def __init__(self, device: int = 0, max_rows: int = 256, max_vocab: int = 131072):
+        self._lib = _abi.load()
+        h = ctypes.c_void_p()
+        st = self._lib.nls_create(ctypes.byref(h), int(device), int(max_rows), int(max_vocab))
+        if st != 0:
+            raise NlsError(st, "nls_create")
+        self._h = h
+        self.device = device
+        self.max_rows = max_rows
+        self.max_vocab = max_vocab
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.nls_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return self._lib.nls_last_error(self._h).decode()
+
+    def _check(self, st: int, what: str):
+        if st != 0:
+            raise NlsError(st, f"{what}: {self.last_error()}" if st == _abi.NLS_ERR_CUDA else what)
+
+    # -- batched sampling ---------------------------------------------------
+    def sample_batch(self, logits, params, hist_ids=None, hist_off=None, bias_ids=None,
+                     bias_vals=None, bias_off=None, uniforms=None, want_probs: bool = False,
+                     out_ids=None, out_probs=None, stream: int = 0, check: bool = True):
+        """Sample one token per row.
+
+        Host path: numpy arrays (logits [B, V] fp32, params ROW_PARAMS_DTYPE
+        [B], CSR int64 histories and bias lists, float64 uniforms); returns
+        (ids int64[B], probs float32[B] or None) and the status.
+        Device path: torch CUDA tensors for every input (params as an int8/uint8
+        tensor of B*64 bytes or a float64 [B, 8] view); outputs must be given
+        as CUDA tensors; the call is stream-ordered (check=False returns the
+        status without waiting)."""
+        if _is_torch(logits):
+            return self._sample_batch_device(logits, params, hist_ids, hist_off, bias_ids, bias_vals,
+                                             bias_off, uniforms, out_ids, out_probs, stream, check)
+        logits = np.asarray(logits, dtype=np.float32)
+        if logits.ndim == 1:
+            logits = logits[None, :]
+        if logits.strides[1] != 4:
+            logits = np.ascontiguousarray(logits)
+        B, V = logits.shape
+        ld = logits.strides[0] // 4
+        params = np.ascontiguousarray(params, dtype=ROW_PARAMS_DTYPE)
+        assert params.shape == (B,)
+        if hist_ids is not None:
+            hist_ids = np.ascontiguousarray(hist_ids, dtype=np.int64)
+            hist_off = np.ascontiguousarray(hist_off, dtype=np.int64)
+        if bias_ids is not None:
+            bias_ids = np.ascontiguousarray(bias_ids, dtype=np.int64)
+            bias_vals = np.ascontiguousarray(bias_vals, dtype=np.float64)
+            bias_off = np.ascontiguousarray(bias_off, dtype=np.int64)
+        if uniforms is not None:
+            uniforms = np.ascontiguousarray(uniforms, dtype=np.float64)
+        ids = np.empty(B, dtype=np.int64)
+        probs = np.empty(B, dtype=np.float32) if want_probs else None
+        st = self._lib.nls_sample_batch(
+            self._h, _host_ptr(logits), ld, B, V, _host_ptr(params), _host_ptr(hist_ids),
+            _host_ptr(hist_off), _host_ptr(bias_ids), _host_ptr(bias_vals), _host_ptr(bias_off),
+            _host_ptr(uniforms), _host_ptr(ids), _host_ptr(probs), 0, ctypes.c_void_p(stream))
+        if check:
+            self._check(st, "nls_sample_batch")
+        return ids, probs, st
+
+    def _sample_batch_device(self, logits, params, hist_ids, hist_off, bias_ids, bias_vals, bias_off,
+                             uniforms, out_ids, out_probs, stream, check):
+        def dp(t):
+            return None if t is None else ctypes.c_void_p(t.data_ptr())
+        B, V = logits.shape
+        ld = logits.stride(0)
+        assert logits.stride(1) == 1
+        st = self._lib.nls_sample_batch(
+            self._h, dp(logits), ld, B, V, dp(params), dp(hist_ids), dp(hist_off), dp(bias_ids),
+            dp(bias_vals), dp(bias_off), dp(uniforms), dp(out_ids), dp(out_probs),
+            _abi.NLS_DEVICE_INPUTS | _abi.NLS_DEVICE_OUTPUTS, ctypes.c_void_p(stream))
+        if check:
+            self._check(st, "nls_sample_batch")
+            st = self._lib.nls_stream_status(self._h, ctypes.c_void_p(stream))
+            self._check(st, "nls_sample_batch (kernel status)")
+        return out_ids, out_probs, st
+
+    def set_profiling(self, on: bool = True) -> None:
+        self._check(self._lib.nls_set_profiling(self._h, 1 if on else 0), "nls_set_profiling")
+
+    def last_kernel_ms(self) -> tuple[float, float]:
+        """(streaming kernel ms, full-sort kernel ms) of the last profiled call."""
+        out = (ctypes.c_float * 2)()
+        self._check(self._lib.nls_last_kernel_ms(self._h, out, 2), "nls_last_kernel_ms")
+        return float(out[0]), float(out[1])
+
+    def argmax_batch(self, logits) -> np.ndarray:
+        logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        if logits.ndim == 1:
+            logits = logits[None, :]
+        B, V = logits.shape
+        ids = np.empty(B, dtype=np.int64)
+        st = self._lib.nls_argmax_batch(self._h, _host_ptr(logits), V, B, V, _host_ptr(ids), 0,
+                                        ctypes.c_void_p(0))
+        self._check(st, "nls_argmax_batch")
+        return ids
+
+
+_default_engine: Optional[Engine] = None
+
+
+def default_engine() -> Engine:
+    global _default_engine
+    if _default_engine is None:
+        _default_engine = Engine(0, max_rows=256, max_vocab=1 << 18)
+    return _default_engine
+
+
+# ---------------------------------------------------------------------------
+# Sampler (sampler.nim:23-121)
+# ---------------------------------------------------------------------------
+class Sampler:
+    def __init__(self, params: SamplerParams, engine: Optional[Engine] = None):
+        self.params = params
+        self.rng = Rand(params.seed)
+        self.history: list[int] = []
+        self.engine = engine
+
+    def accept(self, tok: int) -> None:                       # sampler.nim:41-43
+        self.history.append(int(tok))
+
+    def sample(self, logitsIn) -> int:                        # sampler.nim:59-121
+        """Choose a token; `logitsIn` is not modified. Draws one uniform from
+        `rng` only when temperature > 0, as the reference does."""
+        p = self.params
+        logits = np.ascontiguousarray(np.asarray(logitsIn, dtype=np.float32))
+        hist = np.asarray(self.history, dtype=np.int64)
+        bias_ids = np.fromiter(p.logitBias.keys(), dtype=np.int64, count=len(p.logitBias))
+        bias_vals = np.fromiter(p.logitBias.values(), dtype=np.float64, count=len(p.logitBias))
+        u = np.array([self.rng.rand(1.0) if p.temperature > 0 else 0.0], dtype=np.float64)
+        eng = self.engine or default_engine()
+        ids, _, _ = eng.sample_batch(
+            logits[None, :], np.array([params_record(p)], dtype=ROW_PARAMS_DTYPE),
+            hist, np.array([0, hist.size], dtype=np.int64),
+            bias_ids, bias_vals, np.array([0, bias_ids.size], dtype=np.int64), u)
+        return int(ids[0])
+
+
+def newSampler(p: Optional[SamplerParams] = None, engine: Optional[Engine] = None) -> Sampler:
+    return Sampler(p if p is not None else defaultSampling(), engine)
+
+
+def accept(s: Sampler, tok: int) -> None:
+    s.accept(tok)
+
+
+def sample(s: Sampler, logitsIn) -> int:
+    return s.sample(logitsIn)
+
+
+def argmax(logits, engine: Optional[Engine] = None) -> int:    # sampler.nim:45-49
+    eng = engine or default_engine()
+    return int(eng.argmax_batch(logits)[0])
+
+
+__all__ = ["SamplerParams", "defaultSampling", "greedySampling", "params_record", "Rand",
+           "Engine", "Sampler", "newSampler", "accept", "sample", "argmax", "default_engine",
+           "NlsError", "ROW_PARAMS_DTYPE"]

@@ -1,0 +1,293 @@
+"""GPU parity: libnimllm_sample.so (through the C ABI) against the CPU oracle.
+
+Bar:
+  - token ids identical, except on rows whose decision margin (draw, top-p or
+    min-p boundary; oracle diag `margin`) is below 1e-6;
+  - probabilities of the drawn token within 1e-5 relative;
+  - top-k survivor sets follow the reference heap's tie rule exactly (the
+    known-answer and golden cases hold many ties).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import case_arrays, kat_arrays
+from kat_cases import KATS
+
+pytestmark = pytest.mark.gpu
+
+PROB_RTOL = 1e-5
+MARGIN_EXCUSE = 1e-6
+
+
+@pytest.fixture(scope="module")
+def big_engine(pkg):
+    eng = pkg.Engine(0, max_rows=1024, max_vocab=1 << 18)
+    yield eng
+    eng.close()
+
+
+def compare(ids, probs, ref_ids, dg, params, what):
+    sampling = params["temperature"] > 0
+    bad = np.nonzero(ids != ref_ids)[0]
+    unexcused = [int(i) for i in bad if not (dg is not None and dg["margin"][i] < MARGIN_EXCUSE)]
+    assert not unexcused, f"{what}: ids differ at rows {unexcused[:10]} " \
+        f"(gpu {ids[unexcused[:10]].tolist()} oracle {ref_ids[unexcused[:10]].tolist()})"
+    if probs is not None and dg is not None:
+        ok = sampling & (ids == ref_ids)
+        want = dg["prob"][ok].astype(np.float64)
+        got = probs[ok].astype(np.float64)
+        rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
+        assert np.all(rel <= PROB_RTOL), f"{what}: prob rel err {rel.max()}"
+    return bad.size
+
+
+def run_both(engine, oracle_mod, a, threads=8):
+    ids, probs, st = engine.sample_batch(**a, want_probs=True, check=False)
+    with np.errstate(all="ignore"):
+        ref, dg = oracle_mod.sample_batch(**a, threads=threads, diag=True)
+    return ids, probs, st, ref, dg
+
+
+# ---- golden vectors and known answers --------------------------------------
+def test_golden_cases(engine, golden):
+    n = golden["ids"].size
+    by_v = {}
+    for i in range(n):
+        by_v.setdefault(int(golden["V"][i]), []).append(i)
+    for V, idx in by_v.items():
+        parts = [case_arrays(golden, i) for i in idx]
+        logits = np.concatenate([p["logits"] for p in parts])
+        params = np.concatenate([p["params"] for p in parts])
+        hist = np.concatenate([p["hist_ids"] for p in parts])
+        hoff = np.concatenate([[0], np.cumsum([p["hist_ids"].size for p in parts])]).astype(np.int64)
+        bids = np.concatenate([p["bias_ids"] for p in parts])
+        bvals = np.concatenate([p["bias_vals"] for p in parts])
+        boff = np.concatenate([[0], np.cumsum([p["bias_ids"].size for p in parts])]).astype(np.int64)
+        u = np.concatenate([p["uniforms"] for p in parts])
+        ids, probs, st = engine.sample_batch(logits, params, hist, hoff, bids, bvals, boff, u,
+                                             want_probs=True)
+        want = golden["ids"][idx]
+        assert np.array_equal(ids, want), f"V={V}: rows {np.nonzero(ids != want)[0].tolist()}"
+        samp = params["temperature"] > 0
+        gp = golden["probs"][idx]
+        both_nan = np.isnan(probs) & np.isnan(gp)
+        assert np.all(both_nan[samp] | (probs[samp] == gp[samp])), f"V={V}: probs"
+
+
+@pytest.mark.parametrize("case", KATS, ids=[c[0] for c in KATS])
+def test_known_answers(engine, case):
+    a, expected = kat_arrays(case)
+    ids, _, st = engine.sample_batch(**a)
+    assert ids[0] == expected
+
+
+# ---- the five configurations ----------------------------------------------
+def replicate(w, n, seed):
+    """n rows of the same logits/params/history with fresh uniforms (the
+    config's repeated draws from one row)."""
+    rng = np.random.default_rng(seed)
+    B = n
+    hl = 0 if w.hist_ids is None else w.hist_ids.size
+    return dict(logits=np.repeat(w.logits[:1], B, axis=0), params=np.repeat(w.params[:1], B),
+                hist_ids=None if w.hist_ids is None else np.tile(w.hist_ids, B),
+                hist_off=None if w.hist_ids is None else np.arange(0, hl * B + 1, hl, dtype=np.int64),
+                uniforms=rng.random(B))
+
+
+def as_args(w):
+    return dict(logits=w.logits, params=w.params, hist_ids=w.hist_ids, hist_off=w.hist_off,
+                bias_ids=w.bias_ids, bias_vals=w.bias_vals, bias_off=w.bias_off, uniforms=w.uniforms)
+
+
+def test_c1_tiny_1000_draws(pkg, big_engine, oracle_mod):
+    w = pkg.workloads.make("c1_tiny", seed=42)
+    a = replicate(w, 1000, 42)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a)
+    compare(ids, probs, ref, dg, a["params"], "c1")
+
+
+def test_c2_llama3_single_row(pkg, big_engine, oracle_mod):
+    w = pkg.workloads.make("c2_llama3_b1", seed=1234)
+    a = replicate(w, 256, 1234)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a)
+    compare(ids, probs, ref, dg, a["params"], "c2")
+    g = pkg.workloads.make("c2_llama3_b1_greedy", seed=1234)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(g))
+    compare(ids, probs, ref, dg, g.params, "c2 greedy")
+
+
+def test_c3_batched_heterogeneous(pkg, big_engine, oracle_mod):
+    w = pkg.workloads.make("c3_batched_hetero", seed=1234)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(w))
+    assert st == 0
+    compare(ids, probs, ref, dg, w.params, "c3")
+
+
+def test_c4_qwen2_rows_subset(pkg, big_engine, oracle_mod):
+    w = pkg.workloads.make("c4_qwen2_sharded", seed=1234, rows=np.arange(0, 8192, 128))
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(w))
+    compare(ids, probs, ref, dg, w.params, "c4")
+
+
+def test_c5_full_vocab_nucleus(pkg, big_engine, oracle_mod):
+    w = pkg.workloads.make("c5_full_vocab_nucleus", seed=1234)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(w))
+    compare(ids, probs, ref, dg, w.params, "c5")
+    g = pkg.workloads.make("c5_full_vocab_greedy", seed=1234)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(g))
+    compare(ids, probs, ref, dg, g.params, "c5 greedy")
+
+
+# ---- edge cases ---------------------------------------------------------------
+def single(logits, prm, hist=(), bias=None, u=0.5):
+    from oracle.oracle import PARAMS_DTYPE
+    P = np.zeros(1, PARAMS_DTYPE)
+    P[0] = prm
+    bias = bias or {}
+    return dict(logits=np.asarray(logits, np.float32)[None, :], params=P,
+                hist_ids=np.array(hist, np.int64), hist_off=np.array([0, len(hist)], np.int64),
+                bias_ids=np.array(list(bias.keys()), np.int64),
+                bias_vals=np.array(list(bias.values()), np.float64),
+                bias_off=np.array([0, len(bias)], np.int64), uniforms=np.array([u]))
+
+
+def test_vocab_one(engine):
+    for prm in [(0.0, 1, 0, 1, 0, 0, 0, 64), (1.0, 0.5, 0.1, 1, 0, 0, 0, 64), (1.0, 0.5, 0.1, 1, 0, 0, 5, 64)]:
+        ids, _, _ = engine.sample_batch(**single([3.0], prm))
+        assert ids[0] == 0
+
+
+@pytest.mark.parametrize("k", [0, 5, 50000])
+def test_all_neg_inf_and_pos_inf_rows(engine, oracle_mod, k):
+    V = 4096
+    rows = [np.full(V, -np.inf, np.float32)]
+    x = np.random.default_rng(1).normal(0, 1, V).astype(np.float32)
+    x[[7, 300, 4000]] = np.inf
+    rows.append(x)
+    for x in rows:
+        for u in (0.0, 0.3, 0.999):
+            a = single(x, (0.9, 0.9, 0.05, 1.0, 0, 0, k, 64), u=u)
+            ids, _, st, ref, dg = run_both(engine, oracle_mod, a)
+            assert ids[0] == ref[0]
+
+
+def test_nan_row_reports_error_others_fine(engine, oracle_mod):
+    rng = np.random.default_rng(3)
+    from oracle.oracle import PARAMS_DTYPE
+    x = rng.normal(0, 2, (3, 5000)).astype(np.float32)
+    x[1, 17] = np.nan
+    P = np.zeros(3, PARAMS_DTYPE)
+    P[:] = (0.8, 0.9, 0.0, 1.0, 0, 0, 40, 64)
+    u = rng.random(3)
+    ids, _, st = engine.sample_batch(x, P, uniforms=u, check=False)
+    assert st == 5 and ids[1] == -1
+    ref = oracle_mod.sample_batch(x[[0, 2]], P[[0, 2]], uniforms=u[[0, 2]])
+    assert ids[0] == ref[0] and ids[2] == ref[1]
+
+
+def test_duplicate_bias_id_is_invalid(engine):
+    a = single(np.zeros(100), (1.0, 1, 0, 1, 0, 0, 10, 64))
+    a["bias_ids"] = np.array([5, 5], np.int64)
+    a["bias_vals"] = np.array([1.0, 2.0])
+    a["bias_off"] = np.array([0, 2], np.int64)
+    ids, _, st = engine.sample_batch(**a, check=False)
+    assert st == 1 and ids[0] == -1
+
+
+@pytest.mark.parametrize("k", [257, 1000, 5000, 9999])
+def test_large_k_heap_path_with_ties(engine, oracle_mod, k):
+    rng = np.random.default_rng(k)
+    V = 10000
+    x = np.round(rng.normal(0, 2, (8, V)) * 4).astype(np.float32) / np.float32(4)
+    from oracle.oracle import PARAMS_DTYPE
+    P = np.zeros(8, PARAMS_DTYPE)
+    P[:] = (0.7, 1.0, 0.0, 1.0, 0, 0, k, 64)
+    P["top_p"][:4] = 0.9
+    a = dict(logits=x, params=P, uniforms=rng.random(8))
+    ids, probs, st, ref, dg = run_both(engine, oracle_mod, a)
+    compare(ids, probs, ref, dg, P, f"k={k}")
+
+
+def test_tie_overflow_goes_to_full_path(engine, oracle_mod):
+    V = 30000
+    from oracle.oracle import PARAMS_DTYPE
+    x = np.full((4, V), 1.5, np.float32)
+    x[1, ::7] = 2.0
+    x[2] = np.round(np.random.default_rng(0).normal(0, 0.5, V)).astype(np.float32)
+    P = np.zeros(4, PARAMS_DTYPE)
+    P[:] = (1.0, 0.95, 0.0, 1.0, 0, 0, 50, 64)
+    a = dict(logits=x, params=P, uniforms=np.array([0.1, 0.5, 0.77, 0.999]))
+    ids, probs, st, ref, dg = run_both(engine, oracle_mod, a)
+    compare(ids, probs, ref, dg, P, "ties")
+
+
+def test_long_history_penalty_window(engine, oracle_mod):
+    rng = np.random.default_rng(11)
+    V = 20000
+    x = rng.normal(0, 2, V).astype(np.float32)
+    hist = rng.permutation(V)[:3000]
+    for k in (40, 0):
+        a = single(x, (0.0, 1.0, 0.0, 1.3, 0.1, 0.05, k, 0), hist=hist)
+        ids, _, st, ref, dg = run_both(engine, oracle_mod, a)
+        assert st == 0 and ids[0] == ref[0]
+        a = single(x, (0.8, 0.9, 0.0, 1.3, 0.1, 0.05, k, 0), hist=hist, u=0.4)
+        ids, _, st, ref, dg = run_both(engine, oracle_mod, a)
+        assert st == 0 and ids[0] == ref[0]
+
+
+def test_strided_rows_host_path(engine, oracle_mod):
+    rng = np.random.default_rng(2)
+    full = rng.normal(0, 2, (16, 3000)).astype(np.float32)
+    x = full[:, :2500]
+    from oracle.oracle import PARAMS_DTYPE
+    P = np.zeros(16, PARAMS_DTYPE)
+    P[:] = (0.8, 0.9, 0.05, 1.0, 0, 0, 20, 64)
+    P["top_k"][8:] = 0
+    u = rng.random(16)
+    ids, _, _ = engine.sample_batch(x, P, uniforms=u)
+    ref = oracle_mod.sample_batch(np.ascontiguousarray(x), P, uniforms=u)
+    assert np.array_equal(ids, ref)
+
+
+def test_device_inputs_match_host_path(pkg, engine):
+    import torch
+    w = pkg.workloads.make("c3_batched_hetero", seed=7, rows=np.arange(32), V=50000)
+    ids_h, probs_h, _ = engine.sample_batch(**as_args(w), want_probs=True)
+    dev = torch.device("cuda:0")
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    params_t = torch.from_numpy(w.params.view(np.uint8).copy()).to(dev)
+    out_ids = torch.empty(w.B, dtype=torch.int64, device=dev)
+    out_probs = torch.empty(w.B, dtype=torch.float32, device=dev)
+    engine.sample_batch(t(w.logits), params_t, t(w.hist_ids), t(w.hist_off), t(w.bias_ids),
+                        t(w.bias_vals), t(w.bias_off), t(w.uniforms), out_ids=out_ids,
+                        out_probs=out_probs)
+    torch.cuda.synchronize()
+    assert np.array_equal(out_ids.cpu().numpy(), ids_h)
+    assert np.array_equal(out_probs.cpu().numpy(), probs_h)
+
+
+def test_repeat_calls_are_deterministic(pkg, big_engine):
+    w = pkg.workloads.make("c3_batched_hetero", seed=5, rows=np.arange(64))
+    a, _, _ = big_engine.sample_batch(**as_args(w))
+    b, _, _ = big_engine.sample_batch(**as_args(w))
+    assert np.array_equal(a, b)
+
+
+def test_python_mirror_api(pkg):
+    """newSampler / accept / sample keep the reference's host state: the
+    history grows only through accept, and greedy calls draw no uniform."""
+    s = pkg.newSampler(pkg.greedySampling())
+    x = np.array([0.1, 2.0, 0.5], np.float32)
+    state = s.rng._g.bit_generator.state
+    assert s.sample(x) == 1
+    assert s.rng._g.bit_generator.state == state
+    s.accept(1)
+    assert s.history == [1]
+    p = pkg.defaultSampling()
+    p.seed = 3
+    s2 = pkg.newSampler(p)
+    tok = s2.sample(np.random.default_rng(0).normal(0, 2, 500).astype(np.float32))
+    assert 0 <= tok < 500
+    assert pkg.argmax(np.array([1.0, 3.0, 3.0], np.float32)) == 1
