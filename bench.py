@@ -221,6 +221,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-iters", type=int, default=200)
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="only the device-resident steps (for ncu captures); prints a short line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -296,6 +298,14 @@ def main():
 
     ms = reduce_max(dist, statistics.mean(step_ms), dev)
     value = B * world / (ms / 1e3)
+    if args.kernels_only:
+        if rank == 0:
+            print(json.dumps({"kernels_only": True, "ms_per_step": ms, "value": value,
+                              "light_ms": statistics.mean(k_light), "full_ms": statistics.mean(k_full)}))
+        eng.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
 
     # roofline of each kernel: algorithmic bytes of the rows it serves / its time
     peak, peak_src = peaks()

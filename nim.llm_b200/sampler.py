@@ -135,10 +135,10 @@ class Engine:
         logits = np.asarray(logits, dtype=np.float32)
         if logits.ndim == 1:
             logits = logits[None, :]
-        if logits.strides[1] != 4:
-            logits = np.ascontiguousarray(logits)
         B, V = logits.shape
-        ld = logits.strides[0] // 4
+        if logits.strides[1] != 4 or (B > 1 and (logits.strides[0] % 4 or logits.strides[0] < 4 * V)):
+            logits = np.ascontiguousarray(logits)
+        ld = V if B == 1 else logits.strides[0] // 4
         params = np.ascontiguousarray(params, dtype=ROW_PARAMS_DTYPE)
         assert params.shape == (B,)
         if hist_ids is not None:
