@@ -123,6 +123,25 @@ NLS_API nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t 
 NLS_API nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
                             int32_t vocab, int64_t* out_ids, uint32_t flags, void* stream);
 
+/* Allocation-free sampling. No counterpart in the reference: it exists for
+ * callers that cannot allocate GPU memory -- code running while a CUDA graph
+ * is captured, allocator-less hosts, serving loops that must not touch the
+ * allocator -- and so cannot use nls_create. Same semantics and arguments as
+ * nls_sample_batch with NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS: every pointer
+ * is device memory of the current device, the call is stream-ordered and
+ * returns after the launches; a row that fails in the kernels gets out id -1.
+ * It calls no cudaMalloc/cudaFree: its scratch is one fixed device array in
+ * the library (about 12 MiB per device, held until exit). Limits: rows <= 4096
+ * and vocab <= 262144, else NLS_ERR_CAPACITY. The first call on a device
+ * looks up that array's address (make it before any stream capture). All
+ * calls share the array; calls that overlap on the GPU race on it. */
+NLS_API nls_status nls_sample_batch_noalloc(const float* logits, int64_t ld, int32_t rows,
+                                            int32_t vocab, const nls_row_params* params,
+                                            const int64_t* hist_ids, const int64_t* hist_off,
+                                            const int64_t* bias_ids, const double* bias_vals,
+                                            const int64_t* bias_off, const double* uniforms,
+                                            int64_t* out_ids, float* out_probs, void* stream);
+
 /* Kernel-side status of the last asynchronous call on this handle: waits for
  * `stream` and returns the first error the kernels recorded (NLS_OK if none). */
 NLS_API nls_status nls_stream_status(nls_handle* h, void* stream);

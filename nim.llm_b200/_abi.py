@@ -30,7 +30,7 @@ NLS_DEVICE_OUTPUTS = 2
 EXPORTS = (
     "nls_create", "nls_destroy", "nls_sample_batch", "nls_argmax_batch",
     "nls_stream_status", "nls_status_str", "nls_last_error", "nls_version",
-    "nls_set_profiling", "nls_last_kernel_ms",
+    "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
 )
 
 # nls_row_params: 6 doubles + 2 int64, 64 bytes, no padding.
@@ -74,6 +74,8 @@ def load(path: str | None = None):
     L.nls_set_profiling.argtypes = [vp, i32]
     L.nls_last_kernel_ms.restype = i32
     L.nls_last_kernel_ms.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i32]
+    L.nls_sample_batch_noalloc.restype = i32
+    L.nls_sample_batch_noalloc.argtypes = [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     _lib = L
     return L
 
