@@ -53,6 +53,12 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
   uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
   return __uint_as_float(u);
 }
+// Float threshold equivalent to "key >= k" for non-NaN values. Keys below the
+// key of -Inf decode to negative NaNs; every non-NaN value passes them.
+__device__ __forceinline__ float key_threshold_float(uint32_t k) {
+  const float f = fkey_inv(k);
+  return (f != f) ? -INFINITY : f;
+}
 
 // expf as the reference computes it (C expf, correctly rounded in practice):
 // the double-precision exponential rounded once to float.
@@ -83,12 +89,21 @@ __device__ __forceinline__ bool penalties_active(const nls_row_params& p, int64_
 struct PatchTable {
   int* key;
   int* cnt;
-  float* bias;
-  int* flag;       // bit 0: has bias
-  uint32_t* bits;  // bitmap over [lo, hi), bit (pos - lo)
+  float* bias;     // bias as float32; after precompute_patches: the patched value
+  int* flag;       // bit 0: has bias, bit 1: bias slot holds the patched value
+  uint32_t* bits;  // bitmap over [lo, hi): bit (pos - lo) >> gshift
   int log2size;
   int lo, hi;
+  int gshift;      // positions per bit = 1 << gshift
 };
+
+__device__ __forceinline__ int patch_bitmap_words(int len, int gshift) {
+  return ((((len + (1 << gshift) - 1) >> gshift)) + 31) >> 5;
+}
+__device__ __forceinline__ bool patch_bit(const PatchTable& T, int off) {
+  const int g = off >> T.gshift;
+  return (T.bits[g >> 5] >> (g & 31)) & 1u;
+}
 
 __device__ __forceinline__ uint32_t patch_hash(int tok, int log2size) {
   return ((uint32_t)tok * 0x9E3779B1u) >> (32 - log2size);
@@ -115,11 +130,15 @@ __device__ __forceinline__ bool patch_insert(PatchTable& T, int tok, int cnt_add
   return false;
 }
 
+// Slot of `tok`, or -1. Linear probing without deletions: an empty slot ends
+// the probe sequence of a key that is not in the table.
 __device__ __forceinline__ int patch_find(const PatchTable& T, int tok) {
   const uint32_t mask = (1u << T.log2size) - 1u;
   uint32_t h = patch_hash(tok, T.log2size);
   for (uint32_t probe = 0; probe <= mask; ++probe) {
-    if (T.key[h] == tok) return (int)h;
+    const int k = T.key[h];
+    if (k == tok) return (int)h;
+    if (k == -1) return -1;
     h = (h + 1u) & mask;
   }
   return -1;
@@ -142,6 +161,24 @@ __device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int s
   return x;
 }
 
+// Replace each slot's bias by the final patched logit of its position, read
+// from `chunk` (the row's logits from position lo). Block-wide; after it,
+// patched_value() gives the logit the reference sees at a patched position.
+__device__ inline void precompute_patches(PatchTable& T, const float* chunk,
+                                          const nls_row_params& p) {
+  const int hs = 1 << T.log2size;
+  for (int i = threadIdx.x; i < hs; i += blockDim.x) {
+    const int k = T.key[i];
+    if (k >= 0) {
+      const float v = patch_apply(__ldg(chunk + (k - T.lo)), T, i, p);
+      T.bias[i] = v;
+      T.flag[i] |= 2;
+    }
+  }
+  __syncthreads();
+}
+__device__ __forceinline__ float patched_value(const PatchTable& T, int slot) { return T.bias[slot]; }
+
 // Block-wide construction of the patch table for positions [lo, hi) of `row`.
 // Returns the number of patched positions (block-uniform). Sets *overflow /
 // *dup (shared ints) on a full table / a duplicate bias id.
@@ -150,7 +187,7 @@ __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_p
   const int tid = threadIdx.x, nt = blockDim.x;
   const int hs = 1 << T.log2size;
   for (int i = tid; i < hs; i += nt) { T.key[i] = -1; T.cnt[i] = 0; T.flag[i] = 0; }
-  const int nwords = (T.hi - T.lo + 31) >> 5;
+  const int nwords = patch_bitmap_words(T.hi - T.lo, T.gshift);
   for (int i = tid; i < nwords; i += nt) T.bits[i] = 0u;
   if (tid == 0) { *s_counter = 0; *s_overflow = 0; *s_dup = 0; }
   __syncthreads();
@@ -181,7 +218,7 @@ __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_p
   for (int i = tid; i < hs; i += nt) {
     int k = T.key[i];
     if (k >= 0) {
-      int off = k - T.lo;
+      int off = (k - T.lo) >> T.gshift;
       atomicOr(&T.bits[off >> 5], 1u << (off & 31));
       atomicAdd(s_counter, 1);
     }
@@ -192,25 +229,36 @@ __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_p
 
 // ---------------------------------------------------------------------------
 // Block-wide radix select: the K-th largest key (1-based) among the entries i
-// in [0, n) for which get(i, &key) returns true. 8-bit digits, 4 rounds.
-// `hist` is 256 shared words, `sh` at least 4 shared words. All threads call.
+// in [0, n) for which get(i, &key) returns true. 8-bit digits, 4 rounds; the
+// shared histogram is filled with warp-aggregated atomics (__match_any_sync),
+// since sampler keys are heavily skewed onto a few top-byte values.
+// `hist` is 256 shared words, `sh` at least 4 shared words. All threads call;
+// blockDim.x must be a multiple of 32.
 // ---------------------------------------------------------------------------
+//
+// With rounds < 4 only the top 8*rounds bits are resolved: the result is then
+// that prefix with the low bits zero, a lower bound of the K-th largest key,
+// and sh[2] receives the number of entries at or above it.
 template <class Get>
 __device__ uint32_t block_select_kth_largest(int n, uint32_t K, Get get, uint32_t* hist,
-                                             uint32_t* sh) {
-  const int tid = threadIdx.x, nt = blockDim.x;
+                                             uint32_t* sh, int rounds = 4) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
   uint32_t prefix = 0, pmask = 0;
-  if (tid == 0) sh[1] = K;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  if (tid == 0) { sh[0] = 0; sh[1] = K; sh[2] = 0; sh[3] = 0; }
+  const int nround = (n + nt - 1) / nt * nt;
+  const int last_shift = 32 - 8 * rounds;
+  for (int shift = 24; shift >= last_shift; shift -= 8) {
     for (int i = tid; i < 256; i += nt) hist[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < n; i += nt) {
-      uint32_t k;
-      if (get(i, &k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+    for (int i = tid; i < nround; i += nt) {
+      uint32_t k = 0;
+      const bool ok = (i < n) && get(i, &k) && ((k & pmask) == prefix);
+      const int bin = ok ? (int)((k >> shift) & 255u) : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (ok && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
     }
     __syncthreads();
     if (tid < 32) {
-      const int lane = tid;
       uint32_t rem = sh[1];
       // lane l owns bins 255-8l .. 248-8l (descending)
       uint32_t c = 0;
@@ -235,6 +283,8 @@ __device__ uint32_t block_select_kth_largest(int n, uint32_t K, Get get, uint32_
         }
         sh[0] = (uint32_t)d;
         sh[1] = rem - above;
+        sh[2] = sh[3] + above + hist[d];  // entries >= the new prefix
+        sh[3] += above;                   // entries strictly above the prefix
       }
     }
     __syncthreads();

@@ -261,7 +261,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     const bool heap = (K64 < V);
     const int ncand = heap ? (int)K64 : V;
 
-    PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, FT_HASH_LOG2, 0, V};
+    PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, FT_HASH_LOG2, 0, V, 0};
     const int npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
     if (S.patch_overflow || S.dup) {
       if (tid == 0) {
@@ -281,7 +281,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       int gi = INT_MAX;
       for (int i = tid; i < V; i += FT_THREADS) {
         float x = rowp[i];
-        if (npatch > 0 && ((T.bits[i >> 5] >> (i & 31)) & 1u)) {
+        if (npatch > 0 && patch_bit(T, i)) {
           const int slot = patch_find(T, i);
           if (slot >= 0) x = patch_apply(x, T, slot, p);
         }
@@ -316,7 +316,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int anynan = 0;
     for (int i = tid; i < V; i += FT_THREADS) {
       float x = rowp[i];
-      if (npatch > 0 && ((T.bits[i >> 5] >> (i & 31)) & 1u)) {
+      if (npatch > 0 && patch_bit(T, i)) {
         const int slot = patch_find(T, i);
         if (slot >= 0) x = patch_apply(x, T, slot, p);
       }

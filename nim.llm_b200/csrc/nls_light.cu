@@ -1,41 +1,54 @@
 // nls_light.cu -- streaming kernel for greedy rows and top-k rows (k <= 256).
 //
-// One thread-block cluster per row (cluster size C = 1..16). CTA c streams the
-// chunk [c*chunk, (c+1)*chunk) of the row from HBM exactly once with 16-byte
-// loads, applying the row's penalties and bias (a bitmap marks the patched
-// positions) and the temperature on the fly (src/nimllm/sampler.nim:63-81).
+// One thread-block cluster per row (cluster size C = 1..8). CTA c owns the
+// chunk [c*chunk, (c+1)*chunk) of the row and reads it from HBM exactly once:
+// one thread issues bulk copies (cp.async.bulk, 16 KB stages, LT_NSTAGE in
+// flight, mbarrier completion) into a shared-memory ring while the block
+// consumes earlier stages. On the fly it applies the row's penalties and bias
+// (a bitmap marks the patched float4 groups) and the temperature
+// (src/nimllm/sampler.nim:63-81):
 //  - greedy rows (temperature <= 0): argmax with the reference's strict `>`
 //    (sampler.nim:45-49, 77-78);
-//  - top-k rows: every element whose order key reaches a running threshold
-//    is appended to a shared-memory candidate buffer; when the buffer fills,
-//    a radix select over it raises the threshold to the current k-th largest
-//    key, keeping all ties. At the end each CTA holds a superset of its
-//    chunk's top-k, including every element equal to the row's k-th largest
-//    value, which the reference's heap tie rule needs (sampler.nim:88-95).
-// CTA 0 then gathers the candidates of the cluster through distributed
-// shared memory, selects the reference's exact survivor set, sorts it in heap
-// output order (value descending, ties by index descending), and one warp
-// replays softmax, top-p, min-p and the draw with the reference's sequential
-// fp32 loops (sampler.nim:98-121). Rows whose ties overflow the buffers are
-// handed to the full-sort kernel.
+//  - top-k rows: the first stage sets a threshold (a lower bound of its k-th
+//    largest order key); every later element at or above the running
+//    threshold is appended to a shared candidate buffer, and when the buffer
+//    passes half full a radix select raises the threshold again. The
+//    threshold never exceeds the chunk's true k-th largest value, so each CTA
+//    ends with a superset of its chunk's top-k that contains every element
+//    equal to the row's k-th largest value -- what the reference heap's tie
+//    rule needs (sampler.nim:88-95).
+// CTA 0 gathers the cluster's candidates through distributed shared memory,
+// selects the reference's exact survivor set, sorts it in heap output order
+// (value descending, ties by index descending), and one warp replays softmax,
+// top-p, min-p and the draw with the reference's sequential fp32 loops
+// (sampler.nim:98-121). Rows whose candidates overflow the buffers, or whose
+// penalty window overflows the patch table, are handed to the full-sort
+// kernel.
 #include <cooperative_groups.h>
 
 #include "nls_common.cuh"
 #include "nls_kernels.h"
+#include "nls_tma.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace nls {
 
-constexpr int LT_THREADS = 512;
-constexpr int LT_UNROLL = 2;                          // float4 loads in flight per thread
-constexpr int LT_TILE = LT_THREADS * LT_UNROLL * 4;   // elements per tile
-constexpr int LT_SLOT = 512;                          // candidates a CTA hands to the merge
-constexpr int LT_CAP = LT_SLOT + LT_TILE;             // candidate buffer
+constexpr int LT_THREADS = 256;
+constexpr int LT_STAGE = 4096;                        // floats per bulk-copy stage (16 KB)
+constexpr int LT_NSTAGE = 4;                          // stages in flight
+constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per thread per stage
+constexpr int LT_CAP = 2048;                          // candidate buffer
+constexpr int LT_LIMIT = LT_CAP / 2;                  // compact above this after a stage
+constexpr int LT_SLOT = LT_LIMIT;                     // candidates a CTA hands to the merge
 constexpr int LT_HASH_LOG2 = 10;
-constexpr int LT_PER_THREAD = (LT_CAP + LT_THREADS - 1) / LT_THREADS;
+constexpr int LT_PER_THREAD = LT_CAP / LT_THREADS;
+constexpr int LT_GSHIFT = 2;                          // one patch bit per float4 group
+static_assert(LT_STAGE % (4 * LT_THREADS) == 0, "a stage splits into whole float4 groups");
 
 struct LightShared {
+  float ring[LT_NSTAGE][LT_STAGE];
+  uint64_t full_bar[LT_NSTAGE];
   uint32_t cand_key[LT_CAP];
   int cand_idx[LT_CAP];
   int hkey[1 << LT_HASH_LOG2];
@@ -45,41 +58,53 @@ struct LightShared {
   unsigned long long sortbuf[kLightKMax];
   float tval[kLightKMax];
   float pval[kLightKMax];
+  float seq[kLightKMax];
   uint32_t hist[256];
   uint32_t sel[4];
   float gbest_w[LT_THREADS / 32];
   int gidx_w[LT_THREADS / 32];
   // published for the cluster merge
+  uint32_t thr_pub;
   int ncand;
   int nan;
   int overflow;
   int nan0;
+  int failed;
   float gbest;
   int gidx;
   // scratch
   uint32_t thr;
   int counter, patch_overflow, dup;
   int cnt_gt, cnt_ge, nsurv;
-  int mtotal;
 };
 
-static_assert(sizeof(LightShared) % 16 == 0 || true, "");
-
-size_t light_smem_bytes(int C, int chunk) {
-  size_t bm_words = ((size_t)chunk + 31) / 32;
-  bm_words = (bm_words + 3) & ~(size_t)3;
-  size_t base = (sizeof(LightShared) + 15) & ~(size_t)15;
-  size_t merge = (C > 1) ? (size_t)C * LT_SLOT * (sizeof(uint32_t) + sizeof(int)) : 0;
-  return base + bm_words * 4 + merge;
+static int bitmap_words_host(int chunk) {
+  int groups = (chunk + (1 << LT_GSHIFT) - 1) >> LT_GSHIFT;
+  int w = (groups + 31) >> 5;
+  return (w + 3) & ~3;
 }
 
-// Keep the candidates whose key is >= the K-th largest; raises S.thr.
+size_t light_smem_bytes(int C, int chunk) {
+  size_t base = (sizeof(LightShared) + 15) & ~(size_t)15;
+  size_t merge = (C > 1) ? (size_t)C * LT_SLOT * (sizeof(uint32_t) + sizeof(int)) : 0;
+  return base + (size_t)bitmap_words_host(chunk) * 4 + merge;
+}
+
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Keep the candidates whose key is at least a lower bound of the K-th largest
+// (its top 16 bits, or all 32 when that leaves too many); raises S.thr.
 // Returns the new candidate count (the same value in every thread).
 __device__ int light_compact(LightShared& S, uint32_t K) {
   const int tid = threadIdx.x;
   const int n = S.ncand;
-  uint32_t t = block_select_kth_largest(
-      n, K, [&](int i, uint32_t* k) { *k = S.cand_key[i]; return true; }, S.hist, S.sel);
+  auto get = [&](int i, uint32_t* k) { *k = S.cand_key[i]; return S.cand_idx[i] >= 0; };
+  uint32_t t = block_select_kth_largest(n, K, get, S.hist, S.sel, 2);
+  if ((int)S.sel[2] > LT_LIMIT / 2) t = block_select_kth_largest(n, K, get, S.hist, S.sel, 4);
   uint32_t keys[LT_PER_THREAD];
   int ids[LT_PER_THREAD];
 #pragma unroll
@@ -114,14 +139,17 @@ __device__ int light_compact(LightShared& S, uint32_t K) {
   return nnew;
 }
 
-__global__ void __launch_bounds__(LT_THREADS)
+__global__ void __launch_bounds__(LT_THREADS, 2)
 light_kernel(BatchArgs a, int C, int chunk) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   LightShared& S = *reinterpret_cast<LightShared*>(smem_raw);
   const size_t base_bytes = (sizeof(LightShared) + 15) & ~(size_t)15;
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + base_bytes);
-  int bm_words = (chunk + 31) / 32;
-  bm_words = (bm_words + 3) & ~3;
+  const int bm_words = [&] {
+    int groups = (chunk + (1 << LT_GSHIFT) - 1) >> LT_GSHIFT;
+    int w = (groups + 31) >> 5;
+    return (w + 3) & ~3;
+  }();
   uint32_t* mkey = bitmap + bm_words;
   int* midx = reinterpret_cast<int*>(mkey + C * LT_SLOT);
 
@@ -155,105 +183,313 @@ light_kernel(BatchArgs a, int C, int chunk) {
   const int lo = min(V, crank * chunk);
   const int hi = min(V, lo + chunk);
   const int len = hi - lo;
+  const float* rowp = a.logits + (int64_t)row * a.ld + lo;
+  const bool tma = ((reinterpret_cast<uintptr_t>(rowp) & 15u) == 0);
+  const int nvec = tma ? (len & ~3) : 0;                   // elements fetched by bulk copies
+  const int nst = (len + LT_STAGE - 1) / LT_STAGE;         // stages over the whole chunk
+  auto stage_bytes = [&](int si) -> uint32_t {
+    int b = nvec - si * LT_STAGE;
+    b = b < LT_STAGE ? b : LT_STAGE;
+    return b > 0 ? (uint32_t)b * 4u : 0u;
+  };
 
-  PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, LT_HASH_LOG2, lo, hi};
-  int npatch = 0;
-  if (!a.argmax_only) npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
   if (tid == 0) {
+    for (int s = 0; s < LT_NSTAGE; ++s) mbar_init(&S.full_bar[s], 1);
+    fence_mbar_init();
     S.ncand = 0;
     S.thr = 0u;
     S.nan = 0;
     S.overflow = 0;
     S.nan0 = 0;
+    S.failed = 0;
   }
   __syncthreads();
-  const bool bad_patch = (!a.argmax_only) && (S.patch_overflow || S.dup);
+  if (tid == 0 && tma) {
+    for (int s = 0; s < LT_NSTAGE && s < nst; ++s) {
+      const uint32_t b = stage_bytes(s);
+      if (b) {
+        mbar_arrive_expect_tx(&S.full_bar[s], b);
+        bulk_copy_g2s(S.ring[s], rowp + s * LT_STAGE, b, &S.full_bar[s]);
+      }
+    }
+  }
 
-  const float* rowp = a.logits + (int64_t)row * a.ld + lo;
-  const bool vec = ((reinterpret_cast<uintptr_t>(rowp) & 15u) == 0);
+  PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, LT_HASH_LOG2, lo, hi, LT_GSHIFT};
+  int npatch = 0;
+  if (!a.argmax_only) npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
+  const bool bad_patch = (!a.argmax_only) && (S.patch_overflow || S.dup);
+  // Patched positions (penalty window, bias) get their final value once, here;
+  // the streaming loops leave them out and they rejoin the candidates after.
+  if (npatch > 0 && !bad_patch) precompute_patches(T, rowp, p);
   const float invT = (mode == kModeTopK) ? __double2float_rn(__ddiv_rn(1.0, p.temperature)) : 1.0f;
 
-  bool anynan = false;
+  float mnan = 0.0f;       // max.NaN over y: NaN iff some y is NaN
   float gb = 0.0f;
-  int gi = INT_MAX;  // greedy: best non-NaN value and its first index
+  int gi = INT_MAX;        // greedy: best non-NaN value and its first index
   uint32_t thr = 0u;
+  float thrf = -INFINITY;  // fkey_inv(thr); -inf accepts everything but NaN
   bool overflow = false;
+  int my_max = 0;          // largest candidate count this thread's appends produced
 
-  for (int t0 = 0; t0 < len; t0 += LT_TILE) {
-    if (mode == kModeTopK) {
-      // every thread reads the count before any thread appends again
-      int nc = S.ncand;
-      __syncthreads();
-      if (nc > LT_CAP - LT_TILE) {
-        nc = light_compact(S, K);
-        if (nc > LT_CAP - LT_TILE) { overflow = true; break; }
-      }
-      thr = S.thr;
-    }
-    float vals[LT_UNROLL][4];
+  // the four elements of float4 group g (chunk offset `off`) of the stage in `buf`
+  auto load_group = [&](int buf, int g, int off, bool whole, float (&x)[4], bool (&valid)[4]) {
+    if (whole) {
+      const float4 q = *reinterpret_cast<const float4*>(&S.ring[buf][4 * g]);
+      x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
 #pragma unroll
-    for (int u = 0; u < LT_UNROLL; ++u) {
-      const int off = t0 + (u * LT_THREADS + tid) * 4;
-      if (vec && off + 4 <= len) {
-        float4 v4 = __ldcs(reinterpret_cast<const float4*>(rowp + off));
-        vals[u][0] = v4.x; vals[u][1] = v4.y; vals[u][2] = v4.z; vals[u][3] = v4.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) vals[u][e] = (off + e < len) ? __ldcs(rowp + off + e) : 0.0f;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < LT_UNROLL; ++u) {
-      const int off = t0 + (u * LT_THREADS + tid) * 4;
-      uint32_t pbits = 0u;
-      if (npatch > 0 && off < len) pbits = (T.bits[off >> 5] >> (off & 31)) & 0xFu;
+      for (int e = 0; e < 4; ++e) valid[e] = true;
+    } else {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const bool valid = (off + e < len);
-        float x = vals[u][e];
-        const int gidx = lo + off + e;
-        if (valid && (pbits >> e) & 1u) {
-          int slot = patch_find(T, gidx);
-          if (slot >= 0) x = patch_apply(x, T, slot, p);
-        }
-        if (mode == kModeGreedy) {
-          if (valid) {
-            if (gidx == 0 && x != x) S.nan0 = 1;
-            if (!(x != x) && (gi == INT_MAX || x > gb)) { gb = x; gi = gidx; }
+        valid[e] = off + e < len;
+        x[e] = !valid[e] ? 0.0f : (off + e < nvec ? S.ring[buf][4 * g + e] : __ldcs(rowp + off + e));
+      }
+    }
+  };
+  // Append the passing elements of one float4 group (warp-aggregated). A
+  // store past the buffer is dropped; the overflow is detected afterwards.
+  auto append4 = [&](const float (&y)[4], const bool (&pass)[4], int gidx0) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const unsigned m = __ballot_sync(0xffffffffu, pass[e]);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        int basepos = 0;
+        if (lane == leader) basepos = atomicAdd(&S.ncand, __popc(m));
+        basepos = __shfl_sync(0xffffffffu, basepos, leader);
+        const int end = basepos + __popc(m);
+        my_max = end > my_max ? end : my_max;
+        if (pass[e]) {
+          const int pos = basepos + __popc(m & lanemask_lt());
+          if (pos < LT_CAP) {
+            S.cand_key[pos] = fkey(y[e]);
+            S.cand_idx[pos] = gidx0 + e;
           }
-        } else {
+        }
+      }
+    }
+  };
+
+  int si = 0;
+  for (; si < nst; ++si) {
+    const int sbase = si * LT_STAGE;
+    const int buf = si % LT_NSTAGE;
+    bool failed_local = false;
+    if (stage_bytes(si) > 0 && !mbar_wait_bounded(&S.full_bar[buf], (uint32_t)(si / LT_NSTAGE) & 1u)) {
+      failed_local = true;
+      S.failed = 1;
+    }
+    const bool whole = (sbase + LT_STAGE <= nvec);  // every element of the stage is in the ring
+
+    if (mode == kModeTopK && si == 0) {
+      // initial threshold: a lower bound of the K-th largest key of stage 0
+      const int n0 = min(len, LT_STAGE);
+      if (n0 > (int)K) {
+        auto key0 = [&](int i, uint32_t* k) {
+          const float x = (i < nvec) ? S.ring[0][i] : __ldcs(rowp + i);
           const float y = __fmul_rn(x, invT);
-          anynan |= valid && (y != y);
-          const uint32_t key = fkey(y);
-          const bool pass = valid && key >= thr;
-          unsigned m = __ballot_sync(0xffffffffu, pass);
-          if (m) {
-            int leader = __ffs(m) - 1;
-            int basepos = 0;
-            if (lane == leader) basepos = atomicAdd(&S.ncand, __popc(m));
-            basepos = __shfl_sync(0xffffffffu, basepos, leader);
-            if (pass) {
-              int pos = basepos + __popc(m & lanemask_lt());
-              S.cand_key[pos] = key;
-              S.cand_idx[pos] = gidx;
+          if (y != y) return false;  // NaN rows are rejected at the end
+          *k = fkey(y);
+          return true;
+        };
+        // Optimistic threshold: (a lower bound of) the m-th largest key of
+        // stage 0, with m chosen so that about max(512, 2K) elements of the
+        // whole chunk are expected above it. It is verified at the merge: the
+        // candidates are complete iff every chunk's threshold is at most the
+        // row's K-th largest candidate; otherwise the row goes to the
+        // full-sort kernel.
+        int m = (int)(((long long)2 * K * n0 + len - 1) / len);
+        const int m_floor = (int)(((long long)512 * n0 + len - 1) / len);
+        m = max(m, max(m_floor, 16));
+        m = min(m, n0);
+        thr = block_select_kth_largest(n0, (uint32_t)m, key0, S.hist, S.sel, 2);
+        if ((int)S.sel[2] < m) thr = 0u;
+        thrf = key_threshold_float(thr);
+      }
+    }
+
+    if (mode == kModeTopK && whole) {
+      // Hot path: a full stage of a top-k row. All loads first; per element
+      // one multiply, one compare and one NaN-propagating max; the passing
+      // elements of the stage are appended with one warp scan and one atomic.
+      float4 q[LT_GROUPS];
+#pragma unroll
+      for (int j = 0; j < LT_GROUPS; ++j)
+        q[j] = reinterpret_cast<const float4*>(S.ring[buf])[tid + j * LT_THREADS];
+      float y[LT_GROUPS][4];
+      float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
+      int cnt = 0;
+#pragma unroll
+      for (int j = 0; j < LT_GROUPS; ++j) {
+        const int off = sbase + 4 * (tid + j * LT_THREADS);
+        const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+        (void)off;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          y[j][e] = __fmul_rn(x[e], invT);
+          cnt += (y[j][e] >= thrf) ? 1 : 0;
+        }
+        m0 = fmax_nan(m0, y[j][0]);
+        m1 = fmax_nan(m1, y[j][1]);
+        m2 = fmax_nan(m2, y[j][2]);
+        m3 = fmax_nan(m3, y[j][3]);
+      }
+      mnan = fmax_nan(mnan, fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3)));
+      if (__any_sync(0xffffffffu, cnt > 0)) {
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        int base = 0;
+        if (lane == 31) base = atomicAdd(&S.ncand, incl);
+        base = __shfl_sync(0xffffffffu, base, 31);
+        const int end = base + __shfl_sync(0xffffffffu, incl, 31);
+        my_max = end > my_max ? end : my_max;
+        int pos = base + incl - cnt;
+#pragma unroll
+        for (int j = 0; j < LT_GROUPS; ++j) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (y[j][e] >= thrf) {
+              const int off = sbase + 4 * (tid + j * LT_THREADS) + e;
+              // a patched position rejoins later with its patched value
+              const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
+              if (pos < LT_CAP) {
+                S.cand_key[pos] = patched ? 0u : fkey(y[j][e]);
+                S.cand_idx[pos] = patched ? -1 : lo + off;
+              }
+              ++pos;
             }
           }
         }
       }
+    } else {
+#pragma unroll 1
+      for (int j = 0; j < LT_GROUPS; ++j) {
+        const int g = tid + j * LT_THREADS;           // float4 group within the stage
+        const int off = sbase + 4 * g;                // chunk-relative element offset
+        float x[4];
+        bool valid[4];
+        load_group(buf, g, off, whole, x, valid);
+        bool excl[4] = {false, false, false, false};
+        if (npatch > 0 && off < len && patch_bit(T, off)) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int slot = valid[e] ? patch_find(T, lo + off + e) : -1;
+            if (slot >= 0) {
+              if (mode == kModeGreedy) x[e] = patched_value(T, slot);
+              else excl[e] = true;
+            }
+          }
+        }
+        if (mode == kModeGreedy) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (valid[e]) {
+              if (lo + off + e == 0 && x[e] != x[e]) S.nan0 = 1;
+              if (!(x[e] != x[e]) && (gi == INT_MAX || x[e] > gb)) { gb = x[e]; gi = lo + off + e; }
+            }
+          }
+        } else {
+          float y[4];
+          bool pass[4];
+          bool any = false;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            y[e] = __fmul_rn(x[e], invT);
+            if (valid[e] && !excl[e]) mnan = fmax_nan(mnan, y[e]);
+            pass[e] = valid[e] && !excl[e] && y[e] >= thrf;
+            any |= pass[e];
+          }
+          if (__any_sync(0xffffffffu, any)) append4(y, pass, lo + off);
+        }
+      }
     }
+    // One barrier per stage: the ring slot is free, appends are complete, and
+    // the block learns whether the candidate buffer needs a compaction
+    // (S.ncand only grows within a stage, so "some append pushed it past the
+    // limit" is "its final value is past the limit").
+    bool need = false;
+    int ncand_now = 0;
+    if (__syncthreads_or(failed_local || my_max > LT_LIMIT)) {
+      const int fail = S.failed;
+      ncand_now = S.ncand;
+      need = ncand_now > LT_LIMIT;
+      __syncthreads();
+      if (fail) break;
+    }
+    if (tid == 0 && si + LT_NSTAGE < nst) {
+      const uint32_t b = stage_bytes(si + LT_NSTAGE);
+      if (b) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&S.full_bar[buf], b);
+        bulk_copy_g2s(S.ring[buf], rowp + (si + LT_NSTAGE) * LT_STAGE, b, &S.full_bar[buf]);
+      }
+    }
+    if (mode == kModeTopK && need) {
+      if (ncand_now > LT_CAP) { overflow = true; ++si; break; }  // some appends were dropped
+      const int nn = light_compact(S, K);
+      my_max = 0;
+      if (nn > LT_LIMIT) { overflow = true; ++si; break; }
+      thr = S.thr;
+      thrf = key_threshold_float(thr);
+    }
+  }
+  // Leave no bulk copy in flight into this CTA's shared memory (bounded).
+  if (tid == 0 && tma) {
+    for (int s2 = si; s2 < nst && s2 < si + LT_NSTAGE; ++s2) {
+      if (stage_bytes(s2) && !mbar_wait_bounded(&S.full_bar[s2 % LT_NSTAGE], (uint32_t)(s2 / LT_NSTAGE) & 1u))
+        S.failed = 1;
+    }
+  }
+  __syncthreads();
+
+  // Patched positions rejoin the top-k candidates with their patched values.
+  if (mode == kModeTopK && npatch > 0 && !bad_patch && !overflow && !S.failed) {
+    constexpr int HS = 1 << LT_HASH_LOG2;
+    for (int i0 = 0; i0 < HS; i0 += LT_THREADS) {
+      const int i = i0 + tid;
+      const int k = T.key[i];
+      float y = 0.0f;
+      bool pass = false;
+      if (k >= 0) {
+        y = __fmul_rn(patched_value(T, i), invT);
+        mnan = fmax_nan(mnan, y);
+        pass = y >= thrf;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, pass);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        int basepos = 0;
+        if (lane == leader) basepos = atomicAdd(&S.ncand, __popc(m));
+        basepos = __shfl_sync(0xffffffffu, basepos, leader);
+        if (pass) {
+          const int pos = basepos + __popc(m & lanemask_lt());
+          if (pos < LT_CAP) {
+            S.cand_key[pos] = fkey(y);
+            S.cand_idx[pos] = k;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (S.ncand > LT_CAP) overflow = true;
     __syncthreads();
   }
 
   // ---- per-CTA results -------------------------------------------------
   if (mode == kModeTopK) {
-    if (anynan) atomicExch(&S.nan, 1);
-    if (!overflow && S.ncand > (int)K) (void)light_compact(S, K);
+    if (mnan != mnan) atomicExch(&S.nan, 1);
+    // the merge copies at most LT_SLOT candidates per CTA
+    if (!overflow && !S.failed && C > 1 && S.ncand > LT_SLOT) (void)light_compact(S, K);
     __syncthreads();
     if (tid == 0) {
       if (overflow || bad_patch || (C > 1 && S.ncand > LT_SLOT)) S.overflow = 1;
+      S.thr_pub = thr;
     }
   } else {
-    // block argmax reduction: larger value wins, ties keep the lower index
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       float ob = __shfl_down_sync(0xffffffffu, gb, off);
@@ -281,7 +517,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
   uint32_t* keys = S.cand_key;
   int* ids = S.cand_idx;
   int nm = 0;
-  int any_nan = 0, any_over = 0, nan0 = 0;
+  int any_nan = 0, any_over = 0, nan0 = 0, any_fail = 0;
+  uint32_t thr_max = 0u;  // largest chunk threshold of the row
   float gbest = 0.0f;
   int gidx = INT_MAX;
   if (C > 1) {
@@ -294,7 +531,9 @@ light_kernel(BatchArgs a, int C, int chunk) {
         const int nr = R->ncand;
         any_nan |= R->nan;
         any_over |= R->overflow;
+        any_fail |= R->failed;
         nan0 |= R->nan0;
+        thr_max = max(thr_max, R->thr_pub);
         const float ob = R->gbest;
         const int oi = R->gidx;
         if (oi != INT_MAX && (gidx == INT_MAX || ob > gbest || (ob == gbest && oi < gidx))) {
@@ -320,23 +559,26 @@ light_kernel(BatchArgs a, int C, int chunk) {
     nm = S.ncand;
     any_nan = S.nan;
     any_over = S.overflow;
+    any_fail = S.failed;
     nan0 = S.nan0;
+    thr_max = S.thr_pub;
     gbest = S.gbest;
     gidx = S.gidx;
   }
   (void)gbest;
 
   // ---- finish (CTA 0) ---------------------------------------------------
+  if (any_fail) {
+    if (tid == 0) {
+      a.out_ids[row] = -1;
+      record_status(a.status, NLS_ERR_TIMEOUT);
+    }
+    return;
+  }
   if (any_over) {
     if (tid == 0) {
-      if (a.argmax_only || mode == kModeGreedy) {
-        // a greedy row only overflows through its patch table
-        a.out_ids[row] = -1;
-        record_status(a.status, NLS_ERR_CAPACITY);
-      } else {
-        int w = atomicAdd(a.full_count, 1);
-        a.full_list[w] = row;
-      }
+      int w = atomicAdd(a.full_count, 1);
+      a.full_list[w] = row;
     }
     return;
   }
@@ -358,14 +600,23 @@ light_kernel(BatchArgs a, int C, int chunk) {
 
   // exact survivor set of the reference heap (see block comment at top)
   const uint32_t t = block_select_kth_largest(
-      nm, K, [&](int i, uint32_t* k) { *k = keys[i]; return true; }, S.hist, S.sel);
+      nm, K, [&](int i, uint32_t* k) { *k = keys[i]; return ids[i] >= 0; }, S.hist, S.sel);
+  // The candidates hold every element >= t only if no chunk threshold was
+  // above t (and there are K of them); otherwise redo the row exactly.
+  if ((int)S.sel[2] < (int)K || t < thr_max) {
+    if (tid == 0) {
+      int w = atomicAdd(a.full_count, 1);
+      a.full_list[w] = row;
+    }
+    return;
+  }
   if (tid == 0) { S.cnt_gt = 0; S.cnt_ge = 0; S.nsurv = 0; }
   __syncthreads();
   {
     int gt = 0, ge = 0;
     for (int i = tid; i < nm; i += LT_THREADS) {
-      gt += keys[i] > t;
-      ge += keys[i] >= t;
+      gt += ids[i] >= 0 && keys[i] > t;
+      ge += ids[i] >= 0 && keys[i] >= t;
     }
     gt = __reduce_add_sync(0xffffffffu, gt);
     ge = __reduce_add_sync(0xffffffffu, ge);
@@ -380,14 +631,14 @@ light_kernel(BatchArgs a, int C, int chunk) {
     tau = ~block_select_kth_largest(
         nm, K,
         [&](int i, uint32_t* k) {
-          if (keys[i] >= t) { *k = ~(uint32_t)ids[i]; return true; }
+          if (ids[i] >= 0 && keys[i] >= t) { *k = ~(uint32_t)ids[i]; return true; }
           return false;
         },
         S.hist, S.sel);
     rho = block_select_kth_largest(
         nm, K - (uint32_t)cgt,
         [&](int i, uint32_t* k) {
-          if (keys[i] == t && (uint32_t)ids[i] <= tau) { *k = (uint32_t)ids[i]; return true; }
+          if (ids[i] >= 0 && keys[i] == t && (uint32_t)ids[i] <= tau) { *k = (uint32_t)ids[i]; return true; }
           return false;
         },
         S.hist, S.sel);
@@ -399,7 +650,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
   for (int i = tid; i < nm; i += LT_THREADS) {
     const uint32_t k = keys[i];
     const uint32_t id = (uint32_t)ids[i];
-    const bool keep = (k > t) || (k == t && id >= rho && id <= tau);
+    const bool keep = ids[i] >= 0 && ((k > t) || (k == t && id >= rho && id <= tau));
     if (keep) {
       int pos = atomicAdd(&S.nsurv, 1);
       if (pos < kLightKMax) S.sortbuf[pos] = ((unsigned long long)k << 32) | id;
@@ -409,6 +660,9 @@ light_kernel(BatchArgs a, int C, int chunk) {
   block_bitonic_desc(S.sortbuf, n64);
 
   // ---- replay of sampler.nim:98-121 by one warp ----------------------------
+  // The fp32 chains (sum, running sum, draw) run in one lane in the
+  // reference's order; the break conditions are evaluated afterwards on the
+  // stored running values, so the chains carry no data-dependent branches.
   if (warp == 0) {
     const int n = (int)K;
     for (int i = lane; i < n; i += 32) S.tval[i] = fkey_inv((uint32_t)(S.sortbuf[i] >> 32));
@@ -417,34 +671,56 @@ light_kernel(BatchArgs a, int C, int chunk) {
     for (int i = lane; i < n; i += 32) S.tval[i] = ref_expf(__fsub_rn(S.tval[i], mx));
     __syncwarp();
     float s = 0.0f;
-    if (lane == 0)
+    if (lane == 0) {
+#pragma unroll 8
       for (int i = 0; i < n; ++i) s = __fadd_rn(s, S.tval[i]);
+    }
     s = __shfl_sync(0xffffffffu, s, 0);
     for (int i = lane; i < n; i += 32) S.pval[i] = __fdiv_rn(S.tval[i], s);
     __syncwarp();
-    if (lane == 0) {
-      int nn = n;
-      if (p.top_p > 0.0 && p.top_p < 1.0) {
+    int nn = n;
+    if (p.top_p > 0.0 && p.top_p < 1.0) {
+      if (lane == 0) {
         float cum = 0.0f;
-        for (int i = 0; i < nn; ++i) {
-          cum = __fadd_rn(cum, S.pval[i]);
-          if ((double)cum >= p.top_p) { nn = i + 1; break; }
-        }
+#pragma unroll 8
+        for (int i = 0; i < n; ++i) { cum = __fadd_rn(cum, S.pval[i]); S.seq[i] = cum; }
       }
-      if (p.min_p > 0.0) {
-        const float thrp = __fmul_rn(S.pval[0], __double2float_rn(p.min_p));
-        int m = 1;
-        while (m < nn && S.pval[m] >= thrp) ++m;
-        nn = m;
+      __syncwarp();
+      int first = n;
+      for (int c0 = 0; c0 < n; c0 += 32) {
+        const int i = c0 + lane;
+        const unsigned b = __ballot_sync(0xffffffffu, i < n && (double)S.seq[i] >= p.top_p);
+        if (b) { first = c0 + __ffs(b) - 1; break; }
       }
+      if (first < n) nn = first + 1;
+    }
+    if (p.min_p > 0.0) {
+      const float thrp = __fmul_rn(S.pval[0], __double2float_rn(p.min_p));
+      int m = nn;
+      for (int c0 = 0; c0 < nn; c0 += 32) {
+        const int i = c0 + lane;
+        const unsigned b = __ballot_sync(0xffffffffu, i >= 1 && i < nn && !(S.pval[i] >= thrp));
+        if (b) { m = c0 + __ffs(b) - 1; break; }
+      }
+      nn = m < 1 ? 1 : m;
+    }
+    __syncwarp();
+    if (lane == 0) {
       float total = 0.0f;
+#pragma unroll 8
       for (int i = 0; i < nn; ++i) total = __fadd_rn(total, S.pval[i]);
       float r = __fmul_rn(__double2float_rn(a.uniforms[row]), total);
-      int pos = nn - 1;
-      for (int i = 0; i < nn; ++i) {
-        r = __fsub_rn(r, S.pval[i]);
-        if (r <= 0.0f) { pos = i; break; }
-      }
+#pragma unroll 8
+      for (int i = 0; i < nn; ++i) { r = __fsub_rn(r, S.pval[i]); S.seq[i] = r; }
+    }
+    __syncwarp();
+    int pos = nn - 1;
+    for (int c0 = 0; c0 < nn; c0 += 32) {
+      const int i = c0 + lane;
+      const unsigned b = __ballot_sync(0xffffffffu, i < nn && S.seq[i] <= 0.0f);
+      if (b) { pos = c0 + __ffs(b) - 1; break; }
+    }
+    if (lane == 0) {
       a.out_ids[row] = (int64_t)(uint32_t)(S.sortbuf[pos] & 0xffffffffull);
       if (a.out_probs) a.out_probs[row] = S.pval[pos];
     }
@@ -453,15 +729,9 @@ light_kernel(BatchArgs a, int C, int chunk) {
 
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream) {
   const size_t smem = light_smem_bytes(C, chunk);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(light_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(light_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  cudaError_t e = cudaFuncSetAttribute(light_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.rows * C), 1, 1);
   cfg.blockDim = dim3(LT_THREADS, 1, 1);
