@@ -131,7 +131,7 @@ NLS_API nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t 
  * is device memory of the current device, the call is stream-ordered and
  * returns after the launches; a row that fails in the kernels gets out id -1.
  * It calls no cudaMalloc/cudaFree: its scratch is one fixed device array in
- * the library (about 12 MiB per device, held until exit). Limits: rows <= 4096
+ * the library (about 16 MiB per device, held until exit). Limits: rows <= 4096
  * and vocab <= 262144, else NLS_ERR_CAPACITY. The first call on a device
  * looks up that array's address (make it before any stream capture). All
  * calls share the array; calls that overlap on the GPU race on it. */

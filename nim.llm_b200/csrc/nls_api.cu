@@ -36,7 +36,7 @@ struct nls_handle {
   float* d_out_probs = nullptr;
   // [0] status, [1] full_count, [2 ..] full_list
   int* d_work = nullptr;
-  // full-sort scratch: slots x 3 x vpad words
+  // full-sort scratch: slots x 4 x vpad words
   uint32_t* d_scratch = nullptr;
   int vpad = 0;
   int slots = 0;
@@ -215,7 +215,7 @@ nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_
   if (st == NLS_OK) {
     h->vpad = (max_vocab + 31) & ~31;
     h->slots = h->sm_count;
-    size_t words = (size_t)h->slots * 3 * (size_t)h->vpad;
+    size_t words = (size_t)h->slots * 4 * (size_t)h->vpad;
     if ((e = cudaMalloc(&h->d_scratch, words * sizeof(uint32_t))) != cudaSuccess)
       fail(e, "cudaMalloc(scratch)");
   }

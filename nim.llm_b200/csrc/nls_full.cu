@@ -1,17 +1,28 @@
 // nls_full.cu -- rows that need more than a small top-k: top_k <= 0 or
 // top_k >= vocab (the reference's full stable sort, sampler.nim:96-97),
 // 256 < top_k < vocab (the heap path with a large k, sampler.nim:86-95), and
-// rows the streaming kernel handed over (buffers overflowed by ties, or a
-// penalty window with too many distinct ids for its table).
+// rows the streaming kernel handed over (candidate buffers overflowed, an
+// optimistic threshold that proved too high, or a penalty window with too
+// many distinct ids for its table).
 //
 // One 1024-thread CTA per row, persistent over the work list, with its own
-// scratch slot of 3 x vocab words in HBM:
-//   1. transform: penalties, bias, temperature; each logit becomes a 32-bit
-//      key that sorts ascending in the reference's candidate order;
-//   2. LSD radix sort of the keys (4 x 8-bit digits, stable warp ranking);
-//   3. t_j = expf(y_j - max), then the reference's sequential fp32 sums --
-//      softmax denominator, top-p running sum, min-p cut, draw total and the
-//      draw itself -- replayed exactly by the block scan in nls_scan.cuh;
+// scratch slot of 4 x vocab words in HBM/L2:
+//   KY[i]  order key of logit i (index order),
+//   SK[j]  (key << 32 | index), sorted: the reference's candidate order,
+//   TT[j]  expf(y_j - max) in candidate order.
+// Steps:
+//   1. transform: penalties and bias (precomputed per patched position),
+//      temperature; KY gets each logit's key, whose ascending order is the
+//      reference's candidate order (descending value);
+//   2. bucket sort: 4096 buckets linear in (max - y) -- monotone, so bucket
+//      order is candidate order -- filled by a warp-aggregated histogram and
+//      scatter; every bucket is then sorted by (key, index): a warp sorts a
+//      bucket of <= 256 in registers (bitonic), the block sorts a larger one
+//      in shared memory. A row with a bucket beyond 8192 (heavily repeated
+//      values) is sorted by the LSD radix fallback instead;
+//   3. the reference's sequential fp32 sums -- softmax denominator, top-p
+//      running sum, min-p cut, draw total and the draw -- replayed exactly by
+//      the block scans of nls_scan.cuh;
 //   4. the drawn position is mapped back to a token id with the reference's
 //      tie order (ascending index for the stable sort; for the heap path,
 //      descending index and the heap's survivor rule among ties at the k-th
@@ -29,25 +40,57 @@ constexpr int FT_EPT = 4;
 constexpr int FT_TILE = FT_THREADS * FT_EPT;
 constexpr int FT_WARPS = FT_THREADS / 32;
 constexpr int FT_HASH_LOG2 = 12;
+constexpr int FT_GSHIFT = 2;
+constexpr int FT_NB = 256;         // coarse value buckets (first level)
+constexpr int FT_TILE1 = 4096;     // elements per scatter tile
+constexpr int FT_WIN = 4096;       // a window holds the buckets starting in FT_WIN positions
+constexpr int FT_BUCKET_MAX = 4096;  // larger coarse buckets take the LSD fallback
+constexpr int FT_BIG = 8192;       // window capacity (FT_WIN + FT_BUCKET_MAX)
+constexpr int FT_NB2 = 4096;       // fine buckets per window (second level)
+constexpr int FT_INS_MAX = 64;     // fine buckets up to this size: one-thread insertion sort
+constexpr int FT_BIGLIST = 64;
+constexpr float FT_DCAP = 110.0f;  // expf(-110) is 0: beyond this t_j is 0
 
 struct FullShared {
-  int hkey[1 << FT_HASH_LOG2];
-  int hcnt[1 << FT_HASH_LOG2];
-  float hbias[1 << FT_HASH_LOG2];
-  int hflag[1 << FT_HASH_LOG2];
-  int wcnt[FT_WARPS][257];
+  union {  // the patch table is dead once the row is transformed
+    struct {
+      int hkey[1 << FT_HASH_LOG2];
+      int hcnt[1 << FT_HASH_LOG2];
+      float hbias[1 << FT_HASH_LOG2];
+      int hflag[1 << FT_HASH_LOG2];
+    } pt;
+    unsigned long long bufB[FT_BIG];
+  } ph;
+  uint32_t hist2[FT_NB2];
+  uint32_t off2[FT_NB2];
+  union {
+    unsigned long long big[FT_BIG];  // window buffer A / tile staging / block-sort buffer
+    int wcnt[FT_WARPS][257];
+  } u;
+  uint32_t h1[FT_NB];
+  uint32_t s1[FT_NB];
+  uint32_t c1[FT_NB];
+  uint32_t lc[FT_NB];
+  uint32_t lo1[FT_NB];
+  uint32_t gb1[FT_NB];
   uint32_t base[256];
   uint32_t tilecnt[256];
   ScanShared scan;
+  FastScanShared fscan;
   int ired[FT_WARPS];
   float fred[FT_WARPS];
+  uint32_t ured[FT_WARPS];
+  uint32_t ured2[FT_WARPS];
   int ibuf[8];
   float fbuf[8];
+  int biglist[FT_BIGLIST];
+  int nbig;
   int counter, patch_overflow, dup, nan;
 };
 
 size_t full_smem_bytes(int V) {
-  size_t bm_words = ((size_t)V + 31) / 32;
+  size_t groups = ((size_t)V + (1u << FT_GSHIFT) - 1) >> FT_GSHIFT;
+  size_t bm_words = (groups + 31) / 32;
   bm_words = (bm_words + 3) & ~(size_t)3;
   return ((sizeof(FullShared) + 15) & ~(size_t)15) + bm_words * 4;
 }
@@ -63,6 +106,18 @@ __device__ int block_sum_int(int v, FullShared& S) {
   for (int w = 0; w < FT_WARPS; ++w) tot += S.ired[w];
   __syncthreads();
   return tot;
+}
+
+__device__ int block_max_int(int v, FullShared& S) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_max_sync(0xffffffffu, v);
+  if (lane == 0) S.ired[warp] = v;
+  __syncthreads();
+  int m = INT_MIN;
+#pragma unroll 8
+  for (int w = 0; w < FT_WARPS; ++w) m = max(m, S.ired[w]);
+  __syncthreads();
+  return m;
 }
 
 __device__ int block_excl_sum_int(int v, int* total, FullShared& S) {
@@ -147,11 +202,28 @@ __device__ __forceinline__ int upper_bound_u32(const uint32_t* B, int n, uint32_
   }
   return lo;
 }
+// the same on the key (high word) of sorted (key << 32 | index) pairs
+__device__ __forceinline__ int lower_bound_key(const unsigned long long* B, int n, uint32_t key) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (lo + hi) >> 1;
+    if ((uint32_t)(B[mid] >> 32) < key) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+__device__ __forceinline__ int upper_bound_key(const unsigned long long* B, int n, uint32_t key) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (lo + hi) >> 1;
+    if ((uint32_t)(B[mid] >> 32) <= key) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
 
-// ---- LSD radix sort passes (keys only, stable) -----------------------------
+// ---- LSD radix sort passes (keys only, stable): the fallback sort ----------
 __device__ void lsd_count(const uint32_t* src, int n, int sh, FullShared& S) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int d = lane; d < 257; d += 32) S.wcnt[warp][d] = 0;
+  for (int d = lane; d < 257; d += 32) S.u.wcnt[warp][d] = 0;
   __syncwarp();
   for (int t0 = 0; t0 < n; t0 += FT_TILE) {
 #pragma unroll
@@ -159,14 +231,14 @@ __device__ void lsd_count(const uint32_t* src, int n, int sh, FullShared& S) {
       const int i = t0 + warp * (32 * FT_EPT) + j * 32 + lane;
       const int d = (i < n) ? (int)((src[i] >> sh) & 255u) : 256;
       const unsigned peers = __match_any_sync(0xffffffffu, d);
-      if (lane == __ffs(peers) - 1 && d < 256) S.wcnt[warp][d] += __popc(peers);
+      if (lane == __ffs(peers) - 1 && d < 256) S.u.wcnt[warp][d] += __popc(peers);
       __syncwarp();
     }
   }
   __syncthreads();
   if (threadIdx.x < 256) {
     int c = 0;
-    for (int w = 0; w < FT_WARPS; ++w) c += S.wcnt[w][threadIdx.x];
+    for (int w = 0; w < FT_WARPS; ++w) c += S.u.wcnt[w][threadIdx.x];
     S.tilecnt[threadIdx.x] = (uint32_t)c;
   }
   __syncthreads();
@@ -192,7 +264,7 @@ __device__ void lsd_scatter(const uint32_t* src, uint32_t* dst, int n, int sh, F
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned ltmask = lanemask_lt();
   for (int t0 = 0; t0 < n; t0 += FT_TILE) {
-    for (int d = lane; d < 257; d += 32) S.wcnt[warp][d] = 0;
+    for (int d = lane; d < 257; d += 32) S.u.wcnt[warp][d] = 0;
     __syncwarp();
     uint32_t k[FT_EPT];
     int dg[FT_EPT], rk[FT_EPT];
@@ -202,18 +274,18 @@ __device__ void lsd_scatter(const uint32_t* src, uint32_t* dst, int n, int sh, F
       k[j] = (i < n) ? src[i] : 0u;
       dg[j] = (i < n) ? (int)((k[j] >> sh) & 255u) : 256;
       const unsigned peers = __match_any_sync(0xffffffffu, dg[j]);
-      const int before = S.wcnt[warp][dg[j]];
+      const int before = S.u.wcnt[warp][dg[j]];
       __syncwarp();
       rk[j] = before + __popc(peers & ltmask);
-      if (lane == __ffs(peers) - 1) S.wcnt[warp][dg[j]] = before + __popc(peers);
+      if (lane == __ffs(peers) - 1) S.u.wcnt[warp][dg[j]] = before + __popc(peers);
       __syncwarp();
     }
     __syncthreads();
     if (threadIdx.x < 256) {
       int run = 0;
       for (int w = 0; w < FT_WARPS; ++w) {
-        int c = S.wcnt[w][threadIdx.x];
-        S.wcnt[w][threadIdx.x] = run;
+        int c = S.u.wcnt[w][threadIdx.x];
+        S.u.wcnt[w][threadIdx.x] = run;
         run += c;
       }
       S.tilecnt[threadIdx.x] = (uint32_t)run;
@@ -221,11 +293,87 @@ __device__ void lsd_scatter(const uint32_t* src, uint32_t* dst, int n, int sh, F
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < FT_EPT; ++j) {
-      if (dg[j] < 256) dst[S.base[dg[j]] + S.wcnt[warp][dg[j]] + rk[j]] = k[j];
+      if (dg[j] < 256) dst[S.base[dg[j]] + S.u.wcnt[warp][dg[j]] + rk[j]] = k[j];
     }
     __syncthreads();
     if (threadIdx.x < 256) S.base[threadIdx.x] += S.tilecnt[threadIdx.x];
     __syncthreads();
+  }
+}
+
+// ---- sorting small segments -------------------------------------------------
+// Ascending bitonic sort of 32*E keys held by one warp, element lane*E + e in
+// v[e] (E a power of two).
+template <int E>
+__device__ __forceinline__ void warp_bitonic_asc(unsigned long long (&v)[E]) {
+  const int lane = threadIdx.x & 31;
+  constexpr int N = 32 * E;
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= E) {
+        const int lm = j / E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[e], lm);
+          const int i = lane * E + e;
+          const bool up = (i & k) == 0;
+          const bool lower = (lane & lm) == 0;
+          const unsigned long long mn = v[e] < o ? v[e] : o;
+          const unsigned long long mx = v[e] < o ? o : v[e];
+          v[e] = (lower == up) ? mn : mx;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e & j) == 0) {
+            const int e2 = e | j;
+            const int i = lane * E + e;
+            const bool up = (i & k) == 0;
+            if ((v[e] > v[e2]) == up) {
+              const unsigned long long t = v[e];
+              v[e] = v[e2];
+              v[e2] = t;
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void warp_sort_segment(unsigned long long* seg, int n) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    v[e] = i < n ? seg[i] : ~0ull;
+  }
+  warp_bitonic_asc<E>(v);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    if (i < n) seg[i] = v[e];
+  }
+}
+
+// Block-wide ascending bitonic sort of n64 (power of two) keys in shared memory.
+__device__ void block_bitonic_asc(unsigned long long* v, int n64) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int size = 2; size <= n64; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n64 / 2; i += nt) {
+        int lo = 2 * i - (i & (stride - 1));
+        int hi = lo + stride;
+        bool asc = ((lo & size) == 0);
+        unsigned long long x = v[lo], y = v[hi];
+        if ((x > y) == asc) { v[lo] = y; v[hi] = x; }
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -234,17 +382,31 @@ __device__ void lsd_scatter(const uint32_t* src, uint32_t* dst, int n, int sh, F
 __device__ __forceinline__ uint32_t desc_key(float y) { return ~fkey(y); }
 __device__ __forceinline__ float desc_key_value(uint32_t kd) { return fkey_inv(~kd); }
 
+// Value bucket of a key: linear in d = max - y, monotone, so bucket order is
+// candidate order. d >= the cut (or +inf/NaN) goes to the last bucket.
+struct Bucketer {
+  float mx, scale, dcut;
+  __device__ __forceinline__ int operator()(uint32_t kd) const {
+    const float d = __fsub_rn(mx, desc_key_value(kd));
+    if (!(d < dcut)) return FT_NB - 1;
+    const int b = __float2int_rz(__fmul_rn(d, scale));
+    return b < 0 ? 0 : (b > FT_NB - 1 ? FT_NB - 1 : b);
+  }
+};
+
 __global__ void __launch_bounds__(FT_THREADS, 1)
 full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FullShared& S = *reinterpret_cast<FullShared*>(smem_raw);
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + ((sizeof(FullShared) + 15) & ~(size_t)15));
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.V;
-  uint32_t* orig = scratch + (size_t)blockIdx.x * 3 * (size_t)vpad;
-  uint32_t* A = orig + vpad;
-  uint32_t* B = A + vpad;
-  float* Af = reinterpret_cast<float*>(A);
+  uint32_t* KY = scratch + (size_t)blockIdx.x * 4 * (size_t)vpad;
+  unsigned long long* SK = reinterpret_cast<unsigned long long*>(KY + vpad);
+  float* TT = reinterpret_cast<float*>(KY + 3 * (size_t)vpad);
+  // LSD fallback: two key arrays in the SK region
+  uint32_t* LA = KY + vpad;
+  uint32_t* LB = KY + 2 * (size_t)vpad;
   const int nwork = *a.full_count;
 
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
@@ -260,8 +422,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     // heap path iff k < V (sampler.nim:86)
     const bool heap = (K64 < V);
     const int ncand = heap ? (int)K64 : V;
+    const float* rowp = a.logits + (int64_t)row * a.ld;
 
-    PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, FT_HASH_LOG2, 0, V, 0};
+    PatchTable T{S.ph.pt.hkey, S.ph.pt.hcnt, S.ph.pt.hbias, S.ph.pt.hflag, bitmap, FT_HASH_LOG2, 0, V, FT_GSHIFT};
     const int npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
     if (S.patch_overflow || S.dup) {
       if (tid == 0) {
@@ -271,20 +434,24 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       __syncthreads();
       continue;
     }
+    if (npatch > 0) precompute_patches(T, rowp, p);
     if (tid == 0) S.nan = 0;
     __syncthreads();
+    auto logit = [&](int i) -> float {
+      float x = rowp[i];
+      if (npatch > 0 && patch_bit(T, i)) {
+        const int slot = patch_find(T, i);
+        if (slot >= 0) x = patched_value(T, slot);
+      }
+      return x;
+    };
 
-    const float* rowp = a.logits + (int64_t)row * a.ld;
     if (greedy) {
       // argmax over the patched row (sampler.nim:45-49, 77-78)
       float gb = 0.0f;
       int gi = INT_MAX;
       for (int i = tid; i < V; i += FT_THREADS) {
-        float x = rowp[i];
-        if (npatch > 0 && patch_bit(T, i)) {
-          const int slot = patch_find(T, i);
-          if (slot >= 0) x = patch_apply(x, T, slot, p);
-        }
+        const float x = logit(i);
         if (i == 0 && x != x) S.nan = 1;
         if (!(x != x) && (gi == INT_MAX || x > gb)) { gb = x; gi = i; }
       }
@@ -294,7 +461,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         int oi = __shfl_down_sync(0xffffffffu, gi, off);
         if (oi != INT_MAX && (gi == INT_MAX || ob > gb || (ob == gb && oi < gi))) { gb = ob; gi = oi; }
       }
-      if ((tid & 31) == 0) { S.fred[tid >> 5] = gb; S.ired[tid >> 5] = gi; }
+      if (lane == 0) { S.fred[warp] = gb; S.ired[warp] = gi; }
       __syncthreads();
       if (tid == 0) {
         float b = 0.0f;
@@ -311,20 +478,45 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       continue;
     }
 
-    // 1. transform
+    // 1. transform: KY[i] = key of y_i; track the extreme keys and NaNs
     const float invT = __double2float_rn(__ddiv_rn(1.0, p.temperature));
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
     int anynan = 0;
-    for (int i = tid; i < V; i += FT_THREADS) {
-      float x = rowp[i];
-      if (npatch > 0 && patch_bit(T, i)) {
-        const int slot = patch_find(T, i);
-        if (slot >= 0) x = patch_apply(x, T, slot, p);
+    const bool vec = ((reinterpret_cast<uintptr_t>(rowp) & 15u) == 0);
+    const int nv4 = vec ? (V >> 2) : 0;
+    for (int g = tid; g < nv4; g += FT_THREADS) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(rowp) + g);
+      float x[4] = {q.x, q.y, q.z, q.w};
+      if (npatch > 0 && patch_bit(T, 4 * g)) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int slot = patch_find(T, 4 * g + e);
+          if (slot >= 0) x[e] = patched_value(T, slot);
+        }
       }
-      const float y = __fmul_rn(x, invT);
-      anynan |= (y != y);
-      orig[i] = desc_key(y);
+      uint32_t k[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float y = __fmul_rn(x[e], invT);
+        anynan |= (y != y);
+        k[e] = desc_key(y);
+        kmin = min(kmin, k[e]);
+        kmax = max(kmax, k[e]);
+      }
+      reinterpret_cast<uint4*>(KY)[g] = make_uint4(k[0], k[1], k[2], k[3]);
     }
-    if (block_sum_int(anynan, S) > 0) {
+    for (int i = 4 * nv4 + tid; i < V; i += FT_THREADS) {
+      const float y = __fmul_rn(logit(i), invT);
+      anynan |= (y != y);
+      const uint32_t k = desc_key(y);
+      kmin = min(kmin, k);
+      kmax = max(kmax, k);
+      KY[i] = k;
+    }
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) { S.ured[warp] = kmin; S.ured2[warp] = kmax; }
+    if (block_sum_int(anynan, S) > 0) {   // (its barrier also publishes ured)
       if (tid == 0) {
         a.out_ids[row] = -1;
         if (a.out_probs) a.out_probs[row] = 0.0f;
@@ -332,123 +524,390 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       }
       continue;
     }
-    __threadfence_block();
-    __syncthreads();
-    // 2. sort: orig -> A -> B -> A -> B
-    lsd_count(orig, V, 0, S);
-    lsd_scatter(orig, A, V, 0, S);
-    lsd_count(A, V, 8, S);
-    lsd_scatter(A, B, V, 8, S);
-    lsd_count(B, V, 16, S);
-    lsd_scatter(B, A, V, 16, S);
-    lsd_count(A, V, 24, S);
-    lsd_scatter(A, B, V, 24, S);
-    __syncthreads();
+    kmin = 0xffffffffu;
+    kmax = 0u;
+#pragma unroll 8
+    for (int k = 0; k < FT_WARPS; ++k) { kmin = min(kmin, S.ured[k]); kmax = max(kmax, S.ured2[k]); }
+    const float mx = desc_key_value(kmin);
+    const float ymin = desc_key_value(kmax);
 
-    const float mx = desc_key_value(B[0]);
+    // 2. sort into SK: coarse buckets linear in (max - y), scattered through
+    //    shared-memory tiles (coalesced runs); then each window of whole
+    //    coarse buckets is refined in shared memory into fine buckets of about
+    //    one element, finished by insertion sorts on (key, index).
+    Bucketer bk;
+    bk.mx = mx;
+    {
+      const float range = __fsub_rn(mx, ymin);  // +inf when ymin is -inf
+      const float span = (range < FT_DCAP) ? range : FT_DCAP;
+      bk.dcut = (range < FT_DCAP) ? INFINITY : FT_DCAP;
+      bk.scale = (span > 0.0f && isfinite(mx)) ? (float)(FT_NB - 1) / span : 0.0f;
+      if (!isfinite(mx)) bk.dcut = INFINITY;
+    }
+    for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] = 0u;
+    __syncthreads();
+    for (int i = tid; i < V; i += FT_THREADS) atomicAdd(&S.h1[bk(KY[i])], 1u);
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the 256 coarse counts (8 per lane)
+      uint32_t loc[FT_NB / 32], sum = 0;
+#pragma unroll
+      for (int r = 0; r < FT_NB / 32; ++r) { loc[r] = S.h1[lane * (FT_NB / 32) + r]; sum += loc[r]; }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      uint32_t run = incl - sum;
+#pragma unroll
+      for (int r = 0; r < FT_NB / 32; ++r) {
+        S.s1[lane * (FT_NB / 32) + r] = run;
+        S.c1[lane * (FT_NB / 32) + r] = run;
+        run += loc[r];
+      }
+    }
+    int bigmax = 0;
+    for (int b = tid; b < FT_NB; b += FT_THREADS) bigmax = max(bigmax, (int)S.h1[b]);
+    bigmax = block_max_int(bigmax, S);
+    const bool bucketed = bigmax <= FT_BUCKET_MAX;
+    if (bucketed) {
+      // coarse scatter, one tile at a time: counting sort of the tile in
+      // shared memory, then each bucket's run goes out contiguously
+      unsigned long long* stage = S.u.big;
+      for (int t0 = 0; t0 < V; t0 += FT_TILE1) {
+        const int nt = min(FT_TILE1, V - t0);
+        for (int b = tid; b < FT_NB; b += FT_THREADS) S.lc[b] = 0u;
+        __syncthreads();
+        uint32_t kd[FT_TILE1 / FT_THREADS];
+        int bb[FT_TILE1 / FT_THREADS];
+#pragma unroll
+        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
+          const int i = tid + r * FT_THREADS;
+          kd[r] = (i < nt) ? KY[t0 + i] : 0u;
+          bb[r] = (i < nt) ? bk(kd[r]) : -1;
+          if (bb[r] >= 0) atomicAdd(&S.lc[bb[r]], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+          uint32_t loc[FT_NB / 32], sum = 0;
+#pragma unroll
+          for (int r = 0; r < FT_NB / 32; ++r) { loc[r] = S.lc[lane * (FT_NB / 32) + r]; sum += loc[r]; }
+          uint32_t incl = sum;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+          }
+          uint32_t run = incl - sum;
+#pragma unroll
+          for (int r = 0; r < FT_NB / 32; ++r) {
+            const int b = lane * (FT_NB / 32) + r;
+            S.lo1[b] = run;
+            S.gb1[b] = atomicAdd(&S.c1[b], loc[r]);  // this tile's slice of bucket b
+            S.lc[b] = run;                           // becomes the local cursor
+            run += loc[r];
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
+          const int i = tid + r * FT_THREADS;
+          if (bb[r] >= 0) {
+            const uint32_t q = atomicAdd(&S.lc[bb[r]], 1u);
+            stage[q] = ((unsigned long long)kd[r] << 32) | (uint32_t)(t0 + i);
+          }
+        }
+        __syncthreads();
+        for (int q = tid; q < nt; q += FT_THREADS) {
+          const unsigned long long v = stage[q];
+          const int b = bk((uint32_t)(v >> 32));
+          SK[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
+        }
+        __syncthreads();
+      }
+      // windows: the coarse buckets whose start lies in [c*FT_WIN, (c+1)*FT_WIN)
+      auto first_bucket_from = [&](int x) {  // first bucket with start >= x, or FT_NB
+        int lo = 0, hi = FT_NB;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if ((int)S.s1[mid] >= x) hi = mid; else lo = mid + 1;
+        }
+        return lo;
+      };
+      unsigned long long* bufA = S.u.big;
+      unsigned long long* bufB = S.ph.bufB;
+      const int nwin = (V + FT_WIN - 1) / FT_WIN;
+      for (int c = 0; c < nwin; ++c) {
+        if (tid == 0) {
+          const int bA = first_bucket_from(c * FT_WIN);
+          const int bB = first_bucket_from((c + 1) * FT_WIN);
+          S.ibuf[4] = bA;
+          S.ibuf[5] = bB;
+          S.ibuf[6] = (bA < FT_NB) ? (int)S.s1[bA] : V;
+          S.ibuf[7] = (bB < FT_NB) ? (int)S.s1[bB] : V;
+        }
+        __syncthreads();
+        const int bA = S.ibuf[4], bB = S.ibuf[5], ws = S.ibuf[6], we = S.ibuf[7];
+        __syncthreads();
+        const int n = we - ws;
+        if (n <= 1) continue;
+        const int F = FT_NB2 / max(1, bB - bA);  // fine buckets per coarse bucket
+        auto fine = [&](uint32_t kdv) {
+          const int b = bk(kdv);
+          const float d = __fsub_rn(mx, desc_key_value(kdv));
+          int sub = F - 1;
+          if (d < bk.dcut) {
+            const float x = __fmul_rn(d, bk.scale);
+            const int f = __float2int_rz(__fmul_rn(__fsub_rn(x, (float)b), (float)F));
+            sub = f < 0 ? 0 : (f > F - 1 ? F - 1 : f);
+          }
+          return (b - bA) * F + sub;
+        };
+        for (int i = tid; i < FT_NB2; i += FT_THREADS) S.hist2[i] = 0u;
+        for (int i = tid; i < n; i += FT_THREADS) bufA[i] = SK[ws + i];
+        __syncthreads();
+        for (int i = tid; i < n; i += FT_THREADS) atomicAdd(&S.hist2[fine((uint32_t)(bufA[i] >> 32))], 1u);
+        __syncthreads();
+        {  // exclusive scan of the fine counts (FT_NB2 / FT_THREADS per thread)
+          uint32_t cc[FT_NB2 / FT_THREADS];
+          int loc = 0;
+#pragma unroll
+          for (int r = 0; r < FT_NB2 / FT_THREADS; ++r) { cc[r] = S.hist2[tid * (FT_NB2 / FT_THREADS) + r]; loc += (int)cc[r]; }
+          int tot;
+          int ex = block_excl_sum_int(loc, &tot, S);
+#pragma unroll
+          for (int r = 0; r < FT_NB2 / FT_THREADS; ++r) {
+            S.off2[tid * (FT_NB2 / FT_THREADS) + r] = (uint32_t)ex;
+            ex += (int)cc[r];
+          }
+        }
+        if (tid == 0) S.nbig = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += FT_THREADS) {
+          const unsigned long long v = bufA[i];
+          bufB[atomicAdd(&S.off2[fine((uint32_t)(v >> 32))], 1u)] = v;
+        }
+        __syncthreads();
+        // off2[f] is now the end of fine bucket f: insertion-sort the small
+        // ones, list the rare large ones for the block sort
+        for (int f = tid; f < FT_NB2; f += FT_THREADS) {
+          const int m = (int)S.hist2[f];
+          if (m <= 1) continue;
+          unsigned long long* seg = bufB + (S.off2[f] - (uint32_t)m);
+          if (m <= FT_INS_MAX) {
+            for (int x = 1; x < m; ++x) {
+              const unsigned long long v = seg[x];
+              int y = x - 1;
+              while (y >= 0 && seg[y] > v) { seg[y + 1] = seg[y]; --y; }
+              seg[y + 1] = v;
+            }
+          } else {
+            const int slot = atomicAdd(&S.nbig, 1);
+            if (slot < FT_BIGLIST) S.biglist[slot] = f;
+          }
+        }
+        __syncthreads();
+        const int nbig = min(S.nbig, FT_BIGLIST);
+        const bool all_listed = S.nbig <= FT_BIGLIST;
+        for (int q = 0; q < FT_NB2 && q < (all_listed ? nbig : FT_NB2); ++q) {
+          const int f = all_listed ? S.biglist[q] : q;
+          const int m = (int)S.hist2[f];
+          if (m <= FT_INS_MAX) continue;  // (only when scanning every fine bucket)
+          unsigned long long* seg = bufB + (S.off2[f] - (uint32_t)m);
+          int m64 = 1;
+          while (m64 < m) m64 <<= 1;
+          for (int i = tid; i < m64; i += FT_THREADS) bufA[i] = i < m ? seg[i] : ~0ull;
+          __syncthreads();
+          block_bitonic_asc(bufA, m64);
+          for (int i = tid; i < m; i += FT_THREADS) seg[i] = bufA[i];
+          __syncthreads();
+        }
+        for (int i = tid; i < n; i += FT_THREADS) SK[ws + i] = bufB[i];
+        __syncthreads();
+      }
+    } else {
+      // repeated values overflow one bucket: LSD radix sort of the keys
+      lsd_count(KY, V, 0, S);
+      lsd_scatter(KY, LA, V, 0, S);
+      lsd_count(LA, V, 8, S);
+      lsd_scatter(LA, LB, V, 8, S);
+      lsd_count(LB, V, 16, S);
+      lsd_scatter(LB, LA, V, 16, S);
+      lsd_count(LA, V, 24, S);
+      lsd_scatter(LA, LB, V, 24, S);
+    }
+    __syncthreads();
+    // sorted key of candidate position j
+    auto skey = [&](int j) -> uint32_t { return bucketed ? (uint32_t)(SK[j] >> 32) : LB[j]; };
+
     const double u_draw = a.uniforms[row];
     int pos;
-    float s, prob;
+    float prob;
     if (!isfinite(mx)) {
       // Non-finite maximum: the reference's arithmetic produces NaNs that a
       // grid replay cannot represent; run its loops literally (one thread).
       if (tid == 0) {
         float m = -INFINITY;
         for (int j = 0; j < ncand; ++j) {
-          float y = desc_key_value(B[j]);
+          float y = desc_key_value(skey(j));
           m = (m <= y) ? y : m;
         }
         float ss = 0.0f;
         for (int j = 0; j < ncand; ++j) {
-          float tj = ref_expf(__fsub_rn(desc_key_value(B[j]), m));
-          Af[j] = tj;
+          float tj = ref_expf(__fsub_rn(desc_key_value(skey(j)), m));
+          TT[j] = tj;
           ss = __fadd_rn(ss, tj);
         }
-        for (int j = 0; j < ncand; ++j) Af[j] = __fdiv_rn(Af[j], ss);
+        for (int j = 0; j < ncand; ++j) TT[j] = __fdiv_rn(TT[j], ss);
         int n = ncand;
         if (p.top_p > 0.0 && p.top_p < 1.0) {
           float cum = 0.0f;
           for (int j = 0; j < n; ++j) {
-            cum = __fadd_rn(cum, Af[j]);
+            cum = __fadd_rn(cum, TT[j]);
             if ((double)cum >= p.top_p) { n = j + 1; break; }
           }
         }
         if (p.min_p > 0.0) {
-          const float thr = __fmul_rn(Af[0], __double2float_rn(p.min_p));
+          const float thr = __fmul_rn(TT[0], __double2float_rn(p.min_p));
           int m2 = 1;
-          while (m2 < n && Af[m2] >= thr) ++m2;
+          while (m2 < n && TT[m2] >= thr) ++m2;
           n = m2;
         }
         float total = 0.0f;
-        for (int j = 0; j < n; ++j) total = __fadd_rn(total, Af[j]);
+        for (int j = 0; j < n; ++j) total = __fadd_rn(total, TT[j]);
         float r = __fmul_rn(__double2float_rn(u_draw), total);
         int ps = n - 1;
         for (int j = 0; j < n; ++j) {
-          r = __fsub_rn(r, Af[j]);
+          r = __fsub_rn(r, TT[j]);
           if (r <= 0.0f) { ps = j; break; }
         }
         S.ibuf[1] = ps;
-        S.fbuf[1] = Af[ps];
+        S.fbuf[1] = TT[ps];
       }
       __syncthreads();
       pos = S.ibuf[1];
       prob = S.fbuf[1];
       __syncthreads();
     } else {
-      // 3. t_j = expf(y_j - max) in candidate order
-      for (int j = tid; j < ncand; j += FT_THREADS)
-        Af[j] = ref_expf(__fsub_rn(desc_key_value(B[j]), mx));
-      __threadfence_block();
-      __syncthreads();
-      auto tval = [&](int j) { return Af[j]; };
+      // 3. t_j = expf(y_j - max) in candidate order, computed once per chunk
+      //    the first time a scan reaches it (peaked rows stop early)
+      int tt_valid = 0;  // TT holds [0, tt_valid); the same in every thread
+      auto texp = [&](int j) { return ref_expf(__fsub_rn(desc_key_value(skey(j)), mx)); };
+      auto prep = [&](int j0, int j1) {
+        if (j1 > tt_valid) {
+          for (int j = max(j0, tt_valid) + tid; j < j1; j += FT_THREADS) TT[j] = texp(j);
+          tt_valid = j1;
+          __syncthreads();
+        }
+      };
+      auto tval = [&](int j) { return TT[j]; };
+      auto tval_any = [&](int j) { return j < tt_valid ? TT[j] : texp(j); };
       auto nostop = [](float) { return false; };
       // softmax denominator (sampler.nim:54-56)
-      s = exact_scan<FT_THREADS, FT_EPT, false>(0, ncand, 0.0f, tval, nostop, false, true, S.scan).v;
-      auto pval = [&](int j) { return __fdiv_rn(Af[j], s); };
-      // min-p first cut (sampler.nim:110-113): first j >= 1 with p_j < thr
+      const float s = exact_scan_fast<FT_THREADS, FT_EPT, false>(0, ncand, 0.0f, tval, nostop, false,
+                                                                 true, S.scan, S.fscan, prep).v;
+      auto pval = [&](int j) { return __fdiv_rn(TT[j], s); };
+      auto pval_any = [&](int j) { return __fdiv_rn(tval_any(j), s); };
+      // min-p first cut (sampler.nim:110-113): first j >= 1 with p_j < thr;
+      // p is non-increasing along the candidate order, so bisect.
       int nlim = ncand;
       if (p.min_p > 0.0) {
-        const float thr = __fmul_rn(__fdiv_rn(Af[0], s), __double2float_rn(p.min_p));
-        const int q = block_find_nth(ncand, 0, [&](int j) { return j >= 1 && pval(j) < thr; }, S);
-        if (q >= 0) nlim = q;
+        if (tid == 0) {
+          const float thr = __fmul_rn(pval_any(0), __double2float_rn(p.min_p));
+          int lo = 1, hi = ncand;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (pval_any(mid) < thr) hi = mid; else lo = mid + 1;
+          }
+          S.ibuf[2] = lo;
+        }
+        __syncthreads();
+        nlim = S.ibuf[2];
+        __syncthreads();
       }
       // top-p (sampler.nim:103-108) and the draw total (:115-116)
       int n;
       float total;
       if (p.top_p > 0.0 && p.top_p < 1.0) {
         const double tp = p.top_p;
-        ScanResult r = exact_scan<FT_THREADS, FT_EPT, false>(
-            0, nlim, 0.0f, pval, [tp](float v) { return (double)v >= tp; }, true, false, S.scan);
+        ScanResult r = exact_scan_fast<FT_THREADS, FT_EPT, false>(
+            0, nlim, 0.0f, pval, [tp](float v) { return (double)v >= tp; }, true, false, S.scan,
+            S.fscan, prep);
         n = (r.stop_j >= 0) ? r.stop_j + 1 : nlim;
         total = r.v;
       } else {
         n = nlim;
-        total = exact_scan<FT_THREADS, FT_EPT, false>(0, nlim, 0.0f, pval, nostop, false, true, S.scan).v;
+        total = exact_scan_fast<FT_THREADS, FT_EPT, false>(0, nlim, 0.0f, pval, nostop, false, true,
+                                                           S.scan, S.fscan, prep).v;
       }
       // draw (sampler.nim:117-121)
       const float r0 = __fmul_rn(__double2float_rn(u_draw), total);
-      ScanResult d = exact_scan<FT_THREADS, FT_EPT, true>(
-          0, n, r0, pval, [](float v) { return v <= 0.0f; }, true, false, S.scan);
+      ScanResult d = exact_scan_fast<FT_THREADS, FT_EPT, true>(
+          0, n, r0, pval, [](float v) { return v <= 0.0f; }, true, false, S.scan, S.fscan, prep);
       pos = (d.stop_j >= 0) ? d.stop_j : n - 1;
-      prob = pval(pos);
+      prob = pval_any(pos);
     }
 
     // 4. token id of the drawn position
-    const uint32_t kpos = B[pos];
-    const int lb = lower_bound_u32(B, V, kpos);
-    const int o = pos - lb;
-    int id;
-    if (!heap) {
-      id = block_find_nth(V, o, [&](int i) { return orig[i] == kpos; }, S);
+    int id = -1;
+    if (bucketed) {
+      if (tid == 0) {
+        const uint32_t kpos = (uint32_t)(SK[pos] >> 32);
+        if (!heap) {
+          id = (int)(uint32_t)SK[pos];
+        } else {
+          const int lb = lower_bound_key(SK, V, kpos);
+          const int o = pos - lb;
+          const uint32_t tkey = (uint32_t)(SK[ncand - 1] >> 32);
+          if (kpos != tkey) {
+            const int g = upper_bound_key(SK, V, kpos) - lb;
+            id = (int)(uint32_t)SK[lb + g - 1 - o];  // ties in descending index
+          } else {
+            id = -2;  // needs tau (below)
+          }
+        }
+        S.ibuf[3] = id;
+      }
+      __syncthreads();
+      id = S.ibuf[3];
+      __syncthreads();
+      if (id == -2) {
+        // the heap keeps the highest-indexed ties <= tau, where tau is the
+        // index at which the count of values >= t reaches k
+        const uint32_t tkey = (uint32_t)(SK[ncand - 1] >> 32);
+        const int tau = block_find_nth(V, ncand - 1, [&](int i) { return KY[i] <= tkey; }, S);
+        if (tid == 0) {
+          const int lb = lower_bound_key(SK, V, tkey);
+          const int ub = upper_bound_key(SK, V, tkey);
+          // ties <= tau form a prefix of the tie group (ascending index)
+          int lo2 = lb, hi2 = ub;
+          while (lo2 < hi2) {
+            const int mid = (lo2 + hi2) >> 1;
+            if ((int)(uint32_t)SK[mid] <= tau) lo2 = mid + 1; else hi2 = mid;
+          }
+          const int o = pos - lb;
+          S.ibuf[3] = (int)(uint32_t)SK[lo2 - 1 - o];
+        }
+        __syncthreads();
+        id = S.ibuf[3];
+        __syncthreads();
+      }
     } else {
-      const uint32_t tkey = B[ncand - 1];
-      if (kpos != tkey) {
-        const int g = upper_bound_u32(B, V, kpos) - lb;
-        id = block_find_nth(V, g - 1 - o, [&](int i) { return orig[i] == kpos; }, S);
+      const uint32_t kpos = LB[pos];
+      const int lb = lower_bound_u32(LB, V, kpos);
+      const int o = pos - lb;
+      if (!heap) {
+        id = block_find_nth(V, o, [&](int i) { return KY[i] == kpos; }, S);
       } else {
-        const int tau = block_find_nth(V, ncand - 1, [&](int i) { return orig[i] <= tkey; }, S);
-        const int mt = block_count(tau + 1, [&](int i) { return orig[i] == tkey; }, S);
-        id = block_find_nth(tau + 1, mt - 1 - o, [&](int i) { return orig[i] == tkey; }, S);
+        const uint32_t tkey = LB[ncand - 1];
+        if (kpos != tkey) {
+          const int g = upper_bound_u32(LB, V, kpos) - lb;
+          id = block_find_nth(V, g - 1 - o, [&](int i) { return KY[i] == kpos; }, S);
+        } else {
+          const int tau = block_find_nth(V, ncand - 1, [&](int i) { return KY[i] <= tkey; }, S);
+          const int mt = block_count(tau + 1, [&](int i) { return KY[i] == tkey; }, S);
+          id = block_find_nth(tau + 1, mt - 1 - o, [&](int i) { return KY[i] == tkey; }, S);
+        }
       }
     }
     if (tid == 0) {

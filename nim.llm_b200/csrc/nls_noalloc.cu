@@ -8,7 +8,7 @@
 // handle path does with NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS, and runs the
 // same two kernels. The full-sort kernel's scratch and the work counters live
 // in one file-scope device array, g_noalloc_scratch, of fixed size: every GPU
-// that loads the library holds it (about 12 MiB) until the process exits.
+// that loads the library holds it (about 16 MiB) until the process exits.
 //
 // The first call on a device looks up the array's device address with
 // cudaGetSymbolAddress while that device is current, and caches it. Make
@@ -28,7 +28,7 @@ constexpr int kNoallocSlots = 4;                      // full-sort CTAs (scratch
 constexpr int kNoallocVpad = nls::kMaxVocab;          // words per slot array (vocab limit)
 constexpr int kWorkWords = ((2 + kNoallocMaxRows) + 63) / 64 * 64;  // status, count, list
 constexpr size_t kScratchWords =
-    (size_t)kWorkWords + (size_t)kNoallocSlots * 3 * (size_t)kNoallocVpad;
+    (size_t)kWorkWords + (size_t)kNoallocSlots * 4 * (size_t)kNoallocVpad;
 
 static __device__ __align__(256) uint32_t g_noalloc_scratch[kScratchWords];
 

@@ -79,6 +79,27 @@ __device__ __forceinline__ int binade_exp(float v) {
   return e < -126 ? -126 : e;
 }
 
+// Contribution of a >= 0 (finite) on the grid 2^ue, from its bits: returns
+// rne(a / 2^ue) with ties reported separately (tie = true means a/2^ue is
+// k + 1/2 and the returned value is k). Values at or above 2^40 are clamped;
+// they only occur at a binade change, which the caller recomputes exactly.
+__device__ __forceinline__ long long grid_units(float a, int ue, bool* tie) {
+  const uint32_t bits = __float_as_uint(a);
+  *tie = false;
+  if (bits == 0u) return 0;
+  const int be = (int)(bits >> 23);
+  const uint32_t m = (bits & 0x7fffffu) | (be ? 0x800000u : 0u);
+  const int d = (be ? be : 1) - 150 - ue;  // a = m * 2^(d + ue)
+  if (d >= 0) return d >= 17 ? (1LL << 40) : ((long long)m << d);
+  const int sh = -d;
+  if (sh > 25) return 0;
+  const uint32_t q = m >> sh;
+  const uint32_t rem = m & ((1u << sh) - 1u);
+  const uint32_t half = 1u << (sh - 1);
+  if (rem == half) { *tie = true; return q; }
+  return q + (rem > half ? 1u : 0u);
+}
+
 struct ScanShared {
   Fn warp_tot[32];
   long long S_end;
@@ -166,7 +187,9 @@ __device__ ScanResult exact_scan(int j0, int j1, float v0, Elem elem, Stop stop,
       int jj = j + tid * EPT + e;
       fe[e] = fn_identity();
       if (jj < cend) {
-        fe[e] = fn_of(elem(jj), ue);
+        bool tie;
+        const long long k = grid_units(elem(jj), ue, &tie);
+        fe[e] = Fn{k, 0, tie ? 1 : 0};
         F = fn_compose(F, fe[e]);
       }
     }
@@ -218,4 +241,113 @@ __device__ ScanResult exact_scan(int j0, int j1, float v0, Elem elem, Stop stop,
   return ScanResult{v, -1};
 }
 
+
+struct FastScanShared {
+  long long red[32];
+  int flag[32];
+};
+
+// Same contract as exact_scan, for long sequences: each chunk first takes the
+// fast path -- the sum of its elements' grid units, one block reduction -- and
+// only a chunk that holds a tie, a binade change or the stop takes the
+// element-by-element path of exact_scan. `stop` must be monotone along the
+// sequence (true from some element on); elem(j) is called once per element
+// and chunk attempt.
+//
+// prep(j, jend) is called by every thread at the start of each chunk, before
+// any elem() of it: a block-wide hook that may fill a cache elem() reads
+// (it must end with a barrier if it writes).
+template <int NT, int EPT, bool DEC, class Elem, class Stop, class Prep>
+__device__ ScanResult exact_scan_fast(int j0, int j1, float v0, Elem elem, Stop stop,
+                                      bool has_stop, bool absorb, ScanShared& sm,
+                                      FastScanShared& fs, Prep prep) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int CH = NT * EPT;
+  float v = v0;
+  int j = j0;
+  while (j < j1) {
+    const int E = binade_exp(v);
+    const int ue = E - 23;
+    long long S0 = (long long)ldexp((double)v, -ue);
+    if (DEC) S0 = -S0;
+    const int cend = (j1 - j > CH) ? j + CH : j1;
+    prep(j, cend);
+    if (!DEC && absorb) {
+      const float a0 = elem(j);
+      if ((double)a0 < ldexp(1.0, ue - 1)) break;
+    }
+    long long sum = 0;
+    bool tie = false;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int jj = j + e * NT + tid;  // strided: coalesced loads
+      if (jj < cend) {
+        bool t;
+        sum += grid_units(elem(jj), ue, &t);
+        tie |= t;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const unsigned anytie = __ballot_sync(0xffffffffu, tie);
+    if (lane == 0) { fs.red[warp] = sum; fs.flag[warp] = anytie != 0u; }
+    __syncthreads();
+    long long tot = 0;
+    int any = 0;
+#pragma unroll 8
+    for (int w = 0; w < NT / 32; ++w) { tot += fs.red[w]; any |= fs.flag[w]; }
+    __syncthreads();
+    const long long Se = S0 + tot;
+    bool fast = !any;
+    if (fast) {
+      if (!DEC) fast = Se < (1LL << 24);
+      else fast = (E == -126) ? (Se < 0) : (Se < -(1LL << 23));
+    }
+    if (fast && has_stop) fast = !stop(grid_value(DEC ? -Se : Se, ue));
+    if (fast) {
+      v = grid_value(DEC ? -Se : Se, ue);
+      j = cend;
+      continue;
+    }
+    // Something happens inside this chunk: retry its sub-chunks of NT
+    // elements on the fast path and replay only the failing ones element by
+    // element.
+    for (int sj = j; sj < cend; sj += NT) {
+      const int send = (cend - sj > NT) ? sj + NT : cend;
+      const int E2 = binade_exp(v);
+      const int ue2 = E2 - 23;
+      long long S2 = (long long)ldexp((double)v, -ue2);
+      if (DEC) S2 = -S2;
+      bool t2 = false;
+      long long sum2 = 0;
+      if (sj + tid < send) sum2 = grid_units(elem(sj + tid), ue2, &t2);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
+      const unsigned tie2 = __ballot_sync(0xffffffffu, t2);
+      if (lane == 0) { fs.red[warp] = sum2; fs.flag[warp] = tie2 != 0u; }
+      __syncthreads();
+      long long tot2 = 0;
+      int any2 = 0;
+#pragma unroll 8
+      for (int w = 0; w < NT / 32; ++w) { tot2 += fs.red[w]; any2 |= fs.flag[w]; }
+      __syncthreads();
+      const long long Se2 = S2 + tot2;
+      bool fast2 = !any2;
+      if (fast2) {
+        if (!DEC) fast2 = Se2 < (1LL << 24);
+        else fast2 = (E2 == -126) ? (Se2 < 0) : (Se2 < -(1LL << 23));
+      }
+      if (fast2 && has_stop) fast2 = !stop(grid_value(DEC ? -Se2 : Se2, ue2));
+      if (fast2) {
+        v = grid_value(DEC ? -Se2 : Se2, ue2);
+        continue;
+      }
+      ScanResult r = exact_scan<NT, 1, DEC>(sj, send, v, elem, stop, has_stop, false, sm);
+      if (r.stop_j >= 0) return r;
+      v = r.v;
+    }
+    j = cend;
+  }
+  return ScanResult{v, -1};
+}
 }  // namespace nls
