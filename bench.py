@@ -24,7 +24,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -59,61 +58,80 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of one GPU, polled through
+    NVML (read-only queries) every few milliseconds during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.lines: list[str] = []
-        self.proc = None
+    def __init__(self, device, period_s: float = 0.002):
+        self.device = device
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.smax = None
+        self.stop_ev = threading.Event()
         self.thread = None
+        self.err = None
+        self.nvml = None
+        self.handle = None
+
+    def _open(self):
+        import pynvml as nv
+        import torch
+        nv.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        h = None
+        try:
+            h = nv.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+        except Exception:  # older drivers / formats: match the PCI address
+            bus = "%08X:%02X:%02X.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+        self.nvml, self.handle = nv, h
+        self.smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((int(sm), int(rs)))
+            except Exception as e:  # keep what was collected
+                self.err = repr(e)
+                return
+            if self.stop_ev.wait(self.period):
+                return
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            self._open()
+        except Exception as e:
+            self.err = f"NVML unavailable: {e!r}"
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._poll, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        self.stop_ev.set()
+        self.thread.join(timeout=5)
+        nv = self.nvml
+        reasons = set()
+        for _, rs in self.samples:
+            for name, const in self.REASONS:
+                if rs & getattr(nv, const, 0):
+                    reasons.add(name)
+        sm = [c for c, _ in self.samples]
         try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self.thread:
-            self.thread.join(timeout=5)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+            nv.nvmlShutdown()
+        except Exception:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "NVML poll every 2 ms"}
 
 
 def row_is_full(params, V):
@@ -273,7 +291,7 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
     clocks.start()
     step_ms, k_light, k_full = [], [], []
     for _ in range(args.steps):
@@ -283,7 +301,7 @@ def main():
         e0.record(stream)
         step()
         e1.record(stream)
-        kl, kf = eng.last_kernel_ms()
+        kl, kf, _ = eng.last_kernel_ms()
         e1.synchronize()
         step_ms.append(e0.elapsed_time(e1))
         k_light.append(kl)
@@ -396,7 +414,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": B * world / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "latency_b1": latency,
             "clocks": clk,
         }

@@ -34,17 +34,22 @@ struct nls_handle {
   // outputs for host-output calls
   int64_t* d_out_ids = nullptr;
   float* d_out_probs = nullptr;
-  // [0] status, [1] full_count, [2 ..] full_list
+  // [0] status, [1] full_count, [2] row_claim, [3] unused, [4 ..] full_list
   int* d_work = nullptr;
   // full-sort scratch: slots x 4 x vpad words
   uint32_t* d_scratch = nullptr;
   int vpad = 0;
   int slots = 0;
   int* h_status = nullptr;  // pinned
-  // profiling: events around the two kernels of the last call
+  // the streaming kernel runs on `side`, forked from and joined back into the
+  // caller's stream, concurrently with the full-sort kernel
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  // profiling: [0] start, [1] streaming kernel done, [2] full-sort kernel
+  // done, [3] fallback launch done
   int profiling = 0;
   int profiled = 0;
-  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
   char last_err[256] = {0};
 };
 
@@ -98,8 +103,7 @@ int pick_cluster(const nls_handle* h, int rows, int vocab) {
   if (env && *env) {
     C = atoi(env);
   } else if (vocab >= 8192) {
-    int want = (2 * h->sm_count + rows - 1) / (rows > 0 ? rows : 1);
-    C = want;
+    C = (h->sm_count + rows - 1) / (rows > 0 ? rows : 1);  // split rows only when SMs are left
   }
   int maxc = vocab / 2048;
   if (C > maxc) C = maxc;
@@ -108,21 +112,46 @@ int pick_cluster(const nls_handle* h, int rows, int vocab) {
   return C;
 }
 
+// One batch: the streaming kernel (greedy and top-k <= 256 rows) on the side
+// stream, concurrently with the full-sort kernel, which claims the full-path
+// rows itself; then a second full-sort launch for the rows the streaming
+// kernel handed back (ties or thresholds it could not settle; usually none).
 nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st) {
   nls::BatchArgs a = a_in;
   a.status = h->d_work;
   a.full_count = h->d_work + 1;
-  a.full_list = h->d_work + 2;
-  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, 2 * sizeof(int), st));
+  a.full_list = h->d_work + 4;
+  a.row_claim = nullptr;
+  a.skip_full = 0;
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, 4 * sizeof(int), st));
   const int C = pick_cluster(h, a.rows, a.V);
   int chunk = (a.V + C - 1) / C;
   chunk = (chunk + 3) & ~3;
   const bool prof = h->profiling != 0;
   if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[0], st));
-  NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
-  if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
-  if (!a.argmax_only) NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st));
-  if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
+  if (a.argmax_only) {
+    NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
+    if (prof) {
+      NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
+      NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
+      NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
+    }
+  } else {
+    NLS_CUDA(h, cudaEventRecord(h->fork, st));
+    NLS_CUDA(h, cudaStreamWaitEvent(h->side, h->fork, 0));
+    nls::BatchArgs af = a;
+    af.row_claim = h->d_work + 2;
+    NLS_CUDA(h, nls::launch_full(af, h->d_scratch, h->vpad, h->slots, st));
+    if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
+    nls::BatchArgs al = a;
+    al.skip_full = 1;
+    NLS_CUDA(h, nls::launch_light(al, C, chunk, h->side));
+    if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[1], h->side));
+    NLS_CUDA(h, cudaEventRecord(h->join, h->side));
+    NLS_CUDA(h, cudaStreamWaitEvent(st, h->join, 0));
+    NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st));
+    if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
+  }
   h->profiled = prof ? 1 : 0;
   NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
   (void)flags;
@@ -168,6 +197,9 @@ void nls_destroy(nls_handle* h) {
     cudaFree(h->d_work);
     cudaFree(h->d_scratch);
     if (h->h_status) cudaFreeHost(h->h_status);
+    if (h->side) cudaStreamDestroy(h->side);
+    if (h->fork) cudaEventDestroy(h->fork);
+    if (h->join) cudaEventDestroy(h->join);
     for (cudaEvent_t e : h->ev)
       if (e) cudaEventDestroy(e);
   }
@@ -207,8 +239,14 @@ nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_
     fail(e, "cudaMalloc(out_ids)");
   } else if ((e = cudaMalloc(&h->d_out_probs, sizeof(float) * max_rows)) != cudaSuccess) {
     fail(e, "cudaMalloc(out_probs)");
-  } else if ((e = cudaMalloc(&h->d_work, sizeof(int) * (2 + max_rows))) != cudaSuccess) {
+  } else if ((e = cudaMalloc(&h->d_work, sizeof(int) * (4 + max_rows))) != cudaSuccess) {
     fail(e, "cudaMalloc(work)");
+  } else if ((e = cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking)) != cudaSuccess) {
+    fail(e, "cudaStreamCreate(side)");
+  } else if ((e = cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming)) != cudaSuccess) {
+    fail(e, "cudaEventCreate(fork)");
+  } else if ((e = cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming)) != cudaSuccess) {
+    fail(e, "cudaEventCreate(join)");
   } else if ((e = cudaMallocHost(&h->h_status, sizeof(int))) != cudaSuccess) {
     fail(e, "cudaMallocHost(status)");
   }
@@ -366,13 +404,12 @@ nls_status nls_last_kernel_ms(nls_handle* h, float* out_ms, int32_t n) {
   if (!h || !out_ms || n < 1) return NLS_ERR_INVALID_ARG;
   if (!h->profiled) return NLS_ERR_INVALID_ARG;
   DeviceGuard g(h->device);
-  NLS_CUDA(h, cudaEventSynchronize(h->ev[2]));
-  float ms = 0.0f;
-  NLS_CUDA(h, cudaEventElapsedTime(&ms, h->ev[0], h->ev[1]));
-  out_ms[0] = ms;
-  if (n > 1) {
-    NLS_CUDA(h, cudaEventElapsedTime(&ms, h->ev[1], h->ev[2]));
-    out_ms[1] = ms;
+  NLS_CUDA(h, cudaEventSynchronize(h->ev[3]));
+  NLS_CUDA(h, cudaEventSynchronize(h->ev[1]));
+  for (int i = 0; i < n && i < 3; ++i) {
+    float ms = 0.0f;
+    NLS_CUDA(h, cudaEventElapsedTime(&ms, h->ev[0], h->ev[i + 1]));
+    out_ms[i] = ms;
   }
   return NLS_OK;
 }

@@ -37,6 +37,13 @@ struct BatchArgs {
   int* full_count;
   int* status;               // first error code recorded by any kernel
   int argmax_only;           // nls_argmax_batch: plain argmax, no params
+  // Full-sort kernel: when set, it claims the rows whose parameters select
+  // the full path straight from [0, rows) through this counter, instead of
+  // reading full_list (lets it run concurrently with the streaming kernel).
+  int* row_claim;
+  // Streaming kernel: leave full-path rows alone (a concurrent full-sort
+  // launch claims them) instead of appending them to full_list.
+  int skip_full;
 };
 
 __device__ __forceinline__ void record_status(int* st, int code) { atomicCAS(st, 0, code); }

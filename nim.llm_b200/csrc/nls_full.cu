@@ -28,6 +28,7 @@
 //      descending index and the heap's survivor rule among ties at the k-th
 //      value).
 #include <climits>
+#include <type_traits>
 
 #include "nls_common.cuh"
 #include "nls_kernels.h"
@@ -49,6 +50,7 @@ constexpr int FT_BIG = 8192;       // window capacity (FT_WIN + FT_BUCKET_MAX)
 constexpr int FT_NB2 = 4096;       // fine buckets per window (second level)
 constexpr int FT_INS_MAX = 64;     // fine buckets up to this size: one-thread insertion sort
 constexpr int FT_BIGLIST = 64;
+constexpr int FT_MAXWIN = kMaxVocab / FT_WIN;  // windows of the largest vocabulary
 constexpr float FT_DCAP = 110.0f;  // expf(-110) is 0: beyond this t_j is 0
 
 struct FullShared {
@@ -85,6 +87,12 @@ struct FullShared {
   float fbuf[8];
   int biglist[FT_BIGLIST];
   int nbig;
+  // windows: window c spans SK positions [wstart[c], wstart[c+1]) and the
+  // coarse buckets [wbkt[c], wbkt[c+1]); wstate[c] = 0 bucket order, 1
+  // bucket order with TT filled, 2 sorted with TT filled
+  int wstart[FT_MAXWIN + 1];
+  int wbkt[FT_MAXWIN + 1];
+  int wstate[FT_MAXWIN];
   int counter, patch_overflow, dup, nan;
 };
 
@@ -407,10 +415,30 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   // LSD fallback: two key arrays in the SK region
   uint32_t* LA = KY + vpad;
   uint32_t* LB = KY + 2 * (size_t)vpad;
-  const int nwork = *a.full_count;
+  const bool claim = (a.row_claim != nullptr);
+  const int nwork = claim ? 0 : *a.full_count;
+  int w = blockIdx.x;
 
-  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
-    const int row = a.full_list[w];
+  for (;;) {
+    int row;
+    if (claim) {  // next row whose parameters select the full path
+      if (tid == 0) {
+        int r;
+        while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
+          int64_t kk;
+          if (row_mode(a.params[r], V, &kk) == kModeFull) break;
+        }
+        S.ibuf[0] = r;
+      }
+      __syncthreads();
+      row = S.ibuf[0];
+      __syncthreads();
+      if (row >= a.rows) break;
+    } else {
+      if (w >= nwork) break;
+      row = a.full_list[w];
+      w += gridDim.x;
+    }
     const nls_row_params p = a.params[row];
     int64_t K64;
     const int mode = row_mode(p, V, &K64);
@@ -570,87 +598,17 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     for (int b = tid; b < FT_NB; b += FT_THREADS) bigmax = max(bigmax, (int)S.h1[b]);
     bigmax = block_max_int(bigmax, S);
     const bool bucketed = bigmax <= FT_BUCKET_MAX;
-    if (bucketed) {
-      // coarse scatter, one tile at a time: counting sort of the tile in
-      // shared memory, then each bucket's run goes out contiguously
-      unsigned long long* stage = S.u.big;
-      for (int t0 = 0; t0 < V; t0 += FT_TILE1) {
-        const int nt = min(FT_TILE1, V - t0);
-        for (int b = tid; b < FT_NB; b += FT_THREADS) S.lc[b] = 0u;
-        __syncthreads();
-        uint32_t kd[FT_TILE1 / FT_THREADS];
-        int bb[FT_TILE1 / FT_THREADS];
-#pragma unroll
-        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
-          const int i = tid + r * FT_THREADS;
-          kd[r] = (i < nt) ? KY[t0 + i] : 0u;
-          bb[r] = (i < nt) ? bk(kd[r]) : -1;
-          if (bb[r] >= 0) atomicAdd(&S.lc[bb[r]], 1u);
-        }
-        __syncthreads();
-        if (warp == 0) {
-          uint32_t loc[FT_NB / 32], sum = 0;
-#pragma unroll
-          for (int r = 0; r < FT_NB / 32; ++r) { loc[r] = S.lc[lane * (FT_NB / 32) + r]; sum += loc[r]; }
-          uint32_t incl = sum;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-          }
-          uint32_t run = incl - sum;
-#pragma unroll
-          for (int r = 0; r < FT_NB / 32; ++r) {
-            const int b = lane * (FT_NB / 32) + r;
-            S.lo1[b] = run;
-            S.gb1[b] = atomicAdd(&S.c1[b], loc[r]);  // this tile's slice of bucket b
-            S.lc[b] = run;                           // becomes the local cursor
-            run += loc[r];
-          }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
-          const int i = tid + r * FT_THREADS;
-          if (bb[r] >= 0) {
-            const uint32_t q = atomicAdd(&S.lc[bb[r]], 1u);
-            stage[q] = ((unsigned long long)kd[r] << 32) | (uint32_t)(t0 + i);
-          }
-        }
-        __syncthreads();
-        for (int q = tid; q < nt; q += FT_THREADS) {
-          const unsigned long long v = stage[q];
-          const int b = bk((uint32_t)(v >> 32));
-          SK[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
-        }
-        __syncthreads();
-      }
-      // windows: the coarse buckets whose start lies in [c*FT_WIN, (c+1)*FT_WIN)
-      auto first_bucket_from = [&](int x) {  // first bucket with start >= x, or FT_NB
-        int lo = 0, hi = FT_NB;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          if ((int)S.s1[mid] >= x) hi = mid; else lo = mid + 1;
-        }
-        return lo;
-      };
-      unsigned long long* bufA = S.u.big;
-      unsigned long long* bufB = S.ph.bufB;
-      const int nwin = (V + FT_WIN - 1) / FT_WIN;
-      for (int c = 0; c < nwin; ++c) {
-        if (tid == 0) {
-          const int bA = first_bucket_from(c * FT_WIN);
-          const int bB = first_bucket_from((c + 1) * FT_WIN);
-          S.ibuf[4] = bA;
-          S.ibuf[5] = bB;
-          S.ibuf[6] = (bA < FT_NB) ? (int)S.s1[bA] : V;
-          S.ibuf[7] = (bB < FT_NB) ? (int)S.s1[bB] : V;
-        }
-        __syncthreads();
-        const int bA = S.ibuf[4], bB = S.ibuf[5], ws = S.ibuf[6], we = S.ibuf[7];
-        __syncthreads();
-        const int n = we - ws;
-        if (n <= 1) continue;
+    const int nwin = (V + FT_WIN - 1) / FT_WIN;
+    unsigned long long* bufA = S.u.big;
+    unsigned long long* bufB = S.ph.bufB;
+    auto texp_key = [&](uint32_t kdv) { return ref_expf(__fsub_rn(desc_key_value(kdv), mx)); };
+    // Sort window c in shared memory: fine buckets of about one element
+    // (value-linear inside each coarse bucket), insertion sorts on
+    // (key, index), a block sort for the rare large fine bucket; then TT.
+    auto sort_window = [&](int c) {
+      const int bA = S.wbkt[c], bB = S.wbkt[c + 1], ws = S.wstart[c], we = S.wstart[c + 1];
+      const int n = we - ws;
+      if (n > 1) {
         const int F = FT_NB2 / max(1, bB - bA);  // fine buckets per coarse bucket
         auto fine = [&](uint32_t kdv) {
           const int b = bk(kdv);
@@ -722,8 +680,96 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           for (int i = tid; i < m; i += FT_THREADS) seg[i] = bufA[i];
           __syncthreads();
         }
-        for (int i = tid; i < n; i += FT_THREADS) SK[ws + i] = bufB[i];
+        for (int i = tid; i < n; i += FT_THREADS) {
+          const unsigned long long v = bufB[i];
+          SK[ws + i] = v;
+          TT[ws + i] = texp_key((uint32_t)(v >> 32));
+        }
+      } else if (n == 1) {
+        if (tid == 0) TT[ws] = texp_key((uint32_t)(SK[ws] >> 32));
+      }
+      if (tid == 0) S.wstate[c] = 2;
+      __syncthreads();
+    };
+    // window holding SK position j (the same in every thread)
+    auto window_of = [&](int j) {
+      int lo = 0, hi = nwin - 1;  // last c with wstart[c] <= j
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (S.wstart[mid] <= j) lo = mid; else hi = mid - 1;
+      }
+      return lo;
+    };
+    auto ensure_sorted = [&](int j) {
+      const int c = window_of(j);
+      if (S.wstate[c] != 2) sort_window(c);
+    };
+    if (bucketed) {
+      // coarse scatter, one tile at a time: counting sort of the tile in
+      // shared memory, then each bucket's run goes out contiguously
+      unsigned long long* stage = S.u.big;
+      for (int t0 = 0; t0 < V; t0 += FT_TILE1) {
+        const int nt = min(FT_TILE1, V - t0);
+        for (int b = tid; b < FT_NB; b += FT_THREADS) S.lc[b] = 0u;
         __syncthreads();
+        uint32_t kd[FT_TILE1 / FT_THREADS];
+        int bb[FT_TILE1 / FT_THREADS];
+#pragma unroll
+        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
+          const int i = tid + r * FT_THREADS;
+          kd[r] = (i < nt) ? KY[t0 + i] : 0u;
+          bb[r] = (i < nt) ? bk(kd[r]) : -1;
+          if (bb[r] >= 0) atomicAdd(&S.lc[bb[r]], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+          uint32_t loc[FT_NB / 32], sum = 0;
+#pragma unroll
+          for (int r = 0; r < FT_NB / 32; ++r) { loc[r] = S.lc[lane * (FT_NB / 32) + r]; sum += loc[r]; }
+          uint32_t incl = sum;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+          }
+          uint32_t run = incl - sum;
+#pragma unroll
+          for (int r = 0; r < FT_NB / 32; ++r) {
+            const int b = lane * (FT_NB / 32) + r;
+            S.lo1[b] = run;
+            S.gb1[b] = atomicAdd(&S.c1[b], loc[r]);  // this tile's slice of bucket b
+            S.lc[b] = run;                           // becomes the local cursor
+            run += loc[r];
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
+          const int i = tid + r * FT_THREADS;
+          if (bb[r] >= 0) {
+            const uint32_t q = atomicAdd(&S.lc[bb[r]], 1u);
+            stage[q] = ((unsigned long long)kd[r] << 32) | (uint32_t)(t0 + i);
+          }
+        }
+        __syncthreads();
+        for (int q = tid; q < nt; q += FT_THREADS) {
+          const unsigned long long v = stage[q];
+          const int b = bk((uint32_t)(v >> 32));
+          SK[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
+        }
+        __syncthreads();
+      }
+      // windows: the coarse buckets whose start lies in [c*FT_WIN, (c+1)*FT_WIN)
+      for (int c = tid; c <= nwin; c += FT_THREADS) {
+        const int x = c * FT_WIN;
+        int lo = 0, hi = FT_NB;  // first bucket starting at or after x
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if ((int)S.s1[mid] >= x) hi = mid; else lo = mid + 1;
+        }
+        S.wbkt[c] = lo;
+        S.wstart[c] = (c == nwin || lo >= FT_NB) ? V : (int)S.s1[lo];
+        if (c < nwin) S.wstate[c] = 0;
       }
     } else {
       // repeated values overflow one bucket: LSD radix sort of the keys
@@ -746,6 +792,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     if (!isfinite(mx)) {
       // Non-finite maximum: the reference's arithmetic produces NaNs that a
       // grid replay cannot represent; run its loops literally (one thread).
+      if (bucketed)
+        for (int c = 0; c < nwin; ++c)
+          if (S.wstate[c] != 2) sort_window(c);
       if (tid == 0) {
         float m = -INFINITY;
         for (int j = 0; j < ncand; ++j) {
@@ -789,10 +838,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       prob = S.fbuf[1];
       __syncthreads();
     } else {
-      // 3. t_j = expf(y_j - max) in candidate order, computed once per chunk
-      //    the first time a scan reaches it (peaked rows stop early)
-      int tt_valid = 0;  // TT holds [0, tt_valid); the same in every thread
-      auto texp = [&](int j) { return ref_expf(__fsub_rn(desc_key_value(skey(j)), mx)); };
+      // 3. t_j = expf(y_j - max) in candidate order (TT), then the three
+      //    sequential sums of the reference replayed exactly.
+      int tt_valid = 0;  // LSD path: TT holds [0, tt_valid); the same in every thread
+      auto texp = [&](int j) { return texp_key(skey(j)); };
       auto prep = [&](int j0, int j1) {
         if (j1 > tt_valid) {
           for (int j = max(j0, tt_valid) + tid; j < j1; j += FT_THREADS) TT[j] = texp(j);
@@ -800,52 +849,177 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           __syncthreads();
         }
       };
-      auto tval = [&](int j) { return TT[j]; };
-      auto tval_any = [&](int j) { return j < tt_valid ? TT[j] : texp(j); };
+      auto noprep = [](int, int) {};
       auto nostop = [](float) { return false; };
+      // One sequential fp32 accumulation over candidate positions [0, j1)
+      // whose j-th term is fromt(t_j). Bucketed path: a window whose
+      // elements leave the running value in its binade with no rounding tie
+      // and no stop contributes an order-independent integer sum, so it is
+      // summed in bucket order without sorting; any other window (and one
+      // cut by j1) is sorted first and replayed in order.
+      auto run_scan = [&](auto decc, int j1, float v0, auto fromt, auto stop, bool has_stop,
+                          bool absorb) -> ScanResult {
+        constexpr bool DEC = decltype(decc)::value;
+        auto elem = [&](int j) { return fromt(TT[j]); };
+        if (!bucketed)
+          return exact_scan_fast<FT_THREADS, FT_EPT, DEC>(0, j1, v0, elem, stop, has_stop, absorb,
+                                                          S.scan, S.fscan, prep);
+        float v = v0;
+        for (int c = 0; c < nwin; ++c) {
+          const int ws = S.wstart[c];
+          if (ws >= j1) break;
+          const int we0 = S.wstart[c + 1];
+          if (we0 <= ws) continue;
+          const int we = min(we0, j1);
+          const int st = S.wstate[c];
+          if (st != 2 && we == we0) {
+            const int E = binade_exp(v);
+            const int ue = E - 23;
+            long long S0 = (long long)ldexp((double)v, -ue);
+            if (DEC) S0 = -S0;
+            long long sum = 0;
+            bool tie = false;
+            float amax = 0.0f;
+            for (int j = ws + tid; j < we; j += FT_THREADS) {
+              float t;
+              if (st == 0) {
+                t = texp_key((uint32_t)(SK[j] >> 32));
+                TT[j] = t;
+              } else {
+                t = TT[j];
+              }
+              const float e = fromt(t);
+              bool tj;
+              sum += grid_units(e, ue, &tj);
+              tie |= tj;
+              amax = fmaxf(amax, e);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              sum += __shfl_xor_sync(0xffffffffu, sum, o);
+              amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            }
+            const unsigned anytie = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) { S.fscan.red[warp] = sum; S.fscan.flag[warp] = anytie != 0u; S.fred[warp] = amax; }
+            __syncthreads();
+            if (tid == 0 && st == 0) S.wstate[c] = 1;
+            long long tot = 0;
+            int any = 0;
+            float wmax = 0.0f;
+#pragma unroll 8
+            for (int w = 0; w < FT_WARPS; ++w) {
+              tot += S.fscan.red[w];
+              any |= S.fscan.flag[w];
+              wmax = fmaxf(wmax, S.fred[w]);
+            }
+            __syncthreads();
+            // every later term is at most this window's largest
+            if (!DEC && absorb && (double)wmax < ldexp(1.0, ue - 1)) return ScanResult{v, -1};
+            const long long Se = S0 + tot;
+            bool fast = !any;
+            if (fast) {
+              if (!DEC) fast = Se < (1LL << 24);
+              else fast = (E == -126) ? (Se < 0) : (Se < -(1LL << 23));
+            }
+            if (fast && has_stop) fast = !stop(grid_value(DEC ? -Se : Se, ue));
+            if (fast) {
+              v = grid_value(DEC ? -Se : Se, ue);
+              continue;
+            }
+          }
+          if (S.wstate[c] != 2) sort_window(c);
+          const ScanResult r = exact_scan_fast<FT_THREADS, FT_EPT, DEC>(
+              ws, we, v, elem, stop, has_stop, absorb, S.scan, S.fscan, noprep);
+          if (r.stop_j >= 0) return r;
+          v = r.v;
+          if (!DEC && absorb && (double)elem(we - 1) < ldexp(1.0, binade_exp(v) - 24))
+            return ScanResult{v, -1};
+        }
+        return ScanResult{v, -1};
+      };
+      using inc_t = std::integral_constant<bool, false>;
+      using dec_t = std::integral_constant<bool, true>;
+      if (bucketed && heap) ensure_sorted(ncand - 1);
       // softmax denominator (sampler.nim:54-56)
-      const float s = exact_scan_fast<FT_THREADS, FT_EPT, false>(0, ncand, 0.0f, tval, nostop, false,
-                                                                 true, S.scan, S.fscan, prep).v;
-      auto pval = [&](int j) { return __fdiv_rn(TT[j], s); };
-      auto pval_any = [&](int j) { return __fdiv_rn(tval_any(j), s); };
-      // min-p first cut (sampler.nim:110-113): first j >= 1 with p_j < thr;
-      // p is non-increasing along the candidate order, so bisect.
+      const float s = run_scan(inc_t{}, ncand, 0.0f, [](float t) { return t; }, nostop, false, true).v;
+      auto pfrom = [s](float t) { return __fdiv_rn(t, s); };
+      // min-p first cut (sampler.nim:110-113): first j >= 1 with p_j < thr.
+      // p is a non-increasing function of the candidate's key, so the kept
+      // prefix is {key <= K*} for the largest key K* with p(K*) >= thr.
       int nlim = ncand;
       if (p.min_p > 0.0) {
-        if (tid == 0) {
-          const float thr = __fmul_rn(pval_any(0), __double2float_rn(p.min_p));
-          int lo = 1, hi = ncand;
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (pval_any(mid) < thr) hi = mid; else lo = mid + 1;
+        if (!bucketed) {
+          auto pval_any = [&](int j) { return __fdiv_rn(j < tt_valid ? TT[j] : texp(j), s); };
+          if (tid == 0) {
+            const float thr = __fmul_rn(pval_any(0), __double2float_rn(p.min_p));
+            int lo = 1, hi = ncand;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (pval_any(mid) < thr) hi = mid; else lo = mid + 1;
+            }
+            S.ibuf[2] = lo;
           }
-          S.ibuf[2] = lo;
+          __syncthreads();
+          nlim = S.ibuf[2];
+          __syncthreads();
+        } else {
+          // t of the maximum is expf(0) = 1
+          const float thr = __fmul_rn(__fdiv_rn(1.0f, s), __double2float_rn(p.min_p));
+          auto pk = [&](uint32_t kdv) { return __fdiv_rn(texp_key(kdv), s); };
+          if (tid == 0) {
+            uint32_t lo = kmin, hi = kmax;  // pk(lo) >= thr unless min_p > 1
+            if (!(pk(lo) >= thr)) {
+              S.ibuf[2] = -1;
+            } else {
+              while (lo < hi) {  // largest key with pk >= thr
+                const uint32_t mid = lo + (uint32_t)((hi - lo + 1u) >> 1);
+                if (pk(mid) >= thr) lo = mid; else hi = mid - 1u;
+              }
+              S.ibuf[2] = bk(lo);
+              S.ibuf[3] = (int)lo;
+            }
+          }
+          __syncthreads();
+          const int bs = S.ibuf[2];
+          const uint32_t kstar = (uint32_t)S.ibuf[3];
+          __syncthreads();
+          if (bs < 0) {
+            nlim = 1;
+          } else {
+            // buckets before bs hold keys <= K*, buckets after it keys > K*
+            const int b0 = (int)S.s1[bs], b1 = b0 + (int)S.h1[bs];
+            int cnt = 0;
+            for (int j = b0 + tid; j < b1; j += FT_THREADS) cnt += (uint32_t)(SK[j] >> 32) <= kstar;
+            cnt = block_sum_int(cnt, S);
+            nlim = max(1, min(ncand, b0 + cnt));
+          }
         }
-        __syncthreads();
-        nlim = S.ibuf[2];
-        __syncthreads();
       }
       // top-p (sampler.nim:103-108) and the draw total (:115-116)
       int n;
       float total;
       if (p.top_p > 0.0 && p.top_p < 1.0) {
         const double tp = p.top_p;
-        ScanResult r = exact_scan_fast<FT_THREADS, FT_EPT, false>(
-            0, nlim, 0.0f, pval, [tp](float v) { return (double)v >= tp; }, true, false, S.scan,
-            S.fscan, prep);
+        const ScanResult r = run_scan(inc_t{}, nlim, 0.0f, pfrom, [tp](float v) { return (double)v >= tp; },
+                                      true, false);
         n = (r.stop_j >= 0) ? r.stop_j + 1 : nlim;
         total = r.v;
       } else {
         n = nlim;
-        total = exact_scan_fast<FT_THREADS, FT_EPT, false>(0, nlim, 0.0f, pval, nostop, false, true,
-                                                           S.scan, S.fscan, prep).v;
+        total = run_scan(inc_t{}, nlim, 0.0f, pfrom, nostop, false, true).v;
       }
       // draw (sampler.nim:117-121)
       const float r0 = __fmul_rn(__double2float_rn(u_draw), total);
-      ScanResult d = exact_scan_fast<FT_THREADS, FT_EPT, true>(
-          0, n, r0, pval, [](float v) { return v <= 0.0f; }, true, false, S.scan, S.fscan, prep);
+      const ScanResult d = run_scan(dec_t{}, n, r0, pfrom, [](float v) { return v <= 0.0f; }, true, false);
       pos = (d.stop_j >= 0) ? d.stop_j : n - 1;
-      prob = pval_any(pos);
+      if (bucketed) {
+        ensure_sorted(pos);
+      } else if (pos >= tt_valid) {
+        if (tid == 0) TT[pos] = texp(pos);
+        __syncthreads();
+      }
+      prob = __fdiv_rn(TT[pos], s);
+      __syncthreads();
     }
 
     // 4. token id of the drawn position
@@ -856,11 +1030,14 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         if (!heap) {
           id = (int)(uint32_t)SK[pos];
         } else {
-          const int lb = lower_bound_key(SK, V, kpos);
+          // equal keys share a coarse bucket, hence a (sorted) window
+          const int c = window_of(pos);
+          const int w0 = S.wstart[c], wn = S.wstart[c + 1] - w0;
+          const int lb = w0 + lower_bound_key(SK + w0, wn, kpos);
           const int o = pos - lb;
           const uint32_t tkey = (uint32_t)(SK[ncand - 1] >> 32);
           if (kpos != tkey) {
-            const int g = upper_bound_key(SK, V, kpos) - lb;
+            const int g = w0 + upper_bound_key(SK + w0, wn, kpos) - lb;
             id = (int)(uint32_t)SK[lb + g - 1 - o];  // ties in descending index
           } else {
             id = -2;  // needs tau (below)
@@ -877,8 +1054,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         const uint32_t tkey = (uint32_t)(SK[ncand - 1] >> 32);
         const int tau = block_find_nth(V, ncand - 1, [&](int i) { return KY[i] <= tkey; }, S);
         if (tid == 0) {
-          const int lb = lower_bound_key(SK, V, tkey);
-          const int ub = upper_bound_key(SK, V, tkey);
+          const int c = window_of(ncand - 1);
+          const int w0 = S.wstart[c], wn = S.wstart[c + 1] - w0;
+          const int lb = w0 + lower_bound_key(SK + w0, wn, tkey);
+          const int ub = w0 + upper_bound_key(SK + w0, wn, tkey);
           // ties <= tau form a prefix of the tie group (ascending index)
           int lo2 = lb, hi2 = ub;
           while (lo2 < hi2) {
@@ -924,7 +1103,8 @@ cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slo
   cudaError_t e = cudaFuncSetAttribute(full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  full_kernel<<<slots, FT_THREADS, smem, stream>>>(a, scratch, vpad);
+  const int grid = (a.row_claim && a.rows < slots) ? a.rows : slots;
+  full_kernel<<<grid, FT_THREADS, smem, stream>>>(a, scratch, vpad);
   return cudaGetLastError();
 }
 

@@ -166,7 +166,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
     mode = row_mode(p, V, &K64);
   }
   if (mode == kModeFull) {
-    if (crank == 0 && tid == 0) {
+    if (!a.skip_full && crank == 0 && tid == 0) {
       int w = atomicAdd(a.full_count, 1);
       a.full_list[w] = row;
     }

@@ -180,11 +180,13 @@ class Engine:
     def set_profiling(self, on: bool = True) -> None:
         self._check(self._lib.nls_set_profiling(self._h, 1 if on else 0), "nls_set_profiling")
 
-    def last_kernel_ms(self) -> tuple[float, float]:
-        """(streaming kernel ms, full-sort kernel ms) of the last profiled call."""
-        out = (ctypes.c_float * 2)()
-        self._check(self._lib.nls_last_kernel_ms(self._h, out, 2), "nls_last_kernel_ms")
-        return float(out[0]), float(out[1])
+    def last_kernel_ms(self) -> tuple[float, float, float]:
+        """Device ms of the last profiled call, each from the call's start: to
+        the end of the streaming kernel, of the (concurrent) full-sort kernel,
+        and of the call's last kernel."""
+        out = (ctypes.c_float * 3)()
+        self._check(self._lib.nls_last_kernel_ms(self._h, out, 3), "nls_last_kernel_ms")
+        return float(out[0]), float(out[1]), float(out[2])
 
     def argmax_batch(self, logits) -> np.ndarray:
         logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
