@@ -71,6 +71,15 @@ __device__ __forceinline__ float key_threshold_float(uint32_t k) {
 // the double-precision exponential rounded once to float.
 __device__ __forceinline__ float ref_expf(float x) { return __double2float_rn(exp((double)x)); }
 
+// Cheap bracket of ref_expf(x). CUDA documents expf at 2 ulp and exp at
+// 1 ulp (double) of the true value, so while expf(x) >= 2^-120 (both results
+// normal) ref_expf(x) lies within 2.6 ulp of a = expf(x):
+// a (1 - 2^-20) <= ref_expf(x) <= a (1 + 2^-20), rounded outwards (8 ulp).
+// Below 2^-120 the bracket is not used (the caller computes ref_expf).
+constexpr float kBracketMin = 0x1p-120f;
+__device__ __forceinline__ float bracket_lo(float a) { return __fmul_rd(a, 1.0f - 0x1p-20f); }
+__device__ __forceinline__ float bracket_hi(float a) { return __fmul_ru(a, 1.0f + 0x1p-20f); }
+
 // Row classification (sampler.nim:77-78, 85-86).
 __device__ __forceinline__ int row_mode(const nls_row_params& p, int V, int64_t* k_out) {
   int64_t k = (p.top_k > 0) ? (p.top_k < V ? p.top_k : (int64_t)V) : (int64_t)V;

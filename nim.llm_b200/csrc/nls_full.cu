@@ -43,7 +43,7 @@ constexpr int FT_WARPS = FT_THREADS / 32;
 constexpr int FT_HASH_LOG2 = 12;
 constexpr int FT_GSHIFT = 2;
 constexpr int FT_NB = 256;         // coarse value buckets (first level)
-constexpr int FT_TILE1 = 4096;     // elements per scatter tile
+constexpr int FT_TILE1 = 8192;     // elements per scatter tile
 constexpr int FT_WIN = 4096;       // a window holds the buckets starting in FT_WIN positions
 constexpr int FT_BUCKET_MAX = 4096;  // larger coarse buckets take the LSD fallback
 constexpr int FT_BIG = 8192;       // window capacity (FT_WIN + FT_BUCKET_MAX)
@@ -402,6 +402,27 @@ struct Bucketer {
   }
 };
 
+// Terms of the three accumulations as functions of t = expf(y - max): the
+// softmax denominator sums t itself, the top-p / total / draw sums sum
+// p = t / s. exact() is the reference's arithmetic; lo()/hi() map a lower /
+// upper bound of t to a lower / upper bound of the term (monotone).
+// mid(a) for a = expf(x) estimates the exact term (from t = ref_expf(x))
+// to a relative error: TermT within 2^-20 (the bracket of bracket_lo, checked
+// over every float in [-110, 0]); TermP adds the roundings of 1/s, of the
+// product and of the reference's quotient, within 1.2 * 2^-20. `margin` is
+// at least twice that.
+struct TermT {
+  static constexpr float margin = 0x1p-19f;
+  __device__ float exact(float t) const { return t; }
+  __device__ float mid(float a) const { return a; }
+};
+struct TermP {
+  static constexpr float margin = 0x1p-18f;
+  float s, rinv;  // rinv = 1/s rounded to nearest
+  __device__ float exact(float t) const { return __fdiv_rn(t, s); }
+  __device__ float mid(float a) const { return __fmul_rn(a, rinv); }
+};
+
 __global__ void __launch_bounds__(FT_THREADS, 1)
 full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -708,18 +729,24 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       // coarse scatter, one tile at a time: counting sort of the tile in
       // shared memory, then each bucket's run goes out contiguously
       unsigned long long* stage = S.u.big;
+      constexpr int PT = FT_TILE1 / FT_THREADS;
+      for (int b = tid; b < FT_NB; b += FT_THREADS) S.lc[b] = 0u;
+      uint32_t kd[PT];  // this tile's keys, loaded one tile ahead
+#pragma unroll
+      for (int r = 0; r < PT; ++r) {
+        const int i = tid + r * FT_THREADS;
+        kd[r] = (i < V) ? KY[i] : 0u;
+      }
+      __syncthreads();
       for (int t0 = 0; t0 < V; t0 += FT_TILE1) {
         const int nt = min(FT_TILE1, V - t0);
-        for (int b = tid; b < FT_NB; b += FT_THREADS) S.lc[b] = 0u;
-        __syncthreads();
-        uint32_t kd[FT_TILE1 / FT_THREADS];
-        int bb[FT_TILE1 / FT_THREADS];
+        int bb[PT];
+        uint32_t rk[PT];  // rank inside the tile's bucket
 #pragma unroll
-        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
+        for (int r = 0; r < PT; ++r) {
           const int i = tid + r * FT_THREADS;
-          kd[r] = (i < nt) ? KY[t0 + i] : 0u;
           bb[r] = (i < nt) ? bk(kd[r]) : -1;
-          if (bb[r] >= 0) atomicAdd(&S.lc[bb[r]], 1u);
+          rk[r] = (bb[r] >= 0) ? atomicAdd(&S.lc[bb[r]], 1u) : 0u;
         }
         __syncthreads();
         if (warp == 0) {
@@ -736,29 +763,33 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 #pragma unroll
           for (int r = 0; r < FT_NB / 32; ++r) {
             const int b = lane * (FT_NB / 32) + r;
-            S.lo1[b] = run;
-            S.gb1[b] = atomicAdd(&S.c1[b], loc[r]);  // this tile's slice of bucket b
-            S.lc[b] = run;                           // becomes the local cursor
+            S.lo1[b] = run;       // the bucket's run inside the staged tile
+            S.gb1[b] = S.c1[b];   // and its destination in SK
+            S.c1[b] += loc[r];
+            S.lc[b] = 0u;
             run += loc[r];
           }
         }
         __syncthreads();
 #pragma unroll
-        for (int r = 0; r < FT_TILE1 / FT_THREADS; ++r) {
-          const int i = tid + r * FT_THREADS;
-          if (bb[r] >= 0) {
-            const uint32_t q = atomicAdd(&S.lc[bb[r]], 1u);
-            stage[q] = ((unsigned long long)kd[r] << 32) | (uint32_t)(t0 + i);
-          }
+        for (int r = 0; r < PT; ++r) {
+          if (bb[r] >= 0)
+            stage[S.lo1[bb[r]] + rk[r]] = ((unsigned long long)kd[r] << 32) | (uint32_t)(t0 + tid + r * FT_THREADS);
+        }
+#pragma unroll
+        for (int r = 0; r < PT; ++r) {
+          const int i = t0 + FT_TILE1 + tid + r * FT_THREADS;
+          kd[r] = (i < V) ? KY[i] : 0u;
         }
         __syncthreads();
+        // (the next tile touches lo1/gb1/stage only after its first barrier)
         for (int q = tid; q < nt; q += FT_THREADS) {
           const unsigned long long v = stage[q];
           const int b = bk((uint32_t)(v >> 32));
           SK[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
         }
-        __syncthreads();
       }
+      __syncthreads();
       // windows: the coarse buckets whose start lies in [c*FT_WIN, (c+1)*FT_WIN)
       for (int c = tid; c <= nwin; c += FT_THREADS) {
         const int x = c * FT_WIN;
@@ -860,7 +891,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       auto run_scan = [&](auto decc, int j1, float v0, auto fromt, auto stop, bool has_stop,
                           bool absorb) -> ScanResult {
         constexpr bool DEC = decltype(decc)::value;
-        auto elem = [&](int j) { return fromt(TT[j]); };
+        auto elem = [&](int j) { return fromt.exact(TT[j]); };
         if (!bucketed)
           return exact_scan_fast<FT_THREADS, FT_EPT, DEC>(0, j1, v0, elem, stop, has_stop, absorb,
                                                           S.scan, S.fscan, prep);
@@ -873,6 +904,11 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const int we = min(we0, j1);
           const int st = S.wstate[c];
           if (st != 2 && we == we0) {
+            // Order-independent pass. TT holds, per element, a = expf(x)
+            // (ref_expf bracketed, see bracket_lo) or, with the sign bit set,
+            // the exact -ref_expf(x) where no bracket applies. An element's
+            // grid units are settled by its bracket unless a rounding
+            // boundary falls inside it; then ref_expf is evaluated.
             const int E = binade_exp(v);
             const int ue = E - 23;
             long long S0 = (long long)ldexp((double)v, -ue);
@@ -880,19 +916,57 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             long long sum = 0;
             bool tie = false;
             float amax = 0.0f;
-            for (int j = ws + tid; j < we; j += FT_THREADS) {
-              float t;
+            // grid 2^ue as a float scale (when representable)
+            const bool scale_ok = (ue >= -120 && ue <= 126);  // terms near a grid step stay normal
+            const float gscale = scale_ok ? __int_as_float((127 - ue) << 23) : 0.0f;
+            constexpr int WPT = FT_BIG / FT_THREADS;  // a window has < FT_BIG elements
+            const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
+            uint32_t raw[WPT];  // all loads first: one memory latency per window
+#pragma unroll
+            for (int r = 0; r < WPT; ++r) {
+              const int j = ws + tid + r * FT_THREADS;
+              raw[r] = (j < we) ? (st == 0 ? SKw[2 * j + 1] : __float_as_uint(TT[j])) : 0u;
+            }
+#pragma unroll
+            for (int r = 0; r < WPT; ++r) {
+              const int j = ws + tid + r * FT_THREADS;
+              if (j >= we) continue;
+              float a;
               if (st == 0) {
-                t = texp_key((uint32_t)(SK[j] >> 32));
-                TT[j] = t;
+                const float x = __fsub_rn(desc_key_value(raw[r]), mx);
+                a = expf(x);
+                if (!(a >= kBracketMin)) a = -ref_expf(x);
+                TT[j] = a;
               } else {
-                t = TT[j];
+                a = __uint_as_float(raw[r]);
               }
-              const float e = fromt(t);
-              bool tj;
-              sum += grid_units(e, ue, &tj);
+              long long un = 0;
+              bool tj = false;
+              float emid = 0.0f;
+              bool settled = false;
+              if (!signbit(a) && scale_ok) {
+                // q = term / grid; the exact term lies within q * margin / 2
+                // of q, so if no half-integer is that close, rne(q) is its
+                // grid value and it is no tie.
+                emid = fromt.mid(a);
+                const float q = __fmul_rn(emid, gscale);
+                const float k = rintf(q);
+                const float f = fabsf(__fsub_rn(q, k));
+                if (__fsub_rn(0.5f, f) > __fmul_rn(q, fromt.margin)) {
+                  un = (long long)k;
+                  settled = true;
+                }
+              }
+              if (!settled) {
+                const float t = signbit(a) ? -a
+                    : ref_expf(__fsub_rn(desc_key_value(SKw[2 * j + 1]), mx));
+                const float e = fromt.exact(t);
+                un = grid_units(e, ue, &tj);
+                emid = e;
+              }
+              sum += un;
               tie |= tj;
-              amax = fmaxf(amax, e);
+              amax = fmaxf(amax, emid);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -914,7 +988,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             }
             __syncthreads();
             // every later term is at most this window's largest
-            if (!DEC && absorb && (double)wmax < ldexp(1.0, ue - 1)) return ScanResult{v, -1};
+            // (wmax estimates the largest term within 1.2 * 2^-20; 2^-17 covers it)
+            if (!DEC && absorb && (double)wmax * (1.0 + 0x1p-17) < ldexp(1.0, ue - 1))
+              return ScanResult{v, -1};
             const long long Se = S0 + tot;
             bool fast = !any;
             if (fast) {
@@ -941,8 +1017,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       using dec_t = std::integral_constant<bool, true>;
       if (bucketed && heap) ensure_sorted(ncand - 1);
       // softmax denominator (sampler.nim:54-56)
-      const float s = run_scan(inc_t{}, ncand, 0.0f, [](float t) { return t; }, nostop, false, true).v;
-      auto pfrom = [s](float t) { return __fdiv_rn(t, s); };
+      const float s = run_scan(inc_t{}, ncand, 0.0f, TermT{}, nostop, false, true).v;
+      const TermP pfrom{s, __frcp_rn(s)};
       // min-p first cut (sampler.nim:110-113): first j >= 1 with p_j < thr.
       // p is a non-increasing function of the candidate's key, so the kept
       // prefix is {key <= K*} for the largest key K* with p(K*) >= thr.
