@@ -33,6 +33,7 @@
 #include "nls_common.cuh"
 #include "nls_kernels.h"
 #include "nls_scan.cuh"
+#include "nls_tma.cuh"
 
 namespace nls {
 
@@ -40,6 +41,7 @@ constexpr int FT_THREADS = 1024;
 constexpr int FT_EPT = 4;
 constexpr int FT_TILE = FT_THREADS * FT_EPT;
 constexpr int FT_WARPS = FT_THREADS / 32;
+static_assert(FT_WARPS == 32, "block reductions keep one warp partial per lane");
 constexpr int FT_HASH_LOG2 = 12;
 constexpr int FT_GSHIFT = 2;
 constexpr int FT_NB = 256;         // coarse value buckets (first level)
@@ -88,11 +90,12 @@ struct FullShared {
   int biglist[FT_BIGLIST];
   int nbig;
   // windows: window c spans SK positions [wstart[c], wstart[c+1]) and the
-  // coarse buckets [wbkt[c], wbkt[c+1]); wstate[c] = 0 bucket order, 1
-  // bucket order with TT filled, 2 sorted with TT filled
+  // coarse buckets [wbkt[c], wbkt[c+1]); wstate[c] = 0 bucket order, 2 sorted
+  // with TT (exact t per position) filled
   int wstart[FT_MAXWIN + 1];
   int wbkt[FT_MAXWIN + 1];
   int wstate[FT_MAXWIN];
+  int cwin;  // window whose exact t values sit in u.big (as floats), or -1
   int counter, patch_overflow, dup, nan;
 };
 
@@ -109,9 +112,7 @@ __device__ int block_sum_int(int v, FullShared& S) {
   v = __reduce_add_sync(0xffffffffu, v);
   if (lane == 0) S.ired[warp] = v;
   __syncthreads();
-  int tot = 0;
-#pragma unroll 8
-  for (int w = 0; w < FT_WARPS; ++w) tot += S.ired[w];
+  const int tot = __reduce_add_sync(0xffffffffu, S.ired[lane]);  // FT_WARPS == 32
   __syncthreads();
   return tot;
 }
@@ -121,9 +122,7 @@ __device__ int block_max_int(int v, FullShared& S) {
   v = __reduce_max_sync(0xffffffffu, v);
   if (lane == 0) S.ired[warp] = v;
   __syncthreads();
-  int m = INT_MIN;
-#pragma unroll 8
-  for (int w = 0; w < FT_WARPS; ++w) m = max(m, S.ired[w]);
+  const int m = __reduce_max_sync(0xffffffffu, S.ired[lane]);
   __syncthreads();
   return m;
 }
@@ -138,12 +137,9 @@ __device__ int block_excl_sum_int(int v, int* total, FullShared& S) {
   }
   if (lane == 31) S.ired[warp] = incl;
   __syncthreads();
-  int wpre = 0, tot = 0;
-  for (int w = 0; w < FT_WARPS; ++w) {
-    int c = S.ired[w];
-    if (w < warp) wpre += c;
-    tot += c;
-  }
+  const int c = S.ired[lane];  // total of warp `lane`
+  const int wpre = __reduce_add_sync(0xffffffffu, lane < warp ? c : 0);
+  const int tot = __reduce_add_sync(0xffffffffu, c);
   __syncthreads();
   *total = tot;
   return wpre + incl - v;
@@ -406,18 +402,20 @@ struct Bucketer {
 // softmax denominator sums t itself, the top-p / total / draw sums sum
 // p = t / s. exact() is the reference's arithmetic; lo()/hi() map a lower /
 // upper bound of t to a lower / upper bound of the term (monotone).
-// mid(a) for a = expf(x) estimates the exact term (from t = ref_expf(x))
-// to a relative error: TermT within 2^-20 (the bracket of bracket_lo, checked
-// over every float in [-110, 0]); TermP adds the roundings of 1/s, of the
-// product and of the reference's quotient, within 1.2 * 2^-20. `margin` is
-// at least twice that.
+// mid(a) for a = texp_estimate(x) estimates the exact term (from
+// t = ref_expf(x)) to a relative error: TermT within kBracketRel = 2^-14;
+// TermP adds the roundings of 1/s, of the product and of the reference's
+// quotient, within 1.01 * 2^-14. `margin` is at least twice that; `margin2`
+// is the same for texp_estimate2 (2^-20, TermP 1.2 * 2^-20).
 struct TermT {
-  static constexpr float margin = 0x1p-19f;
+  static constexpr float margin = 0x1p-13f;   // for texp_estimate
+  static constexpr float margin2 = 0x1p-19f;  // for texp_estimate2
   __device__ float exact(float t) const { return t; }
   __device__ float mid(float a) const { return a; }
 };
 struct TermP {
-  static constexpr float margin = 0x1p-18f;
+  static constexpr float margin = 0x1p-12f;
+  static constexpr float margin2 = 0x1p-18f;
   float s, rinv;  // rinv = 1/s rounded to nearest
   __device__ float exact(float t) const { return __fdiv_rn(t, s); }
   __device__ float mid(float a) const { return __fmul_rn(a, rinv); }
@@ -622,6 +620,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     const int nwin = (V + FT_WIN - 1) / FT_WIN;
     unsigned long long* bufA = S.u.big;
     unsigned long long* bufB = S.ph.bufB;
+    // the sorted window under replay: exact t per position, in shared memory
+    float* tcache = reinterpret_cast<float*>(S.u.big);
     auto texp_key = [&](uint32_t kdv) { return ref_expf(__fsub_rn(desc_key_value(kdv), mx)); };
     // Sort window c in shared memory: fine buckets of about one element
     // (value-linear inside each coarse bucket), insertion sorts on
@@ -703,13 +703,31 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         }
         for (int i = tid; i < n; i += FT_THREADS) {
           const unsigned long long v = bufB[i];
+          const float t = texp_key((uint32_t)(v >> 32));
           SK[ws + i] = v;
-          TT[ws + i] = texp_key((uint32_t)(v >> 32));
+          TT[ws + i] = t;
+          tcache[i] = t;
         }
       } else if (n == 1) {
-        if (tid == 0) TT[ws] = texp_key((uint32_t)(SK[ws] >> 32));
+        if (tid == 0) {
+          const float t = texp_key((uint32_t)(SK[ws] >> 32));
+          TT[ws] = t;
+          tcache[0] = t;
+        }
       }
-      if (tid == 0) S.wstate[c] = 2;
+      if (tid == 0) {
+        S.wstate[c] = 2;
+        S.cwin = c;
+      }
+      __syncthreads();
+    };
+    // make window c's exact t values resident in tcache (c sorted)
+    auto cache_window = [&](int c) {
+      if (S.cwin == c) return;
+      const int ws = S.wstart[c], n = S.wstart[c + 1] - ws;
+      __syncthreads();
+      for (int i = tid; i < n; i += FT_THREADS) tcache[i] = TT[ws + i];
+      if (tid == 0) S.cwin = c;
       __syncthreads();
     };
     // window holding SK position j (the same in every thread)
@@ -802,6 +820,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         S.wstart[c] = (c == nwin || lo >= FT_NB) ? V : (int)S.s1[lo];
         if (c < nwin) S.wstate[c] = 0;
       }
+      if (tid == 0) S.cwin = -1;  // u.big held the scatter stage
     } else {
       // repeated values overflow one bucket: LSD radix sort of the keys
       lsd_count(KY, V, 0, S);
@@ -904,70 +923,82 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const int we = min(we0, j1);
           const int st = S.wstate[c];
           if (st != 2 && we == we0) {
-            // Order-independent pass. TT holds, per element, a = expf(x)
-            // (ref_expf bracketed, see bracket_lo) or, with the sign bit set,
-            // the exact -ref_expf(x) where no bracket applies. An element's
-            // grid units are settled by its bracket unless a rounding
-            // boundary falls inside it; then ref_expf is evaluated.
+            // Order-independent pass. An element's grid units follow from the
+            // estimate texp_estimate(x) unless a rounding boundary lies
+            // within the estimate's error; then ref_expf is evaluated.
             const int E = binade_exp(v);
             const int ue = E - 23;
             long long S0 = (long long)ldexp((double)v, -ue);
             if (DEC) S0 = -S0;
-            long long sum = 0;
-            bool tie = false;
-            float amax = 0.0f;
             // grid 2^ue as a float scale (when representable)
             const bool scale_ok = (ue >= -120 && ue <= 126);  // terms near a grid step stay normal
             const float gscale = scale_ok ? __int_as_float((127 - ue) << 23) : 0.0f;
             constexpr int WPT = FT_BIG / FT_THREADS;  // a window has < FT_BIG elements
             const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
+            // warm L2 with the next window while this one is summed
+            if (tid == 0 && c + 1 < nwin) {
+              const int p0 = we0 & ~1;                   // 16-byte aligned start
+              const int p1 = (S.wstart[c + 2] + 1) & ~1;  // <= vpad (even)
+              if (p1 > p0) l2_prefetch_bulk(SK + p0, (uint32_t)(p1 - p0) * 8u);
+            }
             uint32_t raw[WPT];  // all loads first: one memory latency per window
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
               const int j = ws + tid + r * FT_THREADS;
-              raw[r] = (j < we) ? (st == 0 ? SKw[2 * j + 1] : __float_as_uint(TT[j])) : 0u;
+              raw[r] = (j < we) ? SKw[2 * j + 1] : 0u;
             }
+            long long sum = 0;
+            float sumf = 0.0f;  // settled units, each < 2^12: exact in fp32
+            bool tie = false;
+            float amax = 0.0f;
+            float xs[WPT];
+            unsigned pending = 0u;  // elements the estimate does not settle
+            // q = term / grid; the exact term lies within q * margin / 2 of q,
+            // so if no half-integer is that close, rne(q) is its grid value
+            // and it is no tie. Straight-line code: the unrolled elements
+            // overlap; the rare unsettled ones are redone below.
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
-              const int j = ws + tid + r * FT_THREADS;
-              if (j >= we) continue;
-              float a;
-              if (st == 0) {
-                const float x = __fsub_rn(desc_key_value(raw[r]), mx);
-                a = expf(x);
-                if (!(a >= kBracketMin)) a = -ref_expf(x);
-                TT[j] = a;
-              } else {
-                a = __uint_as_float(raw[r]);
-              }
-              long long un = 0;
-              bool tj = false;
-              float emid = 0.0f;
+              const bool valid = ws + tid + r * FT_THREADS < we;
+              const float x = __fsub_rn(desc_key_value(raw[r]), mx);
+              xs[r] = x;
+              const float a = texp_estimate(x);
+              const float emid = fromt.mid(a);
+              const float q = __fmul_rn(emid, gscale);
+              const float k = rintf(q);
+              const float f = fabsf(__fsub_rn(q, k));
+              const bool ok = (a >= kBracketMin) && scale_ok && (__fsub_rn(0.5f, f) > __fmul_rn(q, fromt.margin));
+              sumf = __fadd_rn(sumf, (valid && ok) ? k : 0.0f);
+              amax = fmaxf(amax, valid ? emid : 0.0f);
+              pending |= (valid && !ok) ? (1u << r) : 0u;
+            }
+            while (pending) {
+              const int r = __ffs(pending) - 1;
+              pending &= pending - 1u;
+              const float x = xs[r];
+              const float a2 = texp_estimate2(x);
               bool settled = false;
-              if (!signbit(a) && scale_ok) {
-                // q = term / grid; the exact term lies within q * margin / 2
-                // of q, so if no half-integer is that close, rne(q) is its
-                // grid value and it is no tie.
-                emid = fromt.mid(a);
+              float emid = 0.0f;
+              if (a2 >= kBracketMin && scale_ok) {
+                emid = fromt.mid(a2);
                 const float q = __fmul_rn(emid, gscale);
                 const float k = rintf(q);
                 const float f = fabsf(__fsub_rn(q, k));
-                if (__fsub_rn(0.5f, f) > __fmul_rn(q, fromt.margin)) {
-                  un = (long long)k;
+                if (__fsub_rn(0.5f, f) > __fmul_rn(q, fromt.margin2)) {
+                  sumf = __fadd_rn(sumf, k);
                   settled = true;
                 }
               }
               if (!settled) {
-                const float t = signbit(a) ? -a
-                    : ref_expf(__fsub_rn(desc_key_value(SKw[2 * j + 1]), mx));
-                const float e = fromt.exact(t);
-                un = grid_units(e, ue, &tj);
+                const float e = fromt.exact(ref_expf(x));
+                bool tj;
+                sum += grid_units(e, ue, &tj);
+                tie |= tj;
                 emid = e;
               }
-              sum += un;
-              tie |= tj;
               amax = fmaxf(amax, emid);
             }
+            sum += (long long)sumf;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
               sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -976,20 +1007,18 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             const unsigned anytie = __ballot_sync(0xffffffffu, tie);
             if (lane == 0) { S.fscan.red[warp] = sum; S.fscan.flag[warp] = anytie != 0u; S.fred[warp] = amax; }
             __syncthreads();
-            if (tid == 0 && st == 0) S.wstate[c] = 1;
-            long long tot = 0;
-            int any = 0;
-            float wmax = 0.0f;
-#pragma unroll 8
-            for (int w = 0; w < FT_WARPS; ++w) {
-              tot += S.fscan.red[w];
-              any |= S.fscan.flag[w];
-              wmax = fmaxf(wmax, S.fred[w]);
+            long long tot = S.fscan.red[lane];  // FT_WARPS == 32: one partial per lane
+            float wmax = S.fred[lane];
+            const int any = __any_sync(0xffffffffu, S.fscan.flag[lane]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              tot += __shfl_xor_sync(0xffffffffu, tot, o);
+              wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
             }
             __syncthreads();
             // every later term is at most this window's largest
-            // (wmax estimates the largest term within 1.2 * 2^-20; 2^-17 covers it)
-            if (!DEC && absorb && (double)wmax * (1.0 + 0x1p-17) < ldexp(1.0, ue - 1))
+            // (wmax estimates the largest term within 1.01 * 2^-14; 2^-12 covers it)
+            if (!DEC && absorb && (double)wmax * (1.0 + 0x1p-12) < ldexp(1.0, ue - 1))
               return ScanResult{v, -1};
             const long long Se = S0 + tot;
             bool fast = !any;
@@ -1004,11 +1033,13 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             }
           }
           if (S.wstate[c] != 2) sort_window(c);
+          else cache_window(c);
+          auto elemc = [&](int j) { return fromt.exact(tcache[j - ws]); };
           const ScanResult r = exact_scan_fast<FT_THREADS, FT_EPT, DEC>(
-              ws, we, v, elem, stop, has_stop, absorb, S.scan, S.fscan, noprep);
+              ws, we, v, elemc, stop, has_stop, absorb, S.scan, S.fscan, noprep);
           if (r.stop_j >= 0) return r;
           v = r.v;
-          if (!DEC && absorb && (double)elem(we - 1) < ldexp(1.0, binade_exp(v) - 24))
+          if (!DEC && absorb && (double)elemc(we - 1) < ldexp(1.0, binade_exp(v) - 24))
             return ScanResult{v, -1};
         }
         return ScanResult{v, -1};

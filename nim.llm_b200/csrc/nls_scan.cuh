@@ -106,6 +106,8 @@ struct ScanShared {
   float v;
   int trig;
   int stopped;
+  int walk_j;
+  int walk_stop;
 };
 
 template <int NT>
@@ -156,6 +158,78 @@ struct ScanResult {
   float v;     // final (or stopping) value
   int stop_j;  // element at which `stop` fired, or -1
 };
+
+struct WalkResult {
+  float v;     // value after the last replayed element
+  int j;       // next element to replay
+  int stop_j;  // element at which `stop` fired, or -1
+};
+
+// One warp replays elements [j, j1) of the same accumulation as exact_scan,
+// 32 at a time: a warp scan of the grid steps, the first element whose
+// result leaves the binade or stops is redone with a real fp32 operation,
+// and the next group starts right after it. Returns at the stop, at j1,
+// after `max_groups` groups, or after two groups in a row without such an
+// element (the caller's block scan is cheaper from there). Lanes of one warp
+// only; no block barrier.
+template <bool DEC, class Elem, class Stop>
+__device__ WalkResult warp_walk(int j, int j1, float v, Elem elem, Stop stop, bool has_stop,
+                                int max_groups) {
+  const int lane = threadIdx.x & 31;
+  int quiet = 0;
+  for (int g = 0; g < max_groups && j < j1 && quiet < 2; ++g) {
+    const int E = binade_exp(v);
+    const int ue = E - 23;
+    long long S0 = (long long)ldexp((double)v, -ue);
+    if (DEC) S0 = -S0;
+    const int jj = j + lane;
+    const bool in = jj < j1;
+    const float a = in ? elem(jj) : 0.0f;
+    bool tie = false;
+    const long long k = in ? grid_units(a, ue, &tie) : 0;
+    const Fn f = in ? Fn{k, 0, tie ? 1 : 0} : fn_identity();
+    Fn incl = f;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      Fn o;
+      o.a = __shfl_up_sync(0xffffffffu, incl.a, off);
+      o.b = __shfl_up_sync(0xffffffffu, incl.b, off);
+      o.isB = __shfl_up_sync(0xffffffffu, incl.isB, off);
+      if (lane >= off) incl = fn_compose(o, incl);
+    }
+    Fn excl;
+    excl.a = __shfl_up_sync(0xffffffffu, incl.a, 1);
+    excl.b = __shfl_up_sync(0xffffffffu, incl.b, 1);
+    excl.isB = __shfl_up_sync(0xffffffffu, incl.isB, 1);
+    if (lane == 0) excl = fn_identity();
+    const long long Sb = fn_apply(excl, S0);  // before element jj
+    const long long Sn = fn_apply(f, Sb);     // after it
+    bool t = false;
+    if (in) {
+      if (!DEC) t = (Sn >= (1LL << 24));
+      else t = (Sn >= 0) || (E > -126 && Sn >= -(1LL << 23));
+      if (!t && has_stop) t = stop(grid_value(DEC ? -Sn : Sn, ue));
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, t);
+    if (m == 0u) {
+      const int cnt = (j1 - j < 32) ? j1 - j : 32;
+      const long long Se = __shfl_sync(0xffffffffu, Sn, cnt - 1);
+      v = grid_value(DEC ? -Se : Se, ue);
+      j += cnt;
+      ++quiet;
+      continue;
+    }
+    quiet = 0;
+    const int tl = __ffs(m) - 1;
+    const long long Sp = __shfl_sync(0xffffffffu, Sb, tl);
+    const float at = __shfl_sync(0xffffffffu, a, tl);
+    const float vprev = grid_value(DEC ? -Sp : Sp, ue);
+    v = DEC ? __fsub_rn(vprev, at) : __fadd_rn(vprev, at);
+    if (has_stop && stop(v)) return WalkResult{v, j + tl + 1, j + tl};
+    j += tl + 1;
+  }
+  return WalkResult{v, j, -1};
+}
 
 // Replays v <- fl(v + a_j) (DEC: v <- fl(v - a_j)) for j in [j0, j1), with
 // a_j = elem(j) >= 0 and finite. Stops at the first j whose new value makes
@@ -237,6 +311,23 @@ __device__ ScanResult exact_scan(int j0, int j1, float v0, Elem elem, Stop stop,
     __syncthreads();
     if (st) return ScanResult{v, tmin};
     j = tmin + 1;
+    // Binade changes come in runs (the first doublings of a sum, the last
+    // halvings of the draw): one warp takes the elements right after this
+    // one, far cheaper per change than a block scan.
+    if ((threadIdx.x >> 5) == 0) {
+      const WalkResult w = warp_walk<DEC>(j, j1, v, elem, stop, has_stop, 8);
+      if ((threadIdx.x & 31) == 0) {
+        sm.v = w.v;
+        sm.walk_j = w.j;
+        sm.walk_stop = w.stop_j;
+      }
+    }
+    __syncthreads();
+    v = sm.v;
+    j = sm.walk_j;
+    const int wstop = sm.walk_stop;
+    __syncthreads();
+    if (wstop >= 0) return ScanResult{v, wstop};
   }
   return ScanResult{v, -1};
 }
@@ -292,10 +383,10 @@ __device__ ScanResult exact_scan_fast(int j0, int j1, float v0, Elem elem, Stop 
     const unsigned anytie = __ballot_sync(0xffffffffu, tie);
     if (lane == 0) { fs.red[warp] = sum; fs.flag[warp] = anytie != 0u; }
     __syncthreads();
-    long long tot = 0;
-    int any = 0;
-#pragma unroll 8
-    for (int w = 0; w < NT / 32; ++w) { tot += fs.red[w]; any |= fs.flag[w]; }
+    long long tot = (lane < NT / 32) ? fs.red[lane] : 0;
+    const int any = __any_sync(0xffffffffu, (lane < NT / 32) ? fs.flag[lane] : 0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
     __syncthreads();
     const long long Se = S0 + tot;
     bool fast = !any;
@@ -326,10 +417,10 @@ __device__ ScanResult exact_scan_fast(int j0, int j1, float v0, Elem elem, Stop 
       const unsigned tie2 = __ballot_sync(0xffffffffu, t2);
       if (lane == 0) { fs.red[warp] = sum2; fs.flag[warp] = tie2 != 0u; }
       __syncthreads();
-      long long tot2 = 0;
-      int any2 = 0;
-#pragma unroll 8
-      for (int w = 0; w < NT / 32; ++w) { tot2 += fs.red[w]; any2 |= fs.flag[w]; }
+      long long tot2 = (lane < NT / 32) ? fs.red[lane] : 0;
+      const int any2 = __any_sync(0xffffffffu, (lane < NT / 32) ? fs.flag[lane] : 0);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tot2 += __shfl_xor_sync(0xffffffffu, tot2, o);
       __syncthreads();
       const long long Se2 = S2 + tot2;
       bool fast2 = !any2;

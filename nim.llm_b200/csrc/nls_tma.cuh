@@ -74,4 +74,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Ask the TMA unit to pull [p, p + bytes) into L2 (no completion to wait
+// for). p must be 16-byte aligned and bytes a multiple of 16.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 }  // namespace nls
+
