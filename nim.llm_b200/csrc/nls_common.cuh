@@ -6,12 +6,35 @@
 // with -fmad=false, so nothing is contracted into an FMA.
 #pragma once
 
+#include <atomic>
+
 #include <cstdint>
 #include <cuda_runtime.h>
 
 #include "nimllm_sample.h"
 
 namespace nls {
+
+// Raise a kernel's dynamic shared-memory limit on the current device only
+// when a launch needs more than was set before (the attribute call costs
+// host time on every launch otherwise). `done` holds, per device, the largest
+// value set so far.
+constexpr int kMaxDevicesAttr = 64;
+inline cudaError_t ensure_smem_attr(const void* fn, int bytes, std::atomic<int>* done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevicesAttr && done[dev].load(std::memory_order_relaxed) >= bytes)
+    return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevicesAttr) {
+    int cur = done[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !done[dev].compare_exchange_weak(cur, bytes)) {
+    }
+  }
+  return cudaSuccess;
+}
 
 constexpr int kMaxVocab = 1 << 18;   // token ids fit in 18 bits (composite sort keys)
 constexpr int kLightKMax = 256;      // top-k rows with k <= this take the streaming path

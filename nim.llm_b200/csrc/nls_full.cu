@@ -5,29 +5,40 @@
 // optimistic threshold that proved too high, or a penalty window with too
 // many distinct ids for its table).
 //
-// One 1024-thread CTA per row, persistent over the work list, with its own
+// One 1024-thread CTA per row, persistent over its work (rows claimed from
+// the batch, or the list the streaming kernel handed over), with its own
 // scratch slot of 4 x vocab words in HBM/L2:
 //   KY[i]  order key of logit i (index order),
-//   SK[j]  (key << 32 | index), sorted: the reference's candidate order,
-//   TT[j]  expf(y_j - max) in candidate order.
+//   SK[j]  (key << 32 | index) grouped by value bucket, candidate order
+//          between windows, sorted inside a window once a scan needs it,
+//   TT[j]  exact expf(y_j - max) of the positions of sorted windows.
 // Steps:
 //   1. transform: penalties and bias (precomputed per patched position),
 //      temperature; KY gets each logit's key, whose ascending order is the
 //      reference's candidate order (descending value);
-//   2. bucket sort: 4096 buckets linear in (max - y) -- monotone, so bucket
-//      order is candidate order -- filled by a warp-aggregated histogram and
-//      scatter; every bucket is then sorted by (key, index): a warp sorts a
-//      bucket of <= 256 in registers (bitonic), the block sorts a larger one
-//      in shared memory. A row with a bucket beyond 8192 (heavily repeated
-//      values) is sorted by the LSD radix fallback instead;
+//   2. coarse bucketing: 256 buckets linear in (max - y) -- monotone, so
+//      bucket order is candidate order -- filled tile by tile through a
+//      shared-memory counting sort, so SK is written in contiguous runs.
+//      Windows are runs of whole buckets of at most 8191 positions. A row
+//      with a bucket beyond 4096 (heavily repeated values) is sorted by the
+//      LSD radix fallback instead;
 //   3. the reference's sequential fp32 sums -- softmax denominator, top-p
-//      running sum, min-p cut, draw total and the draw -- replayed exactly by
-//      the block scans of nls_scan.cuh;
+//      running sum, draw total and the draw -- replayed exactly
+//      (nls_scan.cuh), window by window. Inside one binade of the running
+//      value, with no rounding tie and no stop, a window's effect is the sum
+//      of its terms' grid units whatever their order, so such a window is
+//      summed in bucket order from cheap exp estimates (exact where an
+//      estimate is too close to a rounding boundary). Only a window where
+//      something order-sensitive happens is sorted in shared memory (fine
+//      buckets and insertion sorts on (key, index)) and replayed in order
+//      from a shared-memory copy of its exact t values. The min-p cut is a
+//      key threshold and is counted without sorting;
 //   4. the drawn position is mapped back to a token id with the reference's
 //      tie order (ascending index for the stable sort; for the heap path,
 //      descending index and the heap's survivor rule among ties at the k-th
 //      value).
 #include <climits>
+#include <atomic>
 #include <type_traits>
 
 #include "nls_common.cuh"
@@ -1204,13 +1215,14 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   }
 }
 
+static std::atomic<int> g_full_smem_set[kMaxDevicesAttr];
+
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
                         cudaStream_t stream) {
   const size_t smem = full_smem_bytes(a.V);
-  cudaError_t e = cudaFuncSetAttribute(full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(full_kernel), (int)smem, g_full_smem_set);
   if (e != cudaSuccess) return e;
-  const int grid = (a.row_claim && a.rows < slots) ? a.rows : slots;
+  const int grid = (a.rows < slots) ? a.rows : slots;  // a CTA takes at most one row at a time
   full_kernel<<<grid, FT_THREADS, smem, stream>>>(a, scratch, vpad);
   return cudaGetLastError();
 }

@@ -26,6 +26,8 @@
 // kernel.
 #include <cooperative_groups.h>
 
+#include <atomic>
+
 #include "nls_common.cuh"
 #include "nls_kernels.h"
 #include "nls_tma.cuh"
@@ -727,10 +729,11 @@ light_kernel(BatchArgs a, int C, int chunk) {
   }
 }
 
+static std::atomic<int> g_light_smem_set[kMaxDevicesAttr];
+
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream) {
   const size_t smem = light_smem_bytes(C, chunk);
-  cudaError_t e = cudaFuncSetAttribute(light_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(light_kernel), (int)smem, g_light_smem_set);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.rows * C), 1, 1);
