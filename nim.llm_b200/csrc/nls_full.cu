@@ -52,7 +52,7 @@ constexpr int FT_THREADS = 1024;
 constexpr int FT_EPT = 4;
 constexpr int FT_TILE = FT_THREADS * FT_EPT;
 constexpr int FT_WARPS = FT_THREADS / 32;
-static_assert(FT_WARPS == 32, "block reductions keep one warp partial per lane");
+static_assert(FT_WARPS <= 32, "block reductions keep one warp partial per lane");
 constexpr int FT_HASH_LOG2 = 12;
 constexpr int FT_GSHIFT = 2;
 constexpr int FT_NB = 256;         // coarse value buckets (first level)
@@ -123,7 +123,7 @@ __device__ int block_sum_int(int v, FullShared& S) {
   v = __reduce_add_sync(0xffffffffu, v);
   if (lane == 0) S.ired[warp] = v;
   __syncthreads();
-  const int tot = __reduce_add_sync(0xffffffffu, S.ired[lane]);  // FT_WARPS == 32
+  const int tot = __reduce_add_sync(0xffffffffu, lane < FT_WARPS ? S.ired[lane] : 0);
   __syncthreads();
   return tot;
 }
@@ -133,7 +133,7 @@ __device__ int block_max_int(int v, FullShared& S) {
   v = __reduce_max_sync(0xffffffffu, v);
   if (lane == 0) S.ired[warp] = v;
   __syncthreads();
-  const int m = __reduce_max_sync(0xffffffffu, S.ired[lane]);
+  const int m = __reduce_max_sync(0xffffffffu, lane < FT_WARPS ? S.ired[lane] : INT_MIN);
   __syncthreads();
   return m;
 }
@@ -148,7 +148,7 @@ __device__ int block_excl_sum_int(int v, int* total, FullShared& S) {
   }
   if (lane == 31) S.ired[warp] = incl;
   __syncthreads();
-  const int c = S.ired[lane];  // total of warp `lane`
+  const int c = lane < FT_WARPS ? S.ired[lane] : 0;  // total of warp `lane`
   const int wpre = __reduce_add_sync(0xffffffffu, lane < warp ? c : 0);
   const int tot = __reduce_add_sync(0xffffffffu, c);
   __syncthreads();
@@ -926,6 +926,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           return exact_scan_fast<FT_THREADS, FT_EPT, DEC>(0, j1, v0, elem, stop, has_stop, absorb,
                                                           S.scan, S.fscan, prep);
         float v = v0;
+        constexpr int WPT = FT_BIG / FT_THREADS;  // a window has < FT_BIG elements
+        const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
         for (int c = 0; c < nwin; ++c) {
           const int ws = S.wstart[c];
           if (ws >= j1) break;
@@ -944,14 +946,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             // grid 2^ue as a float scale (when representable)
             const bool scale_ok = (ue >= -120 && ue <= 126);  // terms near a grid step stay normal
             const float gscale = scale_ok ? __int_as_float((127 - ue) << 23) : 0.0f;
-            constexpr int WPT = FT_BIG / FT_THREADS;  // a window has < FT_BIG elements
-            const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
-            // warm L2 with the next window while this one is summed
-            if (tid == 0 && c + 1 < nwin) {
-              const int p0 = we0 & ~1;                   // 16-byte aligned start
-              const int p1 = (S.wstart[c + 2] + 1) & ~1;  // <= vpad (even)
-              if (p1 > p0) l2_prefetch_bulk(SK + p0, (uint32_t)(p1 - p0) * 8u);
-            }
+            const int rounds = (we - ws + FT_THREADS - 1) / FT_THREADS;  // same in every thread
             uint32_t raw[WPT];  // all loads first: one memory latency per window
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
@@ -962,7 +957,6 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             float sumf = 0.0f;  // settled units, each < 2^12: exact in fp32
             bool tie = false;
             float amax = 0.0f;
-            float xs[WPT];
             unsigned pending = 0u;  // elements the estimate does not settle
             // q = term / grid; the exact term lies within q * margin / 2 of q,
             // so if no half-integer is that close, rne(q) is its grid value
@@ -970,9 +964,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             // overlap; the rare unsettled ones are redone below.
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
+              if (r >= rounds) break;
               const bool valid = ws + tid + r * FT_THREADS < we;
               const float x = __fsub_rn(desc_key_value(raw[r]), mx);
-              xs[r] = x;
               const float a = texp_estimate(x);
               const float emid = fromt.mid(a);
               const float q = __fmul_rn(emid, gscale);
@@ -983,10 +977,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
               amax = fmaxf(amax, valid ? emid : 0.0f);
               pending |= (valid && !ok) ? (1u << r) : 0u;
             }
-            while (pending) {
-              const int r = __ffs(pending) - 1;
-              pending &= pending - 1u;
-              const float x = xs[r];
+#pragma unroll
+            for (int r = 0; r < WPT; ++r) {
+              if (!(pending & (1u << r))) continue;
+              const float x = __fsub_rn(desc_key_value(raw[r]), mx);
               const float a2 = texp_estimate2(x);
               bool settled = false;
               float emid = 0.0f;
@@ -1018,9 +1012,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             const unsigned anytie = __ballot_sync(0xffffffffu, tie);
             if (lane == 0) { S.fscan.red[warp] = sum; S.fscan.flag[warp] = anytie != 0u; S.fred[warp] = amax; }
             __syncthreads();
-            long long tot = S.fscan.red[lane];  // FT_WARPS == 32: one partial per lane
-            float wmax = S.fred[lane];
-            const int any = __any_sync(0xffffffffu, S.fscan.flag[lane]);
+            long long tot = lane < FT_WARPS ? S.fscan.red[lane] : 0;  // one partial per lane
+            float wmax = lane < FT_WARPS ? S.fred[lane] : 0.0f;
+            const int any = __any_sync(0xffffffffu, lane < FT_WARPS && S.fscan.flag[lane]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
               tot += __shfl_xor_sync(0xffffffffu, tot, o);
