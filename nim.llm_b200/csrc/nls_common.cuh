@@ -337,6 +337,86 @@ __device__ uint32_t block_select_kth_largest(int n, uint32_t K, Get get, uint32_
   return prefix;
 }
 
+// One warp's version of block_select_kth_largest for small n: the K-th
+// largest key among the accepted entries (get() as above), by four rounds of
+// an 8-bit radix select over a 256-bin shared histogram. Returns the key;
+// *n_ge = entries >= it, *n_gt = entries > it (-1/-1 when fewer than K).
+// Warp-synchronous: all 32 lanes call it, no block barrier.
+template <class Get>
+__device__ uint32_t warp_select_kth_largest(int n, uint32_t K, Get get, uint32_t* hist, int* n_ge,
+                                            int* n_gt) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, pmask = 0, rem = K, above = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+    for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0u;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      uint32_t k = 0;
+      if (get(i, &k) && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    // lane l owns bins 255-8l .. 248-8l (descending key order)
+    uint32_t cnt[8], c = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) { cnt[b] = hist[255 - 8 * lane - b]; c += cnt[b]; }
+    uint32_t incl = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    const unsigned ball = __ballot_sync(0xffffffffu, incl >= rem);
+    if (!ball) {  // fewer than K accepted entries
+      *n_ge = -1;
+      *n_gt = -1;
+      return 0u;
+    }
+    const int L = __ffs(ball) - 1;
+    uint32_t d = 0, a2 = 0, hd = 0;
+    if (lane == L) {
+      uint32_t ab = incl - c;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        if (ab + cnt[b] >= rem) { d = 255u - 8u * (uint32_t)lane - (uint32_t)b; hd = cnt[b]; break; }
+        ab += cnt[b];
+      }
+      a2 = ab;
+    }
+    d = __shfl_sync(0xffffffffu, d, L);
+    a2 = __shfl_sync(0xffffffffu, a2, L);
+    hd = __shfl_sync(0xffffffffu, hd, L);
+    rem -= a2;
+    above += a2;
+    prefix |= d << shift;
+    pmask |= 255u << shift;
+    if (shift == 0) {
+      *n_gt = (int)above;
+      *n_ge = (int)(above + hd);
+    }
+    __syncwarp();
+  }
+  return prefix;
+}
+
+// One warp's bitonic sort of n64 (power of two, >= 2) uint64 keys in shared
+// memory, descending.
+__device__ inline void warp_bitonic_desc(unsigned long long* v, int n64) {
+  const int lane = threadIdx.x & 31;
+  for (int size = 2; size <= n64; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = lane; i < n64 / 2; i += 32) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = ((lo & size) == 0);
+        const unsigned long long x = v[lo], y = v[hi];
+        if ((x < y) == desc) { v[lo] = y; v[hi] = x; }
+      }
+      __syncwarp();
+    }
+  }
+}
+
 // Block-wide bitonic sort of n64 (power of two) uint64 keys, descending.
 __device__ inline void block_bitonic_desc(unsigned long long* v, int n64) {
   const int tid = threadIdx.x, nt = blockDim.x;

@@ -304,8 +304,41 @@ light_kernel(BatchArgs a, int C, int chunk) {
         const int m_floor = (int)(((long long)512 * n0 + len - 1) / len);
         m = max(m, max(m_floor, 16));
         m = min(m, n0);
-        thr = block_select_kth_largest(n0, (uint32_t)m, key0, S.hist, S.sel, 2);
-        if ((int)S.sel[2] < m) thr = 0u;
+        constexpr int NW = LT_THREADS / 32;
+        if (m <= NW * 32) {
+          // Each warp sorts its 32 thread maxima (register bitonic network)
+          // and takes the r-th largest, r = ceil(m / NW); the minimum of
+          // those over the warps has at least NW * r >= m elements of the
+          // stage at or above it, so it is a lower bound of the stage's m-th
+          // largest key.
+          uint32_t v = 0u;  // 0 sorts last: a thread without keys bounds nothing
+          for (int i = tid; i < n0; i += LT_THREADS) {
+            uint32_t k;
+            if (key0(i, &k)) v = k > v ? k : v;
+          }
+#pragma unroll
+          for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+            for (int j = kk >> 1; j > 0; j >>= 1) {
+              const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j);
+              const bool desc_block = (lane & kk) == 0 || kk == 32;
+              const bool lower = (lane & j) == 0;
+              v = (desc_block == lower) ? (v > o ? v : o) : (v < o ? v : o);
+            }
+          }
+          const int r = (m + NW - 1) / NW;
+          const uint32_t wr = __shfl_sync(0xffffffffu, v, r - 1);
+          if (lane == 0) S.cand_key[warp] = wr;
+          __syncthreads();
+          uint32_t tm = 0xffffffffu;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) tm = min(tm, S.cand_key[w]);
+          thr = tm;
+          __syncthreads();
+        } else {
+          thr = block_select_kth_largest(n0, (uint32_t)m, key0, S.hist, S.sel, 2);
+          if ((int)S.sel[2] < m) thr = 0u;
+        }
         thrf = key_threshold_float(thr);
       }
     }
@@ -484,8 +517,10 @@ light_kernel(BatchArgs a, int C, int chunk) {
   // ---- per-CTA results -------------------------------------------------
   if (mode == kModeTopK) {
     if (mnan != mnan) atomicExch(&S.nan, 1);
-    // the merge copies at most LT_SLOT candidates per CTA
-    if (!overflow && !S.failed && C > 1 && S.ncand > LT_SLOT) (void)light_compact(S, K);
+    // Before the merge, keep only this chunk's top K (with all its ties at
+    // the K-th key): the row's K-th largest key is at least every chunk's, so
+    // nothing at or above it is dropped, and CTA 0 gets ~C*K candidates.
+    if (!overflow && !S.failed && C > 1 && S.ncand > 2 * (int)K) (void)light_compact(S, K);
     __syncthreads();
     if (tid == 0) {
       if (overflow || bad_patch || (C > 1 && S.ncand > LT_SLOT)) S.overflow = 1;
@@ -601,65 +636,119 @@ light_kernel(BatchArgs a, int C, int chunk) {
   }
 
   // exact survivor set of the reference heap (see block comment at top)
-  const uint32_t t = block_select_kth_largest(
-      nm, K, [&](int i, uint32_t* k) { *k = keys[i]; return ids[i] >= 0; }, S.hist, S.sel);
-  // The candidates hold every element >= t only if no chunk threshold was
-  // above t (and there are K of them); otherwise redo the row exactly.
-  if ((int)S.sel[2] < (int)K || t < thr_max) {
-    if (tid == 0) {
-      int w = atomicAdd(a.full_count, 1);
-      a.full_list[w] = row;
-    }
-    return;
-  }
-  if (tid == 0) { S.cnt_gt = 0; S.cnt_ge = 0; S.nsurv = 0; }
-  __syncthreads();
-  {
-    int gt = 0, ge = 0;
-    for (int i = tid; i < nm; i += LT_THREADS) {
-      gt += ids[i] >= 0 && keys[i] > t;
-      ge += ids[i] >= 0 && keys[i] >= t;
-    }
-    gt = __reduce_add_sync(0xffffffffu, gt);
-    ge = __reduce_add_sync(0xffffffffu, ge);
-    if (lane == 0) { atomicAdd(&S.cnt_gt, gt); atomicAdd(&S.cnt_ge, ge); }
-  }
-  __syncthreads();
-  const int cgt = S.cnt_gt, cge = S.cnt_ge;
-  uint32_t tau = 0xffffffffu, rho = 0u;
-  if (cge != (int)K) {
-    // tau: index of the K-th element (in index order) with value >= t;
-    // survivors among the ties are the (K - cgt) highest indices <= tau.
-    tau = ~block_select_kth_largest(
-        nm, K,
-        [&](int i, uint32_t* k) {
-          if (ids[i] >= 0 && keys[i] >= t) { *k = ~(uint32_t)ids[i]; return true; }
-          return false;
-        },
-        S.hist, S.sel);
-    rho = block_select_kth_largest(
-        nm, K - (uint32_t)cgt,
-        [&](int i, uint32_t* k) {
-          if (ids[i] >= 0 && keys[i] == t && (uint32_t)ids[i] <= tau) { *k = (uint32_t)ids[i]; return true; }
-          return false;
-        },
-        S.hist, S.sel);
-  }
+  uint32_t t, tau = 0xffffffffu, rho = 0u;
   int n64 = 32;
   while (n64 < (int)K) n64 <<= 1;
-  for (int i = tid; i < n64; i += LT_THREADS) S.sortbuf[i] = 0ull;
-  __syncthreads();
-  for (int i = tid; i < nm; i += LT_THREADS) {
-    const uint32_t k = keys[i];
-    const uint32_t id = (uint32_t)ids[i];
-    const bool keep = ids[i] >= 0 && ((k > t) || (k == t && id >= rho && id <= tau));
-    if (keep) {
-      int pos = atomicAdd(&S.nsurv, 1);
-      if (pos < kLightKMax) S.sortbuf[pos] = ((unsigned long long)k << 32) | id;
+  if (nm <= 1024) {
+    // few candidates: one warp selects and sorts, no block barriers
+    if (warp != 0) return;
+    int nge, ngt;
+    t = warp_select_kth_largest(
+        nm, K, [&](int i, uint32_t* k) { *k = keys[i]; return ids[i] >= 0; }, S.hist, &nge, &ngt);
+    // The candidates hold every element >= t only if no chunk threshold was
+    // above t (and there are K of them); otherwise redo the row exactly.
+    if (nge < (int)K || t < thr_max) {
+      if (lane == 0) {
+        int w = atomicAdd(a.full_count, 1);
+        a.full_list[w] = row;
+      }
+      return;
     }
+    if (nge != (int)K) {
+      // tau: index of the K-th element (in index order) with value >= t;
+      // survivors among the ties are the (K - ngt) highest indices <= tau.
+      int u1, u2;
+      tau = ~warp_select_kth_largest(
+          nm, K,
+          [&](int i, uint32_t* k) {
+            if (ids[i] >= 0 && keys[i] >= t) { *k = ~(uint32_t)ids[i]; return true; }
+            return false;
+          },
+          S.hist, &u1, &u2);
+      rho = warp_select_kth_largest(
+          nm, K - (uint32_t)ngt,
+          [&](int i, uint32_t* k) {
+            if (ids[i] >= 0 && keys[i] == t && (uint32_t)ids[i] <= tau) { *k = (uint32_t)ids[i]; return true; }
+            return false;
+          },
+          S.hist, &u1, &u2);
+    }
+    for (int i = lane; i < n64; i += 32) S.sortbuf[i] = 0ull;
+    __syncwarp();
+    int base = 0;
+    for (int i0 = 0; i0 < nm; i0 += 32) {
+      const int i = i0 + lane;
+      bool keep = false;
+      unsigned long long v = 0ull;
+      if (i < nm) {
+        const uint32_t k = keys[i];
+        const uint32_t id = (uint32_t)ids[i];
+        keep = ids[i] >= 0 && ((k > t) || (k == t && id >= rho && id <= tau));
+        v = ((unsigned long long)k << 32) | id;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const int pos = base + __popc(m & lanemask_lt());
+        if (pos < kLightKMax) S.sortbuf[pos] = v;
+      }
+      base += __popc(m);
+    }
+    __syncwarp();
+    warp_bitonic_desc(S.sortbuf, n64);
+  } else {
+    t = block_select_kth_largest(
+        nm, K, [&](int i, uint32_t* k) { *k = keys[i]; return ids[i] >= 0; }, S.hist, S.sel);
+    if ((int)S.sel[2] < (int)K || t < thr_max) {
+      if (tid == 0) {
+        int w = atomicAdd(a.full_count, 1);
+        a.full_list[w] = row;
+      }
+      return;
+    }
+    if (tid == 0) { S.cnt_gt = 0; S.cnt_ge = 0; S.nsurv = 0; }
+    __syncthreads();
+    {
+      int gt = 0, ge = 0;
+      for (int i = tid; i < nm; i += LT_THREADS) {
+        gt += ids[i] >= 0 && keys[i] > t;
+        ge += ids[i] >= 0 && keys[i] >= t;
+      }
+      gt = __reduce_add_sync(0xffffffffu, gt);
+      ge = __reduce_add_sync(0xffffffffu, ge);
+      if (lane == 0) { atomicAdd(&S.cnt_gt, gt); atomicAdd(&S.cnt_ge, ge); }
+    }
+    __syncthreads();
+    const int cgt = S.cnt_gt, cge = S.cnt_ge;
+    if (cge != (int)K) {
+      tau = ~block_select_kth_largest(
+          nm, K,
+          [&](int i, uint32_t* k) {
+            if (ids[i] >= 0 && keys[i] >= t) { *k = ~(uint32_t)ids[i]; return true; }
+            return false;
+          },
+          S.hist, S.sel);
+      rho = block_select_kth_largest(
+          nm, K - (uint32_t)cgt,
+          [&](int i, uint32_t* k) {
+            if (ids[i] >= 0 && keys[i] == t && (uint32_t)ids[i] <= tau) { *k = (uint32_t)ids[i]; return true; }
+            return false;
+          },
+          S.hist, S.sel);
+    }
+    for (int i = tid; i < n64; i += LT_THREADS) S.sortbuf[i] = 0ull;
+    __syncthreads();
+    for (int i = tid; i < nm; i += LT_THREADS) {
+      const uint32_t k = keys[i];
+      const uint32_t id = (uint32_t)ids[i];
+      const bool keep = ids[i] >= 0 && ((k > t) || (k == t && id >= rho && id <= tau));
+      if (keep) {
+        int pos = atomicAdd(&S.nsurv, 1);
+        if (pos < kLightKMax) S.sortbuf[pos] = ((unsigned long long)k << 32) | id;
+      }
+    }
+    __syncthreads();
+    block_bitonic_desc(S.sortbuf, n64);
   }
-  __syncthreads();
-  block_bitonic_desc(S.sortbuf, n64);
 
   // ---- replay of sampler.nim:98-121 by one warp ----------------------------
   // The fp32 chains (sum, running sum, draw) run in one lane in the
