@@ -155,8 +155,9 @@ NLS_API nls_status nls_set_profiling(nls_handle* h, int32_t on);
 /* Device times in milliseconds of the last profiled call, each measured from
  * the call's start on its stream: out_ms[0] to the end of the streaming
  * kernel (greedy and top-k <= 256 rows), out_ms[1] to the end of the
- * full-sort kernel (the other rows; it runs concurrently with the streaming
- * kernel), out_ms[2] to the end of the call's last kernel (a second full-sort
+ * full-sort kernel (the other rows; above 8 rows it runs concurrently with the
+ * streaming kernel, else after it), out_ms[2] to the end of the call's last
+ * kernel (above 8 rows, a second full-sort
  * launch over rows the streaming kernel handed back). Waits for those events.
  * `n` is the capacity of out_ms (up to 3 values are written). */
 NLS_API nls_status nls_last_kernel_ms(nls_handle* h, float* out_ms, int32_t n);

@@ -112,10 +112,14 @@ int pick_cluster(const nls_handle* h, int rows, int vocab) {
   return C;
 }
 
+constexpr int kSmallBatch = 8;
+
 // One batch: the streaming kernel (greedy and top-k <= 256 rows) on the side
 // stream, concurrently with the full-sort kernel, which claims the full-path
 // rows itself; then a second full-sort launch for the rows the streaming
 // kernel handed back (ties or thresholds it could not settle; usually none).
+// Batches of at most kSmallBatch rows run the two kernels one after the
+// other instead (the fork/join costs more than the overlap gains).
 nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st) {
   nls::BatchArgs a = a_in;
   a.status = h->d_work;
@@ -133,6 +137,16 @@ nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, 
     NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
     if (prof) {
       NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
+      NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
+      NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
+    }
+  } else if (a.rows <= kSmallBatch) {
+    // a few rows: the streaming kernel hands full-path rows to one
+    // full-sort launch after it (two launches, no fork/join)
+    NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
+    if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
+    NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st));
+    if (prof) {
       NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
       NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
     }

@@ -78,6 +78,14 @@ struct LightShared {
   uint32_t thr;
   int counter, patch_overflow, dup;
   int cnt_gt, cnt_ge, nsurv;
+  // cluster merge: each CTA's summary, pushed into every CTA of the cluster
+  struct MergeRec {
+    int ncand;
+    int flags;  // 1 nan, 2 overflow, 4 failed, 8 nan at index 0
+    uint32_t thr;
+    float gbest;
+    int gidx;
+  } rec[8];
 };
 
 static int bitmap_words_host(int chunk) {
@@ -560,31 +568,42 @@ light_kernel(BatchArgs a, int C, int chunk) {
   int gidx = INT_MAX;
   if (C > 1) {
     cg::cluster_group cluster = cg::this_cluster();
+    // Push: thread j stores this CTA's summary into CTA j (remote stores do
+    // not wait); after the barrier every CTA knows all counts locally.
+    if (tid < C) {
+      LightShared* R = cluster.map_shared_rank(&S, tid);
+      LightShared::MergeRec m;
+      m.ncand = S.ncand;
+      m.flags = (S.nan ? 1 : 0) | (S.overflow ? 2 : 0) | (S.failed ? 4 : 0) | (S.nan0 ? 8 : 0);
+      m.thr = S.thr_pub;
+      m.gbest = S.gbest;
+      m.gidx = S.gidx;
+      R->rec[crank] = m;
+    }
     cluster.sync();
-    if (crank == 0) {
-      int offs = 0;
-      for (int r = 0; r < C; ++r) {
-        LightShared* R = cluster.map_shared_rank(&S, r);
-        const int nr = R->ncand;
-        any_nan |= R->nan;
-        any_over |= R->overflow;
-        any_fail |= R->failed;
-        nan0 |= R->nan0;
-        thr_max = max(thr_max, R->thr_pub);
-        const float ob = R->gbest;
-        const int oi = R->gidx;
-        if (oi != INT_MAX && (gidx == INT_MAX || ob > gbest || (ob == gbest && oi < gidx))) {
-          gbest = ob;
-          gidx = oi;
-        }
-        if (mode == kModeTopK && !any_over) {
-          const int ncopy = nr < LT_SLOT ? nr : LT_SLOT;
-          for (int i = tid; i < ncopy; i += LT_THREADS) {
-            mkey[offs + i] = R->cand_key[i];
-            midx[offs + i] = R->cand_idx[i];
-          }
-          offs += ncopy;
-        }
+    int offs = 0, myoff = 0;
+    for (int r = 0; r < C; ++r) {
+      const LightShared::MergeRec m = S.rec[r];
+      any_nan |= m.flags & 1;
+      any_over |= (m.flags >> 1) & 1;
+      any_fail |= (m.flags >> 2) & 1;
+      nan0 |= (m.flags >> 3) & 1;
+      thr_max = max(thr_max, m.thr);
+      if (m.gidx != INT_MAX && (gidx == INT_MAX || m.gbest > gbest || (m.gbest == gbest && m.gidx < gidx))) {
+        gbest = m.gbest;
+        gidx = m.gidx;
+      }
+      if (r == crank) myoff = offs;
+      offs += m.ncand < LT_SLOT ? m.ncand : LT_SLOT;
+    }
+    if (mode == kModeTopK && !any_over) {
+      // this CTA's candidates go to CTA 0's merge buffer at its offset
+      uint32_t* mk0 = cluster.map_shared_rank(mkey, 0);
+      int* mi0 = cluster.map_shared_rank(midx, 0);
+      const int ncopy = S.ncand < LT_SLOT ? S.ncand : LT_SLOT;
+      for (int i = tid; i < ncopy; i += LT_THREADS) {
+        mk0[myoff + i] = S.cand_key[i];
+        mi0[myoff + i] = S.cand_idx[i];
       }
       nm = offs;
     }
