@@ -303,13 +303,13 @@ light_kernel(BatchArgs a, int C, int chunk) {
           return true;
         };
         // Optimistic threshold: (a lower bound of) the m-th largest key of
-        // stage 0, with m chosen so that about max(512, 2K) elements of the
+        // stage 0, with m chosen so that about max(128, 2K) elements of the
         // whole chunk are expected above it. It is verified at the merge: the
         // candidates are complete iff every chunk's threshold is at most the
         // row's K-th largest candidate; otherwise the row goes to the
         // full-sort kernel.
         int m = (int)(((long long)2 * K * n0 + len - 1) / len);
-        const int m_floor = (int)(((long long)512 * n0 + len - 1) / len);
+        const int m_floor = (int)(((long long)128 * n0 + len - 1) / len);
         m = max(m, max(m_floor, 16));
         m = min(m, n0);
         constexpr int NW = LT_THREADS / 32;
@@ -351,14 +351,51 @@ light_kernel(BatchArgs a, int C, int chunk) {
       }
     }
 
-    if (mode == kModeTopK && whole) {
-      // Hot path: a full stage of a top-k row. All loads first; per element
-      // one multiply, one compare and one NaN-propagating max; the passing
-      // elements of the stage are appended with one warp scan and one atomic.
+    (void)whole;
+    // Hot paths: the stage's whole float4 groups in the ring (all of them
+    // except in the last stage). All loads first.
+    if (mode == kModeGreedy && sbase < nvec) {
+      const int ngv = min(nvec - sbase, LT_STAGE) >> 2;  // same in every thread
       float4 q[LT_GROUPS];
 #pragma unroll
-      for (int j = 0; j < LT_GROUPS; ++j)
-        q[j] = reinterpret_cast<const float4*>(S.ring[buf])[tid + j * LT_THREADS];
+      for (int j = 0; j < LT_GROUPS; ++j) {
+        const int g = tid + j * LT_THREADS;
+        q[j] = (g < ngv) ? reinterpret_cast<const float4*>(S.ring[buf])[g]
+                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+      {
+        // argmax: strict > in index order per thread; patched positions are
+        // left out here and compared later with their patched values
+#pragma unroll
+        for (int j = 0; j < LT_GROUPS; ++j) {
+          const int g = tid + j * LT_THREADS;
+          const int off = sbase + 4 * g;
+          const bool gpatch = npatch > 0 && g < ngv && patch_bit(T, off);
+          const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int gi2 = lo + off + e;
+            const bool ok = g < ngv && !(gpatch && patch_find(T, gi2) >= 0);
+            if (ok && gi2 == 0 && x[e] != x[e]) S.nan0 = 1;
+            if (ok && !(x[e] != x[e]) && (gi == INT_MAX || x[e] > gb)) { gb = x[e]; gi = gi2; }
+          }
+        }
+      }
+    }
+    if (mode == kModeTopK && sbase < nvec) {
+      // top-k: per element one multiply, one compare and one NaN-propagating
+      // max; the passing elements of the stage are appended with one warp
+      // scan and one atomic. Groups past the ring (last stage only) hold
+      // -inf and are masked out: with an accept-all threshold (-inf) they
+      // would otherwise pass.
+      float4 q[LT_GROUPS];
+      const int ngv = min(nvec - sbase, LT_STAGE) >> 2;
+#pragma unroll
+      for (int j = 0; j < LT_GROUPS; ++j) {
+        const int g = tid + j * LT_THREADS;
+        q[j] = (g < ngv) ? reinterpret_cast<const float4*>(S.ring[buf])[g]
+                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
       float y[LT_GROUPS][4];
       float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
       int cnt = 0;
@@ -367,10 +404,11 @@ light_kernel(BatchArgs a, int C, int chunk) {
         const int off = sbase + 4 * (tid + j * LT_THREADS);
         const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
         (void)off;
+        const bool gv = (tid + j * LT_THREADS) < ngv;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           y[j][e] = __fmul_rn(x[e], invT);
-          cnt += (y[j][e] >= thrf) ? 1 : 0;
+          cnt += (gv && y[j][e] >= thrf) ? 1 : 0;
         }
         m0 = fmax_nan(m0, y[j][0]);
         m1 = fmax_nan(m1, y[j][1]);
@@ -393,9 +431,10 @@ light_kernel(BatchArgs a, int C, int chunk) {
         int pos = base + incl - cnt;
 #pragma unroll
         for (int j = 0; j < LT_GROUPS; ++j) {
+          const bool gv = (tid + j * LT_THREADS) < ngv;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            if (y[j][e] >= thrf) {
+            if (gv && y[j][e] >= thrf) {
               const int off = sbase + 4 * (tid + j * LT_THREADS) + e;
               // a patched position rejoins later with its patched value
               const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
@@ -408,7 +447,32 @@ light_kernel(BatchArgs a, int C, int chunk) {
           }
         }
       }
-    } else {
+    }
+    if (sbase < nvec && nvec < len && nvec < sbase + LT_STAGE) {
+      // the chunk's last 1-3 elements (past the whole float4 groups) are not
+      // in the ring: one thread each
+      const int i = nvec + tid;
+      if (i < len && i < sbase + LT_STAGE) {
+        const float x = __ldcs(rowp + i);
+        const bool excl = npatch > 0 && patch_bit(T, i) && patch_find(T, lo + i) >= 0;
+        if (mode == kModeGreedy) {
+          if (!excl && lo + i == 0 && x != x) S.nan0 = 1;
+          if (!excl && !(x != x) && (gi == INT_MAX || x > gb)) { gb = x; gi = lo + i; }
+        } else if (mode == kModeTopK) {
+          const float y = __fmul_rn(x, invT);
+          if (!excl) mnan = fmax_nan(mnan, y);
+          if (!excl && y >= thrf) {
+            const int pos = atomicAdd(&S.ncand, 1);
+            my_max = pos + 1 > my_max ? pos + 1 : my_max;
+            if (pos < LT_CAP) {
+              S.cand_key[pos] = fkey(y);
+              S.cand_idx[pos] = lo + i;
+            }
+          }
+        }
+      }
+    }
+    if (sbase >= nvec) {
 #pragma unroll 1
       for (int j = 0; j < LT_GROUPS; ++j) {
         const int g = tid + j * LT_THREADS;           // float4 group within the stage
@@ -522,13 +586,28 @@ light_kernel(BatchArgs a, int C, int chunk) {
     __syncthreads();
   }
 
+  // Patched positions of a greedy row compete with their patched values
+  // (lowest index among equal values, as the reference's strict `>`).
+  if (mode == kModeGreedy && npatch > 0 && !bad_patch) {
+    constexpr int HS = 1 << LT_HASH_LOG2;
+    for (int i0 = 0; i0 < HS; i0 += LT_THREADS) {
+      const int i = i0 + tid;
+      const int k = T.key[i];
+      if (k >= 0) {
+        const float x = patched_value(T, i);
+        if (k == 0 && x != x) S.nan0 = 1;
+        if (!(x != x) && (gi == INT_MAX || x > gb || (x == gb && k < gi))) { gb = x; gi = k; }
+      }
+    }
+  }
+
   // ---- per-CTA results -------------------------------------------------
   if (mode == kModeTopK) {
     if (mnan != mnan) atomicExch(&S.nan, 1);
     // Before the merge, keep only this chunk's top K (with all its ties at
     // the K-th key): the row's K-th largest key is at least every chunk's, so
     // nothing at or above it is dropped, and CTA 0 gets ~C*K candidates.
-    if (!overflow && !S.failed && C > 1 && S.ncand > 2 * (int)K) (void)light_compact(S, K);
+    if (!overflow && !S.failed && C > 1 && S.ncand > 4 * (int)K) (void)light_compact(S, K);
     __syncthreads();
     if (tid == 0) {
       if (overflow || bad_patch || (C > 1 && S.ncand > LT_SLOT)) S.overflow = 1;
