@@ -142,6 +142,42 @@ NLS_API nls_status nls_sample_batch_noalloc(const float* logits, int64_t ld, int
                                             const int64_t* bias_off, const double* uniforms,
                                             int64_t* out_ids, float* out_probs, void* stream);
 
+/* ---- vocab-sharded mode ----------------------------------------------------
+ * For logits produced by a tensor-parallel lm_head: each of P ranks (one
+ * process and GPU each) holds the columns [r*Vs, min(vocab, (r+1)*Vs)) of
+ * every row, Vs = ceil(vocab / P). No counterpart in the reference, which
+ * samples one host row (sampler.nim:59); the results equal nls_sample_batch
+ * on the whole rows bit for bit. The exact sequential sums need each row's
+ * whole candidate order, so the call exchanges data rather than partial sums:
+ * an NCCL send/recv transpose gives rank q every column of the rows it owns
+ * (rows [floor(B*q/P), floor(B*(q+1)/P))), rank q samples those rows with the
+ * batch kernels, and an NCCL all-gather returns every row's id (and prob) to
+ * every rank. NCCL is the process's own libnccl.so.2, found at run time. */
+typedef struct nls_comm nls_comm;
+
+/* An NCCL unique id (128 bytes) for nls_comm_create; make it on one rank and
+ * send it to the others out of band. */
+NLS_API nls_status nls_comm_unique_id(uint8_t* out128);
+
+/* Join the communicator of `nranks` ranks as `rank`, on CUDA `device` (the
+ * device of the handle used with it). Collective: every rank calls it. */
+NLS_API nls_status nls_comm_create(nls_comm** out, const uint8_t* id128, int32_t nranks,
+                                   int32_t rank, int32_t device);
+NLS_API void nls_comm_destroy(nls_comm* c);
+
+/* Sample B rows whose vocabulary is split over the communicator's ranks (see
+ * above). Collective and synchronous: every rank calls it with the same rows,
+ * vocab, params, histories, bias and uniforms (replicated; ids are global
+ * token ids) and its own shard `logits` [rows x ld], ld >= its column count.
+ * Every pointer is device memory of the handle's device; out_ids (and
+ * out_probs, optional) receive all B rows on every rank. Returns the first
+ * non-zero status of any rank (NLS_ERR_NCCL for a failed collective). */
+NLS_API nls_status nls_sample_batch_vocab_sharded(
+    nls_handle* h, nls_comm* c, const float* logits, int64_t ld, int32_t rows, int32_t vocab,
+    const nls_row_params* params, const int64_t* hist_ids, const int64_t* hist_off,
+    const int64_t* bias_ids, const double* bias_vals, const int64_t* bias_off,
+    const double* uniforms, int64_t* out_ids, float* out_probs, void* stream);
+
 /* Kernel-side status of the last asynchronous call on this handle: waits for
  * `stream` and returns the first error the kernels recorded (NLS_OK if none). */
 NLS_API nls_status nls_stream_status(nls_handle* h, void* stream);

@@ -11,7 +11,8 @@ name `nimllm_b200`).
 """
 from . import workloads
 from ._abi import EXPORTS, LIB_PATH, NlsError, ROW_PARAMS_DTYPE, load
-from .sampler import (Engine, Rand, Sampler, SamplerParams, accept, argmax, default_engine,
-                      defaultSampling, greedySampling, newSampler, params_record, sample)
+from .sampler import (Comm, Engine, Rand, Sampler, SamplerParams, accept, argmax, comm_unique_id,
+                      default_engine, defaultSampling, greedySampling, newSampler, params_record,
+                      row_owner_range, sample, vocab_shard)
 
 __version__ = "0.1.0"

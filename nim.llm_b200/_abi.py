@@ -31,6 +31,7 @@ EXPORTS = (
     "nls_create", "nls_destroy", "nls_sample_batch", "nls_argmax_batch",
     "nls_stream_status", "nls_status_str", "nls_last_error", "nls_version",
     "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
+    "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
 )
 
 # nls_row_params: 6 doubles + 2 int64, 64 bytes, no padding.
@@ -76,6 +77,15 @@ def load(path: str | None = None):
     L.nls_last_kernel_ms.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i32]
     L.nls_sample_batch_noalloc.restype = i32
     L.nls_sample_batch_noalloc.argtypes = [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+    L.nls_comm_unique_id.restype = i32
+    L.nls_comm_unique_id.argtypes = [vp]
+    L.nls_comm_create.restype = i32
+    L.nls_comm_create.argtypes = [ctypes.POINTER(vp), vp, i32, i32, i32]
+    L.nls_comm_destroy.restype = None
+    L.nls_comm_destroy.argtypes = [vp]
+    L.nls_sample_batch_vocab_sharded.restype = i32
+    L.nls_sample_batch_vocab_sharded.argtypes = [vp, vp, vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp,
+                                                 vp, vp, vp]
     _lib = L
     return L
 

@@ -62,7 +62,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         objs.append(obj)
     tmp = LIB + ".tmp"
     subprocess.run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
-                    "-Xcompiler", "-fPIC", "-o", tmp, *objs, "-cudart", "static"], check=True)
+                    "-Xcompiler", "-fPIC", "-o", tmp, *objs, "-cudart", "static", "-ldl"], check=True)
     os.replace(tmp, LIB)
     return LIB
 

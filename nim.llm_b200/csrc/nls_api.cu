@@ -11,6 +11,7 @@
 #include <new>
 
 #include "nls_kernels.h"
+#include "nls_nccl.h"
 #include "nimllm_sample.h"
 
 struct nls_handle {
@@ -50,7 +51,28 @@ struct nls_handle {
   int profiling = 0;
   int profiled = 0;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // vocab-sharded calls: packed shard, received shards, gathered ids/probs
+  float* d_sh_send = nullptr;
+  size_t sh_send_cap = 0;
+  float* d_sh_recv = nullptr;
+  size_t sh_recv_cap = 0;
+  int64_t* d_sh_mine = nullptr;
+  size_t sh_mine_cap = 0;
+  int64_t* d_sh_all = nullptr;
+  size_t sh_all_cap = 0;
+  float* d_sh_pmine = nullptr;
+  size_t sh_pmine_cap = 0;
+  float* d_sh_pall = nullptr;
+  size_t sh_pall_cap = 0;
+  int64_t* h_sh_status = nullptr;  // pinned, one per rank (up to kMaxRanks)
   char last_err[256] = {0};
+};
+
+struct nls_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0;
+  int rank = 0;
+  int device = 0;
 };
 
 namespace {
@@ -113,6 +135,7 @@ int pick_cluster(const nls_handle* h, int rows, int vocab) {
 }
 
 constexpr int kSmallBatch = 8;
+constexpr int kMaxRanks = 64;
 
 // One batch: the streaming kernel (greedy and top-k <= 256 rows) on the side
 // stream, concurrently with the full-sort kernel, which claims the full-path
@@ -212,6 +235,13 @@ void nls_destroy(nls_handle* h) {
     cudaFree(h->d_scratch);
     if (h->h_status) cudaFreeHost(h->h_status);
     if (h->side) cudaStreamDestroy(h->side);
+    cudaFree(h->d_sh_send);
+    cudaFree(h->d_sh_recv);
+    cudaFree(h->d_sh_mine);
+    cudaFree(h->d_sh_all);
+    cudaFree(h->d_sh_pmine);
+    cudaFree(h->d_sh_pall);
+    if (h->h_sh_status) cudaFreeHost(h->h_sh_status);
     if (h->fork) cudaEventDestroy(h->fork);
     if (h->join) cudaEventDestroy(h->join);
     for (cudaEvent_t e : h->ev)
@@ -433,6 +463,163 @@ nls_status nls_stream_status(nls_handle* h, void* stream) {
   DeviceGuard g(h->device);
   NLS_CUDA(h, cudaStreamSynchronize((cudaStream_t)stream));
   return (nls_status)*h->h_status;
+}
+
+
+nls_status nls_comm_unique_id(uint8_t* out) {
+  if (!out) return NLS_ERR_INVALID_ARG;
+  const nls::NcclApi& n = nls::nccl_api();
+  if (!n.ok) return NLS_ERR_NCCL;
+  ncclUniqueId id;
+  if (n.GetUniqueId(&id) != ncclSuccess) return NLS_ERR_NCCL;
+  memcpy(out, id.internal, NCCL_UNIQUE_ID_BYTES);
+  return NLS_OK;
+}
+
+nls_status nls_comm_create(nls_comm** out, const uint8_t* id, int32_t nranks, int32_t rank,
+                           int32_t device) {
+  if (!out) return NLS_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (!id || nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks) return NLS_ERR_INVALID_ARG;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return NLS_ERR_NO_DEVICE;
+  if (device < 0 || device >= ndev) return NLS_ERR_INVALID_ARG;
+  const nls::NcclApi& n = nls::nccl_api();
+  if (!n.ok) return NLS_ERR_NCCL;
+  DeviceGuard g(device);
+  ncclUniqueId uid;
+  memcpy(uid.internal, id, NCCL_UNIQUE_ID_BYTES);
+  nls_comm* c = new (std::nothrow) nls_comm();
+  if (!c) return NLS_ERR_CAPACITY;
+  if (n.CommInitRank(&c->comm, nranks, uid, rank) != ncclSuccess) {
+    delete c;
+    return NLS_ERR_NCCL;
+  }
+  c->nranks = nranks;
+  c->rank = rank;
+  c->device = device;
+  *out = c;
+  return NLS_OK;
+}
+
+void nls_comm_destroy(nls_comm* c) {
+  if (!c) return;
+  const nls::NcclApi& n = nls::nccl_api();
+  if (n.ok && c->comm) {
+    DeviceGuard g(c->device);
+    n.CommDestroy(c->comm);
+  }
+  delete c;
+}
+
+nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const float* logits,
+                                          int64_t ld, int32_t rows, int32_t vocab,
+                                          const nls_row_params* params, const int64_t* hist_ids,
+                                          const int64_t* hist_off, const int64_t* bias_ids,
+                                          const double* bias_vals, const int64_t* bias_off,
+                                          const double* uniforms, int64_t* out_ids,
+                                          float* out_probs, void* stream) {
+  if (!h || !c) return NLS_ERR_INVALID_ARG;
+  const int P = c->nranks, me = c->rank;
+  if (rows < 0 || vocab < 1) return NLS_ERR_INVALID_ARG;
+  const int Vs = (vocab + P - 1) / P;  // columns per rank (the last may have fewer)
+  auto vq = [&](int q) { const int v = vocab - q * Vs; return v < 0 ? 0 : (v < Vs ? v : Vs); };
+  if (vq(P - 1) < 1) return NLS_ERR_INVALID_ARG;  // every rank holds at least one column
+  const int Vr = vq(me);
+  if (ld < Vr) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !params || !out_ids) return NLS_ERR_INVALID_ARG;
+  if ((hist_ids == nullptr) != (hist_off == nullptr)) return NLS_ERR_INVALID_ARG;
+  if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
+    return NLS_ERR_INVALID_ARG;
+  if (c->device != h->device) return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  const nls::NcclApi& n = nls::nccl_api();
+  if (!n.ok) return NLS_ERR_NCCL;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto r0 = [&](int q) { return (int)((int64_t)rows * q / P); };  // rank q owns rows [r0(q), r0(q+1))
+  const int R0 = r0(me), Bown = r0(me + 1) - R0;
+  const int Bmax = (rows + P - 1) / P;
+  nls_status s;
+  if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)Bown * vocab)) != NLS_OK) return s;
+  if ((s = grow(h, &h->d_sh_recv, &h->sh_recv_cap, (size_t)Bown * vocab)) != NLS_OK) return s;
+  if ((s = grow(h, &h->d_sh_mine, &h->sh_mine_cap, (size_t)Bmax + 1)) != NLS_OK) return s;
+  if ((s = grow(h, &h->d_sh_all, &h->sh_all_cap, (size_t)P * (Bmax + 1))) != NLS_OK) return s;
+  if ((s = grow(h, &h->d_sh_pmine, &h->sh_pmine_cap, (size_t)Bmax)) != NLS_OK) return s;
+  if ((s = grow(h, &h->d_sh_pall, &h->sh_pall_cap, (size_t)P * Bmax)) != NLS_OK) return s;
+  if (!h->h_sh_status) NLS_CUDA(h, cudaMallocHost(&h->h_sh_status, sizeof(int64_t) * kMaxRanks));
+  // 1. transpose: rank q receives every rank's columns of the rows it owns
+  const float* src = logits;
+  if (ld != Vr) {
+    if ((s = grow(h, &h->d_sh_send, &h->sh_send_cap, (size_t)rows * Vr)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_sh_send, (size_t)Vr * sizeof(float), logits,
+                                  (size_t)ld * sizeof(float), (size_t)Vr * sizeof(float), rows,
+                                  cudaMemcpyDeviceToDevice, st));
+    src = h->d_sh_send;
+  }
+  auto ncclok = [&](ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return true;
+    snprintf(h->last_err, sizeof h->last_err, "%s: %s", what, n.GetErrorString(r));
+    return false;
+  };
+  if (!ncclok(n.GroupStart(), "ncclGroupStart")) return NLS_ERR_NCCL;
+  bool ok = true;
+  for (int q = 0; q < P && ok; ++q) {
+    const int nq = r0(q + 1) - r0(q);
+    if (nq > 0)
+      ok = ncclok(n.Send(src + (size_t)r0(q) * Vr, (size_t)nq * Vr, ncclFloat, q, c->comm, st), "ncclSend");
+    if (ok && Bown > 0)
+      ok = ncclok(n.Recv(h->d_sh_recv + (size_t)Bown * q * Vs, (size_t)Bown * vq(q), ncclFloat, q,
+                         c->comm, st), "ncclRecv");
+  }
+  if (!ncclok(n.GroupEnd(), "ncclGroupEnd") || !ok) return NLS_ERR_NCCL;
+  // 2. assemble the owned rows and sample them like any batch
+  if (Bown > 0) {
+    for (int q = 0; q < P; ++q)
+      NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits + (size_t)q * Vs, (size_t)vocab * sizeof(float),
+                                    h->d_sh_recv + (size_t)Bown * q * Vs, (size_t)vq(q) * sizeof(float),
+                                    (size_t)vq(q) * sizeof(float), Bown, cudaMemcpyDeviceToDevice, st));
+    nls::BatchArgs a{};
+    a.logits = h->d_logits;
+    a.ld = vocab;
+    a.rows = Bown;
+    a.V = vocab;
+    a.params = params + R0;
+    a.hist_ids = hist_ids;
+    a.hist_off = hist_off ? hist_off + R0 : nullptr;
+    a.bias_ids = bias_ids;
+    a.bias_vals = bias_vals;
+    a.bias_off = bias_off ? bias_off + R0 : nullptr;
+    a.uniforms = uniforms ? uniforms + R0 : nullptr;
+    a.out_ids = h->d_sh_mine;
+    a.out_probs = out_probs ? h->d_sh_pmine : nullptr;
+    if ((s = run_batch(h, a, NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS, st)) != NLS_OK) return s;
+  }
+  // 3. every rank gets every row's result, and every rank's status
+  NLS_CUDA(h, cudaMemsetAsync(h->d_sh_mine + Bmax, 0, sizeof(int64_t), st));
+  if (Bown > 0) NLS_CUDA(h, cudaMemcpyAsync(h->d_sh_mine + Bmax, h->d_work, sizeof(int), cudaMemcpyDeviceToDevice, st));
+  if (!ncclok(n.AllGather(h->d_sh_mine, h->d_sh_all, (size_t)Bmax + 1, ncclInt64, c->comm, st), "ncclAllGather"))
+    return NLS_ERR_NCCL;
+  if (out_probs &&
+      !ncclok(n.AllGather(h->d_sh_pmine, h->d_sh_pall, (size_t)Bmax, ncclFloat, c->comm, st), "ncclAllGather"))
+    return NLS_ERR_NCCL;
+  for (int q = 0; q < P; ++q) {
+    const int nq = r0(q + 1) - r0(q);
+    if (nq > 0) {
+      NLS_CUDA(h, cudaMemcpyAsync(out_ids + r0(q), h->d_sh_all + (size_t)q * (Bmax + 1), sizeof(int64_t) * nq,
+                                  cudaMemcpyDeviceToDevice, st));
+      if (out_probs)
+        NLS_CUDA(h, cudaMemcpyAsync(out_probs + r0(q), h->d_sh_pall + (size_t)q * Bmax, sizeof(float) * nq,
+                                    cudaMemcpyDeviceToDevice, st));
+    }
+    NLS_CUDA(h, cudaMemcpyAsync(h->h_sh_status + q, h->d_sh_all + (size_t)q * (Bmax + 1) + Bmax,
+                                sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+  }
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  for (int q = 0; q < P; ++q)
+    if (h->h_sh_status[q] != 0) return (nls_status)h->h_sh_status[q];
+  return NLS_OK;
 }
 
 }  // extern "C"

@@ -14,7 +14,7 @@ size_t light_smem_bytes(int C, int chunk);
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream);
 
 // Full-sort kernel over the rows listed in a.full_list (count in a.full_count):
-// `slots` persistent CTAs, each with 3*vpad words of `scratch`.
+// `slots` persistent CTAs, each with 4*vpad words of `scratch`.
 size_t full_smem_bytes(int V);
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
                         cudaStream_t stream);

@@ -177,6 +177,26 @@ class Engine:
             self._check(st, "nls_sample_batch (kernel status)")
         return out_ids, out_probs, st
 
+    def sample_batch_vocab_sharded(self, comm: "Comm", logits_shard, vocab: int, params,
+                                   hist_ids=None, hist_off=None, bias_ids=None, bias_vals=None,
+                                   bias_off=None, uniforms=None, out_ids=None, out_probs=None,
+                                   stream: int = 0):
+        """Vocab-sharded sampling (collective over `comm`): `logits_shard` is
+        this rank's columns [rank*Vs, ...) of every row as a CUDA tensor
+        [B, >= its column count]; every other input is the same on every rank
+        (CUDA tensors, global token ids). out_ids (and out_probs) receive all
+        rows on every rank. Synchronous; raises on any rank's error."""
+        def dp(t):
+            return None if t is None else ctypes.c_void_p(t.data_ptr())
+        B = logits_shard.shape[0]
+        assert logits_shard.stride(1) == 1
+        st = self._lib.nls_sample_batch_vocab_sharded(
+            self._h, comm._c, dp(logits_shard), logits_shard.stride(0), B, int(vocab), dp(params),
+            dp(hist_ids), dp(hist_off), dp(bias_ids), dp(bias_vals), dp(bias_off), dp(uniforms),
+            dp(out_ids), dp(out_probs), ctypes.c_void_p(stream))
+        self._check(st, "nls_sample_batch_vocab_sharded")
+        return out_ids, out_probs
+
     def set_profiling(self, on: bool = True) -> None:
         self._check(self._lib.nls_set_profiling(self._h, 1 if on else 0), "nls_set_profiling")
 
@@ -260,3 +280,55 @@ def argmax(logits, engine: Optional[Engine] = None) -> int:    # sampler.nim:45-
 __all__ = ["SamplerParams", "defaultSampling", "greedySampling", "params_record", "Rand",
            "Engine", "Sampler", "newSampler", "accept", "sample", "argmax", "default_engine",
            "NlsError", "ROW_PARAMS_DTYPE"]
+
+
+# ---------------------------------------------------------------------------
+# Vocab-sharded mode: an NCCL communicator of the C library
+# ---------------------------------------------------------------------------
+def vocab_shard(vocab: int, nranks: int, rank: int) -> tuple[int, int]:
+    """Columns [lo, hi) of rank `rank` when `vocab` is split over `nranks`
+    ranks (Vs = ceil(vocab / nranks) columns each, the last ones fewer)."""
+    vs = -(-vocab // nranks)
+    lo = min(vocab, rank * vs)
+    return lo, min(vocab, lo + vs)
+
+
+def row_owner_range(rows: int, nranks: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) that rank `rank` samples in the vocab-sharded call."""
+    return rows * rank // nranks, rows * (rank + 1) // nranks
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Comm()."""
+    lib = _abi.load()
+    buf = ctypes.create_string_buffer(128)
+    st = lib.nls_comm_unique_id(buf)
+    if st != 0:
+        raise NlsError(st, "nls_comm_unique_id")
+    return buf.raw
+
+
+class Comm:
+    """nls_comm: this rank's place in an NCCL communicator (collective to
+    create). `uid` is comm_unique_id() from one rank, sent to all others."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        self._lib = _abi.load()
+        c = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        st = self._lib.nls_comm_create(ctypes.byref(c), buf, int(nranks), int(rank), int(device))
+        if st != 0:
+            raise NlsError(st, "nls_comm_create")
+        self._c = c
+        self.nranks, self.rank, self.device = nranks, rank, device
+
+    def close(self):
+        if getattr(self, "_c", None):
+            self._lib.nls_comm_destroy(self._c)
+            self._c = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
