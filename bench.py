@@ -221,6 +221,53 @@ def run_reference(args, world, rank, dist):
     return 0
 
 
+def vocab_sharded_bench(pkg, dist, world, rank, local, dev, args):
+    """Config 5 vocab-sharded over the `world` ranks: rows/s of the
+    collective nls_sample_batch_vocab_sharded call (inputs resident)."""
+    import torch
+    name = "c5_full_vocab_nucleus"
+    w = pkg.workloads.make(name, seed=SEED)
+    B, V = w.B, w.V
+    lo, hi = pkg.vocab_shard(V, world, rank)
+    shard = torch.from_numpy(np.ascontiguousarray(w.logits[:, lo:hi])).to(dev)
+    params = torch.from_numpy(w.params.view(np.uint8).copy()).to(dev)
+    unif = torch.from_numpy(w.uniforms).to(dev)
+    ids = torch.empty(B, dtype=torch.int64, device=dev)
+    probs = torch.empty(B, dtype=torch.float32, device=dev)
+    box = [pkg.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    comm = pkg.Comm(box[0], world, rank, local)
+    eng = pkg.Engine(local, max_rows=B, max_vocab=V)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        eng.sample_batch_vocab_sharded(comm, shard, V, params, uniforms=unif, out_ids=ids,
+                                       out_probs=probs, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(args.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ms = reduce_max(dist, statistics.mean(times), dev)
+    eng.close()
+    comm.close()
+    return {"config": f"{name}: B={B} rows of V={V} fp32, top-k 0, top-p 0.99, T 1.0; "
+                      f"the vocabulary split over {world} ranks (columns [r*Vs, (r+1)*Vs))",
+            "value": B / (ms / 1e3), "unit": "rows/s", "ms_per_step": ms,
+            "method": "NCCL send/recv transpose to row owners, batch kernels, all-gather of ids"}
+
+
 def config_dict(world):
     return {"workload": f"{WORKLOAD}: B=256 rows per GPU, V=128256 fp32, per-row T~U[0.5,1.2], "
                         "top-k in {0,20,50,100}, top-p~U[0.8,1], min-p in {0,0.05}, "
@@ -239,6 +286,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-iters", type=int, default=200)
+    ap.add_argument("--no-vocab-sharded", action="store_true",
+                    help="skip the vocab-sharded (config 5) measurement at N > 1")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the device-resident steps (for ncu captures); prints a short line")
     args = ap.parse_args()
@@ -397,6 +446,13 @@ def main():
                          "time of the call (library CUDA events), host_* = wall clock of the call "
                          "through the Python binding with a stream sync"}
 
+    # Vocab-sharded mode (BASELINE config 5 over the N ranks: B = 64 rows of
+    # V = 151936, each rank holding its columns of every row): device time of
+    # one collective call, max over ranks.
+    vsh = None
+    if world > 1 and not args.no_vocab_sharded:
+        vsh = vocab_sharded_bench(pkg, dist, world, rank, local, dev, args)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
@@ -425,6 +481,7 @@ def main():
             "gpu_launches": 3 * args.steps,
             "latency_b1": latency,
             "clocks": clk,
+            "vocab_sharded": vsh,
         }
         print(json.dumps(line), flush=True)
     eng.close()
