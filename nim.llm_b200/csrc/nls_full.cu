@@ -107,6 +107,11 @@ struct FullShared {
   int wbkt[FT_MAXWIN + 1];
   int wstate[FT_MAXWIN];
   int cwin;  // window whose exact t values sit in u.big (as floats), or -1
+  // replay of a sorted window: grid-unit sums of its 32-position groups
+  long long gsum[FT_BIG / 32];
+  int gtie[FT_BIG / 32];
+  long long gS;
+  int gev;
   int counter, patch_overflow, dup, nan;
 };
 
@@ -910,7 +915,6 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           __syncthreads();
         }
       };
-      auto noprep = [](int, int) {};
       auto nostop = [](float) { return false; };
       // One sequential fp32 accumulation over candidate positions [0, j1)
       // whose j-th term is fromt(t_j). Bucketed path: a window whose
@@ -918,6 +922,108 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       // and no stop contributes an order-independent integer sum, so it is
       // summed in bucket order without sorting; any other window (and one
       // cut by j1) is sorted first and replayed in order.
+      // Exact replay of positions [j0, j1) of one sorted window (terms from
+      // shared memory): every warp sums the grid units of 32-position groups,
+      // warp 0 finds the first group where a tie, a binade change or the stop
+      // happens, everything before it is taken at once, and one warp replays
+      // from that group; then again with the new grid.
+      auto window_replay = [&](auto decc, int j0, int j1, float v0, auto elem, auto stop,
+                               bool has_stop, bool absorb) -> ScanResult {
+        constexpr bool DEC = decltype(decc)::value;
+        float v = v0;
+        int j = j0;
+        while (j < j1) {
+          const int E = binade_exp(v);
+          const int ue = E - 23;
+          if (!DEC && absorb && (double)elem(j) < ldexp(1.0, ue - 1)) break;
+          long long S0 = (long long)ldexp((double)v, -ue);
+          if (DEC) S0 = -S0;
+          const int ng = (j1 - j + 31) >> 5;  // <= FT_BIG / 32
+          for (int g = warp; g < ng; g += FT_WARPS) {
+            const int jj = j + 32 * g + lane;
+            long long u = 0;
+            bool tie = false;
+            if (jj < j1) u = grid_units(elem(jj), ue, &tie);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+            const unsigned tb = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) {
+              S.gsum[g] = u;
+              S.gtie[g] = tb != 0u;
+            }
+          }
+          __syncthreads();
+          if (warp == 0) {
+            const int per = (ng + 31) >> 5;  // groups per lane, <= 8
+            long long loc = 0;
+            for (int r = 0; r < per; ++r) {
+              const int g = lane * per + r;
+              if (g < ng) loc += S.gsum[g];
+            }
+            long long incl = loc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            long long run = S0 + incl - loc;  // value before this lane's first group
+            int ev = INT_MAX;
+            long long sb = 0;
+            for (int r = 0; r < per; ++r) {
+              const int g = lane * per + r;
+              if (g >= ng) break;
+              const long long after = run + S.gsum[g];
+              bool e = S.gtie[g] != 0;
+              if (!e) {
+                if (!DEC) e = after >= (1LL << 24);
+                else e = (E == -126) ? (after >= 0) : (after >= -(1LL << 23));
+              }
+              if (!e && has_stop) e = stop(grid_value(DEC ? -after : after, ue));
+              if (e) {
+                ev = g;
+                sb = run;
+                break;
+              }
+              run = after;
+            }
+            const unsigned eb = __ballot_sync(0xffffffffu, ev != INT_MAX);
+            const long long total = __shfl_sync(0xffffffffu, incl, 31);
+            int gev = -1;
+            long long gS = S0 + total;
+            if (eb) {
+              const int L = __ffs(eb) - 1;
+              gev = __shfl_sync(0xffffffffu, ev, L);
+              gS = __shfl_sync(0xffffffffu, sb, L);
+            }
+            if (lane == 0) {
+              S.gev = gev;
+              S.gS = gS;
+            }
+          }
+          __syncthreads();
+          const int gev = S.gev;
+          const long long gS = S.gS;
+          __syncthreads();
+          v = grid_value(DEC ? -gS : gS, ue);
+          if (gev < 0) break;  // no event: the whole rest in one step
+          j += 32 * gev;
+          if (warp == 0) {
+            const WalkResult w = warp_walk<DEC>(j, j1, v, elem, stop, has_stop, 8);
+            if (lane == 0) {
+              S.scan.v = w.v;
+              S.scan.walk_j = w.j;
+              S.scan.walk_stop = w.stop_j;
+            }
+          }
+          __syncthreads();
+          v = S.scan.v;
+          j = S.scan.walk_j;
+          const int wstop = S.scan.walk_stop;
+          __syncthreads();
+          if (wstop >= 0) return ScanResult{v, wstop};
+        }
+        return ScanResult{v, -1};
+      };
       auto run_scan = [&](auto decc, int j1, float v0, auto fromt, auto stop, bool has_stop,
                           bool absorb) -> ScanResult {
         constexpr bool DEC = decltype(decc)::value;
@@ -1040,8 +1146,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           if (S.wstate[c] != 2) sort_window(c);
           else cache_window(c);
           auto elemc = [&](int j) { return fromt.exact(tcache[j - ws]); };
-          const ScanResult r = exact_scan_fast<FT_THREADS, FT_EPT, DEC>(
-              ws, we, v, elemc, stop, has_stop, absorb, S.scan, S.fscan, noprep);
+          const ScanResult r = window_replay(decc, ws, we, v, elemc, stop, has_stop, absorb);
           if (r.stop_j >= 0) return r;
           v = r.v;
           if (!DEC && absorb && (double)elemc(we - 1) < ldexp(1.0, binade_exp(v) - 24))
