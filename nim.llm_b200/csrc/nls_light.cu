@@ -27,6 +27,7 @@
 #include <cooperative_groups.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "nls_common.cuh"
 #include "nls_kernels.h"
@@ -313,12 +314,14 @@ light_kernel(BatchArgs a, int C, int chunk) {
         m = max(m, max(m_floor, 16));
         m = min(m, n0);
         constexpr int NW = LT_THREADS / 32;
-        if (m <= NW * 32) {
+        const int r = (2 * m + NW - 1) / NW;  // per-warp rank; j = ceil(m / r) <= NW / 2 + 1
+        if (r <= 32) {
           // Each warp sorts its 32 thread maxima (register bitonic network)
-          // and takes the r-th largest, r = ceil(m / NW); the minimum of
-          // those over the warps has at least NW * r >= m elements of the
-          // stage at or above it, so it is a lower bound of the stage's m-th
-          // largest key.
+          // and publishes its r-th largest; the j-th largest of those, with
+          // j = ceil(m / r), has at least j * r >= m elements of the stage at
+          // or above it, so it is a lower bound of the stage's m-th largest
+          // key.
+          const int jsel = (m + r - 1) / r;
           uint32_t v = 0u;  // 0 sorts last: a thread without keys bounds nothing
           for (int i = tid; i < n0; i += LT_THREADS) {
             uint32_t k;
@@ -334,13 +337,22 @@ light_kernel(BatchArgs a, int C, int chunk) {
               v = (desc_block == lower) ? (v > o ? v : o) : (v < o ? v : o);
             }
           }
-          const int r = (m + NW - 1) / NW;
           const uint32_t wr = __shfl_sync(0xffffffffu, v, r - 1);
           if (lane == 0) S.cand_key[warp] = wr;
           __syncthreads();
-          uint32_t tm = 0xffffffffu;
+          // the jsel-th largest of the NW published values (ties counted)
+          uint32_t tm = 0u;
 #pragma unroll
-          for (int w = 0; w < NW; ++w) tm = min(tm, S.cand_key[w]);
+          for (int w = 0; w < NW; ++w) {
+            const uint32_t x = S.cand_key[w];
+            int above = 0, ge = 0;
+#pragma unroll
+            for (int w2 = 0; w2 < NW; ++w2) {
+              above += S.cand_key[w2] > x;
+              ge += S.cand_key[w2] >= x;
+            }
+            if (above < jsel && ge >= jsel) tm = x;
+          }
           thr = tm;
           __syncthreads();
         } else {
@@ -385,68 +397,74 @@ light_kernel(BatchArgs a, int C, int chunk) {
     if (mode == kModeTopK && sbase < nvec) {
       // top-k: per element one multiply, one compare and one NaN-propagating
       // max; the passing elements of the stage are appended with one warp
-      // scan and one atomic. Groups past the ring (last stage only) hold
-      // -inf and are masked out: with an accept-all threshold (-inf) they
-      // would otherwise pass.
-      float4 q[LT_GROUPS];
+      // scan and one atomic. In the last stage, groups past the ring hold
+      // -inf and are masked out (with an accept-all threshold, -inf, they
+      // would otherwise pass); whole stages are compiled without the masks.
       const int ngv = min(nvec - sbase, LT_STAGE) >> 2;
-#pragma unroll
-      for (int j = 0; j < LT_GROUPS; ++j) {
-        const int g = tid + j * LT_THREADS;
-        q[j] = (g < ngv) ? reinterpret_cast<const float4*>(S.ring[buf])[g]
-                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      }
-      float y[LT_GROUPS][4];
-      float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
-      int cnt = 0;
-#pragma unroll
-      for (int j = 0; j < LT_GROUPS; ++j) {
-        const int off = sbase + 4 * (tid + j * LT_THREADS);
-        const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
-        (void)off;
-        const bool gv = (tid + j * LT_THREADS) < ngv;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          y[j][e] = __fmul_rn(x[e], invT);
-          cnt += (gv && y[j][e] >= thrf) ? 1 : 0;
-        }
-        m0 = fmax_nan(m0, y[j][0]);
-        m1 = fmax_nan(m1, y[j][1]);
-        m2 = fmax_nan(m2, y[j][2]);
-        m3 = fmax_nan(m3, y[j][3]);
-      }
-      mnan = fmax_nan(mnan, fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3)));
-      if (__any_sync(0xffffffffu, cnt > 0)) {
-        int incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += v;
-        }
-        int base = 0;
-        if (lane == 31) base = atomicAdd(&S.ncand, incl);
-        base = __shfl_sync(0xffffffffu, base, 31);
-        const int end = base + __shfl_sync(0xffffffffu, incl, 31);
-        my_max = end > my_max ? end : my_max;
-        int pos = base + incl - cnt;
+      auto topk_stage = [&](auto partial_c) {
+        constexpr bool PARTIAL = decltype(partial_c)::value;
+        float4 q[LT_GROUPS];
 #pragma unroll
         for (int j = 0; j < LT_GROUPS; ++j) {
-          const bool gv = (tid + j * LT_THREADS) < ngv;
+          const int g = tid + j * LT_THREADS;
+          if (PARTIAL)
+            q[j] = (g < ngv) ? reinterpret_cast<const float4*>(S.ring[buf])[g]
+                             : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          else
+            q[j] = reinterpret_cast<const float4*>(S.ring[buf])[g];
+        }
+        float y[LT_GROUPS][4];
+        float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
+        int cnt = 0;
+#pragma unroll
+        for (int j = 0; j < LT_GROUPS; ++j) {
+          const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+          const bool gv = !PARTIAL || (tid + j * LT_THREADS) < ngv;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            if (gv && y[j][e] >= thrf) {
-              const int off = sbase + 4 * (tid + j * LT_THREADS) + e;
-              // a patched position rejoins later with its patched value
-              const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
-              if (pos < LT_CAP) {
-                S.cand_key[pos] = patched ? 0u : fkey(y[j][e]);
-                S.cand_idx[pos] = patched ? -1 : lo + off;
+            y[j][e] = __fmul_rn(x[e], invT);
+            cnt += (gv && y[j][e] >= thrf) ? 1 : 0;
+          }
+          m0 = fmax_nan(m0, y[j][0]);
+          m1 = fmax_nan(m1, y[j][1]);
+          m2 = fmax_nan(m2, y[j][2]);
+          m3 = fmax_nan(m3, y[j][3]);
+        }
+        mnan = fmax_nan(mnan, fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3)));
+        if (__any_sync(0xffffffffu, cnt > 0)) {
+          int incl = cnt;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+          }
+          int base = 0;
+          if (lane == 31) base = atomicAdd(&S.ncand, incl);
+          base = __shfl_sync(0xffffffffu, base, 31);
+          const int end = base + __shfl_sync(0xffffffffu, incl, 31);
+          my_max = end > my_max ? end : my_max;
+          int pos = base + incl - cnt;
+#pragma unroll
+          for (int j = 0; j < LT_GROUPS; ++j) {
+            const bool gv = !PARTIAL || (tid + j * LT_THREADS) < ngv;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (gv && y[j][e] >= thrf) {
+                const int off = sbase + 4 * (tid + j * LT_THREADS) + e;
+                // a patched position rejoins later with its patched value
+                const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
+                if (pos < LT_CAP) {
+                  S.cand_key[pos] = patched ? 0u : fkey(y[j][e]);
+                  S.cand_idx[pos] = patched ? -1 : lo + off;
+                }
+                ++pos;
               }
-              ++pos;
             }
           }
         }
-      }
+      };
+      if (ngv == LT_STAGE / 4) topk_stage(std::false_type{});
+      else topk_stage(std::true_type{});
     }
     if (sbase < nvec && nvec < len && nvec < sbase + LT_STAGE) {
       // the chunk's last 1-3 elements (past the whole float4 groups) are not
@@ -737,8 +755,9 @@ light_kernel(BatchArgs a, int C, int chunk) {
   uint32_t t, tau = 0xffffffffu, rho = 0u;
   int n64 = 32;
   while (n64 < (int)K) n64 <<= 1;
-  if (nm <= 1024) {
-    // few candidates: one warp selects and sorts, no block barriers
+  if (nm <= 384) {
+    // few candidates: one warp selects and sorts, no block barriers (with
+    // more, the block's radix passes are faster)
     if (warp != 0) return;
     int nge, ngt;
     t = warp_select_kth_largest(
