@@ -123,6 +123,18 @@ NLS_API nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t 
 NLS_API nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
                             int32_t vocab, int64_t* out_ids, uint32_t flags, void* stream);
 
+/* topTokens (sampler.nim:123-130) per row: the n most probable tokens of the
+ * softmax over the whole row (its fp32 sum taken in index order, as
+ * softmaxInPlace does, sampler.nim:51-57), ordered by probability descending,
+ * equal probabilities by ascending index. No penalties, bias or temperature
+ * (the reference applies none). out_ids/out_probs are [rows x n]; entries
+ * past min(n, vocab) get id -1 and probability 0. 1 <= n <= 256. A row with a
+ * NaN or a non-finite maximum gets ids -1 and NLS_ERR_NAN_LOGITS (the
+ * reference's probabilities are NaN there). Flags as nls_sample_batch. */
+NLS_API nls_status nls_top_tokens(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                                  int32_t vocab, int32_t n, int64_t* out_ids, float* out_probs,
+                                  uint32_t flags, void* stream);
+
 /* Allocation-free sampling. No counterpart in the reference: it exists for
  * callers that cannot allocate GPU memory -- code running while a CUDA graph
  * is captured, allocator-less hosts, serving loops that must not touch the

@@ -434,6 +434,49 @@ nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int3
   return (nls_status)*h->h_status;
 }
 
+nls_status nls_top_tokens(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                          int32_t vocab, int32_t n, int64_t* out_ids, float* out_probs,
+                          uint32_t flags, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0 || vocab < 1 || ld < vocab || n < 1 || n > 256) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !out_ids) return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  nls_status s;
+  const float* dl = logits;
+  int64_t dld = ld;
+  if (!(flags & NLS_DEVICE_INPUTS)) {
+    if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
+                                  (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
+                                  cudaMemcpyHostToDevice, st));
+    dl = h->d_logits;
+    dld = vocab;
+  }
+  const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
+  int64_t* oid = out_ids;
+  float* opr = out_probs;
+  if (!dev_out) {
+    if ((s = grow(h, &h->d_sh_mine, &h->sh_mine_cap, (size_t)rows * n)) != NLS_OK) return s;
+    if ((s = grow(h, &h->d_sh_pmine, &h->sh_pmine_cap, (size_t)rows * n)) != NLS_OK) return s;
+    oid = h->d_sh_mine;
+    opr = out_probs ? h->d_sh_pmine : nullptr;
+  }
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
+  NLS_CUDA(h, nls::launch_top(dl, dld, rows, vocab, n, oid, opr, h->d_work, h->d_scratch, h->vpad,
+                              h->slots, st));
+  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(out_ids, oid, sizeof(int64_t) * rows * n, cudaMemcpyDeviceToHost, st));
+  if (out_probs)
+    NLS_CUDA(h, cudaMemcpyAsync(out_probs, opr, sizeof(float) * rows * n, cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  return (nls_status)*h->h_status;
+}
+
 nls_status nls_set_profiling(nls_handle* h, int32_t on) {
   if (!h) return NLS_ERR_INVALID_ARG;
   DeviceGuard g(h->device);

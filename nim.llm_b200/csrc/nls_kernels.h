@@ -19,4 +19,10 @@ size_t full_smem_bytes(int V);
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
                         cudaStream_t stream);
 
+// topTokens: one CTA per row (up to `slots`), scratch slots as launch_full.
+size_t top_smem_bytes();
+cudaError_t launch_top(const float* logits, int64_t ld, int rows, int V, int n, int64_t* out_ids,
+                       float* out_probs, int* status, uint32_t* scratch, int vpad, int slots,
+                       cudaStream_t stream);
+
 }  // namespace nls

@@ -208,6 +208,20 @@ class Engine:
         self._check(self._lib.nls_last_kernel_ms(self._h, out, 3), "nls_last_kernel_ms")
         return float(out[0]), float(out[1]), float(out[2])
 
+    def top_tokens(self, logits, n: int = 5):
+        """topTokens per row (host numpy [B, V] or [V]): returns (ids int64
+        [B, n], probs float32 [B, n]); entries past min(n, V) are -1 / 0."""
+        logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        if logits.ndim == 1:
+            logits = logits[None, :]
+        B, V = logits.shape
+        ids = np.empty((B, n), dtype=np.int64)
+        probs = np.empty((B, n), dtype=np.float32)
+        st = self._lib.nls_top_tokens(self._h, _host_ptr(logits), V, B, V, int(n), _host_ptr(ids),
+                                      _host_ptr(probs), 0, ctypes.c_void_p(0))
+        self._check(st, "nls_top_tokens")
+        return ids, probs
+
     def argmax_batch(self, logits) -> np.ndarray:
         logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
         if logits.ndim == 1:
@@ -277,9 +291,19 @@ def argmax(logits, engine: Optional[Engine] = None) -> int:    # sampler.nim:45-
     return int(eng.argmax_batch(logits)[0])
 
 
+def topTokens(logits, n: int = 5, engine: Optional[Engine] = None) -> list:  # sampler.nim:123-130
+    """The `n` most probable tokens of one row as [(id, prob)], like the Nim
+    proc (min(n, V) entries)."""
+    eng = engine or default_engine()
+    x = np.asarray(logits, dtype=np.float32).reshape(-1)
+    ids, probs = eng.top_tokens(x, n)
+    m = min(n, x.size)
+    return [(int(ids[0, i]), float(probs[0, i])) for i in range(m)]
+
+
 __all__ = ["SamplerParams", "defaultSampling", "greedySampling", "params_record", "Rand",
-           "Engine", "Sampler", "newSampler", "accept", "sample", "argmax", "default_engine",
-           "NlsError", "ROW_PARAMS_DTYPE"]
+           "Engine", "Sampler", "newSampler", "accept", "sample", "argmax", "topTokens",
+           "default_engine", "NlsError", "ROW_PARAMS_DTYPE"]
 
 
 # ---------------------------------------------------------------------------
