@@ -932,18 +932,23 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         constexpr bool DEC = decltype(decc)::value;
         float v = v0;
         int j = j0;
+        // positions summed per pass: small right after an event (binade
+        // changes near a sum's start come 1, 2, 4, ... positions apart),
+        // doubling while passes find none
+        int span = 32 * FT_WARPS;
         while (j < j1) {
           const int E = binade_exp(v);
           const int ue = E - 23;
           if (!DEC && absorb && (double)elem(j) < ldexp(1.0, ue - 1)) break;
           long long S0 = (long long)ldexp((double)v, -ue);
           if (DEC) S0 = -S0;
-          const int ng = (j1 - j + 31) >> 5;  // <= FT_BIG / 32
+          const int jend = (j1 - j > span) ? j + span : j1;
+          const int ng = (jend - j + 31) >> 5;  // <= FT_BIG / 32
           for (int g = warp; g < ng; g += FT_WARPS) {
             const int jj = j + 32 * g + lane;
             long long u = 0;
             bool tie = false;
-            if (jj < j1) u = grid_units(elem(jj), ue, &tie);
+            if (jj < jend) u = grid_units(elem(jj), ue, &tie);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
             const unsigned tb = __ballot_sync(0xffffffffu, tie);
@@ -1005,7 +1010,12 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const long long gS = S.gS;
           __syncthreads();
           v = grid_value(DEC ? -gS : gS, ue);
-          if (gev < 0) break;  // no event: the whole rest in one step
+          if (gev < 0) {  // no event in the span: taken in one step
+            j = jend;
+            span = (span < FT_BIG) ? span * 2 : span;
+            continue;
+          }
+          span = 32 * FT_WARPS;
           j += 32 * gev;
           if (warp == 0) {
             const WalkResult w = warp_walk<DEC>(j, j1, v, elem, stop, has_stop, 8);
