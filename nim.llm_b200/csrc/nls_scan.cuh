@@ -187,23 +187,40 @@ __device__ WalkResult warp_walk(int j, int j1, float v, Elem elem, Stop stop, bo
     const float a = in ? elem(jj) : 0.0f;
     bool tie = false;
     const long long k = in ? grid_units(a, ue, &tie) : 0;
-    const Fn f = in ? Fn{k, 0, tie ? 1 : 0} : fn_identity();
-    Fn incl = f;
+    long long Sb, Sn;
+    if (!__any_sync(0xffffffffu, tie)) {
+      // no tie: every step adds its units, so a plain prefix sum. Units are
+      // clamped to 2^25 + 1 for 32-bit arithmetic: an element that large
+      // leaves the binade by itself, so every element before the first
+      // trigger is unclamped and the value before the trigger is exact.
+      const int kc = (int)(k < (1LL << 25) ? k : (1LL << 25) + 1);
+      int incl = kc;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      Fn o;
-      o.a = __shfl_up_sync(0xffffffffu, incl.a, off);
-      o.b = __shfl_up_sync(0xffffffffu, incl.b, off);
-      o.isB = __shfl_up_sync(0xffffffffu, incl.isB, off);
-      if (lane >= off) incl = fn_compose(o, incl);
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      Sb = S0 + (long long)(incl - kc);
+      Sn = Sb + kc;
+    } else {
+      const Fn f = in ? Fn{k, 0, tie ? 1 : 0} : fn_identity();
+      Fn incl = f;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        Fn o;
+        o.a = __shfl_up_sync(0xffffffffu, incl.a, off);
+        o.b = __shfl_up_sync(0xffffffffu, incl.b, off);
+        o.isB = __shfl_up_sync(0xffffffffu, incl.isB, off);
+        if (lane >= off) incl = fn_compose(o, incl);
+      }
+      Fn excl;
+      excl.a = __shfl_up_sync(0xffffffffu, incl.a, 1);
+      excl.b = __shfl_up_sync(0xffffffffu, incl.b, 1);
+      excl.isB = __shfl_up_sync(0xffffffffu, incl.isB, 1);
+      if (lane == 0) excl = fn_identity();
+      Sb = fn_apply(excl, S0);  // before element jj
+      Sn = fn_apply(f, Sb);     // after it
     }
-    Fn excl;
-    excl.a = __shfl_up_sync(0xffffffffu, incl.a, 1);
-    excl.b = __shfl_up_sync(0xffffffffu, incl.b, 1);
-    excl.isB = __shfl_up_sync(0xffffffffu, incl.isB, 1);
-    if (lane == 0) excl = fn_identity();
-    const long long Sb = fn_apply(excl, S0);  // before element jj
-    const long long Sn = fn_apply(f, Sb);     // after it
     bool t = false;
     if (in) {
       if (!DEC) t = (Sn >= (1LL << 24));
