@@ -166,10 +166,12 @@ nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, 
   } else if (a.rows <= kSmallBatch) {
     // a few rows: the streaming kernel hands full-path rows to one
     // full-sort launch after it (two launches, no fork/join)
+    // (no event between the two: the full-sort launch is the streaming
+    // kernel's programmatic dependent; profiling reports the pair's time)
     NLS_CUDA(h, nls::launch_light(a, C, chunk, st));
-    if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
-    NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st));
+    NLS_CUDA(h, nls::launch_full(a, h->d_scratch, h->vpad, h->slots, st, true));
     if (prof) {
+      NLS_CUDA(h, cudaEventRecord(h->ev[1], st));
       NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
       NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
     }

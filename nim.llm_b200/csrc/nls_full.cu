@@ -451,6 +451,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   uint32_t* LA = KY + vpad;
   uint32_t* LB = KY + 2 * (size_t)vpad;
   const bool claim = (a.row_claim != nullptr);
+  // Launched as a programmatic dependent of the streaming kernel (small
+  // batches): wait until that grid has finished and its writes (the hand-back
+  // list) are visible. Without such a launch this returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int nwork = claim ? 0 : *a.full_count;
   int w = blockIdx.x;
 
@@ -1327,13 +1331,26 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 static std::atomic<int> g_full_smem_set[kMaxDevicesAttr];
 
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool after_light) {
   const size_t smem = full_smem_bytes(a.V);
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(full_kernel), (int)smem, g_full_smem_set);
   if (e != cudaSuccess) return e;
   const int grid = (a.rows < slots) ? a.rows : slots;  // a CTA takes at most one row at a time
-  full_kernel<<<grid, FT_THREADS, smem, stream>>>(a, scratch, vpad);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(FT_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (after_light) {
+    // may start before the streaming kernel ends (its launch latency hides
+    // behind that kernel); griddepcontrol.wait orders the reads
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, full_kernel, a, scratch, vpad);
 }
 
 }  // namespace nls

@@ -16,8 +16,10 @@ cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stre
 // Full-sort kernel over the rows listed in a.full_list (count in a.full_count):
 // `slots` persistent CTAs, each with 4*vpad words of `scratch`.
 size_t full_smem_bytes(int V);
+// after_light: launched right behind the streaming kernel on the same
+// stream as its programmatic dependent (it waits for that grid in-kernel).
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool after_light = false);
 
 // topTokens: one CTA per row (up to `slots`), scratch slots as launch_full.
 size_t top_smem_bytes();

@@ -152,6 +152,9 @@ __device__ int light_compact(LightShared& S, uint32_t K) {
 
 __global__ void __launch_bounds__(LT_THREADS, 2)
 light_kernel(BatchArgs a, int C, int chunk) {
+  // a full-sort launch that depends on this grid may be scheduled now; it
+  // waits (griddepcontrol.wait) for this grid's completion before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   LightShared& S = *reinterpret_cast<LightShared*>(smem_raw);
   const size_t base_bytes = (sizeof(LightShared) + 15) & ~(size_t)15;
@@ -323,9 +326,24 @@ light_kernel(BatchArgs a, int C, int chunk) {
           // key.
           const int jsel = (m + r - 1) / r;
           uint32_t v = 0u;  // 0 sorts last: a thread without keys bounds nothing
-          for (int i = tid; i < n0; i += LT_THREADS) {
-            uint32_t k;
-            if (key0(i, &k)) v = k > v ? k : v;
+          if (n0 == LT_STAGE && nvec >= LT_STAGE) {
+            // a whole first stage in the ring: float4 reads
+#pragma unroll
+            for (int j = 0; j < LT_GROUPS; ++j) {
+              const float4 q = reinterpret_cast<const float4*>(S.ring[0])[tid + j * LT_THREADS];
+              const float xs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float y = __fmul_rn(xs[e], invT);
+                const uint32_t k = fkey(y);
+                v = (y == y && k > v) ? k : v;
+              }
+            }
+          } else {
+            for (int i = tid; i < n0; i += LT_THREADS) {
+              uint32_t k;
+              if (key0(i, &k)) v = k > v ? k : v;
+            }
           }
 #pragma unroll
           for (int kk = 2; kk <= 32; kk <<= 1) {
