@@ -94,17 +94,13 @@ __device__ __forceinline__ float key_threshold_float(uint32_t k) {
 // the double-precision exponential rounded once to float.
 __device__ __forceinline__ float ref_expf(float x) { return __double2float_rn(exp((double)x)); }
 
-// Cheap estimate of ref_expf(x): the __expf intrinsic, documented at
-// 2 + floor(|1.173 x|) ulp. For x in [-110, 0] with __expf(x) >= 2^-120 that
-// is within 2^-16 relative of e^x, so ref_expf(x) lies within
-// kBracketRel = 2^-14 of it (a 4x margin, checked on the GPU for every float
-// in [-110, 0]). Below 2^-120 the estimate is not used.
+// Estimate of ref_expf(x): expf, documented at 2 ulp, is within
+// kBracketRel = 2^-20 relative of ref_expf(x) where expf(x) >= 2^-120
+// (checked on the GPU for every float in [-110, 0]). Below 2^-120 the
+// estimate is not used.
 constexpr float kBracketMin = 0x1p-120f;
-constexpr float kBracketRel = 0x1p-14f;
-__device__ __forceinline__ float texp_estimate(float x) { return __expf(x); }
-// A closer one: expf (documented at 2 ulp) is within 2^-20 relative of
-// ref_expf(x) where expf(x) >= 2^-120 (checked on the GPU the same way).
-__device__ __forceinline__ float texp_estimate2(float x) { return expf(x); }
+constexpr float kBracketRel = 0x1p-20f;
+__device__ __forceinline__ float texp_estimate(float x) { return expf(x); }
 
 // Row classification (sampler.nim:77-78, 85-86).
 __device__ __forceinline__ int row_mode(const nls_row_params& p, int V, int64_t* k_out) {

@@ -419,19 +419,16 @@ struct Bucketer {
 // p = t / s. exact() is the reference's arithmetic; lo()/hi() map a lower /
 // upper bound of t to a lower / upper bound of the term (monotone).
 // mid(a) for a = texp_estimate(x) estimates the exact term (from
-// t = ref_expf(x)) to a relative error: TermT within kBracketRel = 2^-14;
+// t = ref_expf(x)) to a relative error: TermT within kBracketRel = 2^-20;
 // TermP adds the roundings of 1/s, of the product and of the reference's
-// quotient, within 1.01 * 2^-14. `margin` is at least twice that; `margin2`
-// is the same for texp_estimate2 (2^-20, TermP 1.2 * 2^-20).
+// quotient, within 1.2 * 2^-20. `margin` is at least twice that.
 struct TermT {
-  static constexpr float margin = 0x1p-13f;   // for texp_estimate
-  static constexpr float margin2 = 0x1p-19f;  // for texp_estimate2
+  static constexpr float margin = 0x1p-19f;
   __device__ float exact(float t) const { return t; }
   __device__ float mid(float a) const { return a; }
 };
 struct TermP {
-  static constexpr float margin = 0x1p-12f;
-  static constexpr float margin2 = 0x1p-18f;
+  static constexpr float margin = 0x1p-18f;
   float s, rinv;  // rinv = 1/s rounded to nearest
   __device__ float exact(float t) const { return __fdiv_rn(t, s); }
   __device__ float mid(float a) const { return __fmul_rn(a, rinv); }
@@ -1046,8 +1043,13 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           return exact_scan_fast<FT_THREADS, FT_EPT, DEC>(0, j1, v0, elem, stop, has_stop, absorb,
                                                           S.scan, S.fscan, prep);
         float v = v0;
-        constexpr int WPT = FT_BIG / FT_THREADS;  // a window has < FT_BIG elements
+        constexpr int WPT = FT_BIG / FT_THREADS;  // a pass covers at most FT_BIG positions
         const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
+        // The last window the order-independent pass settled: its grid, grid
+        // units and size predict whether the next two windows fit one pass.
+        int last_ue = INT_MIN, last_n = 1;
+        long long last_units = 0;
+        int alone = -1;  // a window whose two-window pass failed: taken alone
         for (int c = 0; c < nwin; ++c) {
           const int ws = S.wstart[c];
           if (ws >= j1) break;
@@ -1063,29 +1065,45 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             const int ue = E - 23;
             long long S0 = (long long)ldexp((double)v, -ue);
             if (DEC) S0 = -S0;
+            // Windows c and c+1 in one pass when the last settled window, on
+            // this grid, predicts (terms do not grow along the sorted order)
+            // that the running value stays inside its binade and short of the
+            // stop over both. A wrong guess costs one pass: window c is then
+            // taken alone. Either way the checks below decide.
+            int wend = we;
+            if (c != alone && last_ue == ue && c + 1 < nwin && S.wstate[c + 1] != 2) {
+              const int we2 = S.wstart[c + 2];
+              if (we2 > we && we2 <= j1 && we2 - ws <= FT_BIG) {
+                const double pred = 1.25 * (double)last_units * (double)(we2 - ws) / (double)last_n;
+                const double sp = (double)S0 + pred;
+                bool two = !DEC ? sp < 0x1p24 : (E != -126 && sp < -0x1p23);
+                if (two && has_stop) two = !stop(grid_value(DEC ? -(long long)sp : (long long)sp, ue));
+                if (two) wend = we2;
+              }
+            }
             // grid 2^ue as a float scale (when representable)
             const bool scale_ok = (ue >= -120 && ue <= 126);  // terms near a grid step stay normal
             const float gscale = scale_ok ? __int_as_float((127 - ue) << 23) : 0.0f;
-            const int rounds = (we - ws + FT_THREADS - 1) / FT_THREADS;  // same in every thread
-            uint32_t raw[WPT];  // all loads first: one memory latency per window
+            const int rounds = (wend - ws + FT_THREADS - 1) / FT_THREADS;  // same in every thread
+            uint32_t raw[WPT];  // all loads first: one memory latency per pass
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
               const int j = ws + tid + r * FT_THREADS;
-              raw[r] = (j < we) ? SKw[2 * j + 1] : 0u;
+              raw[r] = (j < wend) ? SKw[2 * j + 1] : 0u;
             }
             long long sum = 0;
-            float sumf = 0.0f;  // settled units, each < 2^12: exact in fp32
+            float sumf = 0.0f;  // settled units, each < 2^18: at most 2^21, exact in fp32
             bool tie = false;
             float amax = 0.0f;
             unsigned pending = 0u;  // elements the estimate does not settle
             // q = term / grid; the exact term lies within q * margin / 2 of q,
             // so if no half-integer is that close, rne(q) is its grid value
             // and it is no tie. Straight-line code: the unrolled elements
-            // overlap; the rare unsettled ones are redone below.
+            // overlap; the rare unsettled ones are redone exactly below.
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
               if (r >= rounds) break;
-              const bool valid = ws + tid + r * FT_THREADS < we;
+              const bool valid = ws + tid + r * FT_THREADS < wend;
               const float x = __fsub_rn(desc_key_value(raw[r]), mx);
               const float a = texp_estimate(x);
               const float emid = fromt.mid(a);
@@ -1101,27 +1119,11 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             for (int r = 0; r < WPT; ++r) {
               if (!(pending & (1u << r))) continue;
               const float x = __fsub_rn(desc_key_value(raw[r]), mx);
-              const float a2 = texp_estimate2(x);
-              bool settled = false;
-              float emid = 0.0f;
-              if (a2 >= kBracketMin && scale_ok) {
-                emid = fromt.mid(a2);
-                const float q = __fmul_rn(emid, gscale);
-                const float k = rintf(q);
-                const float f = fabsf(__fsub_rn(q, k));
-                if (__fsub_rn(0.5f, f) > __fmul_rn(q, fromt.margin2)) {
-                  sumf = __fadd_rn(sumf, k);
-                  settled = true;
-                }
-              }
-              if (!settled) {
-                const float e = fromt.exact(ref_expf(x));
-                bool tj;
-                sum += grid_units(e, ue, &tj);
-                tie |= tj;
-                emid = e;
-              }
-              amax = fmaxf(amax, emid);
+              const float e = fromt.exact(ref_expf(x));
+              bool tj;
+              sum += grid_units(e, ue, &tj);
+              tie |= tj;
+              amax = fmaxf(amax, e);
             }
             sum += (long long)sumf;
 #pragma unroll
@@ -1141,8 +1143,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
               wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
             }
             __syncthreads();
-            // every later term is at most this window's largest
-            // (wmax estimates the largest term within 1.01 * 2^-14; 2^-12 covers it)
+            // every later term is at most this pass's largest
+            // (wmax estimates the largest term within 2^-18; 2^-12 covers it)
             if (!DEC && absorb && (double)wmax * (1.0 + 0x1p-12) < ldexp(1.0, ue - 1))
               return ScanResult{v, -1};
             const long long Se = S0 + tot;
@@ -1154,9 +1156,19 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             if (fast && has_stop) fast = !stop(grid_value(DEC ? -Se : Se, ue));
             if (fast) {
               v = grid_value(DEC ? -Se : Se, ue);
+              last_ue = ue;  // v stayed in its binade
+              last_units = tot;
+              last_n = wend - ws;
+              if (wend != we) ++c;  // window c+1 was in the pass too
+              continue;
+            }
+            if (wend != we) {  // take window c alone
+              alone = c;
+              --c;
               continue;
             }
           }
+          last_ue = INT_MIN;
           if (S.wstate[c] != 2) sort_window(c);
           else cache_window(c);
           auto elemc = [&](int j) { return fromt.exact(tcache[j - ws]); };
