@@ -268,6 +268,39 @@ def test_device_inputs_match_host_path(pkg, engine):
     assert np.array_equal(out_probs.cpu().numpy(), probs_h)
 
 
+@pytest.mark.parametrize("layout", ["mixed", "all_full", "all_streaming", "runs"])
+def test_host_path_matches_device_path(pkg, big_engine, layout):
+    """Host-input batches above 8 rows (staged into the handle's buffers,
+    then the concurrent streaming / full-sort launches) give exactly the
+    device-input path's results, whatever the mix of row kinds."""
+    import torch
+    B, V = 80, 128256
+    w = pkg.workloads.make("c3_batched_hetero", seed=11, rows=np.arange(B), V=V)
+    P = w.params.copy()
+    if layout == "all_full":
+        P["top_k"] = 0
+    elif layout == "all_streaming":
+        P["top_k"] = 40
+        P["temperature"][::5] = 0.0  # greedy rows stream too
+    elif layout == "runs":
+        P["top_k"] = np.where((np.arange(B) // 7) % 2 == 0, 0, 50)
+    a = as_args(w)
+    a["params"] = P
+    ids_h, probs_h, st = big_engine.sample_batch(**a, want_probs=True)
+    assert st == 0
+    dev = torch.device("cuda:0")
+    t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    params_t = torch.from_numpy(P.view(np.uint8).copy()).to(dev)
+    out_ids = torch.empty(B, dtype=torch.int64, device=dev)
+    out_probs = torch.empty(B, dtype=torch.float32, device=dev)
+    big_engine.sample_batch(t(w.logits), params_t, t(w.hist_ids), t(w.hist_off), t(w.bias_ids),
+                            t(w.bias_vals), t(w.bias_off), t(w.uniforms), out_ids=out_ids,
+                            out_probs=out_probs)
+    torch.cuda.synchronize()
+    assert np.array_equal(out_ids.cpu().numpy(), ids_h)
+    assert np.array_equal(out_probs.cpu().numpy(), probs_h)
+
+
 def test_repeat_calls_are_deterministic(pkg, big_engine):
     w = pkg.workloads.make("c3_batched_hetero", seed=5, rows=np.arange(64))
     a, _, _ = big_engine.sample_batch(**as_args(w))
