@@ -223,7 +223,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
       const uint32_t b = stage_bytes(s);
       if (b) {
         mbar_arrive_expect_tx(&S.full_bar[s], b);
-        bulk_copy_g2s(S.ring[s], rowp + s * LT_STAGE, b, &S.full_bar[s]);
+        bulk_copy_g2s_hint(S.ring[s], rowp + s * LT_STAGE, b, &S.full_bar[s], l2_policy_evict_first());
       }
     }
   }
@@ -568,7 +568,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
       if (b) {
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&S.full_bar[buf], b);
-        bulk_copy_g2s(S.ring[buf], rowp + (si + LT_NSTAGE) * LT_STAGE, b, &S.full_bar[buf]);
+        bulk_copy_g2s_hint(S.ring[buf], rowp + (si + LT_NSTAGE) * LT_STAGE, b, &S.full_bar[buf],
+                           l2_policy_evict_first());
       }
     }
     if (mode == kModeTopK && need) {
