@@ -192,8 +192,10 @@ nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, 
     if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
   }
   h->profiled = prof ? 1 : 0;
-  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
-  (void)flags;
+  // host-output calls read the status at their end; device-output calls
+  // leave it in d_work for nls_stream_status (no copy in their stream)
+  if (!(flags & NLS_DEVICE_OUTPUTS))
+    NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
   return NLS_OK;
 }
 
@@ -470,8 +472,8 @@ nls_status nls_top_tokens(nls_handle* h, const float* logits, int64_t ld, int32_
   NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
   NLS_CUDA(h, nls::launch_top(dl, dld, rows, vocab, n, oid, opr, h->d_work, h->d_scratch, h->vpad,
                               h->slots, st));
-  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
   if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
   NLS_CUDA(h, cudaMemcpyAsync(out_ids, oid, sizeof(int64_t) * rows * n, cudaMemcpyDeviceToHost, st));
   if (out_probs)
     NLS_CUDA(h, cudaMemcpyAsync(out_probs, opr, sizeof(float) * rows * n, cudaMemcpyDeviceToHost, st));
@@ -507,7 +509,9 @@ nls_status nls_stream_status(nls_handle* h, void* stream) {
   if (!h) return NLS_ERR_INVALID_ARG;
   DeviceGuard g(h->device);
   NLS_CUDA(h, cudaStreamSynchronize((cudaStream_t)stream));
-  return (nls_status)*h->h_status;
+  int status = 0;
+  NLS_CUDA(h, cudaMemcpy(&status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost));
+  return (nls_status)status;
 }
 
 

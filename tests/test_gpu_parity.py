@@ -187,6 +187,32 @@ def test_nan_row_reports_error_others_fine(engine, oracle_mod):
     assert ids[0] == ref[0] and ids[2] == ref[1]
 
 
+@pytest.mark.parametrize("B", [3, 12])  # the small-batch and the concurrent launch paths
+def test_device_output_status_read_by_stream_status(pkg, engine, B):
+    """A device-output call returns at once; its kernel-side status (here a
+    NaN row) is what nls_stream_status reports, and a clean call after it
+    reports NLS_OK again."""
+    import torch
+    from oracle.oracle import PARAMS_DTYPE
+    rng = np.random.default_rng(4)
+    dev = torch.device("cuda:0")
+    x = rng.normal(0, 2, (B, 5000)).astype(np.float32)
+    P = np.zeros(B, PARAMS_DTYPE)
+    P[:] = (0.8, 0.9, 0.0, 1.0, 0, 0, 40, 64)
+    P["top_k"][::2] = 0  # full-sort rows too
+    u = torch.from_numpy(rng.random(B)).to(dev)
+    params = torch.from_numpy(P.view(np.uint8).copy()).to(dev)
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    for bad, want in ((True, 5), (False, 0)):
+        xx = x.copy()
+        if bad:
+            xx[1, 17] = np.nan
+        _, _, st = engine.sample_batch(torch.from_numpy(xx).to(dev), params, uniforms=u, out_ids=out,
+                                       check=False)
+        assert st == 0  # the call itself
+        assert engine._lib.nls_stream_status(engine._h, None) == want
+
+
 def test_duplicate_bias_id_is_invalid(engine):
     a = single(np.zeros(100), (1.0, 1, 0, 1, 0, 0, 10, 64))
     a["bias_ids"] = np.array([5, 5], np.int64)
