@@ -431,25 +431,28 @@ light_kernel(BatchArgs a, int C, int chunk) {
           else
             q[j] = reinterpret_cast<const float4*>(S.ring[buf])[g];
         }
-        float y[LT_GROUPS][4];
+        // pass bit 4j+e: element e of group j is at or above the threshold
+        static_assert(4 * LT_GROUPS <= 32, "pass bits fit one word");
+        uint32_t pm = 0u;
         float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
-        int cnt = 0;
 #pragma unroll
         for (int j = 0; j < LT_GROUPS; ++j) {
           const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
           const bool gv = !PARTIAL || (tid + j * LT_THREADS) < ngv;
+          float y[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            y[j][e] = __fmul_rn(x[e], invT);
-            cnt += (gv && y[j][e] >= thrf) ? 1 : 0;
+            y[e] = __fmul_rn(x[e], invT);
+            pm |= (gv && y[e] >= thrf) ? (1u << (4 * j + e)) : 0u;
           }
-          m0 = fmax_nan(m0, y[j][0]);
-          m1 = fmax_nan(m1, y[j][1]);
-          m2 = fmax_nan(m2, y[j][2]);
-          m3 = fmax_nan(m3, y[j][3]);
+          m0 = fmax_nan(m0, y[0]);
+          m1 = fmax_nan(m1, y[1]);
+          m2 = fmax_nan(m2, y[2]);
+          m3 = fmax_nan(m3, y[3]);
         }
         mnan = fmax_nan(mnan, fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3)));
-        if (__any_sync(0xffffffffu, cnt > 0)) {
+        if (__any_sync(0xffffffffu, pm != 0u)) {
+          const int cnt = __popc(pm);
           int incl = cnt;
 #pragma unroll
           for (int o = 1; o < 32; o <<= 1) {
@@ -462,22 +465,21 @@ light_kernel(BatchArgs a, int C, int chunk) {
           const int end = base + __shfl_sync(0xffffffffu, incl, 31);
           my_max = end > my_max ? end : my_max;
           int pos = base + incl - cnt;
-#pragma unroll
-          for (int j = 0; j < LT_GROUPS; ++j) {
-            const bool gv = !PARTIAL || (tid + j * LT_THREADS) < ngv;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (gv && y[j][e] >= thrf) {
-                const int off = sbase + 4 * (tid + j * LT_THREADS) + e;
-                // a patched position rejoins later with its patched value
-                const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
-                if (pos < LT_CAP) {
-                  S.cand_key[pos] = patched ? 0u : fkey(y[j][e]);
-                  S.cand_idx[pos] = patched ? -1 : lo + off;
-                }
-                ++pos;
-              }
+          // only the passing elements, in (group, element) order; the value
+          // is read again from the ring (still held until the stage barrier)
+          while (pm) {
+            const int bit = __ffs(pm) - 1;
+            pm &= pm - 1u;
+            const int rel = 4 * (tid + (bit >> 2) * LT_THREADS) + (bit & 3);  // offset in the stage
+            const int off = sbase + rel;
+            const float y = __fmul_rn(S.ring[buf][rel], invT);
+            // a patched position rejoins later with its patched value
+            const bool patched = npatch > 0 && patch_bit(T, off) && patch_find(T, lo + off) >= 0;
+            if (pos < LT_CAP) {
+              S.cand_key[pos] = patched ? 0u : fkey(y);
+              S.cand_idx[pos] = patched ? -1 : lo + off;
             }
+            ++pos;
           }
         }
       };
