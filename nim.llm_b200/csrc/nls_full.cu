@@ -933,10 +933,20 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         constexpr bool DEC = decltype(decc)::value;
         float v = v0;
         int j = j0;
-        // positions summed per pass: small right after an event (binade
-        // changes near a sum's start come 1, 2, 4, ... positions apart),
-        // doubling while passes find none
-        int span = 32 * FT_WARPS;
+        // Positions summed per pass. The terms do not grow along the sorted
+        // order, so the running value cannot leave its binade within
+        // (distance to the binade edge) / elem(j) positions. While that bound
+        // is under one group per warp, a pass takes one group per warp
+        // (binade changes near a sum's start come 1, 2, 4, ... positions
+        // apart); beyond it, FT_BIG positions at once (a pass costs mostly its
+        // barriers). Doubled while passes find no event.
+        auto first_span = [&](int jj, float vv) -> int {
+          const float tj = elem(jj);
+          const int E = binade_exp(vv);
+          const double room = DEC ? (double)vv - ldexp(1.0, E) : ldexp(1.0, E + 1) - (double)vv;
+          return (tj > 0.0f && room < (double)tj * (32 * FT_WARPS)) ? 32 * FT_WARPS : FT_BIG;
+        };
+        int span = first_span(j, v);
         while (j < j1) {
           const int E = binade_exp(v);
           const int ue = E - 23;
@@ -1016,7 +1026,6 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             span = (span < FT_BIG) ? span * 2 : span;
             continue;
           }
-          span = 32 * FT_WARPS;
           j += 32 * gev;
           if (warp == 0) {
             const WalkResult w = warp_walk<DEC>(j, j1, v, elem, stop, has_stop, 8);
@@ -1032,6 +1041,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const int wstop = S.scan.walk_stop;
           __syncthreads();
           if (wstop >= 0) return ScanResult{v, wstop};
+          if (j < j1) span = first_span(j, v);
         }
         return ScanResult{v, -1};
       };
