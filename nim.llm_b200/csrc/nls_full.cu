@@ -548,8 +548,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int anynan = 0;
     const bool vec = ((reinterpret_cast<uintptr_t>(rowp) & 15u) == 0);
     const int nv4 = vec ? (V >> 2) : 0;
-    for (int g = tid; g < nv4; g += FT_THREADS) {
-      const float4 q = __ldcs(reinterpret_cast<const float4*>(rowp) + g);
+    auto transform4 = [&](int g, const float4 q) {
       float x[4] = {q.x, q.y, q.z, q.w};
       if (npatch > 0 && patch_bit(T, 4 * g)) {
 #pragma unroll
@@ -568,6 +567,20 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         kmax = max(kmax, k[e]);
       }
       reinterpret_cast<uint4*>(KY)[g] = make_uint4(k[0], k[1], k[2], k[3]);
+    };
+    {
+      // four loads in flight per thread before any of them is used
+      constexpr int TU = 4;
+      const float4* src = reinterpret_cast<const float4*>(rowp);
+      int g = tid;
+      for (; g + (TU - 1) * FT_THREADS < nv4; g += TU * FT_THREADS) {
+        float4 q[TU];
+#pragma unroll
+        for (int u = 0; u < TU; ++u) q[u] = __ldcs(src + g + u * FT_THREADS);
+#pragma unroll
+        for (int u = 0; u < TU; ++u) transform4(g + u * FT_THREADS, q[u]);
+      }
+      for (; g < nv4; g += FT_THREADS) transform4(g, __ldcs(src + g));
     }
     for (int i = 4 * nv4 + tid; i < V; i += FT_THREADS) {
       const float y = __fmul_rn(logit(i), invT);
@@ -610,7 +623,17 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     }
     for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] = 0u;
     __syncthreads();
-    for (int i = tid; i < V; i += FT_THREADS) atomicAdd(&S.h1[bk(KY[i])], 1u);
+    {
+      const int nk4 = V >> 2;  // KY is 16-byte aligned
+      for (int g = tid; g < nk4; g += FT_THREADS) {
+        const uint4 k = reinterpret_cast<const uint4*>(KY)[g];
+        atomicAdd(&S.h1[bk(k.x)], 1u);
+        atomicAdd(&S.h1[bk(k.y)], 1u);
+        atomicAdd(&S.h1[bk(k.z)], 1u);
+        atomicAdd(&S.h1[bk(k.w)], 1u);
+      }
+      for (int i = 4 * nk4 + tid; i < V; i += FT_THREADS) atomicAdd(&S.h1[bk(KY[i])], 1u);
+    }
     __syncthreads();
     if (warp == 0) {  // exclusive scan of the 256 coarse counts (8 per lane)
       uint32_t loc[FT_NB / 32], sum = 0;
