@@ -194,6 +194,19 @@ NLS_API nls_status nls_sample_batch_vocab_sharded(
  * `stream` and returns the first error the kernels recorded (NLS_OK if none). */
 NLS_API nls_status nls_stream_status(nls_handle* h, void* stream);
 
+/* The per-position term of perplexity (model.nim:570-589): for each row r,
+ * out_nll[r] = -(float64(x[targets[r]] - mx) - ln(s)), where mx is the row's
+ * fp32 maximum, the difference is taken in fp32, and s is the float64 sum of
+ * exp(float64(x_k - mx)) over the row (model.nim:581-584). The caller sums
+ * the terms and takes exp(total / count) (:589). The sum runs in a tree order
+ * rather than index order (float64 rounding differences only). A row with a
+ * NaN or a non-finite maximum gets NaN and NLS_ERR_NAN_LOGITS; a target
+ * outside [0, vocab) gets NaN and NLS_ERR_INVALID_ARG. Flags as
+ * nls_sample_batch (targets is an input, out_nll an output). */
+NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                                 int32_t vocab, const int64_t* targets, double* out_nll,
+                                 uint32_t flags, void* stream);
+
 /* Per-kernel timing of later calls on this handle (tracing; no counterpart
  * in the reference, which only times whole generations with epochTime,
  * chat.nim:191,246-247). With `on` set, every sampling call records CUDA

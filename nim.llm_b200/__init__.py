@@ -13,6 +13,6 @@ from . import workloads
 from ._abi import EXPORTS, LIB_PATH, NlsError, ROW_PARAMS_DTYPE, load
 from .sampler import (Comm, Engine, Rand, Sampler, SamplerParams, accept, argmax, comm_unique_id,
                       default_engine, defaultSampling, greedySampling, newSampler, params_record,
-                      row_owner_range, sample, topTokens, vocab_shard)
+                      perplexity_from_logits, row_owner_range, sample, topTokens, vocab_shard)
 
 __version__ = "0.1.0"

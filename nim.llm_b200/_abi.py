@@ -32,7 +32,7 @@ EXPORTS = (
     "nls_stream_status", "nls_status_str", "nls_last_error", "nls_version",
     "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
     "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
-    "nls_top_tokens",
+    "nls_top_tokens", "nls_token_nll",
 )
 
 # nls_row_params: 6 doubles + 2 int64, 64 bytes, no padding.
@@ -89,6 +89,8 @@ def load(path: str | None = None):
                                                  vp, vp, vp]
     L.nls_top_tokens.restype = i32
     L.nls_top_tokens.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, u32, vp]
+    L.nls_token_nll.restype = i32
+    L.nls_token_nll.argtypes = [vp, vp, i64, i32, i32, vp, vp, u32, vp]
     _lib = L
     return L
 

@@ -65,6 +65,11 @@ struct nls_handle {
   float* d_sh_pall = nullptr;
   size_t sh_pall_cap = 0;
   int64_t* h_sh_status = nullptr;  // pinned, one per rank (up to kMaxRanks)
+  // nls_token_nll with host buffers: targets in, terms out
+  int64_t* d_tgt = nullptr;
+  size_t tgt_cap = 0;
+  double* d_nll = nullptr;
+  size_t nll_cap = 0;
   char last_err[256] = {0};
 };
 
@@ -246,6 +251,8 @@ void nls_destroy(nls_handle* h) {
     cudaFree(h->d_sh_pmine);
     cudaFree(h->d_sh_pall);
     if (h->h_sh_status) cudaFreeHost(h->h_sh_status);
+    cudaFree(h->d_tgt);
+    cudaFree(h->d_nll);
     if (h->fork) cudaEventDestroy(h->fork);
     if (h->join) cudaEventDestroy(h->join);
     for (cudaEvent_t e : h->ev)
@@ -477,6 +484,47 @@ nls_status nls_top_tokens(nls_handle* h, const float* logits, int64_t ld, int32_
   NLS_CUDA(h, cudaMemcpyAsync(out_ids, oid, sizeof(int64_t) * rows * n, cudaMemcpyDeviceToHost, st));
   if (out_probs)
     NLS_CUDA(h, cudaMemcpyAsync(out_probs, opr, sizeof(float) * rows * n, cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  return (nls_status)*h->h_status;
+}
+
+nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                         int32_t vocab, const int64_t* targets, double* out_nll, uint32_t flags,
+                         void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0 || vocab < 1 || ld < vocab) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !targets || !out_nll) return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  nls_status s;
+  const float* dl = logits;
+  int64_t dld = ld;
+  const int64_t* dt = targets;
+  if (!(flags & NLS_DEVICE_INPUTS)) {
+    if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+    if ((s = grow(h, &h->d_tgt, &h->tgt_cap, (size_t)rows)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
+                                  (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
+                                  cudaMemcpyHostToDevice, st));
+    NLS_CUDA(h, cudaMemcpyAsync(h->d_tgt, targets, sizeof(int64_t) * rows, cudaMemcpyHostToDevice, st));
+    dl = h->d_logits;
+    dld = vocab;
+    dt = h->d_tgt;
+  }
+  const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
+  double* dout = out_nll;
+  if (!dev_out) {
+    if ((s = grow(h, &h->d_nll, &h->nll_cap, (size_t)rows)) != NLS_OK) return s;
+    dout = h->d_nll;
+  }
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
+  NLS_CUDA(h, nls::launch_nll(dl, dld, rows, vocab, dt, dout, h->d_work, h->sm_count, st));
+  if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaMemcpyAsync(out_nll, dout, sizeof(double) * rows, cudaMemcpyDeviceToHost, st));
   NLS_CUDA(h, cudaStreamSynchronize(st));
   return (nls_status)*h->h_status;
 }

@@ -27,4 +27,9 @@ cudaError_t launch_top(const float* logits, int64_t ld, int rows, int V, int n, 
                        float* out_probs, int* status, uint32_t* scratch, int vpad, int slots,
                        cudaStream_t stream);
 
+// perplexity's per-position negative log-likelihood: out[r] for row r and
+// target token targets[r] (grid-stride over rows, up to 4 CTAs per SM).
+cudaError_t launch_nll(const float* logits, int64_t ld, int rows, int V, const int64_t* targets,
+                       double* out, int* status, int sm_count, cudaStream_t stream);
+
 }  // namespace nls

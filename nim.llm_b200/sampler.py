@@ -222,6 +222,28 @@ class Engine:
         self._check(st, "nls_top_tokens")
         return ids, probs
 
+    def token_nll(self, logits, targets, check: bool = True):
+        """Perplexity's per-position term (model.nim:581-584) for each row of
+        host numpy logits [B, V] and its target token: returns (float64 [B],
+        status). A row with a NaN or non-finite maximum, or a target outside
+        [0, V), gets NaN and a non-zero status (raised unless check=False)."""
+        logits = np.asarray(logits, dtype=np.float32)
+        if logits.ndim == 1:
+            logits = logits[None, :]
+        if logits.strides[1] != 4 or logits.strides[0] % 4 != 0:
+            logits = np.ascontiguousarray(logits)  # rows may be strided (ld > V)
+        B, V = logits.shape
+        ld = logits.strides[0] // 4 if B > 1 else V
+        targets = np.ascontiguousarray(np.asarray(targets, dtype=np.int64).reshape(-1))
+        if targets.size != B:
+            raise ValueError("one target per row")
+        out = np.empty(B, dtype=np.float64)
+        st = self._lib.nls_token_nll(self._h, _host_ptr(logits), ld, B, V, _host_ptr(targets),
+                                     _host_ptr(out), 0, ctypes.c_void_p(0))
+        if check:
+            self._check(st, "nls_token_nll")
+        return out, st
+
     def argmax_batch(self, logits) -> np.ndarray:
         logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
         if logits.ndim == 1:
@@ -301,9 +323,27 @@ def topTokens(logits, n: int = 5, engine: Optional[Engine] = None) -> list:  # s
     return [(int(ids[0, i]), float(probs[0, i])) for i in range(m)]
 
 
+def perplexity_from_logits(logits, tokens, engine: Optional[Engine] = None) -> float:
+    """The perplexity of one chunk (model.nim:570-589) from its logits
+    [T, V] (row t predicts tokens[t+1]) and its T tokens: the per-position
+    terms come from the GPU, their float64 sum runs in position order as in
+    the reference loop, then exp(total / max(1, count))."""
+    eng = engine or default_engine()
+    x = np.asarray(logits, dtype=np.float32)
+    tok = np.asarray(tokens, dtype=np.int64).reshape(-1)
+    n = tok.size - 1
+    if n <= 0:
+        return 1.0  # exp(0 / 1): the reference's loop body never runs
+    nll, _ = eng.token_nll(x[:n], tok[1:n + 1])
+    total = 0.0
+    for v in nll:
+        total += float(v)
+    return float(np.exp(total / max(1, n)))
+
+
 __all__ = ["SamplerParams", "defaultSampling", "greedySampling", "params_record", "Rand",
            "Engine", "Sampler", "newSampler", "accept", "sample", "argmax", "topTokens",
-           "default_engine", "NlsError", "ROW_PARAMS_DTYPE"]
+           "perplexity_from_logits", "default_engine", "NlsError", "ROW_PARAMS_DTYPE"]
 
 
 # ---------------------------------------------------------------------------

@@ -74,6 +74,8 @@ def lib():
                                  P(ctypes.c_int64), P(ctypes.c_double), ctypes.c_int64,
                                  P(ctypes.c_float), ctypes.c_int64, ctypes.c_double,
                                  P(NloDiag)]
+        L.nlo_token_nll.restype = ctypes.c_double
+        L.nlo_token_nll.argtypes = [P(ctypes.c_float), ctypes.c_int64, ctypes.c_int64]
         L.nlo_top_tokens.restype = ctypes.c_int64
         L.nlo_top_tokens.argtypes = [P(ctypes.c_float), ctypes.c_int64, ctypes.c_int64,
                                      P(ctypes.c_int64), P(ctypes.c_float)]
@@ -122,6 +124,15 @@ def softmax_inplace(x: np.ndarray) -> np.ndarray:
     x = np.array(x, dtype=np.float32, copy=True)
     lib().nlo_softmax_inplace(x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), x.size)
     return x
+
+
+def token_nll(logits: np.ndarray, targets) -> np.ndarray:
+    """perplexity's per-position term (model.nim:580-584) for each row."""
+    x = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+    t = np.asarray(targets, dtype=np.int64).reshape(-1)
+    P = ctypes.POINTER(ctypes.c_float)
+    return np.array([lib().nlo_token_nll(x[r].ctypes.data_as(P), x.shape[1], int(t[r]))
+                     for r in range(x.shape[0])], dtype=np.float64)
 
 
 def top_tokens(x: np.ndarray, n: int = 5):

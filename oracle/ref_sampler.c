@@ -329,6 +329,23 @@ int64_t nlo_top_tokens(const float* logits, int64_t V, int64_t n, int64_t* out_i
   return m;
 }
 
+/* perplexity's per-position term (model.nim:580-584): mx = the fp32 maximum
+ * of the row (:581), s = the float64 sum, in index order, of
+ * exp(float64(x_k - mx)) with the difference in fp32 (:582-583), and the
+ * term -(float64(x_target - mx) - ln(s)) (:584). Nim's exp/ln on float64 are
+ * C's exp/log. */
+double nlo_token_nll(const float* logits, int64_t V, int64_t target) {
+  float mx = -INFINITY;
+  for (int64_t k = 0; k < V; ++k) mx = logits[k] > mx ? logits[k] : mx;
+  double s = 0.0;
+  for (int64_t k = 0; k < V; ++k) {
+    const float d = logits[k] - mx;
+    s += exp((double)d);
+  }
+  const float dt = logits[target] - mx;
+  return -((double)dt - log(s));
+}
+
 typedef struct {
   const float* logits; int64_t ld, rows, V;
   const nlo_params* params;

@@ -71,6 +71,9 @@ void nlo_sample_batch(const float* logits, int64_t ld, int64_t rows, int64_t n_v
                       const double* uniforms, int64_t* out_ids, nlo_diag* diag,
                       int threads);
 
+/* perplexity's per-position term (model.nim:580-584) for one row. */
+double nlo_token_nll(const float* logits, int64_t V, int64_t target);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,6 +27,10 @@ import numpy as np
 _libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
 _libm.expf.restype = ctypes.c_float
 _libm.expf.argtypes = [ctypes.c_float]
+_libm.exp.restype = ctypes.c_double
+_libm.exp.argtypes = [ctypes.c_double]
+_libm.log.restype = ctypes.c_double
+_libm.log.argtypes = [ctypes.c_double]
 
 f32 = np.float32
 
@@ -151,6 +155,18 @@ def sample(p: SamplerParams, history: list, logitsIn, u: float, diag: dict | Non
     if diag is not None:
         diag.update(n=n, pos=pos, prob=float(probs[pos]), ncand=len(idx), total=float(total))
     return result
+
+
+def token_nll(logits, target):                              # model.nim:580-584
+    """One position of perplexity: Nim `float` is float64, so exp/ln are
+    C's exp/log on float64; `logits[..] - mx` is a float32 subtraction."""
+    mx = f32(float("-inf"))
+    for v in logits:                                          # :581
+        mx = max(mx, f32(v))
+    s = 0.0
+    for v in logits:                                          # :582-583
+        s += _libm.exp(float(f32(f32(v) - mx)))
+    return -(float(f32(f32(logits[target]) - mx)) - _libm.log(s))   # :584
 
 
 def top_tokens(logits, n=5):                                 # sampler.nim:123-130
