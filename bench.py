@@ -21,6 +21,7 @@ this host's cores over the same workload.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -446,6 +447,45 @@ def main():
                          "time of the call (library CUDA events), host_* = wall clock of the call "
                          "through the Python binding with a stream sync"}
 
+    # perplexity's per-position term over one nCtx-512 chunk (511 positions,
+    # V = 128256), device inputs and outputs: device time of a call
+    nll = None
+    if rank == 0:
+        T1 = 511
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(SEED)
+        xl = torch.randn((T1, w.V), generator=gen, device=dev) * 3.0
+        tg = torch.randint(0, w.V, (T1,), generator=gen, device=dev)
+        on = torch.empty(T1, dtype=torch.float64, device=dev)
+        eng_n = pkg.Engine(local, max_rows=T1, max_vocab=w.V)
+        L = eng_n._lib
+
+        def nll_call():
+            return L.nls_token_nll(eng_n._h, ctypes.c_void_p(xl.data_ptr()), w.V, T1, w.V,
+                                   ctypes.c_void_p(tg.data_ptr()), ctypes.c_void_p(on.data_ptr()),
+                                   3, ctypes.c_void_p(sptr))
+        for _ in range(3):
+            nll_call()
+        nms = []
+        for _ in range(10):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            nll_call()
+            e1.record(stream)
+            e1.synchronize()
+            nms.append(e0.elapsed_time(e1))
+        if L.nls_stream_status(eng_n._h, ctypes.c_void_p(sptr)) != 0:
+            raise RuntimeError("token_nll status")
+        eng_n.close()
+        nms.sort()
+        nbytes = T1 * w.V * 4 + T1 * 16
+        nll = {"ms": nms[len(nms) // 2], "positions_per_s": T1 / (nms[len(nms) // 2] / 1e3),
+               "achieved_gbs": nbytes / (nms[len(nms) // 2] / 1e3) / 1e9, "peak_gbs": peak,
+               "config": "nls_token_nll (perplexity's per-position term, model.nim:580-584): "
+                         "511 positions x V=128256 fp32, device inputs, L2 flushed before each call"}
+
     # Vocab-sharded mode (BASELINE config 5 over the N ranks: B = 64 rows of
     # V = 151936, each rank holding its columns of every row): device time of
     # one collective call, max over ranks.
@@ -482,6 +522,7 @@ def main():
             "latency_b1": latency,
             "clocks": clk,
             "vocab_sharded": vsh,
+            "token_nll": nll,
         }
         print(json.dumps(line), flush=True)
     eng.close()
