@@ -27,8 +27,10 @@
 //      (nls_scan.cuh), window by window. Inside one binade of the running
 //      value, with no rounding tie and no stop, a window's effect is the sum
 //      of its terms' grid units whatever their order, so such a window is
-//      summed in bucket order from cheap exp estimates (exact where an
-//      estimate is too close to a rounding boundary). Only a window where
+//      summed in bucket order from exp estimates (exact where an estimate
+//      is too close to a rounding boundary), two adjacent windows in one
+//      pass when the previous window predicts that the binade holds over
+//      both. Only a window where
 //      something order-sensitive happens is sorted in shared memory (fine
 //      buckets and insertion sorts on (key, index)) and replayed in order
 //      from a shared-memory copy of its exact t values. The min-p cut is a
