@@ -43,6 +43,8 @@
 #include <atomic>
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "nls_common.cuh"
 #include "nls_kernels.h"
 #include "nls_scan.cuh"
@@ -114,6 +116,11 @@ struct FullShared {
   int gtie[FT_BIG / 32];
   long long gS;
   int gev;
+  // a cluster pair's first row: values pushed here by the partner CTA
+  int x_row;
+  int x_nan;
+  uint32_t x_kmin, x_kmax;
+  uint32_t x_h1[FT_NB];
   int counter, patch_overflow, dup, nan;
 };
 
@@ -436,6 +443,14 @@ struct TermP {
   __device__ float mid(float a) const { return __fmul_rn(a, rinv); }
 };
 
+// PAIR: launched as clusters of two CTAs (row-claiming launches of batches
+// larger than the GPU). The pair shares the first phase of the first row it
+// claims -- transform, histogram and scatter, each CTA taking one half of the
+// row in CTA 0's scratch slot, the extremes and bucket counts pushed into the
+// partner's shared memory before each cluster barrier -- then CTA 0 finishes
+// that row and each CTA claims further rows alone; CTA 1's SM is free early
+// for the streaming kernel. Without PAIR none of this is compiled.
+template <bool PAIR>
 __global__ void __launch_bounds__(FT_THREADS, 1)
 full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -450,6 +465,13 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
   uint32_t* LA = KY + vpad;
   uint32_t* LB = KY + 2 * (size_t)vpad;
   const bool claim = (a.row_claim != nullptr);
+  namespace cg = cooperative_groups;
+  bool pair = PAIR && claim && cg::this_cluster().num_blocks() == 2;
+  // this CTA's rank in the pair and the partner's shared memory, read where
+  // used (no register held across a row)
+  auto crank_now = []() { return (int)cg::this_cluster().block_rank(); };
+  auto partner = [&]() { return cg::this_cluster().map_shared_rank(&S, crank_now() ^ 1); };
+  auto cluster_sync = []() { cg::this_cluster().sync(); };
   // Launched as a programmatic dependent of the streaming kernel (small
   // batches): wait until that grid has finished and its writes (the hand-back
   // list) are visible. Without such a launch this returns at once.
@@ -459,7 +481,20 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 
   for (;;) {
     int row;
-    if (claim) {  // next row whose parameters select the full path
+    if (PAIR && pair) {  // CTA 0 claims for both
+      if (crank_now() == 0 && tid == 0) {
+        int r;
+        while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
+          int64_t kk;
+          if (row_mode(a.params[r], V, &kk) == kModeFull) break;
+        }
+        S.ibuf[0] = r;
+        partner()->x_row = r;
+      }
+      cluster_sync();
+      row = (crank_now() == 0) ? S.ibuf[0] : S.x_row;
+      if (row >= a.rows) break;
+    } else if (claim) {  // next row whose parameters select the full path
       if (tid == 0) {
         int r;
         while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
@@ -481,8 +516,11 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int64_t K64;
     const int mode = row_mode(p, V, &K64);
     const bool greedy = (mode == kModeGreedy);
+    // the pair's CTA 1 writes no results
+    const bool lead = !PAIR || !pair || crank_now() == 0;
     if (!greedy && a.uniforms == nullptr) {
-      if (tid == 0) { a.out_ids[row] = -1; record_status(a.status, NLS_ERR_INVALID_ARG); }
+      if (tid == 0 && lead) { a.out_ids[row] = -1; record_status(a.status, NLS_ERR_INVALID_ARG); }
+      if (PAIR) pair = false;  // (both CTAs alike: no more cluster barriers)
       continue;
     }
     // heap path iff k < V (sampler.nim:86)
@@ -493,11 +531,12 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     PatchTable T{S.ph.pt.hkey, S.ph.pt.hcnt, S.ph.pt.hbias, S.ph.pt.hflag, bitmap, FT_HASH_LOG2, 0, V, FT_GSHIFT};
     const int npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
     if (S.patch_overflow || S.dup) {
-      if (tid == 0) {
+      if (tid == 0 && lead) {
         a.out_ids[row] = -1;
         record_status(a.status, S.dup ? NLS_ERR_INVALID_ARG : NLS_ERR_CAPACITY);
       }
       __syncthreads();
+      if (PAIR) pair = false;
       continue;
     }
     if (npatch > 0) precompute_patches(T, rowp, p);
@@ -550,6 +589,13 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int anynan = 0;
     const bool vec = ((reinterpret_cast<uintptr_t>(rowp) & 15u) == 0);
     const int nv4 = vec ? (V >> 2) : 0;
+    // this CTA's positions [e0, e1) of the first phase (a pair splits the row
+    // at a multiple of 4), written to the pair's shared slot (CTA 0's)
+    const int half = (PAIR && pair) ? min(V, ((V >> 1) + 3) & ~3) : V;
+    const int e0 = (PAIR && pair && crank_now() == 1) ? half : 0;
+    const int e1 = (PAIR && pair && crank_now() == 0) ? half : V;
+    uint32_t* const KYp = PAIR ? KY - (pair ? (size_t)crank_now() * 4 * (size_t)vpad : 0) : KY;
+    unsigned long long* const SKp = PAIR ? reinterpret_cast<unsigned long long*>(KYp + vpad) : SK;
     auto transform4 = [&](int g, const float4 q) {
       float x[4] = {q.x, q.y, q.z, q.w};
       if (npatch > 0 && patch_bit(T, 4 * g)) {
@@ -568,45 +614,74 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         kmin = min(kmin, k[e]);
         kmax = max(kmax, k[e]);
       }
-      reinterpret_cast<uint4*>(KY)[g] = make_uint4(k[0], k[1], k[2], k[3]);
+      reinterpret_cast<uint4*>(KYp)[g] = make_uint4(k[0], k[1], k[2], k[3]);
     };
     {
       // four loads in flight per thread before any of them is used
       constexpr int TU = 4;
       const float4* src = reinterpret_cast<const float4*>(rowp);
-      int g = tid;
-      for (; g + (TU - 1) * FT_THREADS < nv4; g += TU * FT_THREADS) {
+      const int g1 = PAIR ? min(e1 >> 2, nv4) : nv4;
+      int g = PAIR ? (e0 >> 2) + tid : tid;
+      for (; g + (TU - 1) * FT_THREADS < g1; g += TU * FT_THREADS) {
         float4 q[TU];
 #pragma unroll
         for (int u = 0; u < TU; ++u) q[u] = __ldcs(src + g + u * FT_THREADS);
 #pragma unroll
         for (int u = 0; u < TU; ++u) transform4(g + u * FT_THREADS, q[u]);
       }
-      for (; g < nv4; g += FT_THREADS) transform4(g, __ldcs(src + g));
+      for (; g < g1; g += FT_THREADS) transform4(g, __ldcs(src + g));
     }
-    for (int i = 4 * nv4 + tid; i < V; i += FT_THREADS) {
+    for (int i = (PAIR ? max(e0, 4 * nv4) : 4 * nv4) + tid; i < e1; i += FT_THREADS) {
       const float y = __fmul_rn(logit(i), invT);
       anynan |= (y != y);
       const uint32_t k = desc_key(y);
       kmin = min(kmin, k);
       kmax = max(kmax, k);
-      KY[i] = k;
+      KYp[i] = k;
     }
     kmin = __reduce_min_sync(0xffffffffu, kmin);
     kmax = __reduce_max_sync(0xffffffffu, kmax);
     if (lane == 0) { S.ured[warp] = kmin; S.ured2[warp] = kmax; }
-    if (block_sum_int(anynan, S) > 0) {   // (its barrier also publishes ured)
-      if (tid == 0) {
-        a.out_ids[row] = -1;
-        if (a.out_probs) a.out_probs[row] = 0.0f;
-        record_status(a.status, NLS_ERR_NAN_LOGITS);
-      }
-      continue;
-    }
-    kmin = 0xffffffffu;
-    kmax = 0u;
+    if constexpr (PAIR) {
+      int nnan = block_sum_int(anynan, S);  // (its barrier also publishes ured)
+      kmin = 0xffffffffu;
+      kmax = 0u;
 #pragma unroll 8
-    for (int k = 0; k < FT_WARPS; ++k) { kmin = min(kmin, S.ured[k]); kmax = max(kmax, S.ured2[k]); }
+      for (int k = 0; k < FT_WARPS; ++k) { kmin = min(kmin, S.ured[k]); kmax = max(kmax, S.ured2[k]); }
+      if (pair) {  // the other half's extremes and NaNs (KY complete after the barrier)
+        if (tid == 0) {
+          partner()->x_kmin = kmin;
+          partner()->x_kmax = kmax;
+          partner()->x_nan = nnan;
+        }
+        cluster_sync();
+        kmin = min(kmin, S.x_kmin);
+        kmax = max(kmax, S.x_kmax);
+        nnan += S.x_nan;
+      }
+      if (nnan > 0) {
+        if (tid == 0 && lead) {
+          a.out_ids[row] = -1;
+          if (a.out_probs) a.out_probs[row] = 0.0f;
+          record_status(a.status, NLS_ERR_NAN_LOGITS);
+        }
+        pair = false;
+        continue;
+      }
+    } else {
+      if (block_sum_int(anynan, S) > 0) {   // (its barrier also publishes ured)
+        if (tid == 0) {
+          a.out_ids[row] = -1;
+          if (a.out_probs) a.out_probs[row] = 0.0f;
+          record_status(a.status, NLS_ERR_NAN_LOGITS);
+        }
+        continue;
+      }
+      kmin = 0xffffffffu;
+      kmax = 0u;
+#pragma unroll 8
+      for (int k = 0; k < FT_WARPS; ++k) { kmin = min(kmin, S.ured[k]); kmax = max(kmax, S.ured2[k]); }
+    }
     const float mx = desc_key_value(kmin);
     const float ymin = desc_key_value(kmax);
 
@@ -626,17 +701,26 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] = 0u;
     __syncthreads();
     {
-      const int nk4 = V >> 2;  // KY is 16-byte aligned
-      for (int g = tid; g < nk4; g += FT_THREADS) {
-        const uint4 k = reinterpret_cast<const uint4*>(KY)[g];
+      // this CTA's positions [e0, e1); e0 is a multiple of 4, KY 16-byte aligned
+      const int gk1 = PAIR ? e1 >> 2 : V >> 2;
+      for (int g = (PAIR ? (e0 >> 2) : 0) + tid; g < gk1; g += FT_THREADS) {
+        const uint4 k = reinterpret_cast<const uint4*>(KYp)[g];
         atomicAdd(&S.h1[bk(k.x)], 1u);
         atomicAdd(&S.h1[bk(k.y)], 1u);
         atomicAdd(&S.h1[bk(k.z)], 1u);
         atomicAdd(&S.h1[bk(k.w)], 1u);
       }
-      for (int i = 4 * nk4 + tid; i < V; i += FT_THREADS) atomicAdd(&S.h1[bk(KY[i])], 1u);
+      for (int i = (PAIR ? max(e0, 4 * gk1) : 4 * gk1) + tid; i < e1; i += FT_THREADS) atomicAdd(&S.h1[bk(KYp[i])], 1u);
     }
     __syncthreads();
+    if constexpr (PAIR) {
+      if (pair) {  // totals; CTA 1 writes each bucket's run after CTA 0's
+        for (int b = tid; b < FT_NB; b += FT_THREADS) partner()->x_h1[b] = S.h1[b];
+        cluster_sync();
+        for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] += S.x_h1[b];
+        __syncthreads();
+      }
+    }
     if (warp == 0) {  // exclusive scan of the 256 coarse counts (8 per lane)
       uint32_t loc[FT_NB / 32], sum = 0;
 #pragma unroll
@@ -650,8 +734,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       uint32_t run = incl - sum;
 #pragma unroll
       for (int r = 0; r < FT_NB / 32; ++r) {
-        S.s1[lane * (FT_NB / 32) + r] = run;
-        S.c1[lane * (FT_NB / 32) + r] = run;
+        const int b = lane * (FT_NB / 32) + r;
+        S.s1[b] = run;
+        S.c1[b] = run + ((PAIR && pair && crank_now() == 1) ? S.x_h1[b] : 0u);
         run += loc[r];
       }
     }
@@ -659,6 +744,12 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     for (int b = tid; b < FT_NB; b += FT_THREADS) bigmax = max(bigmax, (int)S.h1[b]);
     bigmax = block_max_int(bigmax, S);
     const bool bucketed = bigmax <= FT_BUCKET_MAX;
+    if constexpr (PAIR) {
+      if (pair && !bucketed) {  // CTA 0 radix-sorts the whole (complete) KY alone
+        pair = false;
+        if (crank_now() == 1) continue;
+      }
+    }
     const int nwin = (V + FT_WIN - 1) / FT_WIN;
     unsigned long long* bufA = S.u.big;
     unsigned long long* bufB = S.ph.bufB;
@@ -794,12 +885,12 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       uint32_t kd[PT];  // this tile's keys, loaded one tile ahead
 #pragma unroll
       for (int r = 0; r < PT; ++r) {
-        const int i = tid + r * FT_THREADS;
-        kd[r] = (i < V) ? KY[i] : 0u;
+        const int i = e0 + tid + r * FT_THREADS;
+        kd[r] = (i < e1) ? KYp[i] : 0u;
       }
       __syncthreads();
-      for (int t0 = 0; t0 < V; t0 += FT_TILE1) {
-        const int nt = min(FT_TILE1, V - t0);
+      for (int t0 = e0; t0 < e1; t0 += FT_TILE1) {
+        const int nt = min(FT_TILE1, e1 - t0);
         int bb[PT];
         uint32_t rk[PT];  // rank inside the tile's bucket
 #pragma unroll
@@ -839,17 +930,24 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 #pragma unroll
         for (int r = 0; r < PT; ++r) {
           const int i = t0 + FT_TILE1 + tid + r * FT_THREADS;
-          kd[r] = (i < V) ? KY[i] : 0u;
+          kd[r] = (i < e1) ? KYp[i] : 0u;
         }
         __syncthreads();
         // (the next tile touches lo1/gb1/stage only after its first barrier)
         for (int q = tid; q < nt; q += FT_THREADS) {
           const unsigned long long v = stage[q];
           const int b = bk((uint32_t)(v >> 32));
-          SK[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
+          SKp[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
         }
       }
       __syncthreads();
+      if constexpr (PAIR) {
+        if (pair) {  // every SK entry of the row is written; CTA 1 moves on
+          cluster_sync();
+          pair = false;
+          if (crank_now() == 1) continue;
+        }
+      }
       // windows: the coarse buckets whose start lies in [c*FT_WIN, (c+1)*FT_WIN)
       for (int c = tid; c <= nwin; c += FT_THREADS) {
         const int x = c * FT_WIN;
@@ -1376,19 +1474,38 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 }
 
 static std::atomic<int> g_full_smem_set[kMaxDevicesAttr];
+static std::atomic<int> g_full_pair_smem_set[kMaxDevicesAttr];
 
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
                         cudaStream_t stream, bool after_light) {
   const size_t smem = full_smem_bytes(a.V);
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(full_kernel), (int)smem, g_full_smem_set);
+  int grid = (a.rows < slots) ? a.rows : slots;  // a CTA takes at most one row at a time
+  // A row-claiming launch over a batch larger than the GPU runs as cluster
+  // pairs (an even grid within the scratch slots): a pair shares its first
+  // row's first phase, and CTA 1's SM then goes to the concurrent streaming
+  // kernel, which has rows to fill it. With fewer rows than SMs there is no
+  // such work, and the single-CTA kernel is used.
+  const bool pairs = a.row_claim != nullptr && !after_light && a.rows > slots && grid >= 2;
+  if (pairs) grid &= ~1;
+  const void* fn = pairs ? reinterpret_cast<const void*>(full_kernel<true>)
+                         : reinterpret_cast<const void*>(full_kernel<false>);
+  cudaError_t e = ensure_smem_attr(fn, (int)smem, pairs ? g_full_pair_smem_set : g_full_smem_set);
   if (e != cudaSuccess) return e;
-  const int grid = (a.rows < slots) ? a.rows : slots;  // a CTA takes at most one row at a time
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3(FT_THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
+  if (pairs) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, full_kernel<true>, a, scratch, vpad);
+  }
   if (after_light) {
     // may start before the streaming kernel ends (its launch latency hides
     // behind that kernel); griddepcontrol.wait orders the reads
@@ -1397,7 +1514,7 @@ cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slo
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, full_kernel, a, scratch, vpad);
+  return cudaLaunchKernelEx(&cfg, full_kernel<false>, a, scratch, vpad);
 }
 
 }  // namespace nls

@@ -327,6 +327,25 @@ def test_host_path_matches_device_path(pkg, big_engine, layout):
     assert np.array_equal(out_probs.cpu().numpy(), probs_h)
 
 
+def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
+    """More rows than SMs: the full-sort kernel runs as cluster pairs that
+    share the first phase of their first row (each CTA one half of the row)."""
+    w = pkg.workloads.make("c3_batched_hetero", seed=21, rows=np.arange(300), V=20000)
+    a = as_args(w)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a)
+    assert st == 0
+    compare(ids, probs, ref, dg, a["params"], "B=300")
+    # a NaN in the first full-path row, which a pair claims first: that row
+    # fails alone
+    full = np.nonzero((a["params"]["top_k"] <= 0) | (a["params"]["top_k"] > 256))[0]
+    a["logits"] = a["logits"].copy()
+    a["logits"][full[0], 123] = np.nan
+    ids2, _, st2 = big_engine.sample_batch(**a, check=False)
+    assert st2 == 5 and ids2[full[0]] == -1
+    keep = np.arange(300) != full[0]
+    assert np.array_equal(ids2[keep], ids[keep])
+
+
 def test_repeat_calls_are_deterministic(pkg, big_engine):
     w = pkg.workloads.make("c3_batched_hetero", seed=5, rows=np.arange(64))
     a, _, _ = big_engine.sample_batch(**as_args(w))
