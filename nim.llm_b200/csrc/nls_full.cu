@@ -1504,7 +1504,16 @@ cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slo
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, full_kernel<true>, a, scratch, vpad);
+    e = cudaLaunchKernelEx(&cfg, full_kernel<true>, a, scratch, vpad);
+    if (e == cudaSuccess) return e;
+    // no room for a cluster pair right now (another context holds the SMs):
+    // the single-CTA kernel over the same grid does the same work
+    (void)cudaGetLastError();
+    e = ensure_smem_attr(reinterpret_cast<const void*>(full_kernel<false>), (int)smem, g_full_smem_set);
+    if (e != cudaSuccess) return e;
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;
+    return cudaLaunchKernelEx(&cfg, full_kernel<false>, a, scratch, vpad);
   }
   if (after_light) {
     // may start before the streaming kernel ends (its launch latency hides
