@@ -343,7 +343,29 @@ __device__ uint32_t warp_select_kth_largest(int n, uint32_t K, Get get, uint32_t
                                             int* n_gt) {
   const int lane = threadIdx.x & 31;
   uint32_t prefix = 0, pmask = 0, rem = K, above = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  // The accepted keys often share their top bytes (a row's best candidates):
+  // the rounds start at the first byte where the smallest and the largest
+  // differ (the last round always runs: it counts n_ge and n_gt).
+  int start = 24;
+  {
+    uint32_t kmn = 0xffffffffu, kmx = 0u;
+    for (int i = lane; i < n; i += 32) {
+      uint32_t k = 0;
+      if (get(i, &k)) {
+        kmn = min(kmn, k);
+        kmx = max(kmx, k);
+      }
+    }
+    kmn = __reduce_min_sync(0xffffffffu, kmn);
+    kmx = __reduce_max_sync(0xffffffffu, kmx);
+    if (kmn <= kmx) {
+      const int skip = min(__clz(kmn ^ kmx) / 8, 3);  // whole bytes shared
+      start = 24 - 8 * skip;
+      pmask = skip ? (0xffffffffu << (32 - 8 * skip)) : 0u;
+      prefix = kmn & pmask;
+    }
+  }
+  for (int shift = start; shift >= 0; shift -= 8) {
 #pragma unroll
     for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0u;
     __syncwarp();
