@@ -134,7 +134,10 @@ int pick_cluster(const nls_handle* h, int rows, int vocab) {
   }
   int maxc = vocab / 2048;
   if (C > maxc) C = maxc;
-  if (C > 8) C = 8;
+  if (C > 8) {
+    const int big = nls::light_max_cluster(vocab);
+    if (C > big) C = big;
+  }
   if (C < 1) C = 1;
   return C;
 }

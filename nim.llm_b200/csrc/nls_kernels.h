@@ -12,6 +12,9 @@ namespace nls {
 // cluster of C CTAs per row, CTA c owning positions [c*chunk, (c+1)*chunk).
 size_t light_smem_bytes(int C, int chunk);
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream);
+// the largest cluster (CTAs per row) the device schedules for this vocab:
+// 16 where a GPC has room for it, else 8 (checked once per device)
+int light_max_cluster(int V);
 
 // Full-sort kernel over the rows listed in a.full_list (count in a.full_count):
 // `slots` persistent CTAs, each with 4*vpad words of `scratch`.

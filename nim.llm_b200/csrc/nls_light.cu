@@ -44,6 +44,9 @@ constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per threa
 constexpr int LT_CAP = 2048;                          // candidate buffer
 constexpr int LT_LIMIT = LT_CAP / 2;                  // compact above this after a stage
 constexpr int LT_SLOT = LT_LIMIT;                     // candidates a CTA hands to the merge
+constexpr int LT_CMAX = 16;                           // CTAs per row at most (clusters above 8 are non-portable)
+// a CTA's merge slot: halved above 8 CTAs so that CTA 0's merge buffer fits
+__host__ __device__ constexpr int lt_slot(int C) { return C > 8 ? LT_SLOT / 2 : LT_SLOT; }
 constexpr int LT_HASH_LOG2 = 10;
 constexpr int LT_PER_THREAD = LT_CAP / LT_THREADS;
 constexpr int LT_GSHIFT = 2;                          // one patch bit per float4 group
@@ -86,7 +89,7 @@ struct LightShared {
     uint32_t thr;
     float gbest;
     int gidx;
-  } rec[8];
+  } rec[LT_CMAX];
 };
 
 static int bitmap_words_host(int chunk) {
@@ -97,7 +100,7 @@ static int bitmap_words_host(int chunk) {
 
 size_t light_smem_bytes(int C, int chunk) {
   size_t base = (sizeof(LightShared) + 15) & ~(size_t)15;
-  size_t merge = (C > 1) ? (size_t)C * LT_SLOT * (sizeof(uint32_t) + sizeof(int)) : 0;
+  size_t merge = (C > 1) ? (size_t)C * lt_slot(C) * (sizeof(uint32_t) + sizeof(int)) : 0;
   return base + (size_t)bitmap_words_host(chunk) * 4 + merge;
 }
 
@@ -165,7 +168,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
     return (w + 3) & ~3;
   }();
   uint32_t* mkey = bitmap + bm_words;
-  int* midx = reinterpret_cast<int*>(mkey + C * LT_SLOT);
+  const int slot = lt_slot(C);
+  int* midx = reinterpret_cast<int*>(mkey + C * slot);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int crank = (C > 1) ? (int)cg::this_cluster().block_rank() : 0;
@@ -646,10 +650,10 @@ light_kernel(BatchArgs a, int C, int chunk) {
     // Before the merge, keep only this chunk's top K (with all its ties at
     // the K-th key): the row's K-th largest key is at least every chunk's, so
     // nothing at or above it is dropped, and CTA 0 gets ~C*K candidates.
-    if (!overflow && !S.failed && C > 1 && S.ncand > 4 * (int)K) (void)light_compact(S, K);
+    if (!overflow && !S.failed && C > 1 && S.ncand > min(4 * (int)K, slot / 2)) (void)light_compact(S, K);
     __syncthreads();
     if (tid == 0) {
-      if (overflow || bad_patch || (C > 1 && S.ncand > LT_SLOT)) S.overflow = 1;
+      if (overflow || bad_patch || (C > 1 && S.ncand > slot)) S.overflow = 1;
       S.thr_pub = thr;
     }
   } else {
@@ -712,13 +716,13 @@ light_kernel(BatchArgs a, int C, int chunk) {
         gidx = m.gidx;
       }
       if (r == crank) myoff = offs;
-      offs += m.ncand < LT_SLOT ? m.ncand : LT_SLOT;
+      offs += m.ncand < slot ? m.ncand : slot;
     }
     if (mode == kModeTopK && !any_over) {
       // this CTA's candidates go to CTA 0's merge buffer at its offset
       uint32_t* mk0 = cluster.map_shared_rank(mkey, 0);
       int* mi0 = cluster.map_shared_rank(midx, 0);
-      const int ncopy = S.ncand < LT_SLOT ? S.ncand : LT_SLOT;
+      const int ncopy = S.ncand < slot ? S.ncand : slot;
       for (int i = tid; i < ncopy; i += LT_THREADS) {
         mk0[myoff + i] = S.cand_key[i];
         mi0[myoff + i] = S.cand_idx[i];
@@ -957,6 +961,44 @@ light_kernel(BatchArgs a, int C, int chunk) {
 }
 
 static std::atomic<int> g_light_smem_set[kMaxDevicesAttr];
+
+static std::atomic<int> g_light_big_cluster[kMaxDevicesAttr];  // 0 unknown, 1 no, 2 yes
+
+// Clusters of more than 8 CTAs need the non-portable size allowed, and room
+// on one GPC for 16 CTAs of this size; answered once per device.
+int light_max_cluster(int V) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevicesAttr) return 8;
+  const int known = g_light_big_cluster[dev].load(std::memory_order_relaxed);
+  if (known) return known == 2 ? LT_CMAX : 8;
+  int ok = 1;
+  const int chunk = ((V + LT_CMAX - 1) / LT_CMAX + 3) & ~3;
+  const size_t smem = light_smem_bytes(LT_CMAX, chunk);
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(light_kernel),
+                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+      ensure_smem_attr(reinterpret_cast<const void*>(light_kernel), (int)smem, g_light_smem_set) ==
+          cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(LT_CMAX, 1, 1);
+    cfg.blockDim = dim3(LT_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = LT_CMAX;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(light_kernel), &cfg) ==
+            cudaSuccess &&
+        n >= 1)
+      ok = 2;
+  }
+  (void)cudaGetLastError();
+  g_light_big_cluster[dev].store(ok, std::memory_order_relaxed);
+  return ok == 2 ? LT_CMAX : 8;
+}
 
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream) {
   const size_t smem = light_smem_bytes(C, chunk);

@@ -327,6 +327,21 @@ def test_host_path_matches_device_path(pkg, big_engine, layout):
     assert np.array_equal(out_probs.cpu().numpy(), probs_h)
 
 
+@pytest.mark.parametrize("B", [1, 2, 5, 9])
+def test_small_batches_wide_clusters(pkg, big_engine, oracle_mod, B):
+    """A few rows of a large vocabulary: each row is split over up to 16 CTAs
+    of a cluster (8 where the device cannot schedule 16), whose candidates
+    merge in CTA 0; top-k from 1 to 256, with penalties and bias."""
+    w = pkg.workloads.make("c3_batched_hetero", seed=30 + B, rows=np.arange(B), V=128256)
+    a = as_args(w)
+    P = a["params"].copy()
+    P["top_k"] = np.array([40, 256, 1, 100, 7, 255, 64, 200, 3])[:B]
+    a["params"] = P
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a)
+    assert st == 0
+    compare(ids, probs, ref, dg, P, f"B={B}")
+
+
 def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     """More rows than SMs: the full-sort kernel runs as cluster pairs that
     share the first phase of their first row (each CTA one half of the row)."""
