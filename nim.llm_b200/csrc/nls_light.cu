@@ -1,6 +1,6 @@
 // nls_light.cu -- streaming kernel for greedy rows and top-k rows (k <= 256).
 //
-// One thread-block cluster per row (cluster size C = 1..8). CTA c owns the
+// One thread-block cluster per row (cluster size C = 1..16). CTA c owns the
 // chunk [c*chunk, (c+1)*chunk) of the row and reads it from HBM exactly once:
 // one thread issues bulk copies (cp.async.bulk, 16 KB stages, LT_NSTAGE in
 // flight, mbarrier completion) into a shared-memory ring while the block
