@@ -9,6 +9,8 @@ Bar:
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -359,6 +361,39 @@ def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     assert st2 == 5 and ids2[full[0]] == -1
     keep = np.arange(300) != full[0]
     assert np.array_equal(ids2[keep], ids[keep])
+
+
+def test_two_handles_on_two_streams_concurrently(pkg):
+    """Several samplers served at once (one handle per stream): two batches
+    in flight on two streams give the results each gives alone."""
+    import torch
+    dev = torch.device("cuda:0")
+    t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    ws = [pkg.workloads.make("c3_batched_hetero", seed=40 + i, rows=np.arange(64), V=128256)
+          for i in range(2)]
+    engs = [pkg.Engine(0, max_rows=64, max_vocab=128256) for _ in range(2)]
+    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    args = []
+    for w in ws:
+        args.append((t(w.logits), torch.from_numpy(w.params.view(np.uint8).copy()).to(dev),
+                     t(w.hist_ids), t(w.hist_off), t(w.bias_ids), t(w.bias_vals), t(w.bias_off),
+                     t(w.uniforms)))
+    torch.cuda.synchronize()
+    alone = []
+    for e, s, a in zip(engs, streams, args):
+        out = torch.empty(64, dtype=torch.int64, device=dev)
+        e.sample_batch(*a, out_ids=out, stream=s.cuda_stream)
+        s.synchronize()
+        alone.append(out.cpu().numpy())
+    outs = [torch.empty(64, dtype=torch.int64, device=dev) for _ in range(2)]
+    for rep in range(3):
+        for e, s, a, o in zip(engs, streams, args, outs):  # both in flight
+            e.sample_batch(*a, out_ids=o, stream=s.cuda_stream, check=False)
+        for e, s, o, want in zip(engs, streams, outs, alone):
+            assert e._lib.nls_stream_status(e._h, ctypes.c_void_p(s.cuda_stream)) == 0
+            assert np.array_equal(o.cpu().numpy(), want)
+    for e in engs:
+        e.close()
 
 
 def test_repeat_calls_are_deterministic(pkg, big_engine):
