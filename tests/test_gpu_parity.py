@@ -363,6 +363,22 @@ def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     assert np.array_equal(ids2[keep], ids[keep])
 
 
+def test_pair_rows_with_repeated_values(pkg, big_engine, oracle_mod):
+    """More rows than SMs, the first full-path rows made of three distinct
+    values: a bucket overflows, and the pair's CTA 0 radix-sorts the row
+    alone after the shared transform."""
+    w = pkg.workloads.make("c3_batched_hetero", seed=50, rows=np.arange(200), V=20000)
+    a = as_args(w)
+    a["logits"] = a["logits"].copy()
+    full = np.nonzero((a["params"]["top_k"] <= 0) | (a["params"]["top_k"] > 256))[0]
+    rng = np.random.default_rng(51)
+    for r in full[:20]:
+        a["logits"][r] = rng.integers(0, 3, 20000).astype(np.float32)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a)
+    assert st == 0
+    compare(ids, probs, ref, dg, a["params"], "repeated values")
+
+
 def test_two_handles_on_two_streams_concurrently(pkg):
     """Several samplers served at once (one handle per stream): two batches
     in flight on two streams give the results each gives alone."""
