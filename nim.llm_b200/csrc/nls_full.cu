@@ -762,6 +762,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     auto sort_window = [&](int c) {
       const int bA = S.wbkt[c], bB = S.wbkt[c + 1], ws = S.wstart[c], we = S.wstart[c + 1];
       const int n = we - ws;
+      // a thread may still read the previous window's exact t (u.big, e.g.
+      // the absorption check after a replay) while another starts here
+      __syncthreads();
       if (n > 1) {
         const int F = FT_NB2 / max(1, bB - bA);  // fine buckets per coarse bucket
         auto fine = [&](uint32_t kdv) {
