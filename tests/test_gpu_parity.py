@@ -363,6 +363,31 @@ def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     assert np.array_equal(ids2[keep], ids[keep])
 
 
+@pytest.mark.parametrize("seed", range(100, 108))
+def test_seed_sweep(pkg, big_engine, oracle_mod, seed):
+    """Fresh seeds over three launch shapes: config 3 as benched (claiming
+    full-sort CTAs beside the streaming kernel), 300 rows of a ragged
+    vocabulary (cluster pairs), and 1..9 rows of 128256 with top-k drawn
+    from 1..256 (wide clusters)."""
+    w = pkg.workloads.make("c3_batched_hetero", seed=seed)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(w), threads=16)
+    assert st == 0
+    compare(ids, probs, ref, dg, w.params, f"c3 seed {seed}")
+    w = pkg.workloads.make("c3_batched_hetero", seed=seed, rows=np.arange(300), V=20000 + seed)
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, as_args(w), threads=16)
+    assert st == 0
+    compare(ids, probs, ref, dg, w.params, f"B=300 seed {seed}")
+    B = 1 + seed % 9
+    w = pkg.workloads.make("c3_batched_hetero", seed=seed, rows=np.arange(B), V=128256)
+    a = as_args(w)
+    P = a["params"].copy()
+    P["top_k"] = np.random.default_rng(seed).integers(1, 257, B)
+    a["params"] = P
+    ids, probs, st, ref, dg = run_both(big_engine, oracle_mod, a, threads=16)
+    assert st == 0
+    compare(ids, probs, ref, dg, P, f"B={B} seed {seed}")
+
+
 def test_pair_rows_with_repeated_values(pkg, big_engine, oracle_mod):
     """More rows than SMs, the first full-path rows made of three distinct
     values: a bucket overflows, and the pair's CTA 0 radix-sorts the row
