@@ -207,6 +207,58 @@ NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld,
                                  int32_t vocab, const int64_t* targets, double* out_nll,
                                  uint32_t flags, void* stream);
 
+/* ---- output projection ----------------------------------------------------
+ * The matmul that produces the sampler's logits, matmul(m.output, xb, logits,
+ * nb) (model.nim:466-470 -> :179-189, row task :144-169), computed on the GPU
+ * bit for bit: the same path choice (int8 activations by default, the float
+ * path under exactMatmul), the same integer block products and the same fp32
+ * rounding order per output. No LoRA (the reference adds LoRA after the
+ * projection, model.nim:190-195). */
+
+/* ggml weight types accepted (GgmlType codes, quant.nim:14-19) */
+#define NLS_WT_F32 0
+#define NLS_WT_F16 1
+#define NLS_WT_Q4_0 2
+#define NLS_WT_Q8_0 8
+#define NLS_WT_Q6_K 14
+/* flag: the reference's `exactMatmul = true` (model.nim:173): float path
+ * (dequantRow + dotF32) for every weight type */
+#define NLS_EXACT_MATMUL 4u
+
+/* y[b*rows + r] = weight row r . x[b*cols ..] for b < nb (matmul, model.nim:179).
+ *  weights  device memory of the handle's device, 16-byte aligned: `rows`
+ *           rows of `cols` values in the ggml layout of `wtype` (rowBytes,
+ *           quant.nim:65-71), rows back to back (QMatrix.data, model.nim:88)
+ *  x        [nb x cols] fp32 activations (the normalised hidden state)
+ *  y        [nb x rows] fp32
+ * Path, as model.nim:185: with int8 activations (quantizeAct per block of 32,
+ * or 256 for Q6_K, then integer block dot products) unless NLS_EXACT_MATMUL
+ * is set, the type is F32/F16, or the type is Q8_0 and nb > 4; otherwise
+ * dequantised weights and the eight-accumulator fp32 dot product.
+ * cols must be a whole number of blocks (32 for Q4_0/Q8_0, 256 for Q6_K) and
+ * at most 16384 for F32/F16. Non-finite activations on the int8 path give
+ * NLS_ERR_NAN_LOGITS (the reference's int8 conversion of them is undefined).
+ * Flags: NLS_DEVICE_INPUTS (x), NLS_DEVICE_OUTPUTS (y), NLS_EXACT_MATMUL. */
+NLS_API nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
+                               int32_t cols, const float* x, int32_t nb, float* y,
+                               uint32_t flags, void* stream);
+
+/* The output projection followed by sampling, the two steps of one decode
+ * step's tail (model.nim:466-470, then Sampler.sample, sampler.nim:59-121):
+ * logits = nls_lm_head(weights, wtype, vocab, cols, x, rows) stay in the
+ * handle's device memory (never copied to the host) and nls_sample_batch
+ * samples them with the given params, histories, bias and uniforms.
+ * Flags and outputs as nls_sample_batch (NLS_DEVICE_INPUTS covers x and the
+ * sampling inputs; weights are always device memory), plus NLS_EXACT_MATMUL.
+ * rows <= the handle's max_rows, vocab <= its max_vocab. */
+NLS_API nls_status nls_lm_head_sample(nls_handle* h, const void* weights, int32_t wtype,
+                                      int32_t vocab, int32_t cols, const float* x, int32_t rows,
+                                      const nls_row_params* params, const int64_t* hist_ids,
+                                      const int64_t* hist_off, const int64_t* bias_ids,
+                                      const double* bias_vals, const int64_t* bias_off,
+                                      const double* uniforms, int64_t* out_ids, float* out_probs,
+                                      uint32_t flags, void* stream);
+
 /* Per-kernel timing of later calls on this handle (tracing; no counterpart
  * in the reference, which only times whole generations with epochTime,
  * chat.nim:191,246-247). With `on` set, every sampling call records CUDA

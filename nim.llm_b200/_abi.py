@@ -32,8 +32,12 @@ EXPORTS = (
     "nls_stream_status", "nls_status_str", "nls_last_error", "nls_version",
     "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
     "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
-    "nls_top_tokens", "nls_token_nll",
+    "nls_top_tokens", "nls_token_nll", "nls_lm_head", "nls_lm_head_sample",
 )
+
+# ggml weight types of nls_lm_head (GgmlType codes, quant.nim:14-19)
+NLS_WT = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q6_k": 14}
+NLS_EXACT_MATMUL = 4
 
 # nls_row_params: 6 doubles + 2 int64, 64 bytes, no padding.
 ROW_PARAMS_DTYPE = np.dtype([
@@ -91,6 +95,11 @@ def load(path: str | None = None):
     L.nls_top_tokens.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, u32, vp]
     L.nls_token_nll.restype = i32
     L.nls_token_nll.argtypes = [vp, vp, i64, i32, i32, vp, vp, u32, vp]
+    L.nls_lm_head.restype = i32
+    L.nls_lm_head.argtypes = [vp, vp, i32, i32, i32, vp, i32, vp, u32, vp]
+    L.nls_lm_head_sample.restype = i32
+    L.nls_lm_head_sample.argtypes = [vp, vp, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp,
+                                     vp, u32, vp]
     _lib = L
     return L
 

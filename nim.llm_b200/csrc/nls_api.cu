@@ -70,6 +70,13 @@ struct nls_handle {
   size_t tgt_cap = 0;
   double* d_nll = nullptr;
   size_t nll_cap = 0;
+  // output projection: staged activations, host-output logits, int8 activations
+  float* d_lmx = nullptr;
+  size_t lmx_cap = 0;
+  float* d_lmy = nullptr;
+  size_t lmy_cap = 0;
+  uint8_t* d_lmact = nullptr;
+  size_t lmact_cap = 0;
   char last_err[256] = {0};
 };
 
@@ -151,14 +158,20 @@ constexpr int kMaxRanks = 64;
 // kernel handed back (ties or thresholds it could not settle; usually none).
 // Batches of at most kSmallBatch rows run the two kernels one after the
 // other instead (the fork/join costs more than the overlap gains).
-nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st) {
+// keep_status: d_work[0] already holds the status of an earlier kernel of
+// the same call (the output projection), which must survive.
+nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st,
+                     bool keep_status = false) {
   nls::BatchArgs a = a_in;
   a.status = h->d_work;
   a.full_count = h->d_work + 1;
   a.full_list = h->d_work + 4;
   a.row_claim = nullptr;
   a.skip_full = 0;
-  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, 4 * sizeof(int), st));
+  if (keep_status)
+    NLS_CUDA(h, cudaMemsetAsync(h->d_work + 1, 0, 3 * sizeof(int), st));
+  else
+    NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, 4 * sizeof(int), st));
   const int C = pick_cluster(h, a.rows, a.V);
   int chunk = (a.V + C - 1) / C;
   chunk = (chunk + 3) & ~3;
@@ -256,6 +269,9 @@ void nls_destroy(nls_handle* h) {
     if (h->h_sh_status) cudaFreeHost(h->h_sh_status);
     cudaFree(h->d_tgt);
     cudaFree(h->d_nll);
+    cudaFree(h->d_lmx);
+    cudaFree(h->d_lmy);
+    cudaFree(h->d_lmact);
     if (h->fork) cudaEventDestroy(h->fork);
     if (h->join) cudaEventDestroy(h->join);
     for (cudaEvent_t e : h->ev)
@@ -324,23 +340,20 @@ nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_
   return NLS_OK;
 }
 
-nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
-                            int32_t vocab, const nls_row_params* params,
-                            const int64_t* hist_ids, const int64_t* hist_off,
-                            const int64_t* bias_ids, const double* bias_vals,
-                            const int64_t* bias_off, const double* uniforms, int64_t* out_ids,
-                            float* out_probs, uint32_t flags, void* stream) {
-  if (!h) return NLS_ERR_INVALID_ARG;
-  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
-  if (rows < 0 || vocab < 1 || ld < vocab) return NLS_ERR_INVALID_ARG;
-  if (rows == 0) return NLS_OK;
-  if (!logits || !params || !out_ids) return NLS_ERR_INVALID_ARG;
-  if ((hist_ids == nullptr) != (hist_off == nullptr)) return NLS_ERR_INVALID_ARG;
-  if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
-    return NLS_ERR_INVALID_ARG;
-  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
-  DeviceGuard g(h->device);
-  cudaStream_t st = (cudaStream_t)stream;
+}  // extern "C"
+
+namespace {
+
+// nls_sample_batch after its argument checks. logits_dev: the logits are
+// device memory even when the other inputs are host memory (the output
+// projection wrote them); keep_status as run_batch.
+nls_status sample_impl(nls_handle* h, const float* logits, int64_t ld, bool logits_dev,
+                       bool keep_status, int32_t rows, int32_t vocab,
+                       const nls_row_params* params, const int64_t* hist_ids,
+                       const int64_t* hist_off, const int64_t* bias_ids,
+                       const double* bias_vals, const int64_t* bias_off,
+                       const double* uniforms, int64_t* out_ids, float* out_probs,
+                       uint32_t flags, cudaStream_t st) {
   const bool dev_in = (flags & NLS_DEVICE_INPUTS) != 0;
   const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
 
@@ -360,14 +373,19 @@ nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int3
     a.uniforms = uniforms;
   } else {
     nls_status s;
-    if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
-    NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
-                                  (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
-                                  cudaMemcpyHostToDevice, st));
+    if (logits_dev) {
+      a.logits = logits;
+      a.ld = ld;
+    } else {
+      if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+      NLS_CUDA(h, cudaMemcpy2DAsync(h->d_logits, (size_t)vocab * sizeof(float), logits,
+                                    (size_t)ld * sizeof(float), (size_t)vocab * sizeof(float), rows,
+                                    cudaMemcpyHostToDevice, st));
+      a.logits = h->d_logits;
+      a.ld = vocab;
+    }
     NLS_CUDA(h, cudaMemcpyAsync(h->d_params, params, sizeof(nls_row_params) * rows,
                                 cudaMemcpyHostToDevice, st));
-    a.logits = h->d_logits;
-    a.ld = vocab;
     a.params = h->d_params;
     if (uniforms) {
       NLS_CUDA(h, cudaMemcpyAsync(h->d_uniforms, uniforms, sizeof(double) * rows,
@@ -402,7 +420,7 @@ nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int3
   }
   a.out_ids = dev_out ? out_ids : h->d_out_ids;
   a.out_probs = dev_out ? out_probs : (out_probs ? h->d_out_probs : nullptr);
-  nls_status s = run_batch(h, a, flags, st);
+  nls_status s = run_batch(h, a, flags, st, keep_status);
   if (s != NLS_OK) return s;
   if (dev_out) return NLS_OK;
   NLS_CUDA(h, cudaMemcpyAsync(out_ids, h->d_out_ids, sizeof(int64_t) * rows, cudaMemcpyDeviceToHost, st));
@@ -410,6 +428,116 @@ nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int3
     NLS_CUDA(h, cudaMemcpyAsync(out_probs, h->d_out_probs, sizeof(float) * rows, cudaMemcpyDeviceToHost, st));
   NLS_CUDA(h, cudaStreamSynchronize(st));
   return (nls_status)*h->h_status;
+}
+
+// Output projection into dy [nb x rows] (device) from x (host or device per
+// x_dev); the kernel status goes to d_work[0], which the caller has cleared.
+nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
+                        int32_t cols, const float* x, bool x_dev, int32_t nb, float* dy,
+                        bool exact, cudaStream_t st) {
+  nls_status s;
+  const float* dx = x;
+  if (!x_dev) {
+    if ((s = grow(h, &h->d_lmx, &h->lmx_cap, (size_t)nb * cols)) != NLS_OK) return s;
+    NLS_CUDA(h, cudaMemcpyAsync(h->d_lmx, x, sizeof(float) * (size_t)nb * cols, cudaMemcpyHostToDevice, st));
+    dx = h->d_lmx;
+  }
+  if ((s = grow(h, &h->d_lmact, &h->lmact_cap, nls::lm_head_act_scratch(wtype, cols, nb))) != NLS_OK)
+    return s;
+  NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb, dy,
+                                  exact, h->d_lmact, h->d_work, h->sm_count, st));
+  return NLS_OK;
+}
+
+bool lm_head_args_ok(const void* weights, int32_t wtype, int32_t rows, int32_t cols) {
+  int64_t rb = 0;
+  if (!weights || (reinterpret_cast<uintptr_t>(weights) & 15) != 0) return false;
+  if (rows < 1 || cols < 1 || !nls::lm_head_row_bytes(wtype, cols, &rb)) return false;
+  // the float path keeps a batch row of x in shared memory
+  return (wtype != 0 && wtype != 1) || cols <= 16384;
+}
+
+}  // namespace
+
+extern "C" {
+
+nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
+                            int32_t vocab, const nls_row_params* params,
+                            const int64_t* hist_ids, const int64_t* hist_off,
+                            const int64_t* bias_ids, const double* bias_vals,
+                            const int64_t* bias_off, const double* uniforms, int64_t* out_ids,
+                            float* out_probs, uint32_t flags, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0 || vocab < 1 || ld < vocab) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!logits || !params || !out_ids) return NLS_ERR_INVALID_ARG;
+  if ((hist_ids == nullptr) != (hist_off == nullptr)) return NLS_ERR_INVALID_ARG;
+  if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
+    return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  return sample_impl(h, logits, ld, (flags & NLS_DEVICE_INPUTS) != 0, false, rows, vocab, params,
+                     hist_ids, hist_off, bias_ids, bias_vals, bias_off, uniforms, out_ids,
+                     out_probs, flags, (cudaStream_t)stream);
+}
+
+nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
+                       int32_t cols, const float* x, int32_t nb, float* y, uint32_t flags,
+                       void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL)) return NLS_ERR_INVALID_ARG;
+  if (nb < 0 || rows < 0) return NLS_ERR_INVALID_ARG;
+  if (nb == 0 || rows == 0) return NLS_OK;
+  if (!x || !y || !lm_head_args_ok(weights, wtype, rows, cols)) return NLS_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool dev_out = (flags & NLS_DEVICE_OUTPUTS) != 0;
+  nls_status s;
+  float* dy = y;
+  if (!dev_out) {
+    if ((s = grow(h, &h->d_lmy, &h->lmy_cap, (size_t)nb * rows)) != NLS_OK) return s;
+    dy = h->d_lmy;
+  }
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
+  if ((s = lm_head_impl(h, weights, wtype, rows, cols, x, (flags & NLS_DEVICE_INPUTS) != 0, nb, dy,
+                        (flags & NLS_EXACT_MATMUL) != 0, st)) != NLS_OK)
+    return s;
+  if (dev_out) return NLS_OK;
+  NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaMemcpyAsync(y, dy, sizeof(float) * (size_t)nb * rows, cudaMemcpyDeviceToHost, st));
+  NLS_CUDA(h, cudaStreamSynchronize(st));
+  return (nls_status)*h->h_status;
+}
+
+nls_status nls_lm_head_sample(nls_handle* h, const void* weights, int32_t wtype, int32_t vocab,
+                              int32_t cols, const float* x, int32_t rows,
+                              const nls_row_params* params, const int64_t* hist_ids,
+                              const int64_t* hist_off, const int64_t* bias_ids,
+                              const double* bias_vals, const int64_t* bias_off,
+                              const double* uniforms, int64_t* out_ids, float* out_probs,
+                              uint32_t flags, void* stream) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL)) return NLS_ERR_INVALID_ARG;
+  if (rows < 0) return NLS_ERR_INVALID_ARG;
+  if (rows == 0) return NLS_OK;
+  if (!x || !params || !out_ids || !lm_head_args_ok(weights, wtype, vocab, cols))
+    return NLS_ERR_INVALID_ARG;
+  if ((hist_ids == nullptr) != (hist_off == nullptr)) return NLS_ERR_INVALID_ARG;
+  if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
+    return NLS_ERR_INVALID_ARG;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
+  DeviceGuard g(h->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  nls_status s;
+  if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
+  NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
+  if ((s = lm_head_impl(h, weights, wtype, vocab, cols, x, (flags & NLS_DEVICE_INPUTS) != 0, rows,
+                        h->d_logits, (flags & NLS_EXACT_MATMUL) != 0, st)) != NLS_OK)
+    return s;
+  return sample_impl(h, h->d_logits, vocab, true, true, rows, vocab, params, hist_ids, hist_off,
+                     bias_ids, bias_vals, bias_off, uniforms, out_ids, out_probs,
+                     flags & ~NLS_EXACT_MATMUL, st);
 }
 
 nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,

@@ -1,0 +1,592 @@
+// nls_lmhead.cu -- the output projection that produces the sampler's logits:
+// matmul(m.output, xb, logits, nb) (model.nim:466-470 -> :179-189, row task
+// :144-169), bit for bit.
+//
+// The reference computes, per output row r and batch row b, one dot product
+// whose fp32 rounding order is fixed by the code:
+//  * int8 activation path (the default; quantizeAct quant.nim:646-662 with
+//    dotQ8_0i / dotQ4_0i / dotQ6K quant.nim:731-786): per weight block an
+//    exact integer dot product, then acc += (d_w * d_a) * float(sumi) block
+//    after block (Q6_K: (d_a * d_w) * float(sumi));
+//  * float path (exactMatmul, Q8_0 with more than 4 batch rows, F32/F16):
+//    dequantRow then dotF32 (quant.nim:362-374): eight strided fp32
+//    accumulators combined as ((s0+s1) + (s2+s3)) + (s4+s5)) + (s6+s7).
+// Both are HBM-bound on the weights (one pass over rows x rowBytes per call at
+// small batch). The kernel streams row tiles of the weights through a ring of
+// shared-memory slots with cp.async.bulk (no multicast) and:
+//  * int8 path: warps 1.. compute every block term of a tile in parallel
+//    (dp4a on the packed int8 values) into a shared-memory table; warp 0 then
+//    replays each (row, batch) sum in block order, one lane per sum, while the
+//    other warps already work on the next tile;
+//  * float path: one lane per (row, batch, accumulator) walks its strided
+//    elements in order, dequantising on the fly.
+// Everything is exact fp32 arithmetic in the reference's order: the library
+// is built with -fmad=false, so no multiply-add is fused.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "nls_kernels.h"
+#include "nls_tma.cuh"
+
+namespace nls {
+
+namespace {
+
+constexpr int kLmhThreads = 256;
+constexpr int kLmhMaxChains = 32;     // int8 path: one warp replays the sums
+constexpr int kLmhSlotTarget = 48 * 1024;
+constexpr int kLmhSmemMax = 226 * 1024;  // the kernel also has static shared variables
+
+struct LmhArgs {
+  const uint8_t* w;  // rows x row_bytes, 16-byte aligned
+  int64_t row_bytes;
+  int rows, cols;
+  int nblk;          // weight blocks per row (int8 path)
+  int nb;            // batch rows of this launch
+  const int8_t* aq;  // int8 path: [nb x cols] quantised activations of this launch
+  const float* ad;   //            [nb x cols/bl] their scales
+  const float* x;    // float path: [nb x cols]
+  float* y;          // y[b * ldy + r]
+  int64_t ldy;
+  int R;             // rows per tile
+  int ntiles;
+  int slot_bytes;    // one ring slot (multiple of 16)
+  int nst;           // ring slots
+  int padded;        // 1: row i of a tile at slot + i*pitch; 0: one contiguous copy
+  int pitch;
+  int act_bytes;     // shared bytes of the activation region (multiple of 16)
+  int tpitch;        // int8 path: floats per sum in the term table (odd)
+  int* status;
+};
+
+__device__ __forceinline__ void set_status(int* st, int code) { atomicCAS(st, 0, code); }
+
+// Bytes [p, p + 4n) of shared memory as n 32-bit words, p 2-byte aligned.
+// Reads one aligned word past the end (the caller keeps that inside the
+// CTA's shared memory).
+template <int N>
+__device__ __forceinline__ void ld_words(const uint8_t* p, uint32_t (&out)[N]) {
+  const uint32_t* a = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+  const uint32_t sel = (reinterpret_cast<uintptr_t>(p) & 2) ? 0x5432u : 0x3210u;
+  uint32_t prev = a[0];
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const uint32_t next = a[k + 1];
+    out[k] = __byte_perm(prev, next, sel);
+    prev = next;
+  }
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
+}
+
+// ---- int8 path: one block term per (row, block) for every batch row ---------
+
+// dotQ8_0i (quant.nim:762-772): s = sum of 32 int8 products, term = (dw * da) * float(s)
+template <int NB>
+__device__ __forceinline__ void terms_q8_0(const uint8_t* blk, int ib, const LmhArgs& a,
+                                           const int32_t* aqw, const float* ad, float* T, int tp) {
+  uint32_t W[9];
+  ld_words<9>(blk, W);
+  const float dw = half_bits_to_float(W[0]);
+  int q[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = (int)__byte_perm(W[k], W[k + 1], 0x5432);
+  const int wpb = a.cols >> 2;  // activation words per batch row
+  const int apb = a.cols >> 5;  // activation blocks per batch row
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= a.nb) break;
+    const int32_t* av = aqw + b * wpb + ib * 8;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = __dp4a(q[k], av[k], s);
+    T[b * tp] = (dw * ad[b * apb + ib]) * __int2float_rn(s);
+  }
+}
+
+// dotQ4_0i (quant.nim:774-786): nibbles minus 8 against a[l] and a[l + 16]
+template <int NB>
+__device__ __forceinline__ void terms_q4_0(const uint8_t* blk, int ib, const LmhArgs& a,
+                                           const int32_t* aqw, const float* ad, float* T, int tp) {
+  uint32_t W[5];
+  ld_words<5>(blk, W);
+  const float dw = half_bits_to_float(W[0]);
+  int lo[4], hi[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t q = __byte_perm(W[k], W[k + 1], 0x5432);
+    lo[k] = (int)__vsub4(q & 0x0F0F0F0Fu, 0x08080808u);
+    hi[k] = (int)__vsub4((q >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+  }
+  const int wpb = a.cols >> 2;
+  const int apb = a.cols >> 5;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= a.nb) break;
+    const int32_t* av = aqw + b * wpb + ib * 8;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s = __dp4a(lo[k], av[k], s);
+      s = __dp4a(hi[k], av[4 + k], s);
+    }
+    T[b * tp] = (dw * ad[b * apb + ib]) * __int2float_rn(s);
+  }
+}
+
+// dotQ6K (quant.nim:731-760): ql[128] qh[64] int8 scales[16] d at 208
+template <int NB>
+__device__ __forceinline__ void terms_q6_k(const uint8_t* blk, int ib, const LmhArgs& a,
+                                           const int32_t* aqw, const float* ad, float* T, int tp) {
+  uint32_t SC[4], DW[1];
+  ld_words<4>(blk + 192, SC);
+  ld_words<1>(blk + 208, DW);
+  const float dw = half_bits_to_float(DW[0]);
+  const int wpb = a.cols >> 2;
+  const int apb = a.cols >> 8;
+  int sumi[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) sumi[b] = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t QA[4], QB[4], QH[4];
+      ld_words<4>(blk + 64 * h + 16 * half, QA);
+      ld_words<4>(blk + 64 * h + 32 + 16 * half, QB);
+      ld_words<4>(blk + 128 + 32 * h + 16 * half, QH);
+      int q1[4], q2[4], q3[4], q4[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t hq = QH[k];
+        q1[k] = (int)__vsub4((QA[k] & 0x0F0F0F0Fu) | ((hq & 0x03030303u) << 4), 0x20202020u);
+        q2[k] = (int)__vsub4((QB[k] & 0x0F0F0F0Fu) | (((hq >> 2) & 0x03030303u) << 4), 0x20202020u);
+        q3[k] = (int)__vsub4(((QA[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 4) & 0x03030303u) << 4), 0x20202020u);
+        q4[k] = (int)__vsub4(((QB[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 6) & 0x03030303u) << 4), 0x20202020u);
+      }
+      const int so = 8 * h + half;
+      const int sc0 = (int)(int8_t)(SC[so >> 2] >> (8 * (so & 3)));
+      const int sc1 = (int)(int8_t)(SC[(so + 2) >> 2] >> (8 * ((so + 2) & 3)));
+      const int sc2 = (int)(int8_t)(SC[(so + 4) >> 2] >> (8 * ((so + 4) & 3)));
+      const int sc3 = (int)(int8_t)(SC[(so + 6) >> 2] >> (8 * ((so + 6) & 3)));
+      const int w0 = (128 * h + 16 * half) >> 2;  // activation word of l = 16*half
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b >= a.nb) break;
+        const int32_t* av = aqw + b * wpb + ib * 64 + w0;
+        int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          s0 = __dp4a(q1[k], av[k], s0);
+          s1 = __dp4a(q2[k], av[8 + k], s1);
+          s2 = __dp4a(q3[k], av[16 + k], s2);
+          s3 = __dp4a(q4[k], av[24 + k], s3);
+        }
+        sumi[b] += sc0 * s0 + sc1 * s1 + sc2 * s2 + sc3 * s3;
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= a.nb) break;
+    T[b * tp] = (ad[b * apb + ib] * dw) * __int2float_rn(sumi[b]);
+  }
+}
+
+// ---- float path: dequantised element e of a row (dequantRow, quant.nim:336-352)
+template <int WT>
+__device__ __forceinline__ float wval(const uint8_t* row, int e) {
+  if constexpr (WT == 0) {
+    return reinterpret_cast<const float*>(row)[e];
+  } else if constexpr (WT == 1) {
+    return half_bits_to_float(reinterpret_cast<const uint16_t*>(row)[e]);
+  } else if constexpr (WT == 8) {
+    const uint8_t* b = row + (e >> 5) * 34;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
+    return (float)(int)(int8_t)b[2 + (e & 31)] * d;
+  } else if constexpr (WT == 2) {
+    const uint8_t* b = row + (e >> 5) * 18;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b));
+    const int j = e & 31;
+    const uint8_t q = b[2 + (j & 15)];
+    const int v = (j < 16 ? (q & 0xF) : (q >> 4)) - 8;
+    return (float)v * d;
+  } else {  // Q6_K
+    const uint8_t* b = row + (e >> 8) * 210;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b + 208));
+    const int j = e & 255;
+    const int n = j >> 7, jj = j & 127, qd = jj >> 5, l = jj & 31;
+    const uint8_t lb = b[64 * n + l + 32 * (qd & 1)];
+    const uint8_t hb = b[128 + 32 * n + l];
+    const int q = (int)(((qd >= 2) ? (lb >> 4) : (lb & 0xF)) | (((hb >> (2 * qd)) & 3) << 4)) - 32;
+    const float sc = (float)(int)(int8_t)b[192 + 8 * n + (l >> 4) + 2 * qd];
+    return (d * sc) * (float)q;
+  }
+}
+
+// ---- the kernel ------------------------------------------------------------
+
+struct RingPos {
+  int slot;
+  uint32_t parity;
+};
+
+__device__ __forceinline__ RingPos ring_pos(int k, int nst) {
+  return RingPos{k % nst, (uint32_t)((k / nst) & 1)};
+}
+
+// Thread 0: start the copy of tile t into ring slot `slot`.
+__device__ __forceinline__ void issue_tile(const LmhArgs& a, int t, uint8_t* slot, uint64_t* bar) {
+  const int r0 = t * a.R;
+  const int nr = min(a.R, a.rows - r0);
+  if (a.padded) {
+    const uint32_t rb = (uint32_t)a.row_bytes;
+    mbar_arrive_expect_tx(bar, rb * (uint32_t)nr);
+    for (int i = 0; i < nr; ++i)
+      bulk_copy_g2s(slot + (size_t)i * a.pitch, a.w + (size_t)(r0 + i) * a.row_bytes, rb, bar);
+    return;
+  }
+  // one copy of [start & ~15, end rounded up), never past the last whole
+  // 16 bytes of the weights; the few bytes after those go by plain loads
+  const int64_t start = (int64_t)r0 * a.row_bytes;
+  const int64_t end = start + (int64_t)nr * a.row_bytes;
+  const int64_t lo = start & ~int64_t(15);
+  const int64_t last16 = ((int64_t)a.rows * a.row_bytes) & ~int64_t(15);
+  int64_t hi = (end + 15) & ~int64_t(15);
+  if (hi > last16) hi = last16;
+  if (hi < lo) hi = lo;
+  for (int64_t g = max(hi, start); g < end; ++g) slot[g - lo] = a.w[g];
+  mbar_arrive_expect_tx(bar, (uint32_t)(hi - lo));
+  if (hi > lo) bulk_copy_g2s(slot, a.w + lo, (uint32_t)(hi - lo), bar);
+}
+
+__device__ __forceinline__ const uint8_t* tile_row(const LmhArgs& a, const uint8_t* slot, int t, int i) {
+  if (a.padded) return slot + (size_t)i * a.pitch;
+  const int64_t start = (int64_t)t * a.R * a.row_bytes;
+  return slot + (start & 15) + (size_t)i * a.row_bytes;
+}
+
+// WT: ggml type; EXACT: float path; NB: batch rows compiled for (a.nb <= NB)
+template <int WT, bool EXACT, int NB>
+__global__ void __launch_bounds__(kLmhThreads, 1) lmh_kernel(const LmhArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint8_t* act = ring + (size_t)a.nst * a.slot_bytes;
+  float* terms = reinterpret_cast<float*>(act + a.act_bytes);
+  const int tchains = EXACT ? 0 : a.R * a.nb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      reinterpret_cast<uint8_t*>(terms) + (size_t)2 * tchains * a.tpitch * sizeof(float) + 16);
+  full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
+  __shared__ int s_timeout;
+  __shared__ int s_issued;  // tiles whose copies were started
+
+  const int tid = threadIdx.x;
+  const int my_tiles = (a.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  if (tid == 0) {
+    s_timeout = 0;
+    for (int s = 0; s < a.nst; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int k = 0;
+    for (; k < a.nst && k < my_tiles; ++k)
+      issue_tile(a, (int)blockIdx.x + k * (int)gridDim.x, ring + (size_t)k * a.slot_bytes, &full[k]);
+    s_issued = k;
+  }
+  // activations into shared memory (read by every tile)
+  if constexpr (EXACT) {
+    float* xs = reinterpret_cast<float*>(act);
+    for (int i = tid; i < a.nb * a.cols; i += kLmhThreads) xs[i] = a.x[i];
+  } else {
+    int32_t* aw = reinterpret_cast<int32_t*>(act);
+    const int32_t* src = reinterpret_cast<const int32_t*>(a.aq);
+    const int nw = (a.nb * a.cols) >> 2;
+    for (int i = tid; i < nw; i += kLmhThreads) aw[i] = src[i];
+    const int bl = (WT == 14) ? 256 : 32;
+    const int nd = a.nb * (a.cols / bl);
+    float* ds = reinterpret_cast<float*>(act + (size_t)a.nb * a.cols);
+    for (int i = tid; i < nd; i += kLmhThreads) ds[i] = a.ad[i];
+  }
+  __syncthreads();
+
+  const float* xs = reinterpret_cast<const float*>(act);
+  const int32_t* aqw = reinterpret_cast<const int32_t*>(act);
+  const float* ads = reinterpret_cast<const float*>(act + (size_t)a.nb * a.cols);
+  const int warp = tid >> 5, lane = tid & 31;
+
+  for (int k = 0; k < my_tiles; ++k) {
+    const int t = (int)blockIdx.x + k * (int)gridDim.x;
+    const RingPos rp = ring_pos(k, a.nst);
+    uint8_t* slot = ring + (size_t)rp.slot * a.slot_bytes;
+    const int r0 = t * a.R;
+    const int nr = min(a.R, a.rows - r0);
+    if constexpr (EXACT) {
+      // one lane per (row, batch row, accumulator): dotF32 (quant.nim:362-374)
+      bool ok = !s_timeout;
+      if (ok && !mbar_wait_bounded(&full[rp.slot], rp.parity)) {
+        ok = false;
+        s_timeout = 1;
+        set_status(a.status, NLS_ERR_TIMEOUT);
+      }
+      const int c = tid >> 3, kk = tid & 7;
+      const bool active = ok && c < nr * a.nb;
+      const int row = active ? c / a.nb : 0, b = active ? c - row * a.nb : 0;
+      float s = 0.0f;
+      if (active) {
+        const uint8_t* rowp = tile_row(a, slot, t, row);
+        const float* xb = xs + (size_t)b * a.cols;
+        const int n8 = a.cols & ~7;
+        int e = kk;
+#pragma unroll 4
+        for (; e < n8; e += 8) s = s + wval<WT>(rowp, e) * xb[e];
+        if (kk == 0)
+          for (e = n8; e < a.cols; ++e) s = s + wval<WT>(rowp, e) * xb[e];
+      }
+      // every lane takes part in the 8-lane shuffles
+      const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
+      const float s2 = __shfl_down_sync(0xffffffffu, s, 2, 8);
+      const float s3 = __shfl_down_sync(0xffffffffu, s, 3, 8);
+      const float s4 = __shfl_down_sync(0xffffffffu, s, 4, 8);
+      const float s5 = __shfl_down_sync(0xffffffffu, s, 5, 8);
+      const float s6 = __shfl_down_sync(0xffffffffu, s, 6, 8);
+      const float s7 = __shfl_down_sync(0xffffffffu, s, 7, 8);
+      if (active && kk == 0) {
+        float r = s + s1;
+        r = r + (s2 + s3);
+        r = r + (s4 + s5);
+        r = r + (s6 + s7);
+        a.y[(size_t)b * a.ldy + r0 + row] = r;
+      }
+      __syncthreads();
+      if (tid == 0 && k + a.nst < my_tiles && !s_timeout) {
+        fence_proxy_async_smem();
+        issue_tile(a, t + a.nst * (int)gridDim.x, slot, &full[rp.slot]);
+        s_issued = k + a.nst + 1;
+      }
+    } else {
+      float* T = terms + (size_t)(k & 1) * tchains * a.tpitch;
+      if (warp != 0) {
+        bool ok = !s_timeout;
+        if (ok && !mbar_wait_bounded(&full[rp.slot], rp.parity)) {
+          ok = false;
+          s_timeout = 1;
+          set_status(a.status, NLS_ERR_TIMEOUT);
+        }
+        if (ok) {
+          const int items = nr * a.nblk;
+          for (int it = tid - 32; it < items; it += kLmhThreads - 32) {
+            const int row = it / a.nblk, ib = it - row * a.nblk;
+            const uint8_t* rowp = tile_row(a, slot, t, row);
+            float* Tp = T + (size_t)row * a.nb * a.tpitch + ib;
+            if constexpr (WT == 8) terms_q8_0<NB>(rowp + ib * 34, ib, a, aqw, ads, Tp, a.tpitch);
+            else if constexpr (WT == 2) terms_q4_0<NB>(rowp + ib * 18, ib, a, aqw, ads, Tp, a.tpitch);
+            else terms_q6_k<NB>(rowp + ib * 210, ib, a, aqw, ads, Tp, a.tpitch);
+          }
+        }
+      }
+      __syncthreads();  // terms of tile k ready; its slot is free
+      if (warp == 0) {
+        if (tid == 0 && k + a.nst < my_tiles && !s_timeout) {
+          fence_proxy_async_smem();
+          issue_tile(a, t + a.nst * (int)gridDim.x, slot, &full[rp.slot]);
+          s_issued = k + a.nst + 1;
+        }
+        // the reference's block-order fp32 sum, one lane per (row, batch row),
+        // while warps 1.. compute the next tile's terms
+        if (lane < nr * a.nb && !s_timeout) {
+          const float* Tc = T + (size_t)lane * a.tpitch;
+          float acc = 0.0f;
+#pragma unroll 8
+          for (int ib = 0; ib < a.nblk; ++ib) acc = acc + Tc[ib];
+          const int row = lane / a.nb, b = lane - row * a.nb;
+          a.y[(size_t)b * a.ldy + r0 + row] = acc;
+        }
+      }
+    }
+  }
+  // a wait that ran out may leave a copy in flight: drain it (bounded)
+  __syncthreads();
+  if (tid == 0 && s_timeout) {
+    for (int k = max(0, s_issued - a.nst); k < s_issued; ++k) {
+      const RingPos rp = ring_pos(k, a.nst);
+      (void)mbar_wait_bounded(&full[rp.slot], rp.parity);
+    }
+  }
+}
+
+// quantizeAct (quant.nim:646-662): one warp per activation block of bl values
+__global__ void __launch_bounds__(256) lmh_quant_act(const float* x, int nblocks, int bl, float* ad,
+                                                     int8_t* aq, int* status) {
+  const int blk = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (blk >= nblocks) return;
+  const float* xb = x + (size_t)blk * bl;
+  float amax = 0.0f;
+  bool bad = false;
+  for (int i = lane; i < bl; i += 32) {
+    const float v = xb[i];
+    bad |= !isfinite(v);
+    amax = fmaxf(amax, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0) set_status(status, NLS_ERR_NAN_LOGITS);
+  }
+  const float d = amax / 127.0f;
+  const float id = d > 0.0f ? 1.0f / d : 0.0f;
+  if (lane == 0) ad[blk] = d;
+  for (int i = lane; i < bl; i += 32) {
+    const float v = xb[i] * id;
+    const int q = v >= 0.0f ? (int)(v + 0.5f) : -(int)(-v + 0.5f);
+    aq[(size_t)blk * bl + i] = (int8_t)q;
+  }
+}
+
+int block_values(int wt) {
+  switch (wt) {
+    case 0: case 1: return 1;
+    case 2: case 8: return 32;
+    case 14: return 256;
+    default: return 0;
+  }
+}
+
+int block_bytes(int wt) {
+  switch (wt) {
+    case 0: return 4;
+    case 1: return 2;
+    case 2: return 18;
+    case 8: return 34;
+    case 14: return 210;
+    default: return 0;
+  }
+}
+
+template <int WT, bool EXACT, int NB>
+cudaError_t launch_one(const LmhArgs& a, int grid, size_t smem, cudaStream_t st) {
+  auto fn = lmh_kernel<WT, EXACT, NB>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  fn<<<grid, kLmhThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int WT>
+cudaError_t dispatch(const LmhArgs& a, bool exact, int grid, size_t smem, cudaStream_t st) {
+  if (exact || WT == 0 || WT == 1) {
+    if constexpr (WT == 0 || WT == 1 || WT == 2 || WT == 8 || WT == 14)
+      return launch_one<WT, true, 1>(a, grid, smem, st);
+  }
+  if constexpr (WT == 2 || WT == 8 || WT == 14) {
+    if (a.nb <= 1) return launch_one<WT, false, 1>(a, grid, smem, st);
+    if (a.nb <= 2) return launch_one<WT, false, 2>(a, grid, smem, st);
+    if (a.nb <= 4) return launch_one<WT, false, 4>(a, grid, smem, st);
+    return launch_one<WT, false, 8>(a, grid, smem, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int lm_head_row_bytes(int wtype, int64_t cols, int64_t* out) {
+  const int bv = block_values(wtype);
+  if (bv == 0 || cols < 1 || cols % bv != 0) return 0;
+  *out = cols / bv * block_bytes(wtype);
+  return 1;
+}
+
+bool lm_head_int8_path(int wtype, int cols, int nb, bool exact) {
+  const int bl = (wtype == 14) ? 256 : (wtype == 8 || wtype == 2) ? 32 : 0;
+  return !exact && bl > 0 && cols % bl == 0 && (nb <= 4 || wtype != 8);
+}
+
+size_t lm_head_act_scratch(int wtype, int cols, int nb) {
+  const int bl = (wtype == 14) ? 256 : 32;
+  return (size_t)nb * cols + (size_t)nb * (cols / bl) * sizeof(float) + 256;
+}
+
+cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
+                           float* y, bool exact, uint8_t* act_scratch, int* status, int sm_count,
+                           cudaStream_t st) {
+  int64_t rb = 0;
+  if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
+  const bool int8 = lm_head_int8_path(wtype, cols, nb, exact);
+  const int bl = (wtype == 14) ? 256 : 32;
+  int8_t* aq = reinterpret_cast<int8_t*>(act_scratch);
+  float* ad = reinterpret_cast<float*>(act_scratch + (((size_t)nb * cols + 15) & ~size_t(15)));
+  if (int8) {
+    const int nblocks = (int)((int64_t)nb * cols / bl);
+    const int blocks = (nblocks * 32 + 255) / 256;
+    lmh_quant_act<<<blocks, 256, 0, st>>>(x, nblocks, bl, ad, aq, status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const bool padded = (rb % 16) == 0;
+  const int pitch = padded ? (int)(((rb + 127) & ~int64_t(127)) + 32) : (int)rb;
+  const int unit = padded ? pitch : (int)rb;
+  // batch rows per launch: the int8 path replays R x nbt sums in one warp;
+  // the float path runs R x nbt x 8 lanes and keeps x in shared memory
+  const int nbt_max = int8 ? 8 : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
+  for (int b0 = 0; b0 < nb; b0 += nbt_max) {
+    const int nbt = std::min(nbt_max, nb - b0);
+    LmhArgs a{};
+    a.w = w;
+    a.row_bytes = rb;
+    a.rows = rows;
+    a.cols = cols;
+    a.nblk = int8 ? cols / bl : cols;
+    a.nb = nbt;
+    a.aq = aq + (size_t)b0 * cols;
+    a.ad = ad + (size_t)b0 * (cols / bl);
+    a.x = x + (size_t)b0 * cols;
+    a.y = y + (size_t)b0 * rows;
+    a.ldy = rows;
+    a.padded = padded ? 1 : 0;
+    a.pitch = pitch;
+    a.status = status;
+    a.act_bytes = int8 ? (int)(((size_t)nbt * cols + (size_t)nbt * (cols / bl) * 4 + 15) & ~size_t(15))
+                       : (int)(((size_t)nbt * cols * 4 + 15) & ~size_t(15));
+    a.tpitch = int8 ? ((cols / bl) | 1) : 0;
+    auto slot_for = [&](int r) {
+      return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
+    };
+    auto fixed_for = [&](int r) {
+      const size_t terms = int8 ? (size_t)2 * r * nbt * a.tpitch * sizeof(float) : 0;
+      return (size_t)a.act_bytes + terms + 16 + 8 + 8 * 8 + 16;
+    };
+    // int8 path: slots of about kLmhSlotTarget bytes, R x nbt sums per warp;
+    // float path: as many rows as 256 lanes take (8 per sum) that fit twice
+    int R = int8 ? std::max(1, kLmhSlotTarget / unit) : kLmhThreads / 8;
+    R = std::min(R, std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt));
+    R = std::min(R, rows);
+    while (R > 1 && fixed_for(R) + 2 * (size_t)slot_for(R) > (size_t)kLmhSmemMax) --R;
+    a.R = R;
+    a.ntiles = (rows + R - 1) / R;
+    a.slot_bytes = slot_for(R);
+    const size_t fixed = fixed_for(R);
+    int nst = 4;
+    while (nst > 2 && fixed + (size_t)nst * a.slot_bytes > (size_t)kLmhSmemMax) --nst;
+    if (fixed + (size_t)nst * a.slot_bytes > (size_t)kLmhSmemMax) return cudaErrorInvalidValue;
+    a.nst = nst;
+    const size_t smem = fixed + (size_t)nst * a.slot_bytes;
+    const int grid = std::min(a.ntiles, sm_count);
+    cudaError_t e;
+    switch (wtype) {
+      case 0: e = dispatch<0>(a, true, grid, smem, st); break;
+      case 1: e = dispatch<1>(a, true, grid, smem, st); break;
+      case 2: e = dispatch<2>(a, !int8, grid, smem, st); break;
+      case 8: e = dispatch<8>(a, !int8, grid, smem, st); break;
+      case 14: e = dispatch<14>(a, !int8, grid, smem, st); break;
+      default: e = cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace nls

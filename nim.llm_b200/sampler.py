@@ -244,6 +244,73 @@ class Engine:
             self._check(st, "nls_token_nll")
         return out, st
 
+    @staticmethod
+    def _weights_ptr(weights):
+        """Device address of ggml-layout weights: a CUDA tensor or an int."""
+        if isinstance(weights, int):
+            return ctypes.c_void_p(weights)
+        if not _is_torch(weights) or not weights.is_cuda:
+            raise TypeError("weights must be device memory (a CUDA tensor or a device address)")
+        return ctypes.c_void_p(weights.data_ptr())
+
+    def lm_head(self, weights, wtype: int, rows: int, cols: int, x, exact: bool = False,
+                out=None, stream: int = 0, check: bool = True):
+        """matmul(m.output, x, y, nb) (model.nim:179-189): logits [nb, rows] fp32.
+        x: host numpy [nb, cols] (returns numpy) or a CUDA tensor (returns a
+        CUDA tensor, or fills `out`, stream-ordered on `stream`)."""
+        flags = _abi.NLS_EXACT_MATMUL if exact else 0
+        if _is_torch(x):
+            import torch
+            if x.dim() == 1:
+                x = x[None, :]
+            x = x.contiguous()
+            nb = x.shape[0]
+            y = out if out is not None else torch.empty((nb, rows), dtype=torch.float32, device=x.device)
+            st = self._lib.nls_lm_head(self._h, self._weights_ptr(weights), int(wtype), int(rows),
+                                       int(cols), ctypes.c_void_p(x.data_ptr()), nb,
+                                       ctypes.c_void_p(y.data_ptr()),
+                                       flags | _abi.NLS_DEVICE_INPUTS | _abi.NLS_DEVICE_OUTPUTS,
+                                       ctypes.c_void_p(stream))
+            if check:
+                self._check(st, "nls_lm_head")
+                st = self._lib.nls_stream_status(self._h, ctypes.c_void_p(stream))
+                self._check(st, "nls_lm_head (kernel status)")
+            return y
+        x = np.ascontiguousarray(np.atleast_2d(np.asarray(x, dtype=np.float32)))
+        nb = x.shape[0]
+        y = np.empty((nb, rows), dtype=np.float32)
+        st = self._lib.nls_lm_head(self._h, self._weights_ptr(weights), int(wtype), int(rows), int(cols),
+                                   _host_ptr(x), nb, _host_ptr(y), flags, ctypes.c_void_p(stream))
+        if check:
+            self._check(st, "nls_lm_head")
+        return y
+
+    def lm_head_sample(self, weights, wtype: int, vocab: int, cols: int, x, params, hist_ids=None,
+                       hist_off=None, bias_ids=None, bias_vals=None, bias_off=None, uniforms=None,
+                       want_probs: bool = False, exact: bool = False, check: bool = True):
+        """Output projection then sampling of each row (model.nim:466-470, then
+        sampler.nim:59-121), host numpy inputs: returns (ids, probs or None,
+        status). The logits never leave the GPU."""
+        x = np.ascontiguousarray(np.atleast_2d(np.asarray(x, dtype=np.float32)))
+        B = x.shape[0]
+        params = np.ascontiguousarray(params, dtype=ROW_PARAMS_DTYPE)
+        conv = {}
+        for name, arr, dt in (("hist_ids", hist_ids, np.int64), ("hist_off", hist_off, np.int64),
+                              ("bias_ids", bias_ids, np.int64), ("bias_vals", bias_vals, np.float64),
+                              ("bias_off", bias_off, np.int64), ("uniforms", uniforms, np.float64)):
+            conv[name] = None if arr is None else np.ascontiguousarray(arr, dtype=dt)
+        ids = np.empty(B, dtype=np.int64)
+        probs = np.empty(B, dtype=np.float32) if want_probs else None
+        st = self._lib.nls_lm_head_sample(
+            self._h, self._weights_ptr(weights), int(wtype), int(vocab), int(cols), _host_ptr(x), B,
+            _host_ptr(params), _host_ptr(conv["hist_ids"]), _host_ptr(conv["hist_off"]),
+            _host_ptr(conv["bias_ids"]), _host_ptr(conv["bias_vals"]), _host_ptr(conv["bias_off"]),
+            _host_ptr(conv["uniforms"]), _host_ptr(ids), _host_ptr(probs),
+            _abi.NLS_EXACT_MATMUL if exact else 0, ctypes.c_void_p(0))
+        if check:
+            self._check(st, "nls_lm_head_sample")
+        return ids, probs, st
+
     def argmax_batch(self, logits) -> np.ndarray:
         logits = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
         if logits.ndim == 1:

@@ -156,3 +156,84 @@ def shard_rows(B: int, rank: int, world: int) -> np.ndarray:
     lo = (B * rank) // world
     hi = (B * (rank + 1)) // world
     return np.arange(lo, hi, dtype=np.int64)
+
+
+# ---- output-projection weights (ggml layout) ---------------------------------
+# Synthetic weights for nls_lm_head: seeded bytes in the block layout of each
+# ggml type (quant.nim:160-202, 303-321). Values are drawn directly as the
+# stored integers and fp16 scales (no float weights are quantised), scaled so
+# that logits of a unit-normal hidden state have a standard deviation near
+# 1-2, like a trained output layer's.
+
+LM_TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q6_k": 14}
+_BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 8: (32, 34), 14: (256, 210)}
+
+
+def lm_row_bytes(wtype: int, cols: int) -> int:
+    bv, bb = _BLOCK[wtype]
+    if cols % bv:
+        raise ValueError(f"cols={cols} is not a whole number of {bv}-value blocks")
+    return cols // bv * bb
+
+
+def _f16_bytes(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a.astype("<f2")).view(np.uint8)
+
+
+def lm_weights(wtype: int, rows: int, cols: int, seed: int = 7, sigma: float = 0.02) -> np.ndarray:
+    """[rows, rowBytes] uint8 weights of `wtype`, seeded."""
+    rng = np.random.default_rng([seed, wtype, rows, cols])
+    if wtype == 0:
+        return (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma)).view(np.uint8)
+    if wtype == 1:
+        return _f16_bytes(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma)).reshape(rows, -1)
+    bv, bb = _BLOCK[wtype]
+    nblk = cols // bv
+    out = np.empty((rows, nblk, bb), dtype=np.uint8)
+    u = rng.uniform(0.5, 1.5, size=(rows, nblk)).astype(np.float32)
+    if wtype == 8:
+        out[:, :, 0:2] = _f16_bytes(u * np.float32(sigma / 73.0)).reshape(rows, nblk, 2)
+        out[:, :, 2:] = rng.integers(-128, 128, size=(rows, nblk, 32), dtype=np.int8).view(np.uint8)
+    elif wtype == 2:
+        out[:, :, 0:2] = _f16_bytes(u * np.float32(sigma / 4.6)).reshape(rows, nblk, 2)
+        out[:, :, 2:] = rng.integers(0, 256, size=(rows, nblk, 16), dtype=np.uint8)
+    else:  # Q6_K: ql[128] qh[64] int8 scales[16] d
+        out[:, :, 0:192] = rng.integers(0, 256, size=(rows, nblk, 192), dtype=np.uint8)
+        out[:, :, 192:208] = rng.integers(-64, 64, size=(rows, nblk, 16), dtype=np.int8).view(np.uint8)
+        out[:, :, 208:210] = _f16_bytes(u * np.float32(sigma / (18.5 * 37.0))).reshape(rows, nblk, 2)
+    return out.reshape(rows, nblk * bb)
+
+
+def lm_weights_device(wtype: int, rows: int, cols: int, seed: int = 7, sigma: float = 0.02,
+                      device: str = "cuda"):
+    """The same kind of weights generated on the GPU with torch (for
+    full-size benchmarks, where host generation and a copy would take long);
+    not bit-identical to lm_weights."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed) * 1000003 + int(wtype) * 7919 + rows * 31 + cols)
+    if wtype in (0, 1):
+        w = torch.randn((rows, cols), generator=g, device=device, dtype=torch.float32) * sigma
+        w = w if wtype == 0 else w.to(torch.float16)
+        return w.view(torch.uint8).reshape(rows, -1)
+    bv, bb = _BLOCK[wtype]
+    nblk = cols // bv
+    out = torch.empty((rows, nblk, bb), dtype=torch.uint8, device=device)
+    u = torch.rand((rows, nblk), generator=g, device=device) + 0.5
+    scale = {8: sigma / 73.0, 2: sigma / 4.6, 14: sigma / (18.5 * 37.0)}[wtype]
+    d = (u * scale).to(torch.float16).view(torch.uint8).reshape(rows, nblk, 2)
+    if wtype == 8:
+        out[:, :, 0:2] = d
+        out[:, :, 2:] = torch.randint(0, 256, (rows, nblk, 32), generator=g, device=device,
+                                      dtype=torch.uint8)
+    elif wtype == 2:
+        out[:, :, 0:2] = d
+        out[:, :, 2:] = torch.randint(0, 256, (rows, nblk, 16), generator=g, device=device,
+                                      dtype=torch.uint8)
+    else:
+        out[:, :, 0:192] = torch.randint(0, 256, (rows, nblk, 192), generator=g, device=device,
+                                         dtype=torch.uint8)
+        out[:, :, 192:208] = (torch.randint(-64, 64, (rows, nblk, 16), generator=g, device=device,
+                                            dtype=torch.int16) & 0xFF).to(torch.uint8)
+        out[:, :, 208:210] = d
+    return out.reshape(rows, nblk * bb)

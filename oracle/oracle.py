@@ -79,6 +79,15 @@ def lib():
         L.nlo_top_tokens.restype = ctypes.c_int64
         L.nlo_top_tokens.argtypes = [P(ctypes.c_float), ctypes.c_int64, ctypes.c_int64,
                                      P(ctypes.c_int64), P(ctypes.c_float)]
+        L.nlo_row_bytes.restype = ctypes.c_int64
+        L.nlo_row_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64]
+        L.nlo_quantize_act.restype = None
+        L.nlo_quantize_act.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_void_p, ctypes.c_void_p]
+        L.nlo_lm_head.restype = ctypes.c_int
+        L.nlo_lm_head.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32,
+                                  ctypes.c_int32]
         L.nlo_sample_batch.restype = None
         L.nlo_sample_batch.argtypes = [ctypes.c_void_p] * 1 + [ctypes.c_int64] * 3 + \
             [ctypes.c_void_p] * 9 + [ctypes.c_int]
@@ -143,3 +152,36 @@ def top_tokens(x: np.ndarray, n: int = 5):
                              ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
                              pr.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
     return [(int(ids[i]), float(pr[i])) for i in range(m)]
+
+
+# ggml weight type codes (quant.nim:14-19) restated by ref_lmhead.c
+WTYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q6_k": 14}
+
+
+def row_bytes(wtype: int, cols: int) -> int:
+    return int(lib().nlo_row_bytes(int(wtype), int(cols)))
+
+
+def quantize_act(x: np.ndarray, block_len: int):
+    """quantizeAct (quant.nim:646-662): per-block scales and int8 values."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    d = np.empty(x.size // block_len, dtype=np.float32)
+    q = np.empty(x.size, dtype=np.int8)
+    lib().nlo_quantize_act(_ptr(x), x.size, block_len, _ptr(d), _ptr(q))
+    return d, q
+
+
+def lm_head(w: np.ndarray, wtype: int, rows: int, cols: int, x: np.ndarray,
+            exact_matmul: bool = False, threads: int = 1) -> np.ndarray:
+    """matmul(m.output, x, y, nb) (model.nim:179-189): [nb, rows] fp32 logits
+    from ggml-layout weight bytes `w` and activations x [nb, cols]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    nb = x.shape[0]
+    assert x.shape[1] == cols and w.size >= rows * row_bytes(wtype, cols)
+    y = np.empty((nb, rows), dtype=np.float32)
+    rc = lib().nlo_lm_head(_ptr(w), int(wtype), rows, cols, _ptr(x), nb, _ptr(y),
+                           int(bool(exact_matmul)), int(threads))
+    if rc != 0:
+        raise ValueError(f"unsupported weight type {wtype} or shape cols={cols}")
+    return y

@@ -175,3 +175,157 @@ def top_tokens(logits, n=5):                                 # sampler.nim:123-1
     idx = sorted(range(len(probs)), key=functools.cmp_to_key(
         lambda a, b: nim_cmp(probs[b], probs[a])))
     return [(idx[i], float(probs[idx[i]])) for i in range(min(n, len(idx)))]
+
+
+# ---- the output projection (model.nim:144-189, quant.nim) -------------------
+# Mirrors ref_lmhead.c by a separate route: numpy float32 scalars for every
+# float32 operation, Python ints for the integer dot products, numpy's own
+# float16 -> float32 conversion for rdHalf.
+
+def _rd_half(b, o) -> np.float32:                            # quant.nim:144-147
+    return f32(np.frombuffer(bytes(b[o:o + 2]), dtype="<f2")[0])
+
+
+def _i8(v) -> int:
+    return v - 256 if v >= 128 else v
+
+
+def quantize_act(x, bl):                                     # quant.nim:646-662
+    x = [f32(v) for v in x]
+    d_out, qs = [], []
+    for b in range(len(x) // bl):
+        amax = f32(0)
+        for i in range(bl):
+            amax = max(amax, abs(x[b * bl + i]))
+        d = f32(amax / f32(127))
+        idv = f32(f32(1) / d) if d > 0 else f32(0)
+        d_out.append(d)
+        for i in range(bl):
+            v = f32(x[b * bl + i] * idv)
+            qs.append(int(f32(v + f32(0.5))) if v >= 0 else -int(f32(-v + f32(0.5))))
+    return d_out, qs
+
+
+def _dot_f32(a, b):                                          # quant.nim:362-374
+    s = [f32(0)] * 8
+    n, i = len(a), 0
+    while i + 8 <= n:
+        for k in range(8):
+            s[k] = f32(s[k] + f32(a[i + k] * b[i + k]))
+        i += 8
+    while i < n:
+        s[0] = f32(s[0] + f32(a[i] * b[i]))
+        i += 1
+    t = f32(s[0] + s[1])
+    t = f32(t + f32(s[2] + s[3]))
+    t = f32(t + f32(s[4] + s[5]))
+    return f32(t + f32(s[6] + s[7]))
+
+
+def _dequant_row(t, s, n):                                   # quant.nim:160-202,303-352
+    y = [f32(0)] * n
+    if t == 0:
+        return [f32(v) for v in np.frombuffer(bytes(s[:4 * n]), dtype="<f4")]
+    if t == 1:
+        return [_rd_half(s, 2 * i) for i in range(n)]
+    if t == 8:
+        for ib in range(n // 32):
+            b = s[ib * 34:(ib + 1) * 34]
+            d = _rd_half(b, 0)
+            for j in range(32):
+                y[ib * 32 + j] = f32(f32(_i8(b[2 + j])) * d)
+        return y
+    if t == 2:
+        for ib in range(n // 32):
+            b = s[ib * 18:(ib + 1) * 18]
+            d = _rd_half(b, 0)
+            for j in range(16):
+                q = b[2 + j]
+                y[ib * 32 + j] = f32(f32((q & 0xF) - 8) * d)
+                y[ib * 32 + j + 16] = f32(f32((q >> 4) - 8) * d)
+        return y
+    if t == 14:
+        for ib in range(n // 256):
+            b = s[ib * 210:(ib + 1) * 210]
+            d = _rd_half(b, 208)
+            qlo, qho, sco, yo = 0, 128, 192, ib * 256
+            for _ in range(2):
+                for l in range(32):
+                    isc = l // 16
+                    qh = b[qho + l]
+                    q1 = ((b[qlo + l] & 0xF) | ((qh & 3) << 4)) - 32
+                    q2 = ((b[qlo + l + 32] & 0xF) | (((qh >> 2) & 3) << 4)) - 32
+                    q3 = ((b[qlo + l] >> 4) | (((qh >> 4) & 3) << 4)) - 32
+                    q4 = ((b[qlo + l + 32] >> 4) | (((qh >> 6) & 3) << 4)) - 32
+                    y[yo + l] = f32(f32(d * f32(_i8(b[sco + isc]))) * f32(q1))
+                    y[yo + l + 32] = f32(f32(d * f32(_i8(b[sco + isc + 2]))) * f32(q2))
+                    y[yo + l + 64] = f32(f32(d * f32(_i8(b[sco + isc + 4]))) * f32(q3))
+                    y[yo + l + 96] = f32(f32(d * f32(_i8(b[sco + isc + 6]))) * f32(q4))
+                yo += 128
+                qlo += 64
+                qho += 32
+                sco += 8
+        return y
+    raise ValueError(t)
+
+
+def _dot_act(t, w, ad, aq, off, n):                         # quant.nim:731-786
+    acc = f32(0)
+    if t in (8, 2):
+        for ib in range(n // 32):
+            ab = off // 32 + ib
+            q8 = aq[ab * 32:(ab + 1) * 32]
+            if t == 8:
+                o = ib * 34
+                s = sum(_i8(w[o + 2 + l]) * q8[l] for l in range(32))
+            else:
+                o = ib * 18
+                s = sum(((w[o + 2 + l] & 0xF) - 8) * q8[l] + ((w[o + 2 + l] >> 4) - 8) * q8[l + 16]
+                        for l in range(16))
+            acc = f32(acc + f32(f32(_rd_half(w, o) * ad[ab]) * f32(s)))
+        return acc
+    for ib in range(n // 256):                               # Q6_K
+        b = w[ib * 210:(ib + 1) * 210]
+        ab = off // 256 + ib
+        q8 = aq[ab * 256:(ab + 1) * 256]
+        d = _rd_half(b, 208)
+        sumi = 0
+        for h in range(2):
+            ql, qh = 64 * h, 128 + 32 * h
+            for half in range(2):
+                s = [0, 0, 0, 0]
+                for l in range(16 * half, 16 * half + 16):
+                    hb = b[qh + l]
+                    q = [((b[ql + l] & 0xF) | ((hb & 3) << 4)) - 32,
+                         ((b[ql + l + 32] & 0xF) | (((hb >> 2) & 3) << 4)) - 32,
+                         ((b[ql + l] >> 4) | (((hb >> 4) & 3) << 4)) - 32,
+                         ((b[ql + l + 32] >> 4) | (((hb >> 6) & 3) << 4)) - 32]
+                    for k in range(4):
+                        s[k] += q[k] * q8[128 * h + l + 32 * k]
+                so = 8 * h + half
+                sumi += sum(_i8(b[192 + so + 2 * k]) * s[k] for k in range(4))
+        acc = f32(acc + f32(f32(ad[ab] * d) * f32(sumi)))
+    return acc
+
+
+def lm_head(w, t, rows, cols, x, exact_matmul=False):        # model.nim:144-189
+    """[nb][rows] float32 logits; w is the ggml-layout row bytes."""
+    bs = {0: 1, 1: 1, 2: 32, 8: 32, 14: 256}[t]
+    rb = cols // bs * {0: 4, 1: 2, 2: 18, 8: 34, 14: 210}[t]
+    x = [[f32(v) for v in row] for row in x]
+    nb = len(x)
+    bl = {2: 32, 8: 32, 14: 256}.get(t, 0)
+    y = [[f32(0)] * rows for _ in range(nb)]
+    w = bytes(w)
+    if not exact_matmul and bl > 0 and cols % bl == 0 and (nb <= 4 or t != 8):
+        flat = [v for row in x for v in row]
+        ad, aq = quantize_act(flat, bl)
+        for r in range(rows):
+            for b in range(nb):
+                y[b][r] = _dot_act(t, w[r * rb:(r + 1) * rb], ad, aq, b * cols, cols)
+        return y
+    for r in range(rows):
+        rowp = _dequant_row(t, w[r * rb:(r + 1) * rb], cols)
+        for b in range(nb):
+            y[b][r] = _dot_f32(rowp, x[b])
+    return y

@@ -1,0 +1,191 @@
+"""The output projection that feeds the sampler (model.nim:466-470 ->
+matmul, model.nim:179-189): nls_lm_head against the CPU oracle.
+
+CPU: the C restatement (oracle/ref_lmhead.c) equals the line-by-line Python
+transliteration (oracle/translit.py) bit for bit on every weight type, both
+paths (int8 activations, and dequantRow + dotF32) and batch sizes on either
+side of the Q8_0 switch at nb = 4 (model.nim:185), including activation
+blocks that are all zero, hold rounding ties or are all equal.
+
+GPU: every logit equals the oracle's bit for bit (integer block products,
+then the reference's fp32 operations in its order), on both tile layouts
+(rows padded in shared memory when a row is a multiple of 16 bytes, one
+contiguous copy otherwise), ragged row counts, batch tiles, and the
+full-size Llama-3 shape (128256 x 4096).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q6_k": 14}
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def _x(rng, nb, cols, edge=False):
+    x = rng.standard_normal((nb, cols)).astype(np.float32)
+    if edge and cols >= 64:
+        x[0, :32] = 0.0                                    # amax = 0: d = 0, every q = 0
+        x[-1, 32:64] = np.float32(0.25)                    # equal values: q = 127 each
+        # values whose scaled v lands on k + 0.5 exactly (v + 0.5 rounding ties)
+        x[0, 32:64] = np.float32(127.0) * np.linspace(-1, 1, 32, dtype=np.float32)
+        x[0, 33] = np.float32(63.5)
+    return x
+
+
+def test_oracle_matches_transliteration(pkg, oracle_mod):
+    from oracle import translit
+    W = pkg.workloads
+    rng = np.random.default_rng(11)
+    for name, cols in [("f32", 75), ("f16", 64), ("q4_0", 96), ("q8_0", 64), ("q6_k", 256)]:
+        t = TYPES[name]
+        w = W.lm_weights(t, 5, cols, seed=5)
+        if t == 8:  # a zero, a negative, a subnormal and an infinite... scale (finite ones only)
+            w = w.copy()
+            w[0, 0:2] = 0
+            w[1, 0:2] = np.array([0x00, 0xA8], np.uint8)   # -2^-5
+            w[2, 0:2] = np.array([0x01, 0x00], np.uint8)   # smallest subnormal half
+        for nb in (1, 4, 5):
+            x = _x(rng, nb, cols, edge=True)
+            for exact in (False, True):
+                got = oracle_mod.lm_head(w, t, 5, cols, x, exact_matmul=exact)
+                want = np.array(translit.lm_head(w.reshape(-1), t, 5, cols, x, exact_matmul=exact),
+                                dtype=np.float32)
+                assert np.array_equal(_bits(got), _bits(want)), (name, nb, exact)
+
+
+def test_quantize_act_known_answers(oracle_mod):
+    # quantizeAct (quant.nim:646-662): d = amax/127, q = round half away from zero
+    x = np.zeros(32, np.float32)
+    d, q = oracle_mod.quantize_act(x, 32)
+    assert d[0] == 0 and not q.any()
+    x = np.arange(32, dtype=np.float32) - 16            # amax 16: id = 127/16 = 7.9375
+    d, q = oracle_mod.quantize_act(x, 32)
+    assert d[0] == np.float32(16) / np.float32(127)
+    idv = np.float32(1) / d[0]
+    want = [int(np.float32(v * idv) + np.float32(0.5)) if v * idv >= 0 else -int(-np.float32(v * idv) + np.float32(0.5))
+            for v in x]
+    assert q.tolist() == want and q[0] == -127
+
+
+# ---- GPU parity ---------------------------------------------------------------
+
+def _device_weights(w):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(w)).cuda()
+
+
+def _check(engine, oracle_mod, w, t, rows, cols, x, exact, what):
+    dw = _device_weights(w)
+    got = engine.lm_head(dw, t, rows, cols, x, exact=exact)
+    want = oracle_mod.lm_head(w, t, rows, cols, x, exact_matmul=exact, threads=16)
+    bad = np.nonzero(_bits(got) != _bits(want))
+    assert bad[0].size == 0, f"{what}: {bad[0].size} logits differ, first at {bad[0][0]},{bad[1][0]} " \
+        f"gpu {got[bad[0][0], bad[1][0]]!r} oracle {want[bad[0][0], bad[1][0]]!r}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("exact", [False, True])
+def test_types_and_paths(pkg, engine, oracle_mod, name, exact):
+    t = TYPES[name]
+    rng = np.random.default_rng(t + 100 * exact)
+    cols = 4096 if t != 0 else 1024
+    rows = 3001
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=9)
+    for nb in (1, 2, 4, 5, 9):
+        x = _x(rng, nb, cols, edge=True)
+        _check(engine, oracle_mod, w, t, rows, cols, x, exact, f"{name} nb={nb} exact={exact}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,cols", [("q8_0", 96), ("q4_0", 160), ("q6_k", 768), ("f16", 100),
+                                       ("f32", 4099), ("q8_0", 8192), ("q6_k", 3072)])
+def test_row_layouts(pkg, engine, oracle_mod, name, cols):
+    """Rows that are not a multiple of 16 bytes (one contiguous copy per
+    tile, the weights' last bytes by plain loads), a dotF32 tail (cols % 8),
+    and wide rows (few rows per tile)."""
+    t = TYPES[name]
+    rng = np.random.default_rng(cols)
+    rows = 777
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=2)
+    for nb in (1, 3):
+        for exact in (False, True):
+            x = _x(rng, nb, cols)
+            _check(engine, oracle_mod, w, t, rows, cols, x, exact, f"{name} cols={cols} nb={nb}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q6_k"])
+def test_llama3_output_layer(pkg, engine, oracle_mod, name):
+    """The full Llama-3 output projection: 128256 x 4096, one decode row."""
+    t = TYPES[name]
+    rows, cols = 128256, 4096
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=1)
+    x = np.random.default_rng(3).standard_normal((1, cols)).astype(np.float32)
+    _check(engine, oracle_mod, w, t, rows, cols, x, False, f"{name} 128256x4096")
+
+
+@pytest.mark.gpu
+def test_device_tensors_and_status(pkg, engine, oracle_mod):
+    import torch
+    t, rows, cols = 8, 5000, 2048
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=4)
+    dw = _device_weights(w)
+    x = np.random.default_rng(5).standard_normal((3, cols)).astype(np.float32)
+    got = engine.lm_head(dw, t, rows, cols, torch.from_numpy(x).cuda())
+    want = oracle_mod.lm_head(w, t, rows, cols, x, threads=16)
+    assert np.array_equal(_bits(got.cpu().numpy()), _bits(want))
+    # a non-finite activation on the int8 path is an error
+    xb = x.copy()
+    xb[1, 7] = np.inf
+    _, st = None, None
+    y = np.empty((3, rows), np.float32)
+    lib = engine._lib
+    import ctypes
+    st = lib.nls_lm_head(engine._h, ctypes.c_void_p(dw.data_ptr()), t, rows, cols,
+                         ctypes.c_void_p(xb.ctypes.data), 3, ctypes.c_void_p(y.ctypes.data), 0,
+                         ctypes.c_void_p(0))
+    assert st == 5
+    # bad arguments: unaligned weights, an unknown type, cols not whole blocks
+    for wp, tt, cc in [(dw.data_ptr() + 2, 8, cols), (dw.data_ptr(), 3, cols), (dw.data_ptr(), 8, 100)]:
+        st = lib.nls_lm_head(engine._h, ctypes.c_void_p(wp), tt, rows, cc,
+                             ctypes.c_void_p(x.ctypes.data), 1, ctypes.c_void_p(y.ctypes.data), 0,
+                             ctypes.c_void_p(0))
+        assert st == 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q6_k", "f16"])
+def test_lm_head_then_sample(pkg, big_engine_lm, oracle_mod, name):
+    """nls_lm_head_sample: the projection's logits stay on the GPU and are
+    sampled there; ids and probabilities equal the oracle's sampler run on
+    the oracle's logits (config-3 sampling parameters, 64 rows)."""
+    t = TYPES[name]
+    V, cols, B = 32000, 2048, 64
+    w = pkg.workloads.lm_weights(t, V, cols, seed=8, sigma=0.06)
+    x = np.random.default_rng(9).standard_normal((B, cols)).astype(np.float32)
+    s = pkg.workloads.make("c3_batched_hetero", seed=77, rows=np.arange(B), V=V)
+    dw = _device_weights(w)
+    ids, probs, st = big_engine_lm.lm_head_sample(
+        dw, t, V, cols, x, s.params, s.hist_ids, s.hist_off, s.bias_ids, s.bias_vals, s.bias_off,
+        s.uniforms, want_probs=True)
+    assert st == 0
+    logits = oracle_mod.lm_head(w, t, V, cols, x, threads=16)
+    ref, dg = oracle_mod.sample_batch(logits, s.params, s.hist_ids, s.hist_off, s.bias_ids,
+                                      s.bias_vals, s.bias_off, s.uniforms, threads=16, diag=True)
+    bad = [int(i) for i in np.nonzero(ids != ref)[0] if dg["margin"][i] >= 1e-6]
+    assert not bad, f"ids differ at rows {bad[:10]}"
+    ok = (s.params["temperature"] > 0) & (ids == ref)
+    rel = np.abs(probs[ok].astype(np.float64) - dg["prob"][ok]) / np.maximum(np.abs(dg["prob"][ok]), 1e-30)
+    assert np.all(rel <= 1e-5)
+
+
+@pytest.fixture(scope="module")
+def big_engine_lm(pkg):
+    eng = pkg.Engine(0, max_rows=256, max_vocab=1 << 17)
+    yield eng
+    eng.close()
