@@ -269,6 +269,110 @@ def vocab_sharded_bench(pkg, dist, world, rank, local, dev, args):
             "method": "NCCL send/recv transpose to row owners, batch kernels, all-gather of ids"}
 
 
+def lm_head_bench(pkg, local, dev, stream, flush, peak, with_cpu: bool):
+    """The output projection that feeds the sampler (nls_lm_head, model.nim:
+    466-470 -> matmul :179-189) on the Llama-3 output layer, 128256 x 4096,
+    weights resident in HBM: device time of one call (CUDA events on the
+    call's stream, L2 flushed before each call), the weight bytes it streams,
+    and the fused projection + sampling call at B = 1. With with_cpu, the
+    oracle's matmul (all host threads) on the same weights, one call."""
+    import torch
+    rows, cols = 128256, 4096
+    sptr = stream.cuda_stream
+    eng = pkg.Engine(local, max_rows=8, max_vocab=rows)
+    L = eng._lib
+    W = pkg.workloads
+    out = {"config": "nls_lm_head: rows=128256 (vocab) x cols=4096 (Llama-3 8B output layer), "
+                     "ggml-layout synthetic weights resident on the device, fp32 activations on "
+                     "the device; L2 flushed before each call",
+           "peak_gbs": peak}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    for name in ("q8_0", "q6_k"):
+        t = W.LM_TYPES[name]
+        wd = W.lm_weights_device(t, rows, cols, seed=SEED, device=dev)
+        wbytes = rows * W.lm_row_bytes(t, cols)
+        res = {"weight_bytes": wbytes}
+        for nb in (1, 4):
+            x = torch.randn((nb, cols), generator=gen, device=dev)
+            y = torch.empty((nb, rows), dtype=torch.float32, device=dev)
+
+            def call():
+                return L.nls_lm_head(eng._h, ctypes.c_void_p(wd.data_ptr()), t, rows, cols,
+                                     ctypes.c_void_p(x.data_ptr()), nb, ctypes.c_void_p(y.data_ptr()),
+                                     3, ctypes.c_void_p(sptr))
+            for _ in range(3):
+                if call() != 0:
+                    raise RuntimeError("nls_lm_head failed")
+            ms = []
+            for _ in range(10):
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                call()
+                e1.record(stream)
+                e1.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            if L.nls_stream_status(eng._h, ctypes.c_void_p(sptr)) != 0:
+                raise RuntimeError("nls_lm_head status")
+            ms.sort()
+            m = ms[len(ms) // 2]
+            gbs = wbytes / (m / 1e3) / 1e9
+            res[f"nb{nb}"] = {"ms": m, "achieved_gbs": gbs, "frac": gbs / peak}
+        if name == "q8_0":
+            # projection + sampling of one decode row (config 2's sampling
+            # parameters: T 0.7, top-k 40, top-p 0.9, min-p 0.05, rep 1.1)
+            s = pkg.workloads.make("c2_llama3_b1", seed=SEED)
+            prm = torch.from_numpy(s.params.view(np.uint8).copy()).to(dev)
+            hid = torch.from_numpy(s.hist_ids).to(dev)
+            hof = torch.from_numpy(s.hist_off).to(dev)
+            uni = torch.from_numpy(s.uniforms).to(dev)
+            x1 = torch.randn((1, cols), generator=gen, device=dev)
+            oid = torch.empty(1, dtype=torch.int64, device=dev)
+
+            def fused():
+                return L.nls_lm_head_sample(
+                    eng._h, ctypes.c_void_p(wd.data_ptr()), t, rows, cols, ctypes.c_void_p(x1.data_ptr()), 1,
+                    ctypes.c_void_p(prm.data_ptr()), ctypes.c_void_p(hid.data_ptr()),
+                    ctypes.c_void_p(hof.data_ptr()), None, None, None, ctypes.c_void_p(uni.data_ptr()),
+                    ctypes.c_void_p(oid.data_ptr()), None, 3, ctypes.c_void_p(sptr))
+            for _ in range(3):
+                if fused() != 0:
+                    raise RuntimeError("nls_lm_head_sample failed")
+            ms = []
+            for _ in range(20):
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fused()
+                e1.record(stream)
+                e1.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            if L.nls_stream_status(eng._h, ctypes.c_void_p(sptr)) != 0:
+                raise RuntimeError("nls_lm_head_sample status")
+            ms.sort()
+            res["with_sampling_b1_ms"] = ms[len(ms) // 2]
+        if with_cpu:
+            from oracle import oracle
+            oracle.build()
+            threads = os.cpu_count() or 1
+            wh = wd.cpu().numpy()
+            xh = np.random.default_rng(SEED).standard_normal((1, cols)).astype(np.float32)
+            oracle.lm_head(wh[:1024], t, 1024, cols, xh, threads=threads)  # warm
+            t0 = time.perf_counter()
+            oracle.lm_head(wh, t, rows, cols, xh, threads=threads)
+            dt = time.perf_counter() - t0
+            res["cpu"] = {"ms": dt * 1e3, "threads": threads, "kind": "port",
+                          "sample": "one call, nb=1 (C restatement of matmul, oracle/ref_lmhead.c)"}
+            del wh
+        out[name] = res
+        del wd
+    eng.close()
+    return out
+
+
 def config_dict(world):
     return {"workload": f"{WORKLOAD}: B=256 rows per GPU, V=128256 fp32, per-row T~U[0.5,1.2], "
                         "top-k in {0,20,50,100}, top-p~U[0.8,1], min-p in {0,0.05}, "
@@ -286,6 +390,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-lm-head", action="store_true",
+                    help="skip the output-projection timing (nls_lm_head)")
+    ap.add_argument("--lm-head-only", action="store_true",
+                    help="run only the output-projection timing and print it")
     ap.add_argument("--latency-iters", type=int, default=200)
     ap.add_argument("--no-vocab-sharded", action="store_true",
                     help="skip the vocab-sharded (config 5) measurement at N > 1")
@@ -308,6 +416,19 @@ def main():
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
+
+    if args.lm_head_only:
+        # only the output-projection timing (a short command for profiling)
+        if rank == 0:
+            peak, _ = peaks()
+            flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+            print(json.dumps({"lm_head": lm_head_bench(pkg, local, dev, stream, flush, peak,
+                                                       with_cpu=not args.no_cpu_baseline)}),
+                  flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     B = 256
     rows = np.arange(rank * B, (rank + 1) * B, dtype=np.int64)
@@ -486,6 +607,12 @@ def main():
                "config": "nls_token_nll (perplexity's per-position term, model.nim:580-584): "
                          "511 positions x V=128256 fp32, device inputs, L2 flushed before each call"}
 
+    # the output projection feeding the sampler (the next row of the path)
+    lmh = None
+    if rank == 0 and not args.no_lm_head:
+        lmh = lm_head_bench(pkg, local, dev, stream, flush, peak,
+                            with_cpu=(world == 1 and not args.no_cpu_baseline))
+
     # Vocab-sharded mode (BASELINE config 5 over the N ranks: B = 64 rows of
     # V = 151936, each rank holding its columns of every row): device time of
     # one collective call, max over ranks.
@@ -528,6 +655,7 @@ def main():
             "clocks": clk,
             "vocab_sharded": vsh,
             "token_nll": nll,
+            "lm_head": lmh,
         }
         print(json.dumps(line), flush=True)
     eng.close()

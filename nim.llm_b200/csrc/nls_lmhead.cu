@@ -33,8 +33,11 @@ namespace nls {
 
 namespace {
 
-constexpr int kLmhThreads = 256;
+constexpr int kLmhThreads = 256;      // float path
+constexpr int kLmhTermThreads = 256;  // int8 path: warps 1..8 compute block terms,
+constexpr int kLmhInt8Threads = kLmhTermThreads + 32;  // warp 0 replays the sums
 constexpr int kLmhMaxChains = 32;     // int8 path: one warp replays the sums
+constexpr int kLmhInt8MaxNb = 4;      // batch rows per int8 launch
 constexpr int kLmhSlotTarget = 48 * 1024;
 constexpr int kLmhSmemMax = 226 * 1024;  // the kernel also has static shared variables
 
@@ -57,6 +60,9 @@ struct LmhArgs {
   int pitch;
   int act_bytes;     // shared bytes of the activation region (multiple of 16)
   int tpitch;        // int8 path: floats per sum in the term table (odd)
+  int fixed_lg;      // int8 path: log2(blocks per row) when each term thread keeps
+                     // one block's activations in registers (blocks per row a
+                     // power of two dividing the term threads), else -1
   int* status;
 };
 
@@ -196,6 +202,98 @@ __device__ __forceinline__ void terms_q6_k(const uint8_t* blk, int ib, const Lmh
   }
 }
 
+// ---- int8 path, fixed mapping: the thread's block index is fixed, so its
+// activation words (and scale) stay in registers for the whole kernel ------
+
+template <int NB>
+__device__ __forceinline__ void term_q8_0_reg(const uint8_t* blk, const int (&av)[NB][16],
+                                              const float (&da)[NB], int nb, float* T, int tp) {
+  uint32_t W[9];
+  ld_words<9>(blk, W);
+  const float dw = half_bits_to_float(W[0]);
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= nb) break;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = __dp4a((int)__byte_perm(W[k], W[k + 1], 0x5432), av[b][k], s);
+    T[b * tp] = (dw * da[b]) * __int2float_rn(s);
+  }
+}
+
+template <int NB>
+__device__ __forceinline__ void term_q4_0_reg(const uint8_t* blk, const int (&av)[NB][16],
+                                              const float (&da)[NB], int nb, float* T, int tp) {
+  uint32_t W[5];
+  ld_words<5>(blk, W);
+  const float dw = half_bits_to_float(W[0]);
+  int lo[4], hi[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t q = __byte_perm(W[k], W[k + 1], 0x5432);
+    lo[k] = (int)__vsub4(q & 0x0F0F0F0Fu, 0x08080808u);
+    hi[k] = (int)__vsub4((q >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= nb) break;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s = __dp4a(lo[k], av[b][k], s);
+      s = __dp4a(hi[k], av[b][4 + k], s);
+    }
+    T[b * tp] = (dw * da[b]) * __int2float_rn(s);
+  }
+}
+
+// Q6_K: four lanes per block, lane qi taking (h, half) = (qi >> 1, qi & 1);
+// their integer partial sums add up exactly (shuffles within the 4-lane
+// group `gmask`), and lane qi == 0 forms the term.
+template <int NB>
+__device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const int (&av)[NB][16],
+                                              const float (&da)[NB], int nb, float* T, int tp,
+                                              unsigned gmask) {
+  const int h = qi >> 1, half = qi & 1;
+  uint32_t QA[4], QB[4], QH[4], SC[2], DW[1];
+  ld_words<4>(blk + 64 * h + 16 * half, QA);
+  ld_words<4>(blk + 64 * h + 32 + 16 * half, QB);
+  ld_words<4>(blk + 128 + 32 * h + 16 * half, QH);
+  ld_words<2>(blk + 192 + 8 * h, SC);
+  ld_words<1>(blk + 208, DW);
+  int q1[4], q2[4], q3[4], q4[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t hq = QH[k];
+    q1[k] = (int)__vsub4((QA[k] & 0x0F0F0F0Fu) | ((hq & 0x03030303u) << 4), 0x20202020u);
+    q2[k] = (int)__vsub4((QB[k] & 0x0F0F0F0Fu) | (((hq >> 2) & 0x03030303u) << 4), 0x20202020u);
+    q3[k] = (int)__vsub4(((QA[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 4) & 0x03030303u) << 4), 0x20202020u);
+    q4[k] = (int)__vsub4(((QB[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 6) & 0x03030303u) << 4), 0x20202020u);
+  }
+  // scales so, so+2, so+4, so+6 with so = 8h + half (bytes of SC[0], SC[1])
+  const int sc0 = (int)(int8_t)(SC[0] >> (8 * half));
+  const int sc1 = (int)(int8_t)(SC[0] >> (8 * (half + 2)));
+  const int sc2 = (int)(int8_t)(SC[1] >> (8 * half));
+  const int sc3 = (int)(int8_t)(SC[1] >> (8 * (half + 2)));
+  const float dw = half_bits_to_float(DW[0]);
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b >= nb) break;
+    int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s0 = __dp4a(q1[k], av[b][k], s0);
+      s1 = __dp4a(q2[k], av[b][4 + k], s1);
+      s2 = __dp4a(q3[k], av[b][8 + k], s2);
+      s3 = __dp4a(q4[k], av[b][12 + k], s3);
+    }
+    int part = sc0 * s0 + sc1 * s1 + sc2 * s2 + sc3 * s3;
+    part += __shfl_xor_sync(gmask, part, 1);
+    part += __shfl_xor_sync(gmask, part, 2);
+    if (qi == 0) T[b * tp] = (da[b] * dw) * __int2float_rn(part);
+  }
+}
+
 // ---- float path: dequantised element e of a row (dequantRow, quant.nim:336-352)
 template <int WT>
 __device__ __forceinline__ float wval(const uint8_t* row, int e) {
@@ -271,7 +369,7 @@ __device__ __forceinline__ const uint8_t* tile_row(const LmhArgs& a, const uint8
 
 // WT: ggml type; EXACT: float path; NB: batch rows compiled for (a.nb <= NB)
 template <int WT, bool EXACT, int NB>
-__global__ void __launch_bounds__(kLmhThreads, 1) lmh_kernel(const LmhArgs a) {
+__global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_kernel(const LmhArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* act = ring + (size_t)a.nst * a.slot_bytes;
@@ -300,18 +398,59 @@ __global__ void __launch_bounds__(kLmhThreads, 1) lmh_kernel(const LmhArgs a) {
   // activations into shared memory (read by every tile)
   if constexpr (EXACT) {
     float* xs = reinterpret_cast<float*>(act);
-    for (int i = tid; i < a.nb * a.cols; i += kLmhThreads) xs[i] = a.x[i];
+    for (int i = tid; i < a.nb * a.cols; i += (int)blockDim.x) xs[i] = a.x[i];
   } else {
     int32_t* aw = reinterpret_cast<int32_t*>(act);
     const int32_t* src = reinterpret_cast<const int32_t*>(a.aq);
     const int nw = (a.nb * a.cols) >> 2;
-    for (int i = tid; i < nw; i += kLmhThreads) aw[i] = src[i];
+    for (int i = tid; i < nw; i += (int)blockDim.x) aw[i] = src[i];
     const int bl = (WT == 14) ? 256 : 32;
     const int nd = a.nb * (a.cols / bl);
     float* ds = reinterpret_cast<float*>(act + (size_t)a.nb * a.cols);
-    for (int i = tid; i < nd; i += kLmhThreads) ds[i] = a.ad[i];
+    for (int i = tid; i < nd; i += (int)blockDim.x) ds[i] = a.ad[i];
   }
   __syncthreads();
+
+  // fixed mapping (int8 path): term thread j = tid - 32 keeps block fb's
+  // activations of every batch row in registers and visits rows
+  // fr, fr + fg, fr + 2 fg, ... of each tile (Q6_K: four lanes per block)
+  int av[NB][16];
+  float dav[NB];
+  int fb = 0, fr = 0, fg = 1, fq = 0;
+  if constexpr (!EXACT) {
+    if (a.fixed_lg >= 0 && tid >= 32) {
+      const int j = tid - 32;
+      const int32_t* aw = reinterpret_cast<const int32_t*>(act);
+      const float* ds = reinterpret_cast<const float*>(act + (size_t)a.nb * a.cols);
+      const int wpb = a.cols >> 2;
+      if constexpr (WT == 14) {
+        fq = j & 3;
+        fb = (j >> 2) & ((1 << a.fixed_lg) - 1);
+        fr = (j >> 2) >> a.fixed_lg;
+        fg = (kLmhTermThreads / 4) >> a.fixed_lg;
+        const int w0 = (128 * (fq >> 1) + 16 * (fq & 1)) >> 2;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              av[b][4 * m + k] = b < a.nb ? aw[b * wpb + fb * 64 + w0 + 8 * m + k] : 0;
+          dav[b] = b < a.nb ? ds[b * (a.cols >> 8) + fb] : 0.0f;
+        }
+      } else {
+        fb = j & ((1 << a.fixed_lg) - 1);
+        fr = j >> a.fixed_lg;
+        fg = kLmhTermThreads >> a.fixed_lg;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) av[b][k] = (b < a.nb && k < 8) ? aw[b * wpb + fb * 8 + k] : 0;
+          dav[b] = b < a.nb ? ds[b * (a.cols >> 5) + fb] : 0.0f;
+        }
+      }
+    }
+  }
 
   const float* xs = reinterpret_cast<const float*>(act);
   const int32_t* aqw = reinterpret_cast<const int32_t*>(act);
@@ -376,9 +515,25 @@ __global__ void __launch_bounds__(kLmhThreads, 1) lmh_kernel(const LmhArgs a) {
           s_timeout = 1;
           set_status(a.status, NLS_ERR_TIMEOUT);
         }
-        if (ok) {
+        if (ok && a.fixed_lg >= 0) {
+          // two rows per pass for independent work in flight
+          const unsigned gmask = 0xFu << (lane & ~3);
+          for (int row = fr; row < nr; row += 2 * fg) {
+            const int row2 = row + fg;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int rr = u ? row2 : row;
+              if (rr >= nr) break;
+              const uint8_t* rowp = tile_row(a, slot, t, rr);
+              float* Tp = T + (size_t)rr * a.nb * a.tpitch + fb;
+              if constexpr (WT == 8) term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
+              else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, a.nb, Tp, a.tpitch);
+              else term_q6_k_reg<NB>(rowp + fb * 210, fq, av, dav, a.nb, Tp, a.tpitch, gmask);
+            }
+          }
+        } else if (ok) {
           const int items = nr * a.nblk;
-          for (int it = tid - 32; it < items; it += kLmhThreads - 32) {
+          for (int it = tid - 32; it < items; it += (int)blockDim.x - 32) {
             const int row = it / a.nblk, ib = it - row * a.nblk;
             const uint8_t* rowp = tile_row(a, slot, t, row);
             float* Tp = T + (size_t)row * a.nb * a.tpitch + ib;
@@ -472,7 +627,7 @@ cudaError_t launch_one(const LmhArgs& a, int grid, size_t smem, cudaStream_t st)
   auto fn = lmh_kernel<WT, EXACT, NB>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  fn<<<grid, kLmhThreads, smem, st>>>(a);
+  fn<<<grid, EXACT ? kLmhThreads : kLmhInt8Threads, smem, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -485,8 +640,7 @@ cudaError_t dispatch(const LmhArgs& a, bool exact, int grid, size_t smem, cudaSt
   if constexpr (WT == 2 || WT == 8 || WT == 14) {
     if (a.nb <= 1) return launch_one<WT, false, 1>(a, grid, smem, st);
     if (a.nb <= 2) return launch_one<WT, false, 2>(a, grid, smem, st);
-    if (a.nb <= 4) return launch_one<WT, false, 4>(a, grid, smem, st);
-    return launch_one<WT, false, 8>(a, grid, smem, st);
+    return launch_one<WT, false, 4>(a, grid, smem, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -531,7 +685,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   const int unit = padded ? pitch : (int)rb;
   // batch rows per launch: the int8 path replays R x nbt sums in one warp;
   // the float path runs R x nbt x 8 lanes and keeps x in shared memory
-  const int nbt_max = int8 ? 8 : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
+  const int nbt_max = int8 ? kLmhInt8MaxNb : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
   for (int b0 = 0; b0 < nb; b0 += nbt_max) {
     const int nbt = std::min(nbt_max, nb - b0);
     LmhArgs a{};
@@ -552,6 +706,16 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     a.act_bytes = int8 ? (int)(((size_t)nbt * cols + (size_t)nbt * (cols / bl) * 4 + 15) & ~size_t(15))
                        : (int)(((size_t)nbt * cols * 4 + 15) & ~size_t(15));
     a.tpitch = int8 ? ((cols / bl) | 1) : 0;
+    a.fixed_lg = -1;
+    if (int8) {
+      const int nblk = cols / bl;
+      const int lanes_per_row = (wtype == 14) ? 4 * nblk : nblk;
+      if ((nblk & (nblk - 1)) == 0 && lanes_per_row <= kLmhTermThreads) {
+        int lg = 0;
+        while ((1 << lg) < nblk) ++lg;
+        a.fixed_lg = lg;
+      }
+    }
     auto slot_for = [&](int r) {
       return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
     };
