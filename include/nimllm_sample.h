@@ -243,6 +243,14 @@ NLS_API nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype
                                int32_t cols, const float* x, int32_t nb, float* y,
                                uint32_t flags, void* stream);
 
+/* Device copies of caller data (no counterpart in the reference): allocate
+ * `bytes` on the handle's device and copy `host` there (synchronously);
+ * *out_dev receives the device address (256-byte aligned). For the output
+ * layer's weights (QMatrix.data, model.nim:88), uploaded once after loading
+ * the model. Free with nls_device_free. */
+NLS_API nls_status nls_device_upload(nls_handle* h, const void* host, uint64_t bytes, void** out_dev);
+NLS_API void nls_device_free(nls_handle* h, void* dev);
+
 /* The output projection followed by sampling, the two steps of one decode
  * step's tail (model.nim:466-470, then Sampler.sample, sampler.nim:59-121):
  * logits = nls_lm_head(weights, wtype, vocab, cols, x, rows) stay in the

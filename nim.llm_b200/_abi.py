@@ -33,6 +33,7 @@ EXPORTS = (
     "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
     "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
     "nls_top_tokens", "nls_token_nll", "nls_lm_head", "nls_lm_head_sample",
+    "nls_device_upload", "nls_device_free",
 )
 
 # ggml weight types of nls_lm_head (GgmlType codes, quant.nim:14-19)
@@ -95,6 +96,10 @@ def load(path: str | None = None):
     L.nls_top_tokens.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, u32, vp]
     L.nls_token_nll.restype = i32
     L.nls_token_nll.argtypes = [vp, vp, i64, i32, i32, vp, vp, u32, vp]
+    L.nls_device_upload.restype = i32
+    L.nls_device_upload.argtypes = [vp, vp, ctypes.c_uint64, ctypes.POINTER(vp)]
+    L.nls_device_free.restype = None
+    L.nls_device_free.argtypes = [vp, vp]
     L.nls_lm_head.restype = i32
     L.nls_lm_head.argtypes = [vp, vp, i32, i32, i32, vp, i32, vp, u32, vp]
     L.nls_lm_head_sample.restype = i32

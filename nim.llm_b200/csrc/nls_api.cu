@@ -482,6 +482,29 @@ nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int3
                      out_probs, flags, (cudaStream_t)stream);
 }
 
+nls_status nls_device_upload(nls_handle* h, const void* host, uint64_t bytes, void** out_dev) {
+  if (!h || !out_dev || (bytes && !host)) return NLS_ERR_INVALID_ARG;
+  *out_dev = nullptr;
+  DeviceGuard g(h->device);
+  void* d = nullptr;
+  NLS_CUDA(h, cudaMalloc(&d, bytes ? bytes : 16));
+  if (bytes) {
+    const cudaError_t e = cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(d);
+      return cuda_fail(h, e, "cudaMemcpy (nls_device_upload)");
+    }
+  }
+  *out_dev = d;
+  return NLS_OK;
+}
+
+void nls_device_free(nls_handle* h, void* dev) {
+  if (!h || !dev) return;
+  DeviceGuard g(h->device);
+  cudaFree(dev);
+}
+
 nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
                        int32_t cols, const float* x, int32_t nb, float* y, uint32_t flags,
                        void* stream) {

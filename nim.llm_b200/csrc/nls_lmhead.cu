@@ -38,8 +38,13 @@ constexpr int kLmhTermThreads = 256;  // int8 path: warps 1..8 compute block ter
 constexpr int kLmhInt8Threads = kLmhTermThreads + 32;  // warp 0 replays the sums
 constexpr int kLmhMaxChains = 32;     // int8 path: one warp replays the sums
 constexpr int kLmhInt8MaxNb = 4;      // batch rows per int8 launch
-constexpr int kLmhSlotTarget = 48 * 1024;
+// int8 path with at most 2 batch rows: two CTAs per SM (about 110 KB of
+// shared memory each) for twice the warps to hide shared-memory and dp4a
+// latency; otherwise one CTA per SM with the whole shared memory
+constexpr int kLmhSmemMax2 = 110 * 1024;
 constexpr int kLmhSmemMax = 226 * 1024;  // the kernel also has static shared variables
+constexpr int kLmhSlotTarget1 = 48 * 1024, kLmhSlotTarget2 = 32 * 1024;
+constexpr int kLmhGroupChains1 = 64, kLmhGroupChains2 = 32;  // sums replayed per group
 
 struct LmhArgs {
   const uint8_t* w;  // rows x row_bytes, 16-byte aligned
@@ -60,6 +65,8 @@ struct LmhArgs {
   int pitch;
   int act_bytes;     // shared bytes of the activation region (multiple of 16)
   int tpitch;        // int8 path: floats per sum in the term table (odd)
+  int gtiles;        // int8 path: tiles per group (their sums are replayed together)
+  int gchains;       //            gtiles * R * nb, at most 64 (two per replay lane)
   int fixed_lg;      // int8 path: log2(blocks per row) when each term thread keeps
                      // one block's activations in registers (blocks per row a
                      // power of two dividing the term threads), else -1
@@ -369,12 +376,13 @@ __device__ __forceinline__ const uint8_t* tile_row(const LmhArgs& a, const uint8
 
 // WT: ggml type; EXACT: float path; NB: batch rows compiled for (a.nb <= NB)
 template <int WT, bool EXACT, int NB>
-__global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_kernel(const LmhArgs a) {
+__global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT && NB <= 2) ? 2 : 1)
+    lmh_kernel(const LmhArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* act = ring + (size_t)a.nst * a.slot_bytes;
   float* terms = reinterpret_cast<float*>(act + a.act_bytes);
-  const int tchains = EXACT ? 0 : a.R * a.nb;
+  const int tchains = EXACT ? 0 : a.gchains;
   uint64_t* full = reinterpret_cast<uint64_t*>(
       reinterpret_cast<uint8_t*>(terms) + (size_t)2 * tchains * a.tpitch * sizeof(float) + 16);
   full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
@@ -386,6 +394,14 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_
   if (tid == 0) {
     s_timeout = 0;
     for (int s = 0; s < a.nst; ++s) mbar_init(&full[s], 1);
+    if constexpr (!EXACT) {
+      // term table handoff: full[4 + buf] (term threads -> replay warp),
+      // full[6 + buf] (replay warp -> term threads)
+      mbar_init(&full[4], kLmhTermThreads);
+      mbar_init(&full[5], kLmhTermThreads);
+      mbar_init(&full[6], 32);
+      mbar_init(&full[7], 32);
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -457,13 +473,13 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_
   const float* ads = reinterpret_cast<const float*>(act + (size_t)a.nb * a.cols);
   const int warp = tid >> 5, lane = tid & 31;
 
-  for (int k = 0; k < my_tiles; ++k) {
-    const int t = (int)blockIdx.x + k * (int)gridDim.x;
-    const RingPos rp = ring_pos(k, a.nst);
-    uint8_t* slot = ring + (size_t)rp.slot * a.slot_bytes;
-    const int r0 = t * a.R;
-    const int nr = min(a.R, a.rows - r0);
-    if constexpr (EXACT) {
+  if constexpr (EXACT) {
+    for (int k = 0; k < my_tiles; ++k) {
+      const int t = (int)blockIdx.x + k * (int)gridDim.x;
+      const RingPos rp = ring_pos(k, a.nst);
+      uint8_t* slot = ring + (size_t)rp.slot * a.slot_bytes;
+      const int r0 = t * a.R;
+      const int nr = min(a.R, a.rows - r0);
       // one lane per (row, batch row, accumulator): dotF32 (quant.nim:362-374)
       bool ok = !s_timeout;
       if (ok && !mbar_wait_bounded(&full[rp.slot], rp.parity)) {
@@ -506,10 +522,69 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_
         issue_tile(a, t + a.nst * (int)gridDim.x, slot, &full[rp.slot]);
         s_issued = k + a.nst + 1;
       }
-    } else {
-      float* T = terms + (size_t)(k & 1) * tchains * a.tpitch;
-      if (warp != 0) {
+    }
+  } else {
+    // Warp-specialised pipeline. Warps 1..8 compute the block terms of each
+    // tile into the term table of its group (gtiles tiles, gchains sums) and
+    // recycle ring slots among themselves; warp 0 replays each group's sums
+    // in block order (two per lane) while they go on with the next group.
+    uint64_t* tfull = full + 4;
+    uint64_t* tempty = full + 6;
+    const int cpt = a.R * a.nb;  // sums per full tile
+    const int ngroups = (my_tiles + a.gtiles - 1) / a.gtiles;
+    if (warp == 0) {
+      for (int g = 0; g < ngroups; ++g) {
+        const int buf = g & 1;
         bool ok = !s_timeout;
+        if (ok && !mbar_wait_bounded(&tfull[buf], (uint32_t)((g >> 1) & 1))) {
+          ok = false;
+          s_timeout = 1;
+          set_status(a.status, NLS_ERR_TIMEOUT);
+        }
+        if (ok) {
+          const float* Tg = terms + (size_t)buf * a.gchains * a.tpitch;
+          const int k0 = g * a.gtiles;
+          const int nsum = min(a.gtiles, my_tiles - k0) * cpt;
+          const int c0 = lane, c1 = lane + 32;
+          const float* T0 = Tg + (size_t)min(c0, a.gchains - 1) * a.tpitch;
+          const float* T1 = Tg + (size_t)min(c1, a.gchains - 1) * a.tpitch;
+          // the reference's block-order fp32 sums (quant.nim:762-786, :731-760)
+          float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 8
+          for (int ib = 0; ib < a.nblk; ++ib) {
+            acc0 = acc0 + T0[ib];
+            acc1 = acc1 + T1[ib];
+          }
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int c = m ? c1 : c0;
+            if (c >= nsum) break;
+            const int pos = c / cpt, w = c - pos * cpt;
+            const int row = w / a.nb, b = w - row * a.nb;
+            const int r = ((int)blockIdx.x + (k0 + pos) * (int)gridDim.x) * a.R + row;
+            if (r < a.rows) a.y[(size_t)b * a.ldy + r] = m ? acc1 : acc0;
+          }
+        }
+        __syncwarp();
+        mbar_arrive(&tempty[buf]);
+      }
+    } else {
+      for (int k = 0; k < my_tiles; ++k) {
+        const int t = (int)blockIdx.x + k * (int)gridDim.x;
+        const RingPos rp = ring_pos(k, a.nst);
+        uint8_t* slot = ring + (size_t)rp.slot * a.slot_bytes;
+        const int r0 = t * a.R;
+        const int nr = min(a.R, a.rows - r0);
+        const int g = k / a.gtiles, pos = k - g * a.gtiles, buf = g & 1;
+        float* T = terms + (size_t)buf * a.gchains * a.tpitch + (size_t)pos * cpt * a.tpitch;
+        bool ok = !s_timeout;
+        // the replay of group g - 2 has released this term buffer
+        if (ok && pos == 0 && g >= 2 &&
+            !mbar_wait_bounded(&tempty[buf], (uint32_t)(((g >> 1) - 1) & 1))) {
+          ok = false;
+          s_timeout = 1;
+          set_status(a.status, NLS_ERR_TIMEOUT);
+        }
         if (ok && !mbar_wait_bounded(&full[rp.slot], rp.parity)) {
           ok = false;
           s_timeout = 1;
@@ -542,24 +617,14 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, 1) lmh_
             else terms_q6_k<NB>(rowp + ib * 210, ib, a, aqw, ads, Tp, a.tpitch);
           }
         }
-      }
-      __syncthreads();  // terms of tile k ready; its slot is free
-      if (warp == 0) {
-        if (tid == 0 && k + a.nst < my_tiles && !s_timeout) {
+        // all term threads are done with the slot: refill it
+        asm volatile("bar.sync 1, %0;" ::"r"(kLmhTermThreads) : "memory");
+        if (tid == 32 && k + a.nst < my_tiles && !s_timeout) {
           fence_proxy_async_smem();
           issue_tile(a, t + a.nst * (int)gridDim.x, slot, &full[rp.slot]);
           s_issued = k + a.nst + 1;
         }
-        // the reference's block-order fp32 sum, one lane per (row, batch row),
-        // while warps 1.. compute the next tile's terms
-        if (lane < nr * a.nb && !s_timeout) {
-          const float* Tc = T + (size_t)lane * a.tpitch;
-          float acc = 0.0f;
-#pragma unroll 8
-          for (int ib = 0; ib < a.nblk; ++ib) acc = acc + Tc[ib];
-          const int row = lane / a.nb, b = lane - row * a.nb;
-          a.y[(size_t)b * a.ldy + r0 + row] = acc;
-        }
+        if (pos == a.gtiles - 1 || k == my_tiles - 1) mbar_arrive(&tfull[buf]);
       }
     }
   }
@@ -680,14 +745,21 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const bool padded = (rb % 16) == 0;
+  // the int8 path's warps read consecutive blocks of one row, so its tiles
+  // need no padding (one copy per tile); the float path pads rows so that
+  // its 8-lane groups of different rows fall in different banks
+  const bool padded = (rb % 16) == 0 && !int8;
   const int pitch = padded ? (int)(((rb + 127) & ~int64_t(127)) + 32) : (int)rb;
   const int unit = padded ? pitch : (int)rb;
-  // batch rows per launch: the int8 path replays R x nbt sums in one warp;
-  // the float path runs R x nbt x 8 lanes and keeps x in shared memory
+  // batch rows per launch: the int8 path keeps a block's activations of every
+  // batch row in registers; the float path keeps x in shared memory
   const int nbt_max = int8 ? kLmhInt8MaxNb : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
   for (int b0 = 0; b0 < nb; b0 += nbt_max) {
     const int nbt = std::min(nbt_max, nb - b0);
+    const bool two = int8 && nbt <= 2;
+    const size_t smem_max = two ? kLmhSmemMax2 : kLmhSmemMax;
+    const int slot_target = two ? kLmhSlotTarget2 : kLmhSlotTarget1;
+    const int gmax = two ? kLmhGroupChains2 : kLmhGroupChains1;
     LmhArgs a{};
     a.w = w;
     a.row_bytes = rb;
@@ -719,26 +791,29 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     auto slot_for = [&](int r) {
       return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
     };
+    auto gtiles_for = [&](int r) { return std::max(1, gmax / (r * nbt)); };
     auto fixed_for = [&](int r) {
-      const size_t terms = int8 ? (size_t)2 * r * nbt * a.tpitch * sizeof(float) : 0;
+      const size_t terms = int8 ? (size_t)2 * gtiles_for(r) * r * nbt * a.tpitch * sizeof(float) : 0;
       return (size_t)a.act_bytes + terms + 16 + 8 + 8 * 8 + 16;
     };
-    // int8 path: slots of about kLmhSlotTarget bytes, R x nbt sums per warp;
+    // int8 path: slots of about slot_target bytes, R x nbt sums per tile;
     // float path: as many rows as 256 lanes take (8 per sum) that fit twice
-    int R = int8 ? std::max(1, kLmhSlotTarget / unit) : kLmhThreads / 8;
+    int R = int8 ? std::max(1, slot_target / unit) : kLmhThreads / 8;
     R = std::min(R, std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt));
     R = std::min(R, rows);
-    while (R > 1 && fixed_for(R) + 2 * (size_t)slot_for(R) > (size_t)kLmhSmemMax) --R;
+    while (R > 1 && fixed_for(R) + 2 * (size_t)slot_for(R) > smem_max) --R;
     a.R = R;
     a.ntiles = (rows + R - 1) / R;
+    a.gtiles = int8 ? gtiles_for(R) : 1;
+    a.gchains = int8 ? a.gtiles * R * nbt : 0;
     a.slot_bytes = slot_for(R);
     const size_t fixed = fixed_for(R);
     int nst = 4;
-    while (nst > 2 && fixed + (size_t)nst * a.slot_bytes > (size_t)kLmhSmemMax) --nst;
-    if (fixed + (size_t)nst * a.slot_bytes > (size_t)kLmhSmemMax) return cudaErrorInvalidValue;
+    while (nst > 2 && fixed + (size_t)nst * a.slot_bytes > smem_max) --nst;
+    if (fixed + (size_t)nst * a.slot_bytes > smem_max) return cudaErrorInvalidValue;
     a.nst = nst;
     const size_t smem = fixed + (size_t)nst * a.slot_bytes;
-    const int grid = std::min(a.ntiles, sm_count);
+    const int grid = std::min(a.ntiles, sm_count * (two ? 2 : 1));
     cudaError_t e;
     switch (wtype) {
       case 0: e = dispatch<0>(a, true, grid, smem, st); break;

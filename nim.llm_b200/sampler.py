@@ -244,6 +244,19 @@ class Engine:
             self._check(st, "nls_token_nll")
         return out, st
 
+    def upload(self, host) -> int:
+        """Copy a host array to a new device buffer (nls_device_upload);
+        returns its device address, to free with free_device()."""
+        host = np.ascontiguousarray(host)
+        d = ctypes.c_void_p()
+        st = self._lib.nls_device_upload(self._h, ctypes.c_void_p(host.ctypes.data), host.nbytes,
+                                         ctypes.byref(d))
+        self._check(st, "nls_device_upload")
+        return int(d.value)
+
+    def free_device(self, dev: int) -> None:
+        self._lib.nls_device_free(self._h, ctypes.c_void_p(dev))
+
     @staticmethod
     def _weights_ptr(weights):
         """Device address of ggml-layout weights: a CUDA tensor or an int."""

@@ -139,6 +139,13 @@ def test_device_tensors_and_status(pkg, engine, oracle_mod):
     got = engine.lm_head(dw, t, rows, cols, torch.from_numpy(x).cuda())
     want = oracle_mod.lm_head(w, t, rows, cols, x, threads=16)
     assert np.array_equal(_bits(got.cpu().numpy()), _bits(want))
+    # weights uploaded through the library (nls_device_upload), host x and y
+    wdev = engine.upload(w)
+    try:
+        assert wdev % 256 == 0
+        assert np.array_equal(_bits(engine.lm_head(wdev, t, rows, cols, x)), _bits(want))
+    finally:
+        engine.free_device(wdev)
     # a non-finite activation on the int8 path is an error
     xb = x.copy()
     xb[1, 7] = np.inf
