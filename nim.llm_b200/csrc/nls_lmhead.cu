@@ -91,6 +91,16 @@ __device__ __forceinline__ void ld_words(const uint8_t* p, uint32_t (&out)[N]) {
   }
 }
 
+// dot product of four unsigned bytes of a with four signed bytes of b, plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// sum of the four signed bytes of w
+__device__ __forceinline__ int bytesum(int w) { return __dp4a(w, 0x01010101, 0); }
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
 }
@@ -228,27 +238,30 @@ __device__ __forceinline__ void term_q8_0_reg(const uint8_t* blk, const int (&av
   }
 }
 
+// (q - 8) . a = q . a - 8 * sum(a): asum[b] is the sum of the block's 32
+// activation values of batch row b (integers, exact)
 template <int NB>
 __device__ __forceinline__ void term_q4_0_reg(const uint8_t* blk, const int (&av)[NB][16],
-                                              const float (&da)[NB], int nb, float* T, int tp) {
+                                              const float (&da)[NB], const int (&asum)[NB][4],
+                                              int nb, float* T, int tp) {
   uint32_t W[5];
   ld_words<5>(blk, W);
   const float dw = half_bits_to_float(W[0]);
-  int lo[4], hi[4];
+  uint32_t lo[4], hi[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t q = __byte_perm(W[k], W[k + 1], 0x5432);
-    lo[k] = (int)__vsub4(q & 0x0F0F0F0Fu, 0x08080808u);
-    hi[k] = (int)__vsub4((q >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+    lo[k] = q & 0x0F0F0F0Fu;
+    hi[k] = (q >> 4) & 0x0F0F0F0Fu;
   }
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     if (b >= nb) break;
-    int s = 0;
+    int s = -8 * asum[b][0];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      s = __dp4a(lo[k], av[b][k], s);
-      s = __dp4a(hi[k], av[b][4 + k], s);
+      s = dp4a_us(lo[k], av[b][k], s);
+      s = dp4a_us(hi[k], av[b][4 + k], s);
     }
     T[b * tp] = (dw * da[b]) * __int2float_rn(s);
   }
@@ -259,8 +272,8 @@ __device__ __forceinline__ void term_q4_0_reg(const uint8_t* blk, const int (&av
 // group `gmask`), and lane qi == 0 forms the term.
 template <int NB>
 __device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const int (&av)[NB][16],
-                                              const float (&da)[NB], int nb, float* T, int tp,
-                                              unsigned gmask) {
+                                              const float (&da)[NB], const int (&asum)[NB][4],
+                                              int nb, float* T, int tp, unsigned gmask) {
   const int h = qi >> 1, half = qi & 1;
   uint32_t QA[4], QB[4], QH[4], SC[2], DW[1];
   ld_words<4>(blk + 64 * h + 16 * half, QA);
@@ -268,14 +281,16 @@ __device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const 
   ld_words<4>(blk + 128 + 32 * h + 16 * half, QH);
   ld_words<2>(blk + 192 + 8 * h, SC);
   ld_words<1>(blk + 208, DW);
-  int q1[4], q2[4], q3[4], q4[4];
+  // the 6-bit values before the - 32 (quant.nim:744-747): low nibble from
+  // ql, bits 4-5 from the qh byte's bit pair
+  uint32_t q1[4], q2[4], q3[4], q4[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t hq = QH[k];
-    q1[k] = (int)__vsub4((QA[k] & 0x0F0F0F0Fu) | ((hq & 0x03030303u) << 4), 0x20202020u);
-    q2[k] = (int)__vsub4((QB[k] & 0x0F0F0F0Fu) | (((hq >> 2) & 0x03030303u) << 4), 0x20202020u);
-    q3[k] = (int)__vsub4(((QA[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 4) & 0x03030303u) << 4), 0x20202020u);
-    q4[k] = (int)__vsub4(((QB[k] >> 4) & 0x0F0F0F0Fu) | (((hq >> 6) & 0x03030303u) << 4), 0x20202020u);
+    q1[k] = (QA[k] & 0x0F0F0F0Fu) | ((hq << 4) & 0x30303030u);
+    q2[k] = (QB[k] & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u);
+    q3[k] = ((QA[k] >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u);
+    q4[k] = ((QB[k] >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u);
   }
   // scales so, so+2, so+4, so+6 with so = 8h + half (bytes of SC[0], SC[1])
   const int sc0 = (int)(int8_t)(SC[0] >> (8 * half));
@@ -286,13 +301,14 @@ __device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const 
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     if (b >= nb) break;
-    int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    // (q - 32) . a = q . a - 32 * sum(a), sums of the 16 activation values
+    int s0 = -32 * asum[b][0], s1 = -32 * asum[b][1], s2 = -32 * asum[b][2], s3 = -32 * asum[b][3];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      s0 = __dp4a(q1[k], av[b][k], s0);
-      s1 = __dp4a(q2[k], av[b][4 + k], s1);
-      s2 = __dp4a(q3[k], av[b][8 + k], s2);
-      s3 = __dp4a(q4[k], av[b][12 + k], s3);
+      s0 = dp4a_us(q1[k], av[b][k], s0);
+      s1 = dp4a_us(q2[k], av[b][4 + k], s1);
+      s2 = dp4a_us(q3[k], av[b][8 + k], s2);
+      s3 = dp4a_us(q4[k], av[b][12 + k], s3);
     }
     int part = sc0 * s0 + sc1 * s1 + sc2 * s2 + sc3 * s3;
     part += __shfl_xor_sync(gmask, part, 1);
@@ -432,6 +448,7 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
   // fr, fr + fg, fr + 2 fg, ... of each tile (Q6_K: four lanes per block)
   int av[NB][16];
   float dav[NB];
+  int asum[NB][4];  // Q4_0: [b][0] = sum of the block's 32 values; Q6_K: per 16
   int fb = 0, fr = 0, fg = 1, fq = 0;
   if constexpr (!EXACT) {
     if (a.fixed_lg >= 0 && tid >= 32) {
@@ -453,6 +470,10 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
             for (int k = 0; k < 4; ++k)
               av[b][4 * m + k] = b < a.nb ? aw[b * wpb + fb * 64 + w0 + 8 * m + k] : 0;
           dav[b] = b < a.nb ? ds[b * (a.cols >> 8) + fb] : 0.0f;
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            asum[b][m] = bytesum(av[b][4 * m]) + bytesum(av[b][4 * m + 1]) +
+                         bytesum(av[b][4 * m + 2]) + bytesum(av[b][4 * m + 3]);
         }
       } else {
         fb = j & ((1 << a.fixed_lg) - 1);
@@ -463,6 +484,11 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
 #pragma unroll
           for (int k = 0; k < 16; ++k) av[b][k] = (b < a.nb && k < 8) ? aw[b * wpb + fb * 8 + k] : 0;
           dav[b] = b < a.nb ? ds[b * (a.cols >> 5) + fb] : 0.0f;
+          int t8 = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) t8 += bytesum(av[b][k]);
+          asum[b][0] = t8;
+          asum[b][1] = asum[b][2] = asum[b][3] = 0;
         }
       }
     }
@@ -602,8 +628,8 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
               const uint8_t* rowp = tile_row(a, slot, t, rr);
               float* Tp = T + (size_t)rr * a.nb * a.tpitch + fb;
               if constexpr (WT == 8) term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
-              else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, a.nb, Tp, a.tpitch);
-              else term_q6_k_reg<NB>(rowp + fb * 210, fq, av, dav, a.nb, Tp, a.tpitch, gmask);
+              else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, asum, a.nb, Tp, a.tpitch);
+              else term_q6_k_reg<NB>(rowp + fb * 210, fq, av, dav, asum, a.nb, Tp, a.tpitch, gmask);
             }
           }
         } else if (ok) {
