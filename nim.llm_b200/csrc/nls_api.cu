@@ -70,13 +70,11 @@ struct nls_handle {
   size_t tgt_cap = 0;
   double* d_nll = nullptr;
   size_t nll_cap = 0;
-  // output projection: staged activations, host-output logits, int8 activations
+  // output projection: staged activations, host-output logits
   float* d_lmx = nullptr;
   size_t lmx_cap = 0;
   float* d_lmy = nullptr;
   size_t lmy_cap = 0;
-  uint8_t* d_lmact = nullptr;
-  size_t lmact_cap = 0;
   char last_err[256] = {0};
 };
 
@@ -271,7 +269,6 @@ void nls_destroy(nls_handle* h) {
     cudaFree(h->d_nll);
     cudaFree(h->d_lmx);
     cudaFree(h->d_lmy);
-    cudaFree(h->d_lmact);
     if (h->fork) cudaEventDestroy(h->fork);
     if (h->join) cudaEventDestroy(h->join);
     for (cudaEvent_t e : h->ev)
@@ -442,10 +439,8 @@ nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32
     NLS_CUDA(h, cudaMemcpyAsync(h->d_lmx, x, sizeof(float) * (size_t)nb * cols, cudaMemcpyHostToDevice, st));
     dx = h->d_lmx;
   }
-  if ((s = grow(h, &h->d_lmact, &h->lmact_cap, nls::lm_head_act_scratch(wtype, cols, nb))) != NLS_OK)
-    return s;
   NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb, dy,
-                                  exact, h->d_lmact, h->d_work, h->sm_count, st));
+                                  exact, h->d_work, h->sm_count, st));
   return NLS_OK;
 }
 

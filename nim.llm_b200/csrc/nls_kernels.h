@@ -38,11 +38,10 @@ cudaError_t launch_nll(const float* logits, int64_t ld, int rows, int V, const i
 // Output projection (matmul(m.output, x, y, nb), model.nim:179-189): y[b*rows + r]
 // for ggml-layout weights w (rows x row bytes, 16-byte aligned, device) and
 // activations x [nb x cols] (device). wtype: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0,
-// 14 Q6_K. act_scratch holds lm_head_act_scratch() bytes (int8 path).
+// 14 Q6_K. The int8 path quantises x in each CTA (no scratch).
 int lm_head_row_bytes(int wtype, int64_t cols, int64_t* out);
 bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
-size_t lm_head_act_scratch(int wtype, int cols, int nb);
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
-                           float* y, bool exact, uint8_t* act_scratch, int* status, int sm_count,
+                           float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st);
 }  // namespace nls

@@ -52,9 +52,7 @@ struct LmhArgs {
   int rows, cols;
   int nblk;          // weight blocks per row (int8 path)
   int nb;            // batch rows of this launch
-  const int8_t* aq;  // int8 path: [nb x cols] quantised activations of this launch
-  const float* ad;   //            [nb x cols/bl] their scales
-  const float* x;    // float path: [nb x cols]
+  const float* x;    // [nb x cols] activations of this launch
   float* y;          // y[b * ldy + r]
   int64_t ldy;
   int R;             // rows per tile
@@ -432,14 +430,50 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
     float* xs = reinterpret_cast<float*>(act);
     for (int i = tid; i < a.nb * a.cols; i += (int)blockDim.x) xs[i] = a.x[i];
   } else {
-    int32_t* aw = reinterpret_cast<int32_t*>(act);
-    const int32_t* src = reinterpret_cast<const int32_t*>(a.aq);
-    const int nw = (a.nb * a.cols) >> 2;
-    for (int i = tid; i < nw; i += (int)blockDim.x) aw[i] = src[i];
+    // quantizeAct (quant.nim:646-662) of this launch's batch rows, straight
+    // into shared memory: one warp per activation block of bl values
     const int bl = (WT == 14) ? 256 : 32;
-    const int nd = a.nb * (a.cols / bl);
+    const int nblocks = a.nb * (a.cols / bl);
+    int8_t* qs = reinterpret_cast<int8_t*>(act);
     float* ds = reinterpret_cast<float*>(act + (size_t)a.nb * a.cols);
-    for (int i = tid; i < nd; i += (int)blockDim.x) ds[i] = a.ad[i];
+    const int nwarps = (int)blockDim.x >> 5, wl = tid & 31;
+    // loads for several blocks go out together (L2 latency once per chunk)
+    constexpr int kPer = 8;                 // values per lane in flight
+    constexpr int kBlk = (WT == 14) ? 1 : kPer;  // blocks per chunk
+    constexpr int kVals = (WT == 14) ? 8 : 1;    // values per lane per block
+    for (int base = (tid >> 5) * kBlk; base < nblocks; base += nwarps * kBlk) {
+      float v[kPer];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int blk = base + u / kVals;
+        v[u] = blk < nblocks ? a.x[(size_t)blk * bl + (u % kVals) * 32 + wl] : 0.0f;
+      }
+#pragma unroll
+      for (int ub = 0; ub < kBlk; ++ub) {
+        const int blk = base + ub;
+        if (blk >= nblocks) break;  // warp-uniform
+        float amax = 0.0f;
+        bool bad = false;
+#pragma unroll
+        for (int u = 0; u < kVals; ++u) {
+          bad |= !isfinite(v[ub * kVals + u]);
+          amax = fmaxf(amax, fabsf(v[ub * kVals + u]));
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (__any_sync(0xffffffffu, bad) && wl == 0 && blockIdx.x == 0)
+          set_status(a.status, NLS_ERR_NAN_LOGITS);
+        const float d = amax / 127.0f;
+        const float id = d > 0.0f ? 1.0f / d : 0.0f;
+        if (wl == 0) ds[blk] = d;
+#pragma unroll
+        for (int u = 0; u < kVals; ++u) {
+          const float q0 = v[ub * kVals + u] * id;
+          const int q = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
+          qs[(size_t)blk * bl + u * 32 + wl] = (int8_t)q;
+        }
+      }
+    }
   }
   __syncthreads();
 
@@ -664,35 +698,6 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT
   }
 }
 
-// quantizeAct (quant.nim:646-662): one warp per activation block of bl values
-__global__ void __launch_bounds__(256) lmh_quant_act(const float* x, int nblocks, int bl, float* ad,
-                                                     int8_t* aq, int* status) {
-  const int blk = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  if (blk >= nblocks) return;
-  const float* xb = x + (size_t)blk * bl;
-  float amax = 0.0f;
-  bool bad = false;
-  for (int i = lane; i < bl; i += 32) {
-    const float v = xb[i];
-    bad |= !isfinite(v);
-    amax = fmaxf(amax, fabsf(v));
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if (__any_sync(0xffffffffu, bad)) {
-    if (lane == 0) set_status(status, NLS_ERR_NAN_LOGITS);
-  }
-  const float d = amax / 127.0f;
-  const float id = d > 0.0f ? 1.0f / d : 0.0f;
-  if (lane == 0) ad[blk] = d;
-  for (int i = lane; i < bl; i += 32) {
-    const float v = xb[i] * id;
-    const int q = v >= 0.0f ? (int)(v + 0.5f) : -(int)(-v + 0.5f);
-    aq[(size_t)blk * bl + i] = (int8_t)q;
-  }
-}
-
 int block_values(int wt) {
   switch (wt) {
     case 0: case 1: return 1;
@@ -750,27 +755,13 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact) {
   return !exact && bl > 0 && cols % bl == 0 && (nb <= 4 || wtype != 8);
 }
 
-size_t lm_head_act_scratch(int wtype, int cols, int nb) {
-  const int bl = (wtype == 14) ? 256 : 32;
-  return (size_t)nb * cols + (size_t)nb * (cols / bl) * sizeof(float) + 256;
-}
-
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
-                           float* y, bool exact, uint8_t* act_scratch, int* status, int sm_count,
+                           float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st) {
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
   const bool int8 = lm_head_int8_path(wtype, cols, nb, exact);
   const int bl = (wtype == 14) ? 256 : 32;
-  int8_t* aq = reinterpret_cast<int8_t*>(act_scratch);
-  float* ad = reinterpret_cast<float*>(act_scratch + (((size_t)nb * cols + 15) & ~size_t(15)));
-  if (int8) {
-    const int nblocks = (int)((int64_t)nb * cols / bl);
-    const int blocks = (nblocks * 32 + 255) / 256;
-    lmh_quant_act<<<blocks, 256, 0, st>>>(x, nblocks, bl, ad, aq, status);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
   // the int8 path's warps read consecutive blocks of one row, so its tiles
   // need no padding (one copy per tile); the float path pads rows so that
   // its 8-lane groups of different rows fall in different banks
@@ -793,8 +784,6 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     a.cols = cols;
     a.nblk = int8 ? cols / bl : cols;
     a.nb = nbt;
-    a.aq = aq + (size_t)b0 * cols;
-    a.ad = ad + (size_t)b0 * (cols / bl);
     a.x = x + (size_t)b0 * cols;
     a.y = y + (size_t)b0 * rows;
     a.ldy = rows;
