@@ -318,8 +318,16 @@ def lm_head_bench(pkg, local, dev, stream, flush, peak, with_cpu: bool):
                 raise RuntimeError("nls_lm_head status")
             ms.sort()
             m = ms[len(ms) // 2]
-            gbs = wbytes / (m / 1e3) / 1e9
-            res[f"nb{nb}"] = {"ms": m, "achieved_gbs": gbs, "frac": gbs / peak}
+            # algorithmic bytes: the weights once, the activations, the logits
+            algo = wbytes + nb * cols * 4 + nb * rows * 4
+            gbs = algo / (m / 1e3) / 1e9
+            res[f"nb{nb}"] = {"ms": m, "algorithmic_bytes": algo, "achieved_gbs": gbs,
+                              "frac": gbs / peak}
+            if name == "q8_0" and nb == 1:
+                tr = ncu_traffic().get("lmh_kernel_q8_0_nb1")
+                out["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                   "frac": gbs / peak, "traffic": tr, "kernel": "lmh_kernel",
+                                   "case": "q8_0 nb=1"}
         if name == "q8_0":
             # projection + sampling of one decode row (config 2's sampling
             # parameters: T 0.7, top-k 40, top-p 0.9, min-p 0.05, rep 1.1)
