@@ -38,9 +38,10 @@ constexpr int kLmhTermThreads = 256;  // int8 path: warps 1..8 compute block ter
 constexpr int kLmhInt8Threads = kLmhTermThreads + 32;  // warp 0 replays the sums
 constexpr int kLmhMaxChains = 32;     // int8 path: one warp replays the sums
 constexpr int kLmhInt8MaxNb = 4;      // batch rows per int8 launch
-// int8 path with at most 2 batch rows: two CTAs per SM (about 110 KB of
-// shared memory each) for twice the warps to hide shared-memory and dp4a
-// latency; otherwise one CTA per SM with the whole shared memory
+// int8 path: two CTAs per SM (about 110 KB of shared memory each) for twice
+// the warps to hide shared-memory and dp4a latency, except Q6_K with more
+// than 2 batch rows (its activations in registers need more than the 96
+// registers a thread gets then): one CTA per SM with the whole shared memory
 constexpr int kLmhSmemMax2 = 110 * 1024;
 constexpr int kLmhSmemMax = 226 * 1024;  // the kernel also has static shared variables
 constexpr int kLmhSlotTarget1 = 48 * 1024, kLmhSlotTarget2 = 32 * 1024;
@@ -390,7 +391,8 @@ __device__ __forceinline__ const uint8_t* tile_row(const LmhArgs& a, const uint8
 
 // WT: ggml type; EXACT: float path; NB: batch rows compiled for (a.nb <= NB)
 template <int WT, bool EXACT, int NB>
-__global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads, (!EXACT && NB <= 2) ? 2 : 1)
+__global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
+                                  (!EXACT && (NB <= 2 || WT != 14)) ? 2 : 1)
     lmh_kernel(const LmhArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
@@ -773,7 +775,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   const int nbt_max = int8 ? kLmhInt8MaxNb : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
   for (int b0 = 0; b0 < nb; b0 += nbt_max) {
     const int nbt = std::min(nbt_max, nb - b0);
-    const bool two = int8 && nbt <= 2;
+    const bool two = int8 && (nbt <= 2 || wtype != 14);
     const size_t smem_max = two ? kLmhSmemMax2 : kLmhSmemMax;
     const int slot_target = two ? kLmhSlotTarget2 : kLmhSlotTarget1;
     const int gmax = two ? kLmhGroupChains2 : kLmhGroupChains1;
