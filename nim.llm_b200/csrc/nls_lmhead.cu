@@ -816,7 +816,18 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     // int8 path: slots of about slot_target bytes, R x nbt sums per tile;
     // float path: as many rows as 256 lanes take (8 per sum) that fit twice
     int R = int8 ? std::max(1, slot_target / unit) : kLmhThreads / 8;
-    R = std::min(R, std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt));
+    const int rmax = std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt);
+    R = std::min(R, rmax);
+    if (a.fixed_lg >= 0) {
+      // the term threads take rows in passes of `step` (fg rows side by
+      // side, two per thread): a whole number of passes per tile
+      const int fg = ((wtype == 14) ? kLmhTermThreads / 4 : kLmhTermThreads) >> a.fixed_lg;
+      const int step = 2 * fg;
+      // (rounded up where it fits; a smaller tile would cost more per byte)
+      const int Rs = (R + step - 1) / step * step;
+      if (Rs - R <= step / 2 && Rs <= rmax && fixed_for(Rs) + 2 * (size_t)slot_for(Rs) <= smem_max)
+        R = Rs;
+    }
     R = std::min(R, rows);
     while (R > 1 && fixed_for(R) + 2 * (size_t)slot_for(R) > smem_max) --R;
     a.R = R;
