@@ -316,6 +316,44 @@ __device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const 
   }
 }
 
+// Q6_K with one batch row: two lanes per block, lane h taking both 16-value
+// groups of half h (the 32 activation words stay in registers); the two
+// integer partial sums add up exactly through one shuffle.
+__device__ __forceinline__ void term_q6_k_pair(const uint8_t* blk, int h, const int (&av)[32],
+                                               float da, const int (&asum)[8], float* T,
+                                               unsigned gmask) {
+  uint32_t SC[2];
+  ld_words<2>(blk + 192 + 8 * h, SC);
+  int part = 0;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t QA[4], QB[4], QH[4];
+    ld_words<4>(blk + 64 * h + 16 * half, QA);
+    ld_words<4>(blk + 64 * h + 32 + 16 * half, QB);
+    ld_words<4>(blk + 128 + 32 * h + 16 * half, QH);
+    // scales so, so+2, so+4, so+6 with so = 8h + half
+    const int sc0 = (int)(int8_t)(SC[0] >> (8 * half));
+    const int sc1 = (int)(int8_t)(SC[0] >> (8 * (half + 2)));
+    const int sc2 = (int)(int8_t)(SC[1] >> (8 * half));
+    const int sc3 = (int)(int8_t)(SC[1] >> (8 * (half + 2)));
+    int s0 = -32 * asum[4 * half], s1 = -32 * asum[4 * half + 1];
+    int s2 = -32 * asum[4 * half + 2], s3 = -32 * asum[4 * half + 3];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t qa = QA[k], qb = QB[k], hq = QH[k];
+      s0 = dp4a_us((qa & 0x0F0F0F0Fu) | ((hq << 4) & 0x30303030u), av[16 * half + k], s0);
+      s1 = dp4a_us((qb & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u), av[16 * half + 4 + k], s1);
+      s2 = dp4a_us(((qa >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u), av[16 * half + 8 + k], s2);
+      s3 = dp4a_us(((qb >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u), av[16 * half + 12 + k], s3);
+    }
+    part += sc0 * s0 + sc1 * s1 + sc2 * s2 + sc3 * s3;
+  }
+  uint32_t DW[1];
+  ld_words<1>(blk + 208, DW);
+  part += __shfl_xor_sync(gmask, part, 1);
+  if (h == 0) T[0] = (da * half_bits_to_float(DW[0])) * __int2float_rn(part);
+}
+
 // ---- float path: dequantised element e of a row (dequantRow, quant.nim:336-352)
 template <int WT>
 __device__ __forceinline__ float wval(const uint8_t* row, int e) {
@@ -482,9 +520,12 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
   // fixed mapping (int8 path): term thread j = tid - 32 keeps block fb's
   // activations of every batch row in registers and visits rows
   // fr, fr + fg, fr + 2 fg, ... of each tile (Q6_K: four lanes per block)
+  constexpr bool kPair = (WT == 14 && NB == 1);  // Q6_K, one batch row: two lanes per block
   int av[NB][16];
   float dav[NB];
   int asum[NB][4];  // Q4_0: [b][0] = sum of the block's 32 values; Q6_K: per 16
+  int avp[kPair ? 32 : 1];
+  int asp[kPair ? 8 : 1];
   int fb = 0, fr = 0, fg = 1, fq = 0;
   if constexpr (!EXACT) {
     if (a.fixed_lg >= 0 && tid >= 32) {
@@ -492,7 +533,24 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
       const int32_t* aw = reinterpret_cast<const int32_t*>(act);
       const float* ds = reinterpret_cast<const float*>(act + (size_t)a.nb * a.cols);
       const int wpb = a.cols >> 2;
-      if constexpr (WT == 14) {
+      if constexpr (kPair) {
+        fq = j & 1;
+        fb = (j >> 1) & ((1 << a.fixed_lg) - 1);
+        fr = (j >> 1) >> a.fixed_lg;
+        fg = (kLmhTermThreads / 2) >> a.fixed_lg;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int w0 = (128 * fq + 16 * half) >> 2;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) avp[16 * half + 4 * m + k] = aw[fb * 64 + w0 + 8 * m + k];
+            asp[4 * half + m] = bytesum(avp[16 * half + 4 * m]) + bytesum(avp[16 * half + 4 * m + 1]) +
+                                bytesum(avp[16 * half + 4 * m + 2]) + bytesum(avp[16 * half + 4 * m + 3]);
+          }
+        }
+        dav[0] = ds[fb];
+      } else if constexpr (WT == 14) {
         fq = j & 3;
         fb = (j >> 2) & ((1 << a.fixed_lg) - 1);
         fr = (j >> 2) >> a.fixed_lg;
@@ -654,7 +712,7 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
         }
         if (ok && a.fixed_lg >= 0) {
           // two rows per pass for independent work in flight
-          const unsigned gmask = 0xFu << (lane & ~3);
+          const unsigned gmask = kPair ? (0x3u << (lane & ~1)) : (0xFu << (lane & ~3));
           for (int row = fr; row < nr; row += 2 * fg) {
             const int row2 = row + fg;
 #pragma unroll
@@ -665,6 +723,7 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
               float* Tp = T + (size_t)rr * a.nb * a.tpitch + fb;
               if constexpr (WT == 8) term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
               else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, asum, a.nb, Tp, a.tpitch);
+              else if constexpr (kPair) term_q6_k_pair(rowp + fb * 210, fq, avp, dav[0], asp, Tp, gmask);
               else term_q6_k_reg<NB>(rowp + fb * 210, fq, av, dav, asum, a.nb, Tp, a.tpitch, gmask);
             }
           }
@@ -798,7 +857,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     a.fixed_lg = -1;
     if (int8) {
       const int nblk = cols / bl;
-      const int lanes_per_row = (wtype == 14) ? 4 * nblk : nblk;
+      const int lanes_per_row = (wtype == 14) ? (nbt == 1 ? 2 : 4) * nblk : nblk;
       if ((nblk & (nblk - 1)) == 0 && lanes_per_row <= kLmhTermThreads) {
         int lg = 0;
         while ((1 << lg) < nblk) ++lg;
@@ -819,14 +878,17 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     const int rmax = std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt);
     R = std::min(R, rmax);
     if (a.fixed_lg >= 0) {
-      // the term threads take rows in passes of `step` (fg rows side by
-      // side, two per thread): a whole number of passes per tile
-      const int fg = ((wtype == 14) ? kLmhTermThreads / 4 : kLmhTermThreads) >> a.fixed_lg;
-      const int step = 2 * fg;
-      // (rounded up where it fits; a smaller tile would cost more per byte)
-      const int Rs = (R + step - 1) / step * step;
-      if (Rs - R <= step / 2 && Rs <= rmax && fixed_for(Rs) + 2 * (size_t)slot_for(Rs) <= smem_max)
-        R = Rs;
+      // term thread fr takes rows fr, fr + fg, fr + 2 fg, ... of a tile, so a
+      // tile costs ceil(R / fg) rows of work per thread: make R a multiple of
+      // fg, rounded up where that is close and fits, else down where that
+      // halves the work per thread (a tile also has a fixed cost, so a
+      // smaller tile only pays off then)
+      const int fg = ((wtype == 14) ? kLmhTermThreads / (nbt == 1 ? 2 : 4) : kLmhTermThreads) >> a.fixed_lg;
+      const int Ru = (R + fg - 1) / fg * fg;
+      if (Ru - R <= fg / 2 && Ru <= rmax && fixed_for(Ru) + 2 * (size_t)slot_for(Ru) <= smem_max)
+        R = Ru;
+      else if (R > fg && R < 2 * fg)
+        R = fg;
     }
     R = std::min(R, rows);
     while (R > 1 && fixed_for(R) + 2 * (size_t)slot_for(R) > smem_max) --R;
