@@ -66,9 +66,9 @@ struct LmhArgs {
   int tpitch;        // int8 path: floats per sum in the term table (odd)
   int gtiles;        // int8 path: tiles per group (their sums are replayed together)
   int gchains;       //            gtiles * R * nb, at most 64 (two per replay lane)
-  int fixed_lg;      // int8 path: log2(blocks per row) when each term thread keeps
-                     // one block's activations in registers (blocks per row a
-                     // power of two dividing the term threads), else -1
+  int fixed;         // int8 path: 1 when each term thread keeps one block's
+                     // activations in registers (lanes per block x blocks per
+                     // row <= term threads), else 0 (generic loop)
   int* status;
 };
 
@@ -528,16 +528,24 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
   int asp[kPair ? 8 : 1];
   int fb = 0, fr = 0, fg = 1, fq = 0;
   if constexpr (!EXACT) {
-    if (a.fixed_lg >= 0 && tid >= 32) {
+    if (a.fixed && tid >= 32) {
       const int j = tid - 32;
+      // lanes per block lpb; block slots units = term threads / lpb; slot q
+      // takes block q % nblk of rows q / nblk, q / nblk + fg, ...; slots past
+      // the last whole row group stay idle
+      constexpr int lpb = kPair ? 2 : (WT == 14 ? 4 : 1);
+      constexpr int units = kLmhTermThreads / lpb;
+      const int q = j / lpb;
+      const int fb0 = q % a.nblk;
+      fg = units / a.nblk;
+      const int fr0 = q / a.nblk;
       const int32_t* aw = reinterpret_cast<const int32_t*>(act);
       const float* ds = reinterpret_cast<const float*>(act + (size_t)a.nb * a.cols);
       const int wpb = a.cols >> 2;
       if constexpr (kPair) {
         fq = j & 1;
-        fb = (j >> 1) & ((1 << a.fixed_lg) - 1);
-        fr = (j >> 1) >> a.fixed_lg;
-        fg = (kLmhTermThreads / 2) >> a.fixed_lg;
+        fb = fb0;
+        fr = fr0;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int w0 = (128 * fq + 16 * half) >> 2;
@@ -552,9 +560,8 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
         dav[0] = ds[fb];
       } else if constexpr (WT == 14) {
         fq = j & 3;
-        fb = (j >> 2) & ((1 << a.fixed_lg) - 1);
-        fr = (j >> 2) >> a.fixed_lg;
-        fg = (kLmhTermThreads / 4) >> a.fixed_lg;
+        fb = fb0;
+        fr = fr0;
         const int w0 = (128 * (fq >> 1) + 16 * (fq & 1)) >> 2;
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
@@ -570,9 +577,8 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
                          bytesum(av[b][4 * m + 2]) + bytesum(av[b][4 * m + 3]);
         }
       } else {
-        fb = j & ((1 << a.fixed_lg) - 1);
-        fr = j >> a.fixed_lg;
-        fg = kLmhTermThreads >> a.fixed_lg;
+        fb = fb0;
+        fr = fr0;
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
 #pragma unroll
@@ -587,6 +593,8 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
       }
     }
   }
+
+  if (fr >= fg) fr = 1 << 30;  // an idle block slot (past the last whole row group)
 
   const float* xs = reinterpret_cast<const float*>(act);
   const int32_t* aqw = reinterpret_cast<const int32_t*>(act);
@@ -710,7 +718,7 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
           s_timeout = 1;
           set_status(a.status, NLS_ERR_TIMEOUT);
         }
-        if (ok && a.fixed_lg >= 0) {
+        if (ok && a.fixed) {
           // two rows per pass for independent work in flight
           const unsigned gmask = kPair ? (0x3u << (lane & ~1)) : (0xFu << (lane & ~3));
           for (int row = fr; row < nr; row += 2 * fg) {
@@ -854,20 +862,20 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     a.act_bytes = int8 ? (int)(((size_t)nbt * cols + (size_t)nbt * (cols / bl) * 4 + 15) & ~size_t(15))
                        : (int)(((size_t)nbt * cols * 4 + 15) & ~size_t(15));
     a.tpitch = int8 ? ((cols / bl) | 1) : 0;
-    a.fixed_lg = -1;
-    if (int8) {
-      const int nblk = cols / bl;
-      const int lanes_per_row = (wtype == 14) ? (nbt == 1 ? 2 : 4) * nblk : nblk;
-      if ((nblk & (nblk - 1)) == 0 && lanes_per_row <= kLmhTermThreads) {
-        int lg = 0;
-        while ((1 << lg) < nblk) ++lg;
-        a.fixed_lg = lg;
-      }
-    }
+    const int lpb = (wtype == 14) ? (nbt == 1 ? 2 : 4) : 1;  // lanes per block
+    a.fixed = (int8 && lpb * (cols / bl) <= kLmhTermThreads) ? 1 : 0;
     auto slot_for = [&](int r) {
       return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
     };
-    auto gtiles_for = [&](int r) { return std::max(1, gmax / (r * nbt)); };
+    // tiles per replay group: up to gmax sums, and a term table (two
+    // buffers) that leaves room for two ring slots
+    auto gtiles_for = [&](int r) {
+      int g = std::max(1, gmax / (r * nbt));
+      const size_t per = (size_t)2 * r * nbt * a.tpitch * sizeof(float);
+      const size_t other = (size_t)a.act_bytes + 2 * (size_t)slot_for(r) + 128;
+      while (g > 1 && other + g * per > smem_max) --g;
+      return g;
+    };
     auto fixed_for = [&](int r) {
       const size_t terms = int8 ? (size_t)2 * gtiles_for(r) * r * nbt * a.tpitch * sizeof(float) : 0;
       return (size_t)a.act_bytes + terms + 16 + 8 + 8 * 8 + 16;
@@ -877,13 +885,13 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     int R = int8 ? std::max(1, slot_target / unit) : kLmhThreads / 8;
     const int rmax = std::max(1, (int8 ? kLmhMaxChains : kLmhThreads / 8) / nbt);
     R = std::min(R, rmax);
-    if (a.fixed_lg >= 0) {
+    if (a.fixed) {
       // term thread fr takes rows fr, fr + fg, fr + 2 fg, ... of a tile, so a
       // tile costs ceil(R / fg) rows of work per thread: make R a multiple of
       // fg, rounded up where that is close and fits, else down where that
       // halves the work per thread (a tile also has a fixed cost, so a
       // smaller tile only pays off then)
-      const int fg = ((wtype == 14) ? kLmhTermThreads / (nbt == 1 ? 2 : 4) : kLmhTermThreads) >> a.fixed_lg;
+      const int fg = kLmhTermThreads / lpb / (cols / bl);
       const int Ru = (R + fg - 1) / fg * fg;
       if (Ru - R <= fg / 2 && Ru <= rmax && fixed_for(Ru) + 2 * (size_t)slot_for(Ru) <= smem_max)
         R = Ru;

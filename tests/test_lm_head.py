@@ -103,11 +103,13 @@ def test_types_and_paths(pkg, engine, oracle_mod, name, exact):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,cols", [("q8_0", 96), ("q4_0", 160), ("q6_k", 768), ("f16", 100),
-                                       ("f32", 4099), ("q8_0", 8192), ("q6_k", 3072)])
+                                       ("f32", 4099), ("q8_0", 8192), ("q6_k", 3072),
+                                       ("q8_0", 3584), ("q4_0", 3072), ("q8_0", 16384)])
 def test_row_layouts(pkg, engine, oracle_mod, name, cols):
     """Rows that are not a multiple of 16 bytes (one contiguous copy per
     tile, the weights' last bytes by plain loads), a dotF32 tail (cols % 8),
-    and wide rows (few rows per tile)."""
+    block counts that are not powers of two (idle term threads), and wide
+    rows (few rows per tile; Q8_0 at 16384 columns takes the generic loop)."""
     t = TYPES[name]
     rng = np.random.default_rng(cols)
     rows = 777
