@@ -269,6 +269,43 @@ def vocab_sharded_bench(pkg, dist, world, rank, local, dev, args):
             "method": "NCCL send/recv transpose to row owners, batch kernels, all-gather of ids"}
 
 
+def b1_latency(pkg, eng, dev, stream, iters: int):
+    """B=1 latency (BASELINE config 2 shape: one row, V=128256), device
+    inputs: device time of a call (the library's own events from the call's
+    first operation to its last kernel) and host wall-clock of a call through
+    the Python binding with a stream sync."""
+    import torch
+    sptr = stream.cuda_stream
+
+    def t(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    w1 = pkg.workloads.make("c2_llama3_b1", seed=SEED)
+    d1 = dict(logits=t(w1.logits), params=torch.from_numpy(w1.params.view(np.uint8).copy()).to(dev),
+              hist_ids=t(w1.hist_ids), hist_off=t(w1.hist_off), uniforms=t(w1.uniforms))
+    o1 = torch.empty(1, dtype=torch.int64, device=dev)
+    p1 = torch.empty(1, dtype=torch.float32, device=dev)
+    eng.set_profiling(True)
+    lat, host_lat = [], []
+    for i in range(iters + 10):
+        t0 = time.perf_counter()
+        eng.sample_batch(d1["logits"], d1["params"], d1["hist_ids"], d1["hist_off"], None, None,
+                         None, d1["uniforms"], out_ids=o1, out_probs=p1, stream=sptr, check=False)
+        stream.synchronize()
+        t1 = time.perf_counter()
+        if i >= 10:
+            lat.append(eng.last_kernel_ms()[2] * 1e3)
+            host_lat.append((t1 - t0) * 1e6)
+    eng.set_profiling(False)
+    lat.sort()
+    host_lat.sort()
+    return {"p50_us": lat[len(lat) // 2], "p99_us": lat[int(len(lat) * 0.99) - 1],
+            "host_p50_us": host_lat[len(host_lat) // 2],
+            "host_p99_us": host_lat[int(len(host_lat) * 0.99) - 1],
+            "config": "c2_llama3_b1: B=1, V=128256, top-k 40, device inputs; p50/p99 = device "
+                      "time of the call (library CUDA events), host_* = wall clock of the call "
+                      "through the Python binding with a stream sync"}
+
+
 def lm_head_bench(pkg, local, dev, stream, flush, peak, with_cpu: bool):
     """The output projection that feeds the sampler (nls_lm_head, model.nim:
     466-470 -> matmul :179-189) on the Llama-3 output layer, 128256 x 4096,
@@ -283,17 +320,17 @@ def lm_head_bench(pkg, local, dev, stream, flush, peak, with_cpu: bool):
     L = eng._lib
     W = pkg.workloads
     out = {"config": "nls_lm_head: rows=128256 (vocab) x cols=4096 (Llama-3 8B output layer), "
-                     "ggml-layout synthetic weights resident on the device, fp32 activations on "
-                     "the device; L2 flushed before each call",
+                     "ggml-layout synthetic weights resident on the device (Q8_0, Q6_K: int8 path; "
+                     "F16: float path), fp32 activations on the device; L2 flushed before each call",
            "peak_gbs": peak}
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED)
-    for name in ("q8_0", "q6_k"):
+    for name in ("q8_0", "q6_k", "f16"):
         t = W.LM_TYPES[name]
         wd = W.lm_weights_device(t, rows, cols, seed=SEED, device=dev)
         wbytes = rows * W.lm_row_bytes(t, cols)
         res = {"weight_bytes": wbytes}
-        for nb in (1, 4):
+        for nb in ((1, 4) if name != "f16" else (1,)):
             x = torch.randn((nb, cols), generator=gen, device=dev)
             y = torch.empty((nb, rows), dtype=torch.float32, device=dev)
 
@@ -362,7 +399,7 @@ def lm_head_bench(pkg, local, dev, stream, flush, peak, with_cpu: bool):
                 raise RuntimeError("nls_lm_head_sample status")
             ms.sort()
             res["with_sampling_b1_ms"] = ms[len(ms) // 2]
-        if with_cpu:
+        if with_cpu and name != "f16":
             from oracle import oracle
             oracle.build()
             threads = os.cpu_count() or 1
@@ -400,6 +437,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-lm-head", action="store_true",
                     help="skip the output-projection timing (nls_lm_head)")
+    ap.add_argument("--latency-only", action="store_true",
+                    help="run only the B=1 latency loop and print it")
     ap.add_argument("--lm-head-only", action="store_true",
                     help="run only the output-projection timing and print it")
     ap.add_argument("--latency-iters", type=int, default=200)
@@ -424,6 +463,18 @@ def main():
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
+
+    if args.latency_only:
+        # only the B=1 latency loop (a short command for profiling)
+        if rank == 0:
+            eng1 = pkg.Engine(local, max_rows=8, max_vocab=128256)
+            print(json.dumps({"latency_b1": b1_latency(pkg, eng1, dev, stream, args.latency_iters)}),
+                  flush=True)
+            eng1.close()
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     if args.lm_head_only:
         # only the output-projection timing (a short command for profiling)
@@ -546,35 +597,7 @@ def main():
     # device and host paths must agree
     assert np.array_equal(ids_h, out_ids.cpu().numpy()), "host and device paths differ"
 
-    # B=1 latency (BASELINE config 2 shape: one row, V=128256), device inputs
-    w1 = pkg.workloads.make("c2_llama3_b1", seed=SEED)
-    d1 = dict(logits=t(w1.logits), params=torch.from_numpy(w1.params.view(np.uint8).copy()).to(dev),
-              hist_ids=t(w1.hist_ids), hist_off=t(w1.hist_off), uniforms=t(w1.uniforms))
-    o1 = torch.empty(1, dtype=torch.int64, device=dev)
-    p1 = torch.empty(1, dtype=torch.float32, device=dev)
-    # device latency: the library's own events from the call's first
-    # operation to its last kernel; host latency: one whole call through the
-    # Python binding, stream synchronised
-    eng.set_profiling(True)
-    lat, host_lat = [], []
-    for i in range(args.latency_iters + 10):
-        t0 = time.perf_counter()
-        eng.sample_batch(d1["logits"], d1["params"], d1["hist_ids"], d1["hist_off"], None, None,
-                         None, d1["uniforms"], out_ids=o1, out_probs=p1, stream=sptr, check=False)
-        stream.synchronize()
-        t1 = time.perf_counter()
-        if i >= 10:
-            lat.append(eng.last_kernel_ms()[2] * 1e3)
-            host_lat.append((t1 - t0) * 1e6)
-    eng.set_profiling(False)
-    lat.sort()
-    host_lat.sort()
-    latency = {"p50_us": lat[len(lat) // 2], "p99_us": lat[int(len(lat) * 0.99) - 1],
-               "host_p50_us": host_lat[len(host_lat) // 2],
-               "host_p99_us": host_lat[int(len(host_lat) * 0.99) - 1],
-               "config": "c2_llama3_b1: B=1, V=128256, top-k 40, device inputs; p50/p99 = device "
-                         "time of the call (library CUDA events), host_* = wall clock of the call "
-                         "through the Python binding with a stream sync"}
+    latency = b1_latency(pkg, eng, dev, stream, args.latency_iters)
 
     # perplexity's per-position term over one nCtx-512 chunk (511 positions,
     # V = 128256), device inputs and outputs: device time of a call
