@@ -224,6 +224,12 @@ NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld,
 /* flag: the reference's `exactMatmul = true` (model.nim:173): float path
  * (dequantRow + dotF32) for every weight type */
 #define NLS_EXACT_MATMUL 4u
+/* flag: the rows are independent sequences (separate Chats sharing one
+ * model, each evaluating one token): choose the matmul path as
+ * model.nim:185 does for nb = 1, so that every row's logits equal a
+ * one-row call's (without it, Q8_0 weights with nb > 4 take the float path
+ * as one nb-row matmul would) */
+#define NLS_ROWS_INDEPENDENT 8u
 
 /* y[b*rows + r] = weight row r . x[b*cols ..] for b < nb (matmul, model.nim:179).
  *  weights  device memory of the handle's device, 16-byte aligned: `rows`
@@ -238,7 +244,8 @@ NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld,
  * cols must be a whole number of blocks (32 for Q4_0/Q8_0, 256 for Q6_K) and
  * at most 16384 for F32/F16. Non-finite activations on the int8 path give
  * NLS_ERR_NAN_LOGITS (the reference's int8 conversion of them is undefined).
- * Flags: NLS_DEVICE_INPUTS (x), NLS_DEVICE_OUTPUTS (y), NLS_EXACT_MATMUL. */
+ * Flags: NLS_DEVICE_INPUTS (x), NLS_DEVICE_OUTPUTS (y), NLS_EXACT_MATMUL,
+ * NLS_ROWS_INDEPENDENT. */
 NLS_API nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
                                int32_t cols, const float* x, int32_t nb, float* y,
                                uint32_t flags, void* stream);
@@ -257,7 +264,8 @@ NLS_API void nls_device_free(nls_handle* h, void* dev);
  * handle's device memory (never copied to the host) and nls_sample_batch
  * samples them with the given params, histories, bias and uniforms.
  * Flags and outputs as nls_sample_batch (NLS_DEVICE_INPUTS covers x and the
- * sampling inputs; weights are always device memory), plus NLS_EXACT_MATMUL.
+ * sampling inputs; weights are always device memory), plus NLS_EXACT_MATMUL
+ * and NLS_ROWS_INDEPENDENT (one decode step of `rows` separate Chats).
  * rows <= the handle's max_rows, vocab <= its max_vocab. */
 NLS_API nls_status nls_lm_head_sample(nls_handle* h, const void* weights, int32_t wtype,
                                       int32_t vocab, int32_t cols, const float* x, int32_t rows,

@@ -11,8 +11,9 @@ name `nimllm_b200`).
 """
 from . import workloads
 from ._abi import EXPORTS, LIB_PATH, NlsError, ROW_PARAMS_DTYPE, load
-from .sampler import (Comm, Engine, Rand, Sampler, SamplerParams, accept, argmax, comm_unique_id,
-                      default_engine, defaultSampling, greedySampling, newSampler, params_record,
-                      perplexity_from_logits, row_owner_range, sample, topTokens, vocab_shard)
+from .sampler import (Comm, Engine, Rand, Sampler, SamplerParams, accept, argmax, batch_inputs,
+                      comm_unique_id, decode_step_many, default_engine, defaultSampling,
+                      greedySampling, newSampler, params_record, perplexity_from_logits,
+                      row_owner_range, sample, sample_many, topTokens, vocab_shard)
 
 __version__ = "0.1.0"

@@ -39,6 +39,7 @@ EXPORTS = (
 # ggml weight types of nls_lm_head (GgmlType codes, quant.nim:14-19)
 NLS_WT = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q6_k": 14}
 NLS_EXACT_MATMUL = 4
+NLS_ROWS_INDEPENDENT = 8
 
 # nls_row_params: 6 doubles + 2 int64, 64 bytes, no padding.
 ROW_PARAMS_DTYPE = np.dtype([

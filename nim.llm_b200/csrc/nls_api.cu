@@ -431,7 +431,9 @@ nls_status sample_impl(nls_handle* h, const float* logits, int64_t ld, bool logi
 // x_dev); the kernel status goes to d_work[0], which the caller has cleared.
 nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
                         int32_t cols, const float* x, bool x_dev, int32_t nb, float* dy,
-                        bool exact, cudaStream_t st) {
+                        uint32_t flags, cudaStream_t st) {
+  const bool exact = (flags & NLS_EXACT_MATMUL) != 0;
+  const int path_nb = (flags & NLS_ROWS_INDEPENDENT) ? 1 : nb;
   nls_status s;
   const float* dx = x;
   if (!x_dev) {
@@ -439,8 +441,8 @@ nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32
     NLS_CUDA(h, cudaMemcpyAsync(h->d_lmx, x, sizeof(float) * (size_t)nb * cols, cudaMemcpyHostToDevice, st));
     dx = h->d_lmx;
   }
-  NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb, dy,
-                                  exact, h->d_work, h->sm_count, st));
+  NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb,
+                                  path_nb, dy, exact, h->d_work, h->sm_count, st));
   return NLS_OK;
 }
 
@@ -504,7 +506,8 @@ nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_
                        int32_t cols, const float* x, int32_t nb, float* y, uint32_t flags,
                        void* stream) {
   if (!h) return NLS_ERR_INVALID_ARG;
-  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL)) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL | NLS_ROWS_INDEPENDENT))
+    return NLS_ERR_INVALID_ARG;
   if (nb < 0 || rows < 0) return NLS_ERR_INVALID_ARG;
   if (nb == 0 || rows == 0) return NLS_OK;
   if (!x || !y || !lm_head_args_ok(weights, wtype, rows, cols)) return NLS_ERR_INVALID_ARG;
@@ -519,7 +522,7 @@ nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_
   }
   NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
   if ((s = lm_head_impl(h, weights, wtype, rows, cols, x, (flags & NLS_DEVICE_INPUTS) != 0, nb, dy,
-                        (flags & NLS_EXACT_MATMUL) != 0, st)) != NLS_OK)
+                        flags, st)) != NLS_OK)
     return s;
   if (dev_out) return NLS_OK;
   NLS_CUDA(h, cudaMemcpyAsync(h->h_status, h->d_work, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -536,7 +539,8 @@ nls_status nls_lm_head_sample(nls_handle* h, const void* weights, int32_t wtype,
                               const double* uniforms, int64_t* out_ids, float* out_probs,
                               uint32_t flags, void* stream) {
   if (!h) return NLS_ERR_INVALID_ARG;
-  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL)) return NLS_ERR_INVALID_ARG;
+  if (flags & ~(NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS | NLS_EXACT_MATMUL | NLS_ROWS_INDEPENDENT))
+    return NLS_ERR_INVALID_ARG;
   if (rows < 0) return NLS_ERR_INVALID_ARG;
   if (rows == 0) return NLS_OK;
   if (!x || !params || !out_ids || !lm_head_args_ok(weights, wtype, vocab, cols))
@@ -551,11 +555,11 @@ nls_status nls_lm_head_sample(nls_handle* h, const void* weights, int32_t wtype,
   if ((s = grow(h, &h->d_logits, &h->logits_cap, (size_t)rows * vocab)) != NLS_OK) return s;
   NLS_CUDA(h, cudaMemsetAsync(h->d_work, 0, sizeof(int), st));
   if ((s = lm_head_impl(h, weights, wtype, vocab, cols, x, (flags & NLS_DEVICE_INPUTS) != 0, rows,
-                        h->d_logits, (flags & NLS_EXACT_MATMUL) != 0, st)) != NLS_OK)
+                        h->d_logits, flags, st)) != NLS_OK)
     return s;
   return sample_impl(h, h->d_logits, vocab, true, true, rows, vocab, params, hist_ids, hist_off,
                      bias_ids, bias_vals, bias_off, uniforms, out_ids, out_probs,
-                     flags & ~NLS_EXACT_MATMUL, st);
+                     flags & ~(NLS_EXACT_MATMUL | NLS_ROWS_INDEPENDENT), st);
 }
 
 nls_status nls_argmax_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,

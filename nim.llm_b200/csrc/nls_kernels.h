@@ -41,7 +41,8 @@ cudaError_t launch_nll(const float* logits, int64_t ld, int rows, int V, const i
 // 14 Q6_K. The int8 path quantises x in each CTA (no scratch).
 int lm_head_row_bytes(int wtype, int64_t cols, int64_t* out);
 bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
+// path_nb: the batch size the path choice sees (nb, or 1 for independent rows)
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
-                           float* y, bool exact, int* status, int sm_count,
+                           int path_nb, float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st);
 }  // namespace nls

@@ -825,11 +825,11 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact) {
 }
 
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
-                           float* y, bool exact, int* status, int sm_count,
+                           int path_nb, float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st) {
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
-  const bool int8 = lm_head_int8_path(wtype, cols, nb, exact);
+  const bool int8 = lm_head_int8_path(wtype, cols, path_nb, exact);
   const int bl = (wtype == 14) ? 256 : 32;
   // the int8 path's warps read consecutive blocks of one row, so its tiles
   // need no padding (one copy per tile); the float path pads rows so that

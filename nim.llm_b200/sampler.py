@@ -267,11 +267,12 @@ class Engine:
         return ctypes.c_void_p(weights.data_ptr())
 
     def lm_head(self, weights, wtype: int, rows: int, cols: int, x, exact: bool = False,
-                out=None, stream: int = 0, check: bool = True):
+                out=None, stream: int = 0, check: bool = True, independent: bool = False):
         """matmul(m.output, x, y, nb) (model.nim:179-189): logits [nb, rows] fp32.
         x: host numpy [nb, cols] (returns numpy) or a CUDA tensor (returns a
-        CUDA tensor, or fills `out`, stream-ordered on `stream`)."""
-        flags = _abi.NLS_EXACT_MATMUL if exact else 0
+        CUDA tensor, or fills `out`, stream-ordered on `stream`). independent:
+        the rows are separate sequences (path chosen as for nb = 1)."""
+        flags = (_abi.NLS_EXACT_MATMUL if exact else 0) | (_abi.NLS_ROWS_INDEPENDENT if independent else 0)
         if _is_torch(x):
             import torch
             if x.dim() == 1:
@@ -300,7 +301,8 @@ class Engine:
 
     def lm_head_sample(self, weights, wtype: int, vocab: int, cols: int, x, params, hist_ids=None,
                        hist_off=None, bias_ids=None, bias_vals=None, bias_off=None, uniforms=None,
-                       want_probs: bool = False, exact: bool = False, check: bool = True):
+                       want_probs: bool = False, exact: bool = False, check: bool = True,
+                       independent: bool = False):
         """Output projection then sampling of each row (model.nim:466-470, then
         sampler.nim:59-121), host numpy inputs: returns (ids, probs or None,
         status). The logits never leave the GPU."""
@@ -319,7 +321,8 @@ class Engine:
             _host_ptr(params), _host_ptr(conv["hist_ids"]), _host_ptr(conv["hist_off"]),
             _host_ptr(conv["bias_ids"]), _host_ptr(conv["bias_vals"]), _host_ptr(conv["bias_off"]),
             _host_ptr(conv["uniforms"]), _host_ptr(ids), _host_ptr(probs),
-            _abi.NLS_EXACT_MATMUL if exact else 0, ctypes.c_void_p(0))
+            (_abi.NLS_EXACT_MATMUL if exact else 0) | (_abi.NLS_ROWS_INDEPENDENT if independent else 0),
+            ctypes.c_void_p(0))
         if check:
             self._check(st, "nls_lm_head_sample")
         return ids, probs, st
@@ -374,6 +377,58 @@ class Sampler:
             hist, np.array([0, hist.size], dtype=np.int64),
             bias_ids, bias_vals, np.array([0, bias_ids.size], dtype=np.int64), u)
         return int(ids[0])
+
+
+def batch_inputs(samplers: list) -> dict:
+    """The sampling inputs of several independent samplers as one batch (the
+    C ABI's layout): one params record per sampler, their histories and
+    logit biases as CSR lists, and one uniform each, drawn from the
+    sampler's own RNG only when its temperature is above 0 (sampler.nim:77-78,
+    :117), so every RNG advances exactly as if the samplers ran one by one."""
+    params = np.array([params_record(s.params) for s in samplers], dtype=ROW_PARAMS_DTYPE)
+    hist = [np.asarray(s.history, dtype=np.int64) for s in samplers]
+    hist_off = np.zeros(len(samplers) + 1, dtype=np.int64)
+    hist_off[1:] = np.cumsum([h.size for h in hist])
+    bias_ids = [np.fromiter(s.params.logitBias.keys(), dtype=np.int64, count=len(s.params.logitBias))
+                for s in samplers]
+    bias_vals = [np.fromiter(s.params.logitBias.values(), dtype=np.float64, count=len(s.params.logitBias))
+                 for s in samplers]
+    bias_off = np.zeros(len(samplers) + 1, dtype=np.int64)
+    bias_off[1:] = np.cumsum([b.size for b in bias_ids])
+    uniforms = np.array([s.rng.rand(1.0) if s.params.temperature > 0 else 0.0 for s in samplers],
+                        dtype=np.float64)
+    cat = lambda parts, dt: np.concatenate(parts).astype(dt) if parts else np.zeros(0, dt)  # noqa: E731
+    return dict(params=params, hist_ids=cat(hist, np.int64), hist_off=hist_off,
+                bias_ids=cat(bias_ids, np.int64), bias_vals=cat(bias_vals, np.float64),
+                bias_off=bias_off, uniforms=uniforms)
+
+
+def sample_many(samplers: list, logits_rows, engine: Optional[Engine] = None) -> list:
+    """One sampling step of many independent samplers (separate Chats sharing
+    one model) in one batched call: row i of `logits_rows` is sampled with
+    samplers[i]'s params, history, bias and RNG. The ids equal what each
+    sampler's own sample() returns; accept() stays with the caller."""
+    logits = np.ascontiguousarray(np.atleast_2d(np.asarray(logits_rows, dtype=np.float32)))
+    if logits.shape[0] != len(samplers):
+        raise ValueError("one logits row per sampler")
+    a = batch_inputs(samplers)
+    eng = engine or default_engine()
+    ids, _, _ = eng.sample_batch(logits, a["params"], a["hist_ids"], a["hist_off"], a["bias_ids"],
+                                 a["bias_vals"], a["bias_off"], a["uniforms"])
+    return [int(i) for i in ids]
+
+
+def decode_step_many(samplers: list, engine: Engine, weights, wtype: int, vocab: int, cols: int,
+                     hidden_rows) -> list:
+    """The tail of one decode step of many independent Chats sharing one
+    model: the output projection of each one's normalised hidden state
+    (model.nim:470, as a one-row matmul each) and sampling with each one's
+    sampler, in two kernels' worth of GPU work and no logits on the host."""
+    a = batch_inputs(samplers)
+    ids, _, _ = engine.lm_head_sample(weights, wtype, vocab, cols, hidden_rows, a["params"],
+                                      a["hist_ids"], a["hist_off"], a["bias_ids"], a["bias_vals"],
+                                      a["bias_off"], a["uniforms"], independent=True)
+    return [int(i) for i in ids]
 
 
 def newSampler(p: Optional[SamplerParams] = None, engine: Optional[Engine] = None) -> Sampler:
