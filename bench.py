@@ -638,9 +638,10 @@ def main():
                "config": "nls_token_nll (perplexity's per-position term, model.nim:580-584): "
                          "511 positions x V=128256 fp32, device inputs, L2 flushed before each call"}
 
-    # the output projection feeding the sampler (the next row of the path)
+    # the output projection feeding the sampler (the next row of the path):
+    # a one-GPU kernel timing, so only in the N = 1 run
     lmh = None
-    if rank == 0 and not args.no_lm_head:
+    if rank == 0 and world == 1 and not args.no_lm_head:
         lmh = lm_head_bench(pkg, local, dev, stream, flush, peak,
                             with_cpu=(world == 1 and not args.no_cpu_baseline))
 
