@@ -66,6 +66,8 @@ struct LmhArgs {
   int tpitch;        // int8 path: floats per sum in the term table (odd)
   int gtiles;        // int8 path: tiles per group (their sums are replayed together)
   int gchains;       //            gtiles * R * nb, at most 64 (two per replay lane)
+  int par;           // Q6_K, one batch row: slots arranged so that every warp holds
+                     // blocks of one parity (so one 4-byte alignment of the block start)
   int fixed;         // int8 path: 1 when each term thread keeps one block's
                      // activations in registers (lanes per block x blocks per
                      // row <= term threads), else 0 (generic loop)
@@ -99,6 +101,18 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 
 // sum of the four signed bytes of w
 __device__ __forceinline__ int bytesum(int w) { return __dp4a(w, 0x01010101, 0); }
+
+// ld_words for a p known to be 4-byte aligned (A4) or only 2-byte aligned
+template <bool A4, int N>
+__device__ __forceinline__ void ld_words_al(const uint8_t* p, uint32_t (&out)[N]) {
+  if constexpr (A4) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = w[k];
+  } else {
+    ld_words<N>(p, out);
+  }
+}
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
@@ -319,18 +333,21 @@ __device__ __forceinline__ void term_q6_k_reg(const uint8_t* blk, int qi, const 
 // Q6_K with one batch row: two lanes per block, lane h taking both 16-value
 // groups of half h (the 32 activation words stay in registers); the two
 // integer partial sums add up exactly through one shuffle.
+// A4: the block starts on a 4-byte boundary (plain word loads, no byte
+// permutes); else on a 2-byte boundary
+template <bool A4>
 __device__ __forceinline__ void term_q6_k_pair(const uint8_t* blk, int h, const int (&av)[32],
                                                float da, const int (&asum)[8], float* T,
                                                unsigned gmask) {
   uint32_t SC[2];
-  ld_words<2>(blk + 192 + 8 * h, SC);
+  ld_words_al<A4>(blk + 192 + 8 * h, SC);
   int part = 0;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint32_t QA[4], QB[4], QH[4];
-    ld_words<4>(blk + 64 * h + 16 * half, QA);
-    ld_words<4>(blk + 64 * h + 32 + 16 * half, QB);
-    ld_words<4>(blk + 128 + 32 * h + 16 * half, QH);
+    ld_words_al<A4>(blk + 64 * h + 16 * half, QA);
+    ld_words_al<A4>(blk + 64 * h + 32 + 16 * half, QB);
+    ld_words_al<A4>(blk + 128 + 32 * h + 16 * half, QH);
     // scales so, so+2, so+4, so+6 with so = 8h + half
     const int sc0 = (int)(int8_t)(SC[0] >> (8 * half));
     const int sc1 = (int)(int8_t)(SC[0] >> (8 * (half + 2)));
@@ -349,7 +366,7 @@ __device__ __forceinline__ void term_q6_k_pair(const uint8_t* blk, int h, const 
     part += sc0 * s0 + sc1 * s1 + sc2 * s2 + sc3 * s3;
   }
   uint32_t DW[1];
-  ld_words<1>(blk + 208, DW);
+  ld_words_al<A4>(blk + 208, DW);
   part += __shfl_xor_sync(gmask, part, 1);
   if (h == 0) T[0] = (da * half_bits_to_float(DW[0])) * __int2float_rn(part);
 }
@@ -546,6 +563,14 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
         fq = j & 1;
         fb = fb0;
         fr = fr0;
+        if (a.par) {
+          // warp w holds the blocks of parity w & 1 of rgw row groups: slot u
+          // (0..15) takes block 2 (u % hb) + (w & 1) of row group
+          // (w >> 1) rgw + u / hb, hb = nblk / 2, rgw = 16 / hb
+          const int w = j >> 5, u = (j & 31) >> 1, hb = a.nblk >> 1;
+          fr = (w >> 1) * (16 / hb) + u / hb;
+          fb = 2 * (u % hb) + (w & 1);
+        }
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int w0 = (128 * fq + 16 * half) >> 2;
@@ -731,7 +756,11 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
               float* Tp = T + (size_t)rr * a.nb * a.tpitch + fb;
               if constexpr (WT == 8) term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
               else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, asum, a.nb, Tp, a.tpitch);
-              else if constexpr (kPair) term_q6_k_pair(rowp + fb * 210, fq, avp, dav[0], asp, Tp, gmask);
+              else if constexpr (kPair) {
+                // (a warp-uniform branch when a.par: all its blocks share a parity)
+                if (a.par && !(fb & 1)) term_q6_k_pair<true>(rowp + fb * 210, fq, avp, dav[0], asp, Tp, gmask);
+                else term_q6_k_pair<false>(rowp + fb * 210, fq, avp, dav[0], asp, Tp, gmask);
+              }
               else term_q6_k_reg<NB>(rowp + fb * 210, fq, av, dav, asum, a.nb, Tp, a.tpitch, gmask);
             }
           }
@@ -864,6 +893,13 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     a.tpitch = int8 ? ((cols / bl) | 1) : 0;
     const int lpb = (wtype == 14) ? (nbt == 1 ? 2 : 4) : 1;  // lanes per block
     a.fixed = (int8 && lpb * (cols / bl) <= kLmhTermThreads) ? 1 : 0;
+    {
+      // parity-uniform warps: every row base is 4-byte aligned (rb % 4 == 0)
+      // and a warp's 16 slots are whole groups of same-parity blocks
+      const int nblk = cols / bl, hb = nblk / 2;
+      a.par = (a.fixed && wtype == 14 && nbt == 1 && rb % 4 == 0 && nblk % 2 == 0 && hb >= 1 &&
+               16 % hb == 0) ? 1 : 0;
+    }
     auto slot_for = [&](int r) {
       return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
     };

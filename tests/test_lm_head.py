@@ -104,7 +104,8 @@ def test_types_and_paths(pkg, engine, oracle_mod, name, exact):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,cols", [("q8_0", 96), ("q4_0", 160), ("q6_k", 768), ("f16", 100),
                                        ("f32", 4099), ("q8_0", 8192), ("q6_k", 3072),
-                                       ("q8_0", 3584), ("q4_0", 3072), ("q8_0", 16384)])
+                                       ("q8_0", 3584), ("q4_0", 3072), ("q8_0", 16384),
+                                       ("q6_k", 2048), ("q6_k", 8192)])
 def test_row_layouts(pkg, engine, oracle_mod, name, cols):
     """Rows that are not a multiple of 16 bytes (one contiguous copy per
     tile, the weights' last bytes by plain loads), a dotF32 tail (cols % 8),
