@@ -66,8 +66,8 @@ struct LmhArgs {
   int tpitch;        // int8 path: floats per sum in the term table (odd)
   int gtiles;        // int8 path: tiles per group (their sums are replayed together)
   int gchains;       //            gtiles * R * nb, at most 64 (two per replay lane)
-  int par;           // Q6_K, one batch row: slots arranged so that every warp holds
-                     // blocks of one parity (so one 4-byte alignment of the block start)
+  int par;           // Q6_K at one batch row, Q8_0: slots arranged so that every warp
+                     // holds blocks of one parity (so one 4-byte alignment of the block start)
   int fixed;         // int8 path: 1 when each term thread keeps one block's
                      // activations in registers (lanes per block x blocks per
                      // row <= term threads), else 0 (generic loop)
@@ -235,18 +235,33 @@ __device__ __forceinline__ void terms_q6_k(const uint8_t* blk, int ib, const Lmh
 // ---- int8 path, fixed mapping: the thread's block index is fixed, so its
 // activation words (and scale) stay in registers for the whole kernel ------
 
-template <int NB>
+// AL: the block start modulo 4 when known for the whole warp (0 or 2: plain
+// word loads), else -1 (2-byte aligned, byte permutes)
+template <int NB, int AL = -1>
 __device__ __forceinline__ void term_q8_0_reg(const uint8_t* blk, const int (&av)[NB][16],
                                               const float (&da)[NB], int nb, float* T, int tp) {
-  uint32_t W[9];
-  ld_words<9>(blk, W);
-  const float dw = half_bits_to_float(W[0]);
+  int q[8];
+  float dw;
+  if constexpr (AL == 2) {
+    // the 32 values start on a word boundary; the scale is the high half of
+    // the word before them
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(blk + 2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = (int)w[k];
+    dw = half_bits_to_float(w[-1] >> 16);
+  } else {
+    uint32_t W[9];
+    ld_words_al<AL == 0, 9>(blk, W);
+    dw = half_bits_to_float(W[0]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = (int)__byte_perm(W[k], W[k + 1], 0x5432);
+  }
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     if (b >= nb) break;
     int s = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) s = __dp4a((int)__byte_perm(W[k], W[k + 1], 0x5432), av[b][k], s);
+    for (int k = 0; k < 8; ++k) s = __dp4a(q[k], av[b][k], s);
     T[b * tp] = (dw * da[b]) * __int2float_rn(s);
   }
 }
@@ -604,6 +619,13 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
       } else {
         fb = fb0;
         fr = fr0;
+        if (a.par) {
+          // nblk / 32 warps per row group: warp w takes the blocks of parity
+          // p of one 64-block segment: block 2 (32 seg + lane) + p
+          const int w = j >> 5, wpr = a.nblk >> 5, within = w % wpr;
+          fr = w / wpr;
+          fb = 2 * (32 * (within >> 1) + (j & 31)) + (within & 1);
+        }
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
 #pragma unroll
@@ -754,7 +776,15 @@ __global__ void __launch_bounds__(EXACT ? kLmhThreads : kLmhInt8Threads,
               if (rr >= nr) break;
               const uint8_t* rowp = tile_row(a, slot, t, rr);
               float* Tp = T + (size_t)rr * a.nb * a.tpitch + fb;
-              if constexpr (WT == 8) term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
+              if constexpr (WT == 8) {
+                // (warp-uniform when a.par: the block start is 4-aligned for even fb)
+                if (a.par) {
+                  if (fb & 1) term_q8_0_reg<NB, 2>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
+                  else term_q8_0_reg<NB, 0>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
+                } else {
+                  term_q8_0_reg<NB>(rowp + fb * 34, av, dav, a.nb, Tp, a.tpitch);
+                }
+              }
               else if constexpr (WT == 2) term_q4_0_reg<NB>(rowp + fb * 18, av, dav, asum, a.nb, Tp, a.tpitch);
               else if constexpr (kPair) {
                 // (a warp-uniform branch when a.par: all its blocks share a parity)
@@ -899,6 +929,9 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
       const int nblk = cols / bl, hb = nblk / 2;
       a.par = (a.fixed && wtype == 14 && nbt == 1 && rb % 4 == 0 && nblk % 2 == 0 && hb >= 1 &&
                16 % hb == 0) ? 1 : 0;
+      // Q8_0: nblk / 32 warps per row group, an even number (whole 64-block
+      // segments, one parity per warp)
+      if (a.fixed && wtype == 8 && rb % 4 == 0 && nblk % 64 == 0) a.par = 1;
     }
     auto slot_for = [&](int r) {
       return (int)((padded ? (int64_t)r * pitch : (int64_t)r * rb + 32 + 4) + 15) & ~15;
