@@ -199,3 +199,21 @@ def big_engine_lm(pkg):
     eng = pkg.Engine(0, max_rows=256, max_vocab=1 << 17)
     yield eng
     eng.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q6_k"])
+def test_row_slices_equal_whole(pkg, engine, name):
+    """A tensor-parallel lm_head gives rank r the rows [r*Vs, (r+1)*Vs) of the
+    output layer: projecting slices of the rows separately must give exactly
+    the logits of the whole call (a row's dot product never depends on the
+    other rows)."""
+    import torch
+    t, V, cols = TYPES[name], 6000, 4096
+    w = pkg.workloads.lm_weights(t, V, cols, seed=21)
+    dw = torch.from_numpy(w).cuda()
+    x = np.random.default_rng(22).standard_normal((1, cols)).astype(np.float32)
+    whole = engine.lm_head(dw, t, V, cols, x)
+    parts = [engine.lm_head(dw[lo:hi], t, hi - lo, cols, x)
+             for lo, hi in [(0, 2000), (2000, 4000), (4000, 6000)]]
+    assert np.array_equal(whole.view(np.uint32), np.concatenate(parts, axis=1).view(np.uint32))
