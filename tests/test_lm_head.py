@@ -217,3 +217,34 @@ def test_row_slices_equal_whole(pkg, engine, name):
     parts = [engine.lm_head(dw[lo:hi], t, hi - lo, cols, x)
              for lo, hi in [(0, 2000), (2000, 4000), (4000, 6000)]]
     assert np.array_equal(whole.view(np.uint32), np.concatenate(parts, axis=1).view(np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q4_0", "q6_k"])
+def test_special_block_scales(pkg, engine, oracle_mod, name):
+    """Block scales that are +inf, NaN, the smallest subnormal half and -0
+    (a corrupt or extreme model file): the logits follow the same IEEE
+    operations as the oracle's, bit for bit where they are numbers and NaN
+    where its are (NaN payloads are not compared: x86 and the GPU quiet them
+    differently)."""
+    t = TYPES[name]
+    rows, cols = 512, 1024
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=31).copy()
+    bb = {8: 34, 2: 18, 14: 210}[t]
+    off = {8: 0, 2: 0, 14: 208}[t]      # byte offset of the fp16 scale d in a block
+    specials = [0x7C00, 0x7E00, 0x0001, 0x8000, 0xFC00]  # +inf, NaN, subnormal, -0, -inf
+    for i, h in enumerate(specials):
+        for r in range(i, rows, 37):
+            blk = (r * 7 + i) % (w.shape[1] // bb)
+            w[r, blk * bb + off] = h & 0xFF
+            w[r, blk * bb + off + 1] = h >> 8
+    x = np.random.default_rng(32).standard_normal((2, cols)).astype(np.float32)
+    dw = _device_weights(w)
+    for exact in (False, True):
+        got = engine.lm_head(dw, t, rows, cols, x, exact=exact)
+        want = oracle_mod.lm_head(w, t, rows, cols, x, exact_matmul=exact, threads=16)
+        nan_g, nan_w = np.isnan(got), np.isnan(want)
+        assert np.array_equal(nan_g, nan_w), f"{name} exact={exact}: NaN positions differ"
+        assert nan_w.any()
+        ok = ~nan_w
+        assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32)), f"{name} exact={exact}"
