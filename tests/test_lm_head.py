@@ -248,3 +248,33 @@ def test_special_block_scales(pkg, engine, oracle_mod, name):
         assert nan_w.any()
         ok = ~nan_w
         assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32)), f"{name} exact={exact}"
+
+
+# ---- golden fixtures (tests/golden/make_golden_lmhead.py) ---------------------
+
+def _golden_lmhead():
+    import os
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "lmhead_cases.npz"))
+    return {k: z[k] for k in z.files}
+
+
+def _golden_cases(g):
+    for name, t in TYPES.items():
+        for nb in (1, 5):
+            for exact in (0, 1):
+                yield name, t, nb, exact, g[f"w_{name}"], g["x"][:nb], g[f"y_{name}_{nb}_{exact}"]
+
+
+def test_oracle_matches_golden(oracle_mod):
+    g = _golden_lmhead()
+    for name, t, nb, exact, w, x, y in _golden_cases(g):
+        got = oracle_mod.lm_head(w, t, w.shape[0], x.shape[1], x, exact_matmul=bool(exact))
+        assert np.array_equal(_bits(got), _bits(y)), (name, nb, exact)
+
+
+@pytest.mark.gpu
+def test_gpu_matches_golden(engine):
+    g = _golden_lmhead()
+    for name, t, nb, exact, w, x, y in _golden_cases(g):
+        got = engine.lm_head(_device_weights(w), t, w.shape[0], x.shape[1], x, exact=bool(exact))
+        assert np.array_equal(_bits(got), _bits(y)), (name, nb, exact)
