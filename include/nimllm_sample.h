@@ -3,7 +3,9 @@
  * sampler for nimllm.
  *
  * The library replaces the logits->token path of nimllm's Nim sampler
- * (src/nimllm/sampler.nim in the reference repository). Nim reaches it through
+ * (src/nimllm/sampler.nim in the reference repository) and the output
+ * projection that produces those logits (model.nim:466-470), plus
+ * topTokens and perplexity's per-position term. Nim reaches it through
  * {.importc, dynlib: "libnimllm_sample.so".}; the Nim `Sampler` object keeps
  * its params, its history and its RNG on the host and passes one uniform per
  * sampled row. Every entry point below cites the reference interface it
