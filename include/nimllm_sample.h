@@ -54,9 +54,12 @@ enum {
   NLS_ERR_CUDA = 2,        /* a CUDA runtime call failed; see nls_last_error() */
   NLS_ERR_NCCL = 3,        /* a collective failed (vocab-sharded mode) */
   NLS_ERR_TIMEOUT = 4,     /* a bounded wait ran out */
-  NLS_ERR_NAN_LOGITS = 5,  /* a sampling row holds NaN after penalties/bias/temperature;
-                              its out id is -1 (the reference's comparisons are
-                              inconsistent on NaN, so no result can match it) */
+  NLS_ERR_NAN_LOGITS = 5,  /* a full-sort row (top_k <= 0 or >= vocab) holds NaN after
+                              penalties/bias/temperature; its out id is -1 (the
+                              reference's stable sort then meets a comparator that
+                              is not an order, and its output depends on the sort's
+                              internals). Top-k rows with NaN return the
+                              reference's own answer (see nls_sample_batch). */
   NLS_ERR_CAPACITY = 6,    /* rows/vocab beyond the handle's limits, or a row whose
                               penalty window holds more distinct ids than supported */
   NLS_ERR_NO_DEVICE = 7    /* no usable CUDA device */
@@ -112,7 +115,14 @@ NLS_API void nls_destroy(nls_handle* h);
  *  out_probs  [rows] softmax probability of the sampled token among the
  *             candidates (probs[i] in sampler.nim:100,120); NULL = not wanted.
  *             Greedy rows report 1.0.
- *  stream     cudaStream_t (NULL = legacy default stream) */
+ *  stream     cudaStream_t (NULL = legacy default stream)
+ *
+ * NaN after penalties, bias and temperature: a top-k row (0 < top_k < vocab)
+ * gets the reference's answer. A NaN past the first top_k positions is never
+ * pushed into its heap (:91) and is left out; a NaN among them stays in the
+ * heap, every candidate probability is NaN, and the token is idx[0] when
+ * min_p > 0, else idx[top_k - 1], in the heap's output order (:94-121), with
+ * probability NaN. A full-sort row with a NaN fails (NLS_ERR_NAN_LOGITS). */
 NLS_API nls_status nls_sample_batch(nls_handle* h, const float* logits, int64_t ld, int32_t rows,
                             int32_t vocab, const nls_row_params* params,
                             const int64_t* hist_ids, const int64_t* hist_off,
@@ -137,24 +147,40 @@ NLS_API nls_status nls_top_tokens(nls_handle* h, const float* logits, int64_t ld
                                   int32_t vocab, int32_t n, int64_t* out_ids, float* out_probs,
                                   uint32_t flags, void* stream);
 
-/* Allocation-free sampling. No counterpart in the reference: it exists for
- * callers that cannot allocate GPU memory -- code running while a CUDA graph
- * is captured, allocator-less hosts, serving loops that must not touch the
- * allocator -- and so cannot use nls_create. Same semantics and arguments as
- * nls_sample_batch with NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS: every pointer
- * is device memory of the current device, the call is stream-ordered and
- * returns after the launches; a row that fails in the kernels gets out id -1.
- * It calls no cudaMalloc/cudaFree: its scratch is one fixed device array in
- * the library (about 16 MiB per device, held until exit). Limits: rows <= 4096
- * and vocab <= 262144, else NLS_ERR_CAPACITY. The first call on a device
- * looks up that array's address (make it before any stream capture). All
- * calls share the array; calls that overlap on the GPU race on it. */
+/* Allocation-free sampling. No counterpart in the reference. Some callers
+ * cannot call cudaMalloc -- a serving process that has given nearly all of
+ * the GPU's memory to its own pool (an allocation would fail there), a host
+ * whose memory policy forbids allocating after start-up, or a latency-critical
+ * decode loop that cannot afford the device-wide synchronisation that
+ * cudaMalloc/cudaFree imply -- and so cannot use nls_create. Same semantics
+ * and arguments as nls_sample_batch with NLS_DEVICE_INPUTS |
+ * NLS_DEVICE_OUTPUTS: every pointer is device memory of the current device,
+ * the call is stream-ordered and returns after the launches; a row that fails
+ * in the kernels gets out id -1 (its reason: nls_noalloc_status). It calls no
+ * cudaMalloc/cudaFree and no allocating library routine: its scratch is one
+ * fixed device array in the library (about 16 MiB, held by every GPU that
+ * loads the library until the process exits). Limits: rows <= 4096 and
+ * vocab <= 262144, else NLS_ERR_CAPACITY. The first call on a device looks up
+ * that array's address and caches it: make that first call before any stream
+ * capture begins, and do not call this entry point after cudaDeviceReset.
+ * All calls share the array, which keeps the last call's contents (the
+ * status word and counters are cleared by each call); calls that overlap on
+ * the GPU race on it. */
 NLS_API nls_status nls_sample_batch_noalloc(const float* logits, int64_t ld, int32_t rows,
                                             int32_t vocab, const nls_row_params* params,
                                             const int64_t* hist_ids, const int64_t* hist_off,
                                             const int64_t* bias_ids, const double* bias_vals,
                                             const int64_t* bias_off, const double* uniforms,
                                             int64_t* out_ids, float* out_probs, void* stream);
+
+/* Kernel-side status of the last nls_sample_batch_noalloc call on the current
+ * device (NLS_ERR_NAN_LOGITS, NLS_ERR_TIMEOUT, NLS_ERR_INVALID_ARG for a bad
+ * history offset, NLS_ERR_CAPACITY for an overfull penalty window; NLS_OK if
+ * none), copied from the library's status word in stream order. With
+ * NLS_DEVICE_OUTPUTS, `out` is device memory and the copy is asynchronous;
+ * otherwise `out` is host memory and the call waits for `stream`. Allocates
+ * nothing. No counterpart in the reference. */
+NLS_API nls_status nls_noalloc_status(int32_t* out, uint32_t flags, void* stream);
 
 /* ---- vocab-sharded mode ----------------------------------------------------
  * For logits produced by a tensor-parallel lm_head: each of P ranks (one
@@ -292,6 +318,17 @@ NLS_API nls_status nls_set_profiling(nls_handle* h, int32_t on);
  * launch over rows the streaming kernel handed back). Waits for those events.
  * `n` is the capacity of out_ms (up to 3 values are written). */
 NLS_API nls_status nls_last_kernel_ms(nls_handle* h, float* out_ms, int32_t n);
+
+/* The exponential the sampling kernels use for the reference's expf (Nim's
+ * exp(float32), i.e. the C library's expf, sampler.nim:56), evaluated on the
+ * current device for the n consecutive float bit patterns starting at
+ * first_bits: out[i] = expf(float with bits first_bits + i). out_estimate
+ * (optional) receives the cheaper estimate the full-sort kernel uses only to
+ * decide rounding units. Both are device memory; stream-ordered. For tests
+ * that hold the device function against the host's expf bit for bit.
+ * No counterpart in the reference (a numerics check of the library). */
+NLS_API nls_status nls_ref_expf_range(uint32_t first_bits, int64_t n, float* out,
+                                      float* out_estimate, void* stream);
 
 /* Human-readable text of a status code / of the handle's last CUDA error. */
 NLS_API const char* nls_status_str(nls_status s);

@@ -33,7 +33,7 @@ EXPORTS = (
     "nls_set_profiling", "nls_last_kernel_ms", "nls_sample_batch_noalloc",
     "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
     "nls_top_tokens", "nls_token_nll", "nls_lm_head", "nls_lm_head_sample",
-    "nls_device_upload", "nls_device_free",
+    "nls_device_upload", "nls_device_free", "nls_ref_expf_range", "nls_noalloc_status",
 )
 
 # ggml weight types of nls_lm_head (GgmlType codes, quant.nim:14-19)
@@ -106,6 +106,10 @@ def load(path: str | None = None):
     L.nls_lm_head_sample.restype = i32
     L.nls_lm_head_sample.argtypes = [vp, vp, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp,
                                      vp, u32, vp]
+    L.nls_noalloc_status.restype = i32
+    L.nls_noalloc_status.argtypes = [vp, u32, vp]
+    L.nls_ref_expf_range.restype = i32
+    L.nls_ref_expf_range.argtypes = [u32, i64, vp, vp, vp]
     _lib = L
     return L
 

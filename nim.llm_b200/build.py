@@ -7,6 +7,7 @@ the CUDA runtime is linked statically so the .so only needs the driver.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -51,15 +52,19 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     objdir = os.path.join(PKG, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    cmds, objs = [], []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src) + ".o")
         cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", os.path.join(PKG, "csrc"),
                "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # one nvcc per source file, compiled concurrently
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(subprocess.run, c, check=True) for c in cmds]:
+            f.result()
     tmp = LIB + ".tmp"
     subprocess.run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
                     "-Xcompiler", "-fPIC", "-o", tmp, *objs, "-cudart", "static", "-ldl"], check=True)

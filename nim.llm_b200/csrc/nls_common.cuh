@@ -90,9 +90,55 @@ __device__ __forceinline__ float key_threshold_float(uint32_t k) {
   return (f != f) ? -INFINITY : f;
 }
 
-// expf as the reference computes it (C expf, correctly rounded in practice):
-// the double-precision exponential rounded once to float.
-__device__ __forceinline__ float ref_expf(float x) { return __double2float_rn(exp((double)x)); }
+// expf as the reference computes it. Nim's exp(float32) is C expf
+// (sampler.nim:56); on x86-64 Linux that is glibc's expf (glibc >= 2.28),
+// which implements the method published in Arm's optimized-routines
+// (math/expf.c, Szabolcs Nagy, 2017) and is NOT correctly rounded: on
+// 97,052 of the floats in [-104, 0] it differs from the correctly rounded
+// exponential by one ulp. This is that method, restated operation by
+// operation in double precision, with the multiply-adds fused as in glibc's
+// x86-64 FMA build (the variant its resolver picks on any CPU with FMA):
+//   z  = x * 32/ln2;  k = round(z) (by adding 1.5 * 2^52);  r = z - k, with
+//   the product and the subtraction in one fused multiply-add;
+//   2^(k/32) = 2^(k >> 5) * T[k & 31]  (T[j] = 2^(j/32) rounded to double,
+//   stored with j/32 taken out of its exponent field);
+//   2^(r/32) ~ 1 + c2 r + c1 r^2 + c0 r^3 (the published minimax cubic);
+//   the double result rounded once to float.
+// Inputs below -0x1.9fe368p6 give 0, above 0x1.62e42ep6 +inf, NaN gives NaN.
+// Checked bit for bit against the host's glibc expf over every float (host
+// restatement) and on the GPU over [-104, 0].
+// (global memory, read through the read-only cache: a warp's 32 lanes index
+// it at different places, which constant memory would serialise)
+__device__ static const unsigned long long kExp2Tab[32] = {
+    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
+    0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
+    0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
+    0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL,
+    0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL,
+    0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
+    0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
+    0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
+__device__ __forceinline__ float ref_expf(float x) {
+  constexpr double kInvLn2N = 0x1.71547652b82fep0 * 32.0;
+  constexpr double kShift = 0x1.8p+52;
+  constexpr double kC0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
+  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / (32.0 * 32.0);
+  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  if (x != x) return x;
+  if (x < -0x1.9fe368p6f) return 0.0f;
+  if (x > 0x1.62e42ep6f) return INFINITY;
+  const double xd = (double)x;
+  double kd = __fma_rn(kInvLn2N, xd, kShift);
+  const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+  kd = __dsub_rn(kd, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const unsigned long long t = __ldg(&kExp2Tab[ki & 31ull]) + (ki << 47);
+  const double s = __longlong_as_double((long long)t);
+  const double z = __fma_rn(kC0, r, kC1);
+  double y = __fma_rn(kC2, r, 1.0);
+  y = __fma_rn(z, __dmul_rn(r, r), y);
+  return __double2float_rn(__dmul_rn(y, s));
+}
 
 // Estimate of ref_expf(x): expf, documented at 2 ulp, is within
 // kBracketRel = 2^-20 relative of ref_expf(x) where expf(x) >= 2^-120

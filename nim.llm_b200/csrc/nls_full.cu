@@ -443,6 +443,112 @@ struct TermP {
   __device__ float mid(float a) const { return __fmul_rn(a, rinv); }
 };
 
+// ---- a top-k row with a NaN among its first k positions ------------------
+// The reference's heap (sampler.nim:88-95) run as written, by one warp. Nim's
+// tuple `<` on (float32, int) goes through cmp field by field (equal: next
+// field; x < y: less; anything else, NaN included: not less), so a NaN is
+// neither below nor above any item. A NaN pushed in the first k pushes never
+// leaves the heap (only the root is replaced, and `x > h[0][0]` is false
+// for a NaN root), so it is a candidate: the softmax sum is NaN and so is
+// every probability (sampler.nim:51-57,100). Then top-p never stops
+// (`cum >= topP` is false, :107), min-p keeps one candidate (:111-114) and
+// the draw falls through to idx[n - 1] (:118-121): the token is idx[0], the
+// last item popped, when min_p > 0, else idx[k - 1], the first item popped
+// (the root). Its probability is NaN. Items: value bits << 32 | index.
+__device__ __forceinline__ float nheap_val(unsigned long long it) {
+  return __uint_as_float((uint32_t)(it >> 32));
+}
+__device__ __forceinline__ bool nheap_less(unsigned long long a, unsigned long long b) {
+  const float va = nheap_val(a), vb = nheap_val(b);
+  if (va == vb) return (uint32_t)a < (uint32_t)b;
+  return va < vb;
+}
+// heapq's _siftdown and _siftup (the steps of std/heapqueue)
+__device__ void nheap_siftdown(unsigned long long* h, int startpos, int pos) {
+  const unsigned long long item = h[pos];
+  while (pos > startpos) {
+    const int parentpos = (pos - 1) >> 1;
+    const unsigned long long parent = h[parentpos];
+    if (!nheap_less(item, parent)) break;
+    h[pos] = parent;
+    pos = parentpos;
+  }
+  h[pos] = item;
+}
+__device__ void nheap_siftup(unsigned long long* h, int len, int pos) {
+  const int startpos = pos;
+  const unsigned long long item = h[pos];
+  int child = 2 * pos + 1;
+  while (child < len) {
+    const int right = child + 1;
+    if (right < len && !nheap_less(h[child], h[right])) child = right;
+    h[pos] = h[child];
+    pos = child;
+    child = 2 * pos + 1;
+  }
+  h[pos] = item;
+  nheap_siftdown(h, startpos, pos);
+}
+// Called by the 32 lanes of one warp. y(i) is the row's value at position i
+// after penalties, bias and temperature. The heap lives in `sh` (shared
+// memory, FT_BIG items) when k fits, else in the CTA's global scratch `gl`
+// (vocab items). Lane 0 runs every heap step; the warp only looks ahead for
+// the next position that the current root lets in (re-tested after every
+// step, so the order of steps is the reference's).
+template <class LogitFn>
+__device__ void nan_heap_row(const BatchArgs& a, int row, const nls_row_params& p, int V, int K,
+                             float invT, LogitFn logit, unsigned long long* sh,
+                             unsigned long long* gl) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long* h = (K <= FT_BIG) ? sh : gl;
+  int len = 0;
+  float root = 0.0f;  // value of h[0], valid once len == K (lane 0)
+  for (int base = 0; base < V; base += 32) {
+    const int i = base + lane;
+    const float y = (i < V) ? __fmul_rn(logit(i), invT) : 0.0f;
+    int j = -1;
+    for (;;) {
+      const float rv = __shfl_sync(0xffffffffu, root, 0);
+      const unsigned m = __ballot_sync(0xffffffffu, lane > j && i < V && (i < K || y > rv));
+      if (!m) break;
+      j = __ffs(m) - 1;
+      const float yj = __shfl_sync(0xffffffffu, y, j);
+      if (lane == 0) {
+        const unsigned long long it = ((unsigned long long)__float_as_uint(yj) << 32) | (uint32_t)(base + j);
+        if (len < K) {          // h.push((x, i))
+          h[len] = it;
+          ++len;
+          nheap_siftdown(h, 0, len - 1);
+        } else if (yj > nheap_val(h[0])) {  // discard h.replace((x, i))
+          h[0] = it;
+          nheap_siftup(h, len, 0);
+        }
+        root = nheap_val(h[0]);
+      }
+    }
+  }
+  if (lane == 0) {
+    unsigned long long pick = h[0];  // the first pop: idx[k - 1]
+    if (p.min_p > 0.0) {             // the last pop: idx[0]
+      int n = len;
+      while (n > 0) {
+        const unsigned long long last = h[n - 1];
+        --n;
+        if (n > 0) {
+          pick = h[0];
+          h[0] = last;
+          nheap_siftup(h, n, 0);
+        } else {
+          pick = last;
+        }
+      }
+    }
+    a.out_ids[row] = (int64_t)(uint32_t)pick;
+    if (a.out_probs) a.out_probs[row] = __uint_as_float(0x7fc00000u);
+  }
+  __syncwarp();
+}
+
 // PAIR: launched as clusters of two CTAs (row-claiming launches of batches
 // larger than the GPU). The pair shares the first phase of the first row it
 // claims -- transform, histogram and scatter, each CTA taking one half of the
@@ -608,8 +714,13 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       uint32_t k[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float y = __fmul_rn(x[e], invT);
-        anynan |= (y != y);
+        float y = __fmul_rn(x[e], invT);
+        if (y != y) {
+          // heap rows: a NaN past the first k positions is never pushed
+          // (sampler.nim:91, `x > h[0][0]` is false), exactly like -inf there
+          if (heap && 4 * g + e >= ncand) y = -INFINITY;
+          else anynan = 1;
+        }
         k[e] = desc_key(y);
         kmin = min(kmin, k[e]);
         kmax = max(kmax, k[e]);
@@ -632,8 +743,11 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       for (; g < g1; g += FT_THREADS) transform4(g, __ldcs(src + g));
     }
     for (int i = (PAIR ? max(e0, 4 * nv4) : 4 * nv4) + tid; i < e1; i += FT_THREADS) {
-      const float y = __fmul_rn(logit(i), invT);
-      anynan |= (y != y);
+      float y = __fmul_rn(logit(i), invT);
+      if (y != y) {
+        if (heap && i >= ncand) y = -INFINITY;
+        else anynan = 1;
+      }
       const uint32_t k = desc_key(y);
       kmin = min(kmin, k);
       kmax = max(kmax, k);
@@ -660,7 +774,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         nnan += S.x_nan;
       }
       if (nnan > 0) {
-        if (tid == 0 && lead) {
+        if (heap) {
+          if (lead && warp == 0) nan_heap_row(a, row, p, V, ncand, invT, logit, S.u.big, SK);
+          __syncthreads();  // warp 0 read the patch table the next row rebuilds
+        } else if (tid == 0 && lead) {
           a.out_ids[row] = -1;
           if (a.out_probs) a.out_probs[row] = 0.0f;
           record_status(a.status, NLS_ERR_NAN_LOGITS);
@@ -670,7 +787,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       }
     } else {
       if (block_sum_int(anynan, S) > 0) {   // (its barrier also publishes ured)
-        if (tid == 0) {
+        if (heap) {
+          if (warp == 0) nan_heap_row(a, row, p, V, ncand, invT, logit, S.u.big, SK);
+          __syncthreads();  // warp 0 read the patch table the next row rebuilds
+        } else if (tid == 0) {
           a.out_ids[row] = -1;
           if (a.out_probs) a.out_probs[row] = 0.0f;
           record_status(a.status, NLS_ERR_NAN_LOGITS);

@@ -104,12 +104,6 @@ size_t light_smem_bytes(int C, int chunk) {
   return base + (size_t)bitmap_words_host(chunk) * 4 + merge;
 }
 
-__device__ __forceinline__ float fmax_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
 // Keep the candidates whose key is at least a lower bound of the K-th largest
 // (its top 16 bits, or all 32 when that leaves too many); raises S.thr.
 // Returns the new candidate count (the same value in every thread).
@@ -241,7 +235,26 @@ light_kernel(BatchArgs a, int C, int chunk) {
   if (npatch > 0 && !bad_patch) precompute_patches(T, rowp, p);
   const float invT = (mode == kModeTopK) ? __double2float_rn(__ddiv_rn(1.0, p.temperature)) : 1.0f;
 
-  float mnan = 0.0f;       // max.NaN over y: NaN iff some y is NaN
+  // A NaN among the row's first K positions enters the reference's heap in
+  // its first K pushes and never leaves it (sampler.nim:88-91); such a row
+  // goes to the full-sort kernel, which runs the heap as written. A NaN
+  // further on is never pushed (`x > h[0][0]` is false for it), and it never
+  // passes the threshold tests below either: it is simply left out.
+  if (mode == kModeTopK && lo < (int)K) {
+    const int e = min(hi, (int)K) - lo;
+    bool nan_here = false;
+    for (int i = tid; i < e; i += LT_THREADS) {
+      float x = rowp[i];
+      if (npatch > 0 && !bad_patch && patch_bit(T, i)) {
+        const int slot = patch_find(T, lo + i);
+        if (slot >= 0) x = patched_value(T, slot);
+      }
+      const float y = __fmul_rn(x, invT);
+      nan_here |= (y != y);
+    }
+    if (__syncthreads_or(nan_here) && tid == 0) S.nan = 1;
+  }
+
   float gb = 0.0f;
   int gi = INT_MAX;        // greedy: best non-NaN value and its first index
   uint32_t thr = 0u;
@@ -306,7 +319,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
         auto key0 = [&](int i, uint32_t* k) {
           const float x = (i < nvec) ? S.ring[0][i] : __ldcs(rowp + i);
           const float y = __fmul_rn(x, invT);
-          if (y != y) return false;  // NaN rows are rejected at the end
+          if (y != y) return false;  // a NaN is never a candidate (see above)
           *k = fkey(y);
           return true;
         };
@@ -438,7 +451,6 @@ light_kernel(BatchArgs a, int C, int chunk) {
         // pass bit 4j+e: element e of group j is at or above the threshold
         static_assert(4 * LT_GROUPS <= 32, "pass bits fit one word");
         uint32_t pm = 0u;
-        float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
 #pragma unroll
         for (int j = 0; j < LT_GROUPS; ++j) {
           const float x[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
@@ -449,12 +461,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
             y[e] = __fmul_rn(x[e], invT);
             pm |= (gv && y[e] >= thrf) ? (1u << (4 * j + e)) : 0u;
           }
-          m0 = fmax_nan(m0, y[0]);
-          m1 = fmax_nan(m1, y[1]);
-          m2 = fmax_nan(m2, y[2]);
-          m3 = fmax_nan(m3, y[3]);
         }
-        mnan = fmax_nan(mnan, fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3)));
         if (__any_sync(0xffffffffu, pm != 0u)) {
           const int cnt = __popc(pm);
           int incl = cnt;
@@ -502,7 +509,6 @@ light_kernel(BatchArgs a, int C, int chunk) {
           if (!excl && !(x != x) && (gi == INT_MAX || x > gb)) { gb = x; gi = lo + i; }
         } else if (mode == kModeTopK) {
           const float y = __fmul_rn(x, invT);
-          if (!excl) mnan = fmax_nan(mnan, y);
           if (!excl && y >= thrf) {
             const int pos = atomicAdd(&S.ncand, 1);
             my_max = pos + 1 > my_max ? pos + 1 : my_max;
@@ -548,7 +554,6 @@ light_kernel(BatchArgs a, int C, int chunk) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             y[e] = __fmul_rn(x[e], invT);
-            if (valid[e] && !excl[e]) mnan = fmax_nan(mnan, y[e]);
             pass[e] = valid[e] && !excl[e] && y[e] >= thrf;
             any |= pass[e];
           }
@@ -606,7 +611,6 @@ light_kernel(BatchArgs a, int C, int chunk) {
       bool pass = false;
       if (k >= 0) {
         y = __fmul_rn(patched_value(T, i), invT);
-        mnan = fmax_nan(mnan, y);
         pass = y >= thrf;
       }
       const unsigned m = __ballot_sync(0xffffffffu, pass);
@@ -646,7 +650,6 @@ light_kernel(BatchArgs a, int C, int chunk) {
 
   // ---- per-CTA results -------------------------------------------------
   if (mode == kModeTopK) {
-    if (mnan != mnan) atomicExch(&S.nan, 1);
     // Before the merge, keep only this chunk's top K (with all its ties at
     // the K-th key): the row's K-th largest key is at least every chunk's, so
     // nothing at or above it is dropped, and CTA 0 gets ~C*K candidates.
@@ -767,11 +770,10 @@ light_kernel(BatchArgs a, int C, int chunk) {
     }
     return;
   }
-  if (any_nan) {
+  if (any_nan) {  // a NaN among the first K positions: the heap as written
     if (tid == 0) {
-      a.out_ids[row] = -1;
-      if (a.out_probs) a.out_probs[row] = 0.0f;
-      record_status(a.status, NLS_ERR_NAN_LOGITS);
+      int w = atomicAdd(a.full_count, 1);
+      a.full_list[w] = row;
     }
     return;
   }

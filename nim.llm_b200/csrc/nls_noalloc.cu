@@ -1,8 +1,10 @@
 // nls_noalloc.cu -- nls_sample_batch_noalloc: sampling without allocating.
 //
-// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
-// being captured, allocator-less embedded hosts, or serving loops that must
-// never touch the allocator on the hot path. The handle-based entry points
+// Some callers cannot call cudaMalloc: a serving process that has given
+// nearly all of the GPU's memory to its own pool (an allocation would fail),
+// a host whose memory policy forbids allocating after start-up, or a
+// latency-critical decode loop that cannot afford the device-wide
+// synchronisation cudaMalloc/cudaFree imply. The handle-based entry points
 // allocate their staging and scratch in nls_create, so those callers get this
 // entry instead. It takes device pointers for every input and output, as the
 // handle path does with NLS_DEVICE_INPUTS | NLS_DEVICE_OUTPUTS, and runs the
@@ -11,11 +13,15 @@
 // that loads the library holds it (about 16 MiB) until the process exits.
 //
 // The first call on a device looks up the array's device address with
-// cudaGetSymbolAddress while that device is current, and caches it. Make
-// that first call before any stream capture. All calls share the one array
-// and it keeps the last call's contents; the counters are cleared at the
-// start of every call. Calls whose work overlaps on the GPU (different
-// streams, or different host threads on one device) race on the array.
+// cudaGetSymbolAddress while that device is current, and caches it for the
+// life of the process: make that first call before any stream capture, and
+// do not use the entry point after cudaDeviceReset (the module is reloaded
+// and the cached address goes stale). All calls share the one array and it
+// keeps the last call's contents; the status word and the counters are
+// cleared at the start of every call. Calls whose work overlaps on the GPU
+// (different streams, or different host threads on one device) race on the
+// array. nls_noalloc_status reads the status word the last call's kernels
+// left (a NaN row of a full sort, a timeout, a bad history offset).
 #include <mutex>
 
 #include "nimllm_sample.h"
@@ -49,9 +55,12 @@ cudaError_t scratch_base(int dev, uint32_t** out) {
   return cudaSuccess;
 }
 
+// CTAs per row of the streaming kernel: the handle path's choice (split rows
+// only when SMs are left, at least 2048 logits per CTA), within the portable
+// cluster size.
 int noalloc_cluster(int rows, int vocab, int sm_count) {
   int C = 1;
-  if (vocab >= 8192) C = (2 * sm_count + rows - 1) / rows;
+  if (vocab >= 8192) C = (sm_count + rows - 1) / rows;
   if (C > vocab / 2048) C = vocab / 2048;
   if (C > 8) C = 8;
   if (C < 1) C = 1;
@@ -109,5 +118,24 @@ extern "C" nls_status nls_sample_batch_noalloc(
   chunk = (chunk + 3) & ~3;
   if (nls::launch_light(a, C, chunk, st) != cudaSuccess) return NLS_ERR_CUDA;
   if (nls::launch_full(a, scratch, kNoallocVpad, kNoallocSlots, st) != cudaSuccess) return NLS_ERR_CUDA;
+  return NLS_OK;
+}
+
+extern "C" nls_status nls_noalloc_status(int32_t* out, uint32_t flags, void* stream) {
+  if (!out) return NLS_ERR_INVALID_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NLS_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return NLS_ERR_CAPACITY;
+  uint32_t* base = nullptr;
+  if (scratch_base(dev, &base) != cudaSuccess) return NLS_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (flags & NLS_DEVICE_OUTPUTS) {
+    if (cudaMemcpyAsync(out, base, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return NLS_ERR_CUDA;
+    return NLS_OK;
+  }
+  if (cudaMemcpyAsync(out, base, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return NLS_ERR_CUDA;
   return NLS_OK;
 }

@@ -3,7 +3,7 @@
 CPU: the column and row partitions cover the vocabulary and the batch once.
 GPU (2 devices): two ranks, each holding its columns of every row, sample
 through the library's NCCL transpose; every rank's results must equal the CPU
-oracle on the whole rows (the same bar as the single-GPU parity tests). The
+oracle on the whole rows bit for bit (the bar of the single-GPU parity tests). The
 NCCL id is made in this process and handed to the ranks; each rank writes its
 results to a file and exits.
 """
@@ -96,9 +96,10 @@ def test_two_rank_vocab_sharded(tmp_path, oracle_mod):
                                           w.bias_vals, w.bias_off, w.uniforms, diag=True)
         for r in range(NRANKS):
             z = np.load(tmp_path / f"{name}_{r}.npz")
-            bad = [i for i in np.nonzero(z["ids"] != ref)[0] if dg["margin"][i] >= 1e-6]
+            bad = np.nonzero(z["ids"] != ref)[0].tolist()
             assert not bad, f"{name} rank {r}: rows {bad} differ from the oracle"
-            samp = (w.params["temperature"] > 0) & (z["ids"] == ref)
-            rel = np.abs(z["probs"][samp].astype(np.float64) - dg["prob"][samp]) / \
-                np.maximum(np.abs(dg["prob"][samp]), 1e-30)
-            assert np.all(rel <= 1e-5), f"{name} rank {r}: prob rel err {rel.max()}"
+            samp = w.params["temperature"] > 0
+            got = z["probs"][samp].astype(np.float32)
+            want = dg["prob"][samp].astype(np.float32)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+                f"{name} rank {r}: probs differ from the oracle"
