@@ -58,81 +58,81 @@ def ncu_traffic():
     return {}
 
 
+_POLL_SRC = r"""
+import select, sys, time
+import pynvml as nv
+nv.nvmlInit()
+key = sys.argv[1]
+h = nv.nvmlDeviceGetHandleByUUID(key) if key.startswith("GPU-") else nv.nvmlDeviceGetHandleByPciBusId(key)
+print("max", nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), flush=True)
+while True:
+    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+    print("%.6f %d %d" % (time.time(), sm, rs), flush=True)
+    if select.select([sys.stdin], [], [], 0.002)[0]:
+        break
+"""
+
+
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons of one GPU, polled through
-    NVML (read-only queries) every few milliseconds during the timed region."""
+    NVML (read-only queries) every ~2 ms by a separate process, so that the
+    polling neither competes with the timed loop for the interpreter lock nor
+    misses the short timed region. start() returns once the poller runs;
+    stop() keeps the samples taken between the two calls."""
 
-    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
-               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
-               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
-               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
-               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake", 0x80))
 
-    def __init__(self, device, period_s: float = 0.002):
+    def __init__(self, device):
         self.device = device
-        self.period = period_s
-        self.samples: list[tuple[int, int]] = []
+        self.proc = None
         self.smax = None
-        self.stop_ev = threading.Event()
-        self.thread = None
         self.err = None
-        self.nvml = None
-        self.handle = None
-
-    def _open(self):
-        import pynvml as nv
-        import torch
-        nv.nvmlInit()
-        props = torch.cuda.get_device_properties(self.device)
-        h = None
-        try:
-            h = nv.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
-        except Exception:  # older drivers / formats: match the PCI address
-            bus = "%08X:%02X:%02X.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
-            h = nv.nvmlDeviceGetHandleByPciBusId(bus)
-        self.nvml, self.handle = nv, h
-        self.smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-
-    def _poll(self):
-        nv, h = self.nvml, self.handle
-        while True:
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.samples.append((int(sm), int(rs)))
-            except Exception as e:  # keep what was collected
-                self.err = repr(e)
-                return
-            if self.stop_ev.wait(self.period):
-                return
+        self.t0 = self.t1 = None
 
     def start(self):
+        import subprocess
+        import torch
         try:
-            self._open()
+            props = torch.cuda.get_device_properties(self.device)
+            key = "GPU-" + str(props.uuid)
+            self.proc = subprocess.Popen([sys.executable, "-c", _POLL_SRC, key], stdin=subprocess.PIPE,
+                                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            first = self.proc.stdout.readline().split()
+            if len(first) != 2 or first[0] != "max":
+                raise RuntimeError("poller did not start: " + self.proc.stderr.read()[-300:])
+            self.smax = int(first[1])
         except Exception as e:
-            self.err = f"NVML unavailable: {e!r}"
-            return
-        self.thread = threading.Thread(target=self._poll, daemon=True)
-        self.thread.start()
+            self.err = f"NVML poller unavailable: {e!r}"
+            self.proc = None
+        self.t0 = time.time()
 
     def stop(self):
-        if self.thread is None:
+        self.t1 = time.time()
+        if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
-        self.stop_ev.set()
-        self.thread.join(timeout=5)
-        nv = self.nvml
-        reasons = set()
-        for _, rs in self.samples:
-            for name, const in self.REASONS:
-                if rs & getattr(nv, const, 0):
-                    reasons.add(name)
-        sm = [c for c, _ in self.samples]
         try:
-            nv.nvmlShutdown()
+            out, _ = self.proc.communicate(input="x\n", timeout=10)
         except Exception:
-            pass
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        samples = []
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 3:
+                samples.append((float(f[0]), int(f[1]), int(f[2])))
+        inside = [x for x in samples if self.t0 <= x[0] <= self.t1]
+        reasons = set()
+        for _, _, rs in inside:
+            for name, bit in self.REASONS:
+                if rs & bit:
+                    reasons.add(name)
+        sm = [c for _, c, _ in inside]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
-                "reasons": sorted(reasons), "samples": len(sm), "source": "NVML poll every 2 ms"}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window_ms": round((self.t1 - self.t0) * 1e3, 3),
+                "source": "NVML, polled every ~2 ms by a separate process during the timed region"}
 
 
 def row_is_full(params, V):
@@ -211,7 +211,8 @@ def run_reference(args, world, rank, dist):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, BASELINE config 3 shapes and distributions)",
+        "data": "synthetic (seeded numpy PCG64 per row, BASELINE config 3 shapes and "
+                "distributions); uniforms: numpy PCG64, not Nim std/random",
         "config": config_dict(world),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
                          "sample": f"the full {w.B}-row batch per step, rows spread over "
@@ -261,11 +262,26 @@ def vocab_sharded_bench(pkg, dist, world, rank, local, dev, args):
     torch.cuda.synchronize(dev)
     dist.barrier()
     ms = reduce_max(dist, statistics.mean(times), dev)
+    # parity: the sharded call's ids and probabilities (all rows, on every
+    # rank) against one-GPU nls_sample_batch over the whole rows on this GPU
+    full = torch.from_numpy(w.logits).to(dev)
+    ids1 = torch.empty(B, dtype=torch.int64, device=dev)
+    probs1 = torch.empty(B, dtype=torch.float32, device=dev)
+    eng.sample_batch(full, params, None, None, None, None, None, unif, out_ids=ids1, out_probs=probs1,
+                     stream=stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    ok = float(np.array_equal(ids.cpu().numpy(), ids1.cpu().numpy()) and
+               _bits_equal(probs.cpu().numpy(), probs1.cpu().numpy()))
+    flag = torch.tensor([ok], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     eng.close()
     comm.close()
     return {"config": f"{name}: B={B} rows of V={V} fp32, top-k 0, top-p 0.99, T 1.0; "
                       f"the vocabulary split over {world} ranks (columns [r*Vs, (r+1)*Vs))",
             "value": B / (ms / 1e3), "unit": "rows/s", "ms_per_step": ms,
+            "parity_ok": bool(flag.item() == 1.0),
+            "parity": "ids and probabilities of all rows on every rank bitwise equal to one-GPU "
+                      "nls_sample_batch over the whole rows",
             "method": "NCCL send/recv transpose to row owners, batch kernels, all-gather of ids"}
 
 
@@ -304,6 +320,235 @@ def b1_latency(pkg, eng, dev, stream, iters: int):
             "config": "c2_llama3_b1: B=1, V=128256, top-k 40, device inputs; p50/p99 = device "
                       "time of the call (library CUDA events), host_* = wall clock of the call "
                       "through the Python binding with a stream sync"}
+
+
+def _dev_inputs(w, dev):
+    import torch
+
+    def t(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return dict(logits=t(w.logits), params=torch.from_numpy(w.params.view(np.uint8).copy()).to(dev),
+                hist_ids=t(w.hist_ids), hist_off=t(w.hist_off), bias_ids=t(w.bias_ids),
+                bias_vals=t(w.bias_vals), bias_off=t(w.bias_off), uniforms=t(w.uniforms))
+
+
+def _timed_calls(call, stream, steps, warmup, flush=None):
+    """CUDA-event device time (ms) of each of `steps` calls after `warmup`."""
+    import torch
+    for _ in range(warmup):
+        if flush is not None:
+            flush.zero_()
+        call()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call()
+        e1.record(stream)
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    return ms
+
+
+def _bits_equal(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    return bool(np.all((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))))
+
+
+def c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak):
+    """BASELINE config 4 (Qwen2 vocabulary, B = 8192 rows of V = 151936, top-k
+    50, min-p 0.02, frequency/presence penalties over 512 ids): the 8192 rows
+    split evenly over the ranks (strong scaling, no collective). Device time
+    per call, max over ranks; the streaming kernel's own time from the
+    library's events; every rank checks 8 of its rows against the oracle."""
+    import torch
+    name = "c4_qwen2_sharded"
+    B = pkg.workloads.CONFIGS[name][1]
+    rows = pkg.workloads.shard_rows(B, rank, world)
+    w = pkg.workloads.make_parallel(name, seed=SEED, rows=rows)
+    d = _dev_inputs(w, dev)
+    nb, V = w.B, w.V
+    eng = pkg.Engine(local, max_rows=nb, max_vocab=V)
+    ids = torch.empty(nb, dtype=torch.int64, device=dev)
+    probs = torch.empty(nb, dtype=torch.float32, device=dev)
+    kl = []
+
+    def call():
+        eng.sample_batch(d["logits"], d["params"], d["hist_ids"], d["hist_off"], None, None, None,
+                         d["uniforms"], out_ids=ids, out_probs=probs, stream=stream.cuda_stream,
+                         check=False)
+    eng.set_profiling(True)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms = []
+    for _ in range(args.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call()
+        e1.record(stream)
+        kl.append(eng.last_kernel_ms()[0])
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    st = eng._lib.nls_stream_status(eng._h, None)
+    eng.set_profiling(False)
+    # parity on 8 rows of this rank's shard
+    from oracle import oracle
+    oracle.build()
+    sel = np.linspace(0, nb - 1, 8).astype(np.int64)
+    sub = pkg.workloads.make(name, seed=SEED, rows=rows[sel])
+    ref, dg = oracle.sample_batch(sub.logits, sub.params, sub.hist_ids, sub.hist_off, None, None, None,
+                                  sub.uniforms, diag=True, threads=8)
+    got_ids = ids.cpu().numpy()[sel]
+    got_p = probs.cpu().numpy()[sel]
+    ok = int(st == 0 and np.array_equal(got_ids, ref) and _bits_equal(got_p, dg["prob"]))
+    mean_ms = statistics.mean(ms)
+    light_ms = statistics.mean(kl)
+    per = {"rank": rank, "rows": int(nb), "ms": mean_ms, "light_ms": light_ms}
+    eng.close()
+    del d
+    if dist is not None:
+        t = torch.tensor([float(ok)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = int(t.item())
+        allp = [None] * world
+        dist.all_gather_object(allp, per)
+    else:
+        allp = [per]
+    ms_max = reduce_max(dist, mean_ms, dev)
+    light_max = reduce_max(dist, light_ms, dev)
+    algo = int(nb) * (V * 4 + 64 + 8 + 12 + 512 * 8 + 8)  # per rank: logits, params, uniform, out, history
+    ach = algo / (light_max / 1e3) / 1e9
+    return {"config": f"{name}: B={B} rows of V={V} fp32 (N(0,3) with a Student-t(3) mixture on 1% "
+                      f"of entries), T 1.0, top-k 50, top-p 0.95, min-p 0.02, freq/pres 0.2/0.2 over "
+                      f"512 ids; rows split evenly over {world} rank(s) (strong scaling); inputs "
+                      f"{V * 4 * int(nb) / 1e9:.2f} GB per rank (larger than the L2: no flush)",
+            "value": B / (ms_max / 1e3), "unit": "rows/s", "ms_per_step": ms_max, "n_gpus": world,
+            "scaling": "strong",
+            "roofline": {"bound": "hbm", "kernel": "light_kernel", "achieved": ach, "peak": peak,
+                         "unit": "GB/s", "frac": ach / peak, "algorithmic_bytes_per_rank": algo,
+                         "ms": light_max},
+            "parity_ok": bool(ok), "parity_rows_checked": 8 * world, "per_rank": allp}
+
+
+def c5_single_gpu(pkg, local, dev, stream, args, flush):
+    """BASELINE config 5 on one GPU (64 rows of V = 151936, flat N(0,1),
+    top-k 0, top-p 0.99: every row takes the full sort) and its greedy
+    variant; L2 flushed between calls. Returns the timings and the ids/probs
+    of the sampling variant (the vocab-sharded mode's reference)."""
+    import torch
+    out = {}
+    res = {}
+    for name in ("c5_full_vocab_nucleus", "c5_full_vocab_greedy"):
+        w = pkg.workloads.make(name, seed=SEED)
+        d = _dev_inputs(w, dev)
+        eng = pkg.Engine(local, max_rows=w.B, max_vocab=w.V)
+        ids = torch.empty(w.B, dtype=torch.int64, device=dev)
+        probs = torch.empty(w.B, dtype=torch.float32, device=dev)
+
+        def call():
+            eng.sample_batch(d["logits"], d["params"], None, None, None, None, None, d["uniforms"],
+                             out_ids=ids, out_probs=probs, stream=stream.cuda_stream, check=False)
+        ms = _timed_calls(call, stream, args.steps, args.warmup, flush)
+        st = eng._lib.nls_stream_status(eng._h, None)
+        eng.close()
+        m = statistics.mean(ms)
+        out[name] = {"value": w.B / (m / 1e3), "unit": "rows/s", "ms_per_step": m, "status": st,
+                     "gb_per_s_algorithmic": w.algorithmic_bytes() / (m / 1e3) / 1e9}
+        res[name] = (ids.cpu().numpy(), probs.cpu().numpy())
+    out["config"] = ("c5_full_vocab_nucleus / _greedy on one GPU: B=64 rows of V=151936 fp32, N(0,1), "
+                     "T 1.0, top-k 0, top-p 0.99 (greedy: T 0); L2 flushed between calls")
+    return out, res
+
+
+def c1_c2_extra(pkg, local, dev, stream, args, with_cpu):
+    """Config 1 (V = 2000, 1000 draws from one row) as one batch of 1000 rows
+    and as 1000 one-row calls; config 2's greedy variant at B = 1; and the
+    oracle's time for one config-2 call and for config 1's 1000 draws on one
+    host thread (the reference samples one row per call on the caller's
+    thread)."""
+    import torch
+    sptr = stream.cuda_stream
+    out = {}
+    w1 = pkg.workloads.make("c1_tiny", seed=42)
+    rng = np.random.default_rng(42)
+    n = 1000
+    uni = rng.random(n)
+    logits = np.repeat(w1.logits, n, axis=0)
+    params = np.repeat(w1.params, n)
+    hist = np.tile(w1.hist_ids, n)
+    hoff = np.arange(0, w1.hist_ids.size * n + 1, w1.hist_ids.size, dtype=np.int64)
+    eng = pkg.Engine(local, max_rows=n, max_vocab=128256)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dl, dp, dh, dho, du = t(logits), t(params.view(np.uint8)), t(hist), t(hoff), t(uni)
+    ids = torch.empty(n, dtype=torch.int64, device=dev)
+    ms = _timed_calls(lambda: eng.sample_batch(dl, dp, dh, dho, None, None, None, du, out_ids=ids,
+                                               stream=sptr, check=False), stream, args.steps, args.warmup)
+    mb = statistics.mean(ms)
+    # 1000 one-row calls, as the reference draws (device time of each call)
+    eng.set_profiling(True)
+    one = []
+    o1 = torch.empty(1, dtype=torch.int64, device=dev)
+    for i in range(n + 20):
+        eng.sample_batch(dl[i % n:i % n + 1], dp[(i % n) * 64:(i % n + 1) * 64], dh[:64], dho[:2], None,
+                         None, None, du[i % n:i % n + 1], out_ids=o1, stream=sptr, check=False)
+        stream.synchronize()
+        if i >= 20:
+            one.append(eng.last_kernel_ms()[2] * 1e3)
+    eng.set_profiling(False)
+    one.sort()
+    out["c1_tiny"] = {"config": "c1_tiny: one row of V=2000 N(0,2), T 0.8, top-k 40, top-p 0.95, min-p "
+                                "0.05, rep 1.1 over 64 ids; 1000 draws (fresh uniforms)",
+                      "batched_1000_rows": {"ms": mb, "draws_per_s": n / (mb / 1e3)},
+                      "one_row_calls": {"p50_us": one[len(one) // 2], "p99_us": one[int(len(one) * 0.99) - 1]}}
+    # config 2 greedy variant at B = 1
+    g = pkg.workloads.make("c2_llama3_b1_greedy", seed=SEED)
+    gl, gp, gh, gho = t(g.logits), t(g.params.view(np.uint8)), t(g.hist_ids), t(g.hist_off)
+    eng.set_profiling(True)
+    lat = []
+    for i in range(args.latency_iters + 10):
+        eng.sample_batch(gl, gp, gh, gho, None, None, None, None, out_ids=o1, stream=sptr, check=False)
+        stream.synchronize()
+        if i >= 10:
+            lat.append(eng.last_kernel_ms()[2] * 1e3)
+    eng.set_profiling(False)
+    lat.sort()
+    out["c2_greedy_b1"] = {"p50_us": lat[len(lat) // 2], "p99_us": lat[int(len(lat) * 0.99) - 1],
+                           "config": "c2_llama3_b1_greedy: B=1, V=128256, T 0 (argmax after the "
+                                     "repeat penalty), device inputs; device time of a call"}
+    eng.close()
+    if with_cpu:
+        from oracle import oracle
+        oracle.build()
+        w2 = pkg.workloads.make("c2_llama3_b1", seed=SEED)
+        cl = []
+        for i in range(25):
+            t0 = time.perf_counter()
+            oracle.sample_batch(w2.logits, w2.params, w2.hist_ids, w2.hist_off, None, None, None,
+                                w2.uniforms, threads=1)
+            if i >= 5:
+                cl.append((time.perf_counter() - t0) * 1e6)
+        cl.sort()
+        t0 = time.perf_counter()
+        for i in range(n):
+            oracle.sample_batch(w1.logits, w1.params, w1.hist_ids, w1.hist_off, None, None, None,
+                                uni[i:i + 1], threads=1)
+        c1s = time.perf_counter() - t0
+        out["cpu"] = {"kind": "port", "cores": 1,
+                      "c2_one_call_p50_us": cl[len(cl) // 2],
+                      "c1_1000_draws_ms": c1s * 1e3,
+                      "sample": "C restatement of sampler.nim (oracle/) on one host thread: 20 "
+                                "config-2 calls, and config 1's 1000 draws one call each"}
+    return out
+
 
 
 def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
@@ -445,6 +690,8 @@ def main():
     ap.add_argument("--latency-iters", type=int, default=200)
     ap.add_argument("--no-vocab-sharded", action="store_true",
                     help="skip the vocab-sharded (config 5) measurement at N > 1")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config 1/2-greedy/4/5 legs")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the device-resident steps (for ncu captures); prints a short line")
     args = ap.parse_args()
@@ -523,13 +770,15 @@ def main():
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev)
     clocks.start()
-    step_ms, k_light, k_full = [], [], []
+    step_ms, k_light, k_full, host_us = [], [], [], []
     for _ in range(args.steps):
         flush.zero_()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        h0 = time.perf_counter()
         step()
+        host_us.append((time.perf_counter() - h0) * 1e6)
         e1.record(stream)
         kl, kf, _ = eng.last_kernel_ms()
         e1.synchronize()
@@ -546,6 +795,16 @@ def main():
 
     ms = reduce_max(dist, statistics.mean(step_ms), dev)
     value = B * world / (ms / 1e3)
+    # per-rank diagnostics: each rank's own step, kernel and host launch times
+    mine = {"rank": rank, "ms_mean": statistics.mean(step_ms), "ms_max": max(step_ms),
+            "light_ms": statistics.mean(k_light), "full_ms": statistics.mean(k_full),
+            "host_launch_us": statistics.median(host_us),
+            "full_rows": int(row_is_full(w.params, w.V).sum())}
+    if dist is not None:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
+    else:
+        per_rank = [mine]
     if args.kernels_only:
         if rank == 0:
             print(json.dumps({"kernels_only": True, "ms_per_step": ms, "value": value,
@@ -652,6 +911,14 @@ def main():
     if world > 1 and not args.no_vocab_sharded:
         vsh = vocab_sharded_bench(pkg, dist, world, rank, local, dev, args)
 
+    # the other BASELINE configurations
+    c4 = c5 = extra = None
+    if not args.no_configs:
+        c4 = c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak)
+        if rank == 0 and world == 1:
+            c5, _ = c5_single_gpu(pkg, local, dev, stream, args, flush)
+            extra = c1_c2_extra(pkg, local, dev, stream, args, with_cpu=not args.no_cpu_baseline)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
@@ -674,7 +941,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, BASELINE config 3 shapes and distributions)",
+            "data": "synthetic (seeded numpy PCG64 per row, BASELINE config 3 shapes and "
+                    "distributions); uniforms: numpy PCG64, not Nim std/random",
             "config": config_dict(world),
             "roofline": dict(roof[dominant], kernel=dominant),
             "roofline_kernels": roof,
@@ -686,6 +954,10 @@ def main():
             "latency_b1": latency,
             "clocks": clk,
             "vocab_sharded": vsh,
+            "per_rank": per_rank,
+            "step_ms_median_over_ranks": statistics.median([r["ms_mean"] for r in per_rank]),
+            "configs": {"c4_qwen2_sharded": c4, "c5_single_gpu": c5,
+                        "c1_c2": extra},
             "token_nll": nll,
             "lm_head": lmh,
         }

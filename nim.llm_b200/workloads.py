@@ -150,6 +150,39 @@ def make(name: str, seed: int = 1234, rows: Optional[np.ndarray] = None,
                     bias_ids, bias_vals, bias_off if bias_ids is not None else None, uni, rows)
 
 
+def make_parallel(name: str, seed: int = 1234, rows: Optional[np.ndarray] = None,
+                  V: Optional[int] = None, threads: int = 0, block: int = 64) -> Workload:
+    """`make` with the rows generated in blocks on a thread pool (numpy's
+    generators release the GIL while they fill arrays); identical values."""
+    import concurrent.futures
+    import os
+    _, B, _ = CONFIGS[name]
+    rows = np.arange(B) if rows is None else np.asarray(rows, dtype=np.int64)
+    threads = threads or (os.cpu_count() or 1)
+    if threads <= 1 or rows.size <= block:
+        return make(name, seed, rows, V)
+    parts = [rows[i:i + block] for i in range(0, rows.size, block)]
+    with concurrent.futures.ThreadPoolExecutor(max_workers=threads) as ex:
+        ws = list(ex.map(lambda r: make(name, seed, r, V), parts))
+    logits = np.concatenate([w.logits for w in ws])
+    params = np.concatenate([w.params for w in ws])
+    uni = np.concatenate([w.uniforms for w in ws])
+
+    def csr(ids_of, off_of, vals_of=None):
+        if ids_of(ws[0]) is None:
+            return None, None, None
+        ids = np.concatenate([ids_of(w) for w in ws])
+        counts = np.concatenate([np.diff(off_of(w)) for w in ws])
+        off = np.zeros(rows.size + 1, np.int64)
+        off[1:] = np.cumsum(counts)
+        vals = np.concatenate([vals_of(w) for w in ws]) if vals_of else None
+        return ids, off, vals
+
+    hid, hoff, _ = csr(lambda w: w.hist_ids, lambda w: w.hist_off)
+    bid, boff, bval = csr(lambda w: w.bias_ids, lambda w: w.bias_off, lambda w: w.bias_vals)
+    return Workload(name, logits, params, hid, hoff, bid, bval, boff, uni, rows)
+
+
 def shard_rows(B: int, rank: int, world: int) -> np.ndarray:
     """Contiguous batch shard of rank `rank` of `world` (rows are independent,
     so the batch-sharded mode needs no collective)."""

@@ -32,3 +32,21 @@ def test_reference_arm_line():
     assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert "workload" in line["config"]
+
+
+def test_parallel_workload_generation_is_identical():
+    """The bench generates config 4's 8192 rows on a thread pool; the values
+    must equal the one-thread generator's, row for row."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as g
+    pkg = g.load_package()
+    rows = np.arange(37, 37 + 150)
+    for name in ("c4_qwen2_sharded", "c3_batched_hetero"):
+        a = pkg.workloads.make(name, rows=rows, V=3000)
+        b = pkg.workloads.make_parallel(name, rows=rows, V=3000, threads=4, block=64)
+        assert np.array_equal(a.logits, b.logits) and np.array_equal(a.params, b.params)
+        assert np.array_equal(a.uniforms, b.uniforms) and np.array_equal(a.rows, b.rows)
+        for f in ("hist_ids", "hist_off", "bias_ids", "bias_vals", "bias_off"):
+            x, y = getattr(a, f), getattr(b, f)
+            assert (x is None and y is None) or np.array_equal(x, y), f
