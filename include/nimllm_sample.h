@@ -200,10 +200,26 @@ typedef struct nls_comm nls_comm;
 NLS_API nls_status nls_comm_unique_id(uint8_t* out128);
 
 /* Join the communicator of `nranks` ranks as `rank`, on CUDA `device` (the
- * device of the handle used with it). Collective: every rank calls it. */
+ * device of the handle used with it). Collective: every rank calls it. The
+ * communicator is non-blocking: the library polls its state against a host
+ * deadline (120 s here, then nls_comm_set_timeout), and a rank that does not
+ * join in time ends the call with NLS_ERR_TIMEOUT instead of a hang. */
 NLS_API nls_status nls_comm_create(nls_comm** out, const uint8_t* id128, int32_t nranks,
                                    int32_t rank, int32_t device);
 NLS_API void nls_comm_destroy(nls_comm* c);
+
+/* Host deadline, in milliseconds, of each later vocab-sharded call on `c`
+ * (default 120000): a call whose collectives have not finished by then --
+ * another rank left, died or never made the call -- aborts the communicator
+ * (ncclCommAbort, which ends the collectives in flight) and returns
+ * NLS_ERR_TIMEOUT; later calls on it return NLS_ERR_NCCL. No counterpart in
+ * the reference (single process). */
+NLS_API nls_status nls_comm_set_timeout(nls_comm* c, uint64_t ms);
+
+/* Abort the communicator at once (ncclCommAbort): for a rank that learns
+ * out of band that a peer is gone. Local; later calls on `c` return
+ * NLS_ERR_NCCL; release it with nls_comm_destroy. */
+NLS_API nls_status nls_comm_abort(nls_comm* c);
 
 /* Sample B rows whose vocabulary is split over the communicator's ranks (see
  * above). Collective and synchronous: every rank calls it with the same rows,
@@ -211,12 +227,24 @@ NLS_API void nls_comm_destroy(nls_comm* c);
  * token ids) and its own shard `logits` [rows x ld], ld >= its column count.
  * Every pointer is device memory of the handle's device; out_ids (and
  * out_probs, optional) receive all B rows on every rank. Returns the first
- * non-zero status of any rank (NLS_ERR_NCCL for a failed collective). */
+ * non-zero status of any rank (NLS_ERR_NCCL for a failed collective), or
+ * NLS_ERR_TIMEOUT when the collectives did not finish within the
+ * communicator's deadline (the communicator is then aborted). */
 NLS_API nls_status nls_sample_batch_vocab_sharded(
     nls_handle* h, nls_comm* c, const float* logits, int64_t ld, int32_t rows, int32_t vocab,
     const nls_row_params* params, const int64_t* hist_ids, const int64_t* hist_off,
     const int64_t* bias_ids, const double* bias_vals, const int64_t* bias_off,
     const double* uniforms, int64_t* out_ids, float* out_probs, void* stream);
+
+/* Limit, in nanoseconds, of the bounded waits in which the streaming kernel
+ * (greedy and top-k <= 256 rows) waits for its bulk copies of logits
+ * (default 200 ms; later calls on this handle use it). A wait that runs out
+ * fails its row (id -1) with NLS_ERR_TIMEOUT, after the kernel has waited,
+ * with the default limit, for the copies it has in flight. A limit of 0 is a
+ * deadline already past: every such wait gives up at once, which drives that
+ * failure path on purpose (tests of the timeout handling). No counterpart in
+ * the reference (its sampler runs on the host and waits for nothing). */
+NLS_API nls_status nls_set_wait_limit(nls_handle* h, uint64_t ns);
 
 /* Kernel-side status of the last asynchronous call on this handle: waits for
  * `stream` and returns the first error the kernels recorded (NLS_OK if none). */

@@ -34,6 +34,7 @@ EXPORTS = (
     "nls_comm_unique_id", "nls_comm_create", "nls_comm_destroy", "nls_sample_batch_vocab_sharded",
     "nls_top_tokens", "nls_token_nll", "nls_lm_head", "nls_lm_head_sample",
     "nls_device_upload", "nls_device_free", "nls_ref_expf_range", "nls_noalloc_status",
+    "nls_set_wait_limit", "nls_comm_set_timeout", "nls_comm_abort",
 )
 
 # ggml weight types of nls_lm_head (GgmlType codes, quant.nim:14-19)
@@ -106,6 +107,12 @@ def load(path: str | None = None):
     L.nls_lm_head_sample.restype = i32
     L.nls_lm_head_sample.argtypes = [vp, vp, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp,
                                      vp, u32, vp]
+    L.nls_comm_set_timeout.restype = i32
+    L.nls_comm_set_timeout.argtypes = [vp, ctypes.c_uint64]
+    L.nls_comm_abort.restype = i32
+    L.nls_comm_abort.argtypes = [vp]
+    L.nls_set_wait_limit.restype = i32
+    L.nls_set_wait_limit.argtypes = [vp, ctypes.c_uint64]
     L.nls_noalloc_status.restype = i32
     L.nls_noalloc_status.argtypes = [vp, u32, vp]
     L.nls_ref_expf_range.restype = i32

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <ctime>
 #include <new>
 
 #include "nls_kernels.h"
@@ -50,6 +51,8 @@ struct nls_handle {
   // done, [3] fallback launch done
   int profiling = 0;
   int profiled = 0;
+  // limit of the streaming kernel's bulk-copy waits (nls_set_wait_limit)
+  unsigned long long wait_ns = 200ull * 1000ull * 1000ull;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
   // vocab-sharded calls: packed shard, received shards, gathered ids/probs
   float* d_sh_send = nullptr;
@@ -83,6 +86,9 @@ struct nls_comm {
   int nranks = 0;
   int rank = 0;
   int device = 0;
+  // host deadline of each collective call (nls_comm_set_timeout)
+  unsigned long long timeout_ms = 120000ull;
+  bool aborted = false;  // ncclCommAbort has run: the communicator is dead
 };
 
 namespace {
@@ -161,6 +167,7 @@ constexpr int kMaxRanks = 64;
 nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, cudaStream_t st,
                      bool keep_status = false) {
   nls::BatchArgs a = a_in;
+  a.wait_ns = h->wait_ns;
   a.status = h->d_work;
   a.full_count = h->d_work + 1;
   a.full_list = h->d_work + 4;
@@ -239,6 +246,12 @@ const char* nls_status_str(nls_status s) {
 }
 
 const char* nls_last_error(const nls_handle* h) { return h ? h->last_err : "null handle"; }
+
+nls_status nls_set_wait_limit(nls_handle* h, uint64_t ns) {
+  if (!h) return NLS_ERR_INVALID_ARG;
+  h->wait_ns = ns;
+  return NLS_OK;
+}
 
 void nls_destroy(nls_handle* h) {
   if (!h) return;
@@ -716,6 +729,56 @@ nls_status nls_stream_status(nls_handle* h, void* stream) {
 }
 
 
+}  // extern "C"
+
+namespace {
+
+unsigned long long now_ms() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (unsigned long long)ts.tv_sec * 1000ull + (unsigned long long)ts.tv_nsec / 1000000ull;
+}
+
+void pause_us(long us) {
+  timespec ts{0, us * 1000L};
+  nanosleep(&ts, nullptr);
+}
+
+// End the communicator at once (pending collectives on it end too).
+void abort_comm(const nls::NcclApi& n, nls_comm* c) {
+  if (c->comm && !c->aborted) {
+    DeviceGuard g(c->device);
+    n.CommAbort(c->comm);
+  }
+  c->aborted = true;
+}
+
+// Non-blocking communicator: wait until its state leaves ncclInProgress.
+// An error aborts it (NLS_ERR_NCCL); so does the deadline (NLS_ERR_TIMEOUT).
+nls_status comm_settle(const nls::NcclApi& n, nls_comm* c, unsigned long long deadline,
+                       char* err, size_t errlen, const char* what) {
+  for (;;) {
+    ncclResult_t r = ncclSuccess;
+    if (n.CommGetAsyncError(c->comm, &r) != ncclSuccess) r = ncclInternalError;
+    if (r == ncclSuccess) return NLS_OK;
+    if (r != ncclInProgress) {
+      if (err) snprintf(err, errlen, "%s: %s", what, n.GetErrorString(r));
+      abort_comm(n, c);
+      return NLS_ERR_NCCL;
+    }
+    if (now_ms() > deadline) {
+      if (err) snprintf(err, errlen, "%s: no progress within %llu ms", what, c->timeout_ms);
+      abort_comm(n, c);
+      return NLS_ERR_TIMEOUT;
+    }
+    pause_us(20);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
 nls_status nls_comm_unique_id(uint8_t* out) {
   if (!out) return NLS_ERR_INVALID_ARG;
   const nls::NcclApi& n = nls::nccl_api();
@@ -741,23 +804,59 @@ nls_status nls_comm_create(nls_comm** out, const uint8_t* id, int32_t nranks, in
   memcpy(uid.internal, id, NCCL_UNIQUE_ID_BYTES);
   nls_comm* c = new (std::nothrow) nls_comm();
   if (!c) return NLS_ERR_CAPACITY;
-  if (n.CommInitRank(&c->comm, nranks, uid, rank) != ncclSuccess) {
-    delete c;
-    return NLS_ERR_NCCL;
-  }
   c->nranks = nranks;
   c->rank = rank;
   c->device = device;
+  // non-blocking: every call returns at once and the library polls the
+  // communicator's state against a host deadline, so a rank that never
+  // joins (or leaves) ends in NLS_ERR_TIMEOUT and ncclCommAbort, not a hang
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  const ncclResult_t r = n.CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    if (c->comm) n.CommAbort(c->comm);
+    delete c;
+    return NLS_ERR_NCCL;
+  }
+  const nls_status st = comm_settle(n, c, now_ms() + c->timeout_ms, nullptr, 0, "ncclCommInitRankConfig");
+  if (st != NLS_OK) {
+    delete c;
+    return st;
+  }
   *out = c;
+  return NLS_OK;
+}
+
+nls_status nls_comm_set_timeout(nls_comm* c, uint64_t ms) {
+  if (!c || ms == 0) return NLS_ERR_INVALID_ARG;
+  c->timeout_ms = ms;
+  return NLS_OK;
+}
+
+nls_status nls_comm_abort(nls_comm* c) {
+  if (!c) return NLS_ERR_INVALID_ARG;
+  const nls::NcclApi& n = nls::nccl_api();
+  if (!n.ok) return NLS_ERR_NCCL;
+  abort_comm(n, c);
   return NLS_OK;
 }
 
 void nls_comm_destroy(nls_comm* c) {
   if (!c) return;
   const nls::NcclApi& n = nls::nccl_api();
-  if (n.ok && c->comm) {
+  if (n.ok && c->comm && !c->aborted) {
     DeviceGuard g(c->device);
-    n.CommDestroy(c->comm);
+    // a non-blocking communicator may report ncclInProgress while it tears
+    // down; wait for that within its deadline (abort if it runs out)
+    const ncclResult_t r = n.CommDestroy(c->comm);
+    if (r == ncclInProgress) {
+      const unsigned long long deadline = now_ms() + c->timeout_ms;
+      ncclResult_t a = ncclInProgress;
+      while (n.CommGetAsyncError(c->comm, &a) == ncclSuccess && a == ncclInProgress && now_ms() <= deadline)
+        pause_us(20);
+    } else if (r != ncclSuccess) {
+      n.CommAbort(c->comm);
+    }
   }
   delete c;
 }
@@ -783,9 +882,11 @@ nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const floa
   if ((bias_ids == nullptr) != (bias_off == nullptr) || (bias_ids == nullptr) != (bias_vals == nullptr))
     return NLS_ERR_INVALID_ARG;
   if (c->device != h->device) return NLS_ERR_INVALID_ARG;
+  if (c->aborted) return NLS_ERR_NCCL;
   if (rows > h->max_rows || vocab > h->max_vocab) return NLS_ERR_CAPACITY;
   const nls::NcclApi& n = nls::nccl_api();
   if (!n.ok) return NLS_ERR_NCCL;
+  const unsigned long long deadline = now_ms() + c->timeout_ms;
   DeviceGuard g(h->device);
   cudaStream_t st = (cudaStream_t)stream;
   auto r0 = [&](int q) { return (int)((int64_t)rows * q / P); };  // rank q owns rows [r0(q), r0(q+1))
@@ -808,10 +909,16 @@ nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const floa
                                   cudaMemcpyDeviceToDevice, st));
     src = h->d_sh_send;
   }
+  // (a non-blocking communicator may answer ncclInProgress: the operation
+  // is being enqueued; the communicator is settled before the next one)
   auto ncclok = [&](ncclResult_t r, const char* what) {
-    if (r == ncclSuccess) return true;
+    if (r == ncclSuccess || r == ncclInProgress) return true;
     snprintf(h->last_err, sizeof h->last_err, "%s: %s", what, n.GetErrorString(r));
+    abort_comm(n, c);
     return false;
+  };
+  auto settle = [&](const char* what) {
+    return comm_settle(n, c, deadline, h->last_err, sizeof h->last_err, what);
   };
   if (!ncclok(n.GroupStart(), "ncclGroupStart")) return NLS_ERR_NCCL;
   bool ok = true;
@@ -824,6 +931,7 @@ nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const floa
                          c->comm, st), "ncclRecv");
   }
   if (!ncclok(n.GroupEnd(), "ncclGroupEnd") || !ok) return NLS_ERR_NCCL;
+  if ((s = settle("ncclGroupEnd")) != NLS_OK) return s;
   // 2. assemble the owned rows and sample them like any batch
   if (Bown > 0) {
     for (int q = 0; q < P; ++q)
@@ -851,9 +959,11 @@ nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const floa
   if (Bown > 0) NLS_CUDA(h, cudaMemcpyAsync(h->d_sh_mine + Bmax, h->d_work, sizeof(int), cudaMemcpyDeviceToDevice, st));
   if (!ncclok(n.AllGather(h->d_sh_mine, h->d_sh_all, (size_t)Bmax + 1, ncclInt64, c->comm, st), "ncclAllGather"))
     return NLS_ERR_NCCL;
+  if ((s = settle("ncclAllGather")) != NLS_OK) return s;
   if (out_probs &&
       !ncclok(n.AllGather(h->d_sh_pmine, h->d_sh_pall, (size_t)Bmax, ncclFloat, c->comm, st), "ncclAllGather"))
     return NLS_ERR_NCCL;
+  if (out_probs && (s = settle("ncclAllGather")) != NLS_OK) return s;
   for (int q = 0; q < P; ++q) {
     const int nq = r0(q + 1) - r0(q);
     if (nq > 0) {
@@ -866,7 +976,30 @@ nls_status nls_sample_batch_vocab_sharded(nls_handle* h, nls_comm* c, const floa
     NLS_CUDA(h, cudaMemcpyAsync(h->h_sh_status + q, h->d_sh_all + (size_t)q * (Bmax + 1) + Bmax,
                                 sizeof(int64_t), cudaMemcpyDeviceToHost, st));
   }
-  NLS_CUDA(h, cudaStreamSynchronize(st));
+  // wait for the stream against the deadline: a rank that does not take part
+  // (gone, or stuck before this call) leaves the collectives waiting, and the
+  // library then aborts the communicator instead of waiting for good
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return cuda_fail(h, q, "cudaStreamQuery");
+    ncclResult_t ae = ncclSuccess;
+    if (n.CommGetAsyncError(c->comm, &ae) != ncclSuccess || (ae != ncclSuccess && ae != ncclInProgress)) {
+      snprintf(h->last_err, sizeof h->last_err, "NCCL: %s", n.GetErrorString(ae));
+      abort_comm(n, c);
+      return NLS_ERR_NCCL;
+    }
+    if (now_ms() > deadline) {
+      snprintf(h->last_err, sizeof h->last_err, "vocab-sharded call: the collectives did not finish "
+               "within %llu ms; communicator aborted", c->timeout_ms);
+      abort_comm(n, c);
+      // the aborted collectives end; let the stream drain (bounded)
+      const unsigned long long drain = now_ms() + 10000ull;
+      while (cudaStreamQuery(st) == cudaErrorNotReady && now_ms() <= drain) pause_us(100);
+      return NLS_ERR_TIMEOUT;
+    }
+    pause_us(20);
+  }
   for (int q = 0; q < P; ++q)
     if (h->h_sh_status[q] != 0) return (nls_status)h->h_sh_status[q];
   return NLS_OK;

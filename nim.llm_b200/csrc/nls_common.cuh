@@ -67,6 +67,10 @@ struct BatchArgs {
   // Streaming kernel: leave full-path rows alone (a concurrent full-sort
   // launch claims them) instead of appending them to full_list.
   int skip_full;
+  // Limit of the streaming kernel's waits for its bulk copies (ns; 0 gives
+  // up at once). The drain of copies in flight before a CTA exits always
+  // waits up to kWaitLimitNs.
+  unsigned long long wait_ns;
 };
 
 __device__ __forceinline__ void record_status(int* st, int code) { atomicCAS(st, 0, code); }

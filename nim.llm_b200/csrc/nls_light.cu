@@ -306,7 +306,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
     const int sbase = si * LT_STAGE;
     const int buf = si % LT_NSTAGE;
     bool failed_local = false;
-    if (stage_bytes(si) > 0 && !mbar_wait_bounded(&S.full_bar[buf], (uint32_t)(si / LT_NSTAGE) & 1u)) {
+    if (stage_bytes(si) > 0 &&
+        !mbar_wait_bounded(&S.full_bar[buf], (uint32_t)(si / LT_NSTAGE) & 1u, a.wait_ns)) {
       failed_local = true;
       S.failed = 1;
     }
@@ -592,7 +593,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
       thrf = key_threshold_float(thr);
     }
   }
-  // Leave no bulk copy in flight into this CTA's shared memory (bounded).
+  // Leave no bulk copy in flight into this CTA's shared memory (bounded by
+  // the normal limit, whatever the call's: these copies are real and land).
   if (tid == 0 && tma) {
     for (int s2 = si; s2 < nst && s2 < si + LT_NSTAGE; ++s2) {
       if (stage_bytes(s2) && !mbar_wait_bounded(&S.full_bar[s2 % LT_NSTAGE], (uint32_t)(s2 / LT_NSTAGE) & 1u))

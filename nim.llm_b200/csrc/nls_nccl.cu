@@ -32,6 +32,9 @@ const NcclApi& nccl_api() {
     if (!lib) return;
     api.ok = sym(lib, "ncclGetUniqueId", &api.GetUniqueId) &&
              sym(lib, "ncclCommInitRank", &api.CommInitRank) &&
+             sym(lib, "ncclCommInitRankConfig", &api.CommInitRankConfig) &&
+             sym(lib, "ncclCommGetAsyncError", &api.CommGetAsyncError) &&
+             sym(lib, "ncclCommAbort", &api.CommAbort) &&
              sym(lib, "ncclCommDestroy", &api.CommDestroy) &&
              sym(lib, "ncclGroupStart", &api.GroupStart) && sym(lib, "ncclGroupEnd", &api.GroupEnd) &&
              sym(lib, "ncclSend", &api.Send) && sym(lib, "ncclRecv", &api.Recv) &&

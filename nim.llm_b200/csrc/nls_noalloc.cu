@@ -110,6 +110,7 @@ extern "C" nls_status nls_sample_batch_noalloc(
   a.full_count = work + 1;
   a.full_list = work + 2;
   a.argmax_only = 0;
+  a.wait_ns = 200ull * 1000ull * 1000ull;  // the library's default wait limit
   uint32_t* scratch = base + kWorkWords;
 
   if (cudaMemsetAsync(work, 0, 2 * sizeof(int), st) != cudaSuccess) return NLS_ERR_CUDA;

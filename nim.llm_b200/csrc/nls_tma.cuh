@@ -88,13 +88,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete; false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Wait for phase `parity` of `bar` to complete; false once `limit_ns` have
+// passed. A limit of 0 is a deadline already past: the wait gives up at once
+// without looking (a caller's setting that drives the timeout path).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
+  if (limit_ns == 0) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

@@ -197,6 +197,11 @@ class Engine:
         self._check(st, "nls_sample_batch_vocab_sharded")
         return out_ids, out_probs
 
+    def set_wait_limit(self, ns: int) -> None:
+        """Limit of the streaming kernel's bulk-copy waits, in ns (default
+        200 ms); 0 makes every such wait give up (nls_set_wait_limit)."""
+        self._check(self._lib.nls_set_wait_limit(self._h, int(ns)), "nls_set_wait_limit")
+
     def set_profiling(self, on: bool = True) -> None:
         self._check(self._lib.nls_set_profiling(self._h, 1 if on else 0), "nls_set_profiling")
 
@@ -520,6 +525,18 @@ class Comm:
             raise NlsError(st, "nls_comm_create")
         self._c = c
         self.nranks, self.rank, self.device = nranks, rank, device
+
+    def set_timeout(self, ms: int) -> None:
+        """Host deadline of each later vocab-sharded call (nls_comm_set_timeout)."""
+        st = self._lib.nls_comm_set_timeout(self._c, int(ms))
+        if st != 0:
+            raise NlsError(st, "nls_comm_set_timeout")
+
+    def abort(self) -> None:
+        """End the communicator at once (nls_comm_abort)."""
+        st = self._lib.nls_comm_abort(self._c)
+        if st != 0:
+            raise NlsError(st, "nls_comm_abort")
 
     def close(self):
         if getattr(self, "_c", None):

@@ -168,10 +168,12 @@ static NI64 sample(Sampler* s, const NF32* logitsIn, NI64 len, int* raised) {
   NI64 hoff[2] = {0, s->hist_len};
   NI64 boff[2] = {0, s->n_bias};
   NI64 outId = -1;
+  /* an empty list is passed as NULL ids and NULL offsets together */
   NI32 st = L.sample_batch(g_handle, (NF32*)logitsIn, len, 1, (NI32)len, &prm,
-                           s->hist_len ? s->history : NULL, hoff,
+                           s->hist_len ? s->history : NULL, s->hist_len ? hoff : NULL,
                            s->n_bias ? (NI64*)s->bias_ids : NULL,
-                           s->n_bias ? (NF*)s->bias_vals : NULL, boff, &u, &outId, NULL, 0u, NULL);
+                           s->n_bias ? (NF*)s->bias_vals : NULL, s->n_bias ? boff : NULL, &u,
+                           &outId, NULL, 0u, NULL);
   if (st != 0) raise_error("nls_sample_batch", st);
   return outId;
 }
