@@ -176,9 +176,9 @@ __device__ __forceinline__ bool penalties_active(const nls_row_params& p, int64_
 // ---------------------------------------------------------------------------
 struct PatchTable {
   int* key;
-  int* cnt;
-  float* bias;     // bias as float32; after precompute_patches: the patched value
-  int* flag;       // bit 0: has bias, bit 1: bias slot holds the patched value
+  int* cnt;        // count in the penalty window | kPatchHasBias
+  float* bias;     // the position's logit as read; after precompute_patches: the patched value
+  int* flag;       // the bias as float32 bits (valid when cnt has kPatchHasBias)
   uint32_t* bits;  // bitmap over [lo, hi): bit (pos - lo) >> gshift
   int log2size;
   int lo, hi;
@@ -197,19 +197,24 @@ __device__ __forceinline__ uint32_t patch_hash(int tok, int log2size) {
   return ((uint32_t)tok * 0x9E3779B1u) >> (32 - log2size);
 }
 
-// Returns false when the table is full.
+constexpr int kPatchHasBias = 1 << 30;
+constexpr int kPatchCountMask = kPatchHasBias - 1;
+
+// Insert `tok` (with its logit `raw`, read by the caller): the thread that
+// creates the slot stores raw. Returns false when the table is full.
 __device__ __forceinline__ bool patch_insert(PatchTable& T, int tok, int cnt_add,
-                                             bool has_bias, float b, int* dup_flag) {
+                                             bool has_bias, float b, float raw, int* dup_flag) {
   const uint32_t mask = (1u << T.log2size) - 1u;
   uint32_t h = patch_hash(tok, T.log2size);
   for (uint32_t probe = 0; probe <= mask; ++probe) {
     int prev = atomicCAS(&T.key[h], -1, tok);
     if (prev == -1 || prev == tok) {
+      if (prev == -1) T.bias[h] = raw;
       if (cnt_add) atomicAdd(&T.cnt[h], cnt_add);
       if (has_bias) {
-        int old = atomicOr(&T.flag[h], 1);
-        if (old & 1) atomicExch(dup_flag, 1);
-        T.bias[h] = b;
+        int old = atomicOr(&T.cnt[h], kPatchHasBias);
+        if (old & kPatchHasBias) atomicExch(dup_flag, 1);
+        T.flag[h] = __float_as_int(b);
       }
       return true;
     }
@@ -232,11 +237,12 @@ __device__ __forceinline__ int patch_find(const PatchTable& T, int tok) {
   return -1;
 }
 
-// Penalties then bias for one logit (sampler.nim:71-76). `cnt` > 0 only when
-// the penalty block is active for the row.
+// Penalties then bias for one logit (sampler.nim:71-76). The count is > 0
+// only when the penalty block is active for the row.
 __device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int slot,
                                              const nls_row_params& p) {
-  int cnt = T.cnt[slot];
+  const int word = T.cnt[slot];
+  const int cnt = word & kPatchCountMask;
   if (cnt > 0) {
     if (p.repeat_penalty != 1.0) {
       float rp = __double2float_rn(p.repeat_penalty);
@@ -245,71 +251,90 @@ __device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int s
     double d = __dadd_rn(__dmul_rn((double)cnt, p.frequency_penalty), p.presence_penalty);
     x = __fsub_rn(x, __double2float_rn(d));
   }
-  if (T.flag[slot] & 1) x = __fadd_rn(x, T.bias[slot]);
+  if (word & kPatchHasBias) x = __fadd_rn(x, __int_as_float(T.flag[slot]));
   return x;
 }
 
-// Replace each slot's bias by the final patched logit of its position, read
-// from `chunk` (the row's logits from position lo). Block-wide; after it,
-// patched_value() gives the logit the reference sees at a patched position.
-__device__ inline void precompute_patches(PatchTable& T, const float* chunk,
-                                          const nls_row_params& p) {
+// Replace each slot's logit by the final patched logit of its position.
+// Block-wide; after it, patched_value() gives the logit the reference sees at
+// a patched position. (The logits were read while the table was built.)
+__device__ inline void precompute_patches(PatchTable& T, const nls_row_params& p) {
   const int hs = 1 << T.log2size;
   for (int i = threadIdx.x; i < hs; i += blockDim.x) {
     const int k = T.key[i];
-    if (k >= 0) {
-      const float v = patch_apply(__ldg(chunk + (k - T.lo)), T, i, p);
-      T.bias[i] = v;
-      T.flag[i] |= 2;
-    }
+    if (k >= 0) T.bias[i] = patch_apply(T.bias[i], T, i, p);
   }
   __syncthreads();
 }
 __device__ __forceinline__ float patched_value(const PatchTable& T, int slot) { return T.bias[slot]; }
 
-// Block-wide construction of the patch table for positions [lo, hi) of `row`.
-// Returns the number of patched positions (block-uniform). Sets *overflow /
-// *dup (shared ints) on a full table / a duplicate bias id.
+// Block-wide construction of the patch table for positions [lo, hi) of `row`;
+// `chunk` is the row's logits from position lo. Every id's logit is read as
+// its id is read (four ids per thread in flight), so the scattered loads
+// overlap each other and the table's initialisation. Returns the number of
+// patched positions (block-uniform). Sets *overflow / *dup (shared ints) on
+// a full table / a duplicate bias id. hs must be a multiple of blockDim.x.
 __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_params& p,
-                             PatchTable& T, int* s_counter, int* s_overflow, int* s_dup) {
+                                    PatchTable& T, const float* chunk, int* s_counter,
+                                    int* s_overflow, int* s_dup) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int hs = 1 << T.log2size;
-  for (int i = tid; i < hs; i += nt) { T.key[i] = -1; T.cnt[i] = 0; T.flag[i] = 0; }
+  constexpr int U = 4;
+  // the ids of the penalty window and of the bias list, and their logits
+  int64_t h0 = 0, h1 = 0, b0 = 0, b1 = 0;
+  if (a.hist_ids != nullptr) {
+    h0 = a.hist_off[row];
+    h1 = a.hist_off[row + 1];
+    if (!penalties_active(p, h1 - h0)) h1 = h0;
+    else if (p.repeat_last_n > 0 && h1 - h0 > p.repeat_last_n) h0 = h1 - p.repeat_last_n;  // :67
+  }
+  if (a.bias_ids != nullptr) {
+    b0 = a.bias_off[row];
+    b1 = a.bias_off[row + 1];
+  }
+  const int64_t nh = h1 - h0, ntot = nh + (b1 - b0);
+  for (int i = tid; i < hs; i += nt) { T.key[i] = -1; T.cnt[i] = 0; }
   const int nwords = patch_bitmap_words(T.hi - T.lo, T.gshift);
   for (int i = tid; i < nwords; i += nt) T.bits[i] = 0u;
   if (tid == 0) { *s_counter = 0; *s_overflow = 0; *s_dup = 0; }
-  __syncthreads();
-  if (a.hist_ids != nullptr) {
-    int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-    if (penalties_active(p, h1 - h0)) {
-      int64_t start = h0;
-      if (p.repeat_last_n > 0 && h1 - h0 > p.repeat_last_n) start = h1 - p.repeat_last_n;  // :67
-      for (int64_t i = start + tid; i < h1; i += nt) {
-        int64_t tok = a.hist_ids[i];
-        if (tok >= T.lo && tok < T.hi) {
-          if (!patch_insert(T, (int)tok, 1, false, 0.0f, s_dup)) atomicExch(s_overflow, 1);
-        }
+  for (int64_t base = 0; base < ntot; base += (int64_t)U * nt) {
+    int tok[U];
+    float raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t j = base + tid + (int64_t)u * nt;
+      int64_t t = -1;
+      if (j < nh) t = a.hist_ids[h0 + j];
+      else if (j < ntot) t = a.bias_ids[b0 + (j - nh)];
+      tok[u] = (t >= T.lo && t < T.hi) ? (int)t : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = tok[u] >= 0 ? __ldg(chunk + (tok[u] - T.lo)) : 0.0f;
+    if (base == 0) __syncthreads();  // the table is initialised
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t j = base + tid + (int64_t)u * nt;
+      if (tok[u] < 0) continue;
+      bool ok;
+      if (j < nh) {
+        ok = patch_insert(T, tok[u], 1, false, 0.0f, raw[u], s_dup);
+      } else {
+        const float b = __double2float_rn(a.bias_vals[b0 + (j - nh)]);  // b.float32 (:76)
+        ok = patch_insert(T, tok[u], 0, true, b, raw[u], s_dup);
       }
+      if (!ok) atomicExch(s_overflow, 1);
     }
   }
-  if (a.bias_ids != nullptr) {
-    int64_t b0 = a.bias_off[row], b1 = a.bias_off[row + 1];
-    for (int64_t i = b0 + tid; i < b1; i += nt) {
-      int64_t tok = a.bias_ids[i];
-      if (tok >= T.lo && tok < T.hi) {
-        float b = __double2float_rn(a.bias_vals[i]);  // b.float32 (:76)
-        if (!patch_insert(T, (int)tok, 0, true, b, s_dup)) atomicExch(s_overflow, 1);
-      }
-    }
-  }
   __syncthreads();
+  const int lane = tid & 31;
   for (int i = tid; i < hs; i += nt) {
-    int k = T.key[i];
+    const int k = T.key[i];
     if (k >= 0) {
-      int off = (k - T.lo) >> T.gshift;
+      const int off = (k - T.lo) >> T.gshift;
       atomicOr(&T.bits[off >> 5], 1u << (off & 31));
-      atomicAdd(s_counter, 1);
     }
+    const unsigned m = __ballot_sync(0xffffffffu, k >= 0);
+    if (lane == 0 && m) atomicAdd(s_counter, __popc(m));
   }
   __syncthreads();
   return *s_counter;

@@ -635,7 +635,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     const float* rowp = a.logits + (int64_t)row * a.ld;
 
     PatchTable T{S.ph.pt.hkey, S.ph.pt.hcnt, S.ph.pt.hbias, S.ph.pt.hflag, bitmap, FT_HASH_LOG2, 0, V, FT_GSHIFT};
-    const int npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
+    const int npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup);
     if (S.patch_overflow || S.dup) {
       if (tid == 0 && lead) {
         a.out_ids[row] = -1;
@@ -645,7 +645,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       if (PAIR) pair = false;
       continue;
     }
-    if (npatch > 0) precompute_patches(T, rowp, p);
+    if (npatch > 0) precompute_patches(T, p);
     if (tid == 0) S.nan = 0;
     __syncthreads();
     auto logit = [&](int i) -> float {

@@ -40,6 +40,10 @@ namespace nls {
 constexpr int LT_THREADS = 256;
 constexpr int LT_STAGE = 4096;                        // floats per bulk-copy stage (16 KB)
 constexpr int LT_NSTAGE = 4;                          // stages in flight
+// optimistic threshold: at least this many of stage 0's elements above it,
+// and about this many of the whole chunk's expected above it
+constexpr int LT_MFLOOR = 8;
+constexpr int LT_CHUNK_FLOOR = 64;
 constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per thread per stage
 constexpr int LT_CAP = 2048;                          // candidate buffer
 constexpr int LT_LIMIT = LT_CAP / 2;                  // compact above this after a stage
@@ -228,11 +232,11 @@ light_kernel(BatchArgs a, int C, int chunk) {
 
   PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, LT_HASH_LOG2, lo, hi, LT_GSHIFT};
   int npatch = 0;
-  if (!a.argmax_only) npatch = build_patches(a, row, p, T, &S.counter, &S.patch_overflow, &S.dup);
+  if (!a.argmax_only) npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup);
   const bool bad_patch = (!a.argmax_only) && (S.patch_overflow || S.dup);
   // Patched positions (penalty window, bias) get their final value once, here;
   // the streaming loops leave them out and they rejoin the candidates after.
-  if (npatch > 0 && !bad_patch) precompute_patches(T, rowp, p);
+  if (npatch > 0 && !bad_patch) precompute_patches(T, p);
   const float invT = (mode == kModeTopK) ? __double2float_rn(__ddiv_rn(1.0, p.temperature)) : 1.0f;
 
   // A NaN among the row's first K positions enters the reference's heap in
@@ -331,8 +335,8 @@ light_kernel(BatchArgs a, int C, int chunk) {
         // row's K-th largest candidate; otherwise the row goes to the
         // full-sort kernel.
         int m = (int)(((long long)2 * K * n0 + len - 1) / len);
-        const int m_floor = (int)(((long long)128 * n0 + len - 1) / len);
-        m = max(m, max(m_floor, 16));
+        const int m_floor = (int)(((long long)LT_CHUNK_FLOOR * n0 + len - 1) / len);
+        m = max(m, max(m_floor, LT_MFLOOR));
         m = min(m, n0);
         constexpr int NW = LT_THREADS / 32;
         const int r = (2 * m + NW - 1) / NW;  // per-warp rank; j = ceil(m / r) <= NW / 2 + 1
