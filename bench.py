@@ -368,7 +368,7 @@ def c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak):
     library's events; every rank checks 8 of its rows against the oracle."""
     import torch
     name = "c4_qwen2_sharded"
-    B = pkg.workloads.CONFIGS[name][1]
+    B = args.c4_rows
     rows = pkg.workloads.shard_rows(B, rank, world)
     w = pkg.workloads.make_parallel(name, seed=SEED, rows=rows)
     d = _dev_inputs(w, dev)
@@ -692,6 +692,10 @@ def main():
                     help="skip the vocab-sharded (config 5) measurement at N > 1")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the config 1/2-greedy/4/5 legs")
+    ap.add_argument("--c4-only", action="store_true",
+                    help="run only the config-4 leg (rows split over the ranks) and print it")
+    ap.add_argument("--c4-rows", type=int, default=8192,
+                    help="config-4 rows in total (8192 is the configuration; fewer for ncu captures)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the device-resident steps (for ncu captures); prints a short line")
     args = ap.parse_args()
@@ -719,6 +723,16 @@ def main():
             print(json.dumps({"latency_b1": b1_latency(pkg, eng1, dev, stream, args.latency_iters)}),
                   flush=True)
             eng1.close()
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    if args.c4_only:
+        peak, _ = peaks()
+        c4 = c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak)
+        if rank == 0:
+            print(json.dumps({"c4_qwen2_sharded": c4}), flush=True)
         if dist is not None:
             dist.barrier()
             dist.destroy_process_group()
@@ -950,7 +964,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": B * world / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 4 * args.steps,
             "latency_b1": latency,
             "clocks": clk,
             "vocab_sharded": vsh,

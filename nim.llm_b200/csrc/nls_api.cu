@@ -36,7 +36,8 @@ struct nls_handle {
   // outputs for host-output calls
   int64_t* d_out_ids = nullptr;
   float* d_out_probs = nullptr;
-  // [0] status, [1] full_count, [2] row_claim, [3] unused, [4 ..] full_list
+  // [0] status, [1] full_count, [2] row_claim, [3] claim_count,
+  // [4 .. 4+max_rows) full_list, [4+max_rows .. 4+2*max_rows) claim_list
   int* d_work = nullptr;
   // full-sort scratch: slots x 4 x vpad words
   uint32_t* d_scratch = nullptr;
@@ -202,10 +203,17 @@ nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, 
       NLS_CUDA(h, cudaEventRecord(h->ev[3], st));
     }
   } else {
-    NLS_CUDA(h, cudaEventRecord(h->fork, st));
-    NLS_CUDA(h, cudaStreamWaitEvent(h->side, h->fork, 0));
     nls::BatchArgs af = a;
     af.row_claim = h->d_work + 2;
+    af.claim_count = h->d_work + 3;
+    af.claim_list = h->d_work + 4 + h->max_rows;
+    // the full-path rows, listed first: each claim is then one atomic. The
+    // streaming kernel forks only after this, so that the full-sort kernel,
+    // whose slowest row sets the call's time, is dispatched onto the SMs
+    // first (its CTAs cannot share an SM with streaming CTAs).
+    NLS_CUDA(h, nls::launch_classify(af, h->d_work + 4 + h->max_rows, h->d_work + 3, st));
+    NLS_CUDA(h, cudaEventRecord(h->fork, st));
+    NLS_CUDA(h, cudaStreamWaitEvent(h->side, h->fork, 0));
     NLS_CUDA(h, nls::launch_full(af, h->d_scratch, h->vpad, h->slots, st));
     if (prof) NLS_CUDA(h, cudaEventRecord(h->ev[2], st));
     nls::BatchArgs al = a;
@@ -323,7 +331,7 @@ nls_status nls_create(nls_handle** out, int32_t device, int32_t max_rows, int32_
     fail(e, "cudaMalloc(out_ids)");
   } else if ((e = cudaMalloc(&h->d_out_probs, sizeof(float) * max_rows)) != cudaSuccess) {
     fail(e, "cudaMalloc(out_probs)");
-  } else if ((e = cudaMalloc(&h->d_work, sizeof(int) * (4 + max_rows))) != cudaSuccess) {
+  } else if ((e = cudaMalloc(&h->d_work, sizeof(int) * (4 + 2 * (size_t)max_rows))) != cudaSuccess) {
     fail(e, "cudaMalloc(work)");
   } else if ((e = cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking)) != cudaSuccess) {
     fail(e, "cudaStreamCreate(side)");

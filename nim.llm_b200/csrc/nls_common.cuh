@@ -61,9 +61,12 @@ struct BatchArgs {
   int* status;               // first error code recorded by any kernel
   int argmax_only;           // nls_argmax_batch: plain argmax, no params
   // Full-sort kernel: when set, it claims the rows whose parameters select
-  // the full path straight from [0, rows) through this counter, instead of
-  // reading full_list (lets it run concurrently with the streaming kernel).
+  // the full path through this counter from claim_list[0 .. *claim_count)
+  // (written by classify_full_rows), instead of reading full_list (lets it
+  // run concurrently with the streaming kernel).
   int* row_claim;
+  const int* claim_list;
+  const int* claim_count;
   // Streaming kernel: leave full-path rows alone (a concurrent full-sort
   // launch claims them) instead of appending them to full_list.
   int skip_full;

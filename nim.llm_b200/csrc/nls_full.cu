@@ -589,11 +589,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int row;
     if (PAIR && pair) {  // CTA 0 claims for both
       if (crank_now() == 0 && tid == 0) {
-        int r;
-        while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
-          int64_t kk;
-          if (row_mode(a.params[r], V, &kk) == kModeFull) break;
-        }
+        const int i = atomicAdd(a.row_claim, 1);
+        const int r = (i < *a.claim_count) ? a.claim_list[i] : a.rows;
         S.ibuf[0] = r;
         partner()->x_row = r;
       }
@@ -602,12 +599,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       if (row >= a.rows) break;
     } else if (claim) {  // next row whose parameters select the full path
       if (tid == 0) {
-        int r;
-        while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
-          int64_t kk;
-          if (row_mode(a.params[r], V, &kk) == kModeFull) break;
-        }
-        S.ibuf[0] = r;
+        const int i = atomicAdd(a.row_claim, 1);
+        S.ibuf[0] = (i < *a.claim_count) ? a.claim_list[i] : a.rows;
       }
       __syncthreads();
       row = S.ibuf[0];
@@ -1594,6 +1587,41 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     }
     __syncthreads();
   }
+}
+
+// The rows whose parameters select the full path, in ascending order, for a
+// row-claiming full-sort launch: one block, an ordered compaction of the
+// row classification (sampler.nim:77-78, 85-86).
+__global__ void __launch_bounds__(1024) classify_full_rows(BatchArgs a, int* list, int* count) {
+  __shared__ int wsum[32];
+  __shared__ int base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int r0 = 0; r0 < a.rows; r0 += 1024) {
+    const int r = r0 + tid;
+    int64_t kk;
+    const bool full = r < a.rows && row_mode(a.params[r], a.V, &kk) == kModeFull;
+    const unsigned m = __ballot_sync(0xffffffffu, full);
+    if (lane == 0) wsum[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wsum[w];
+      before += (w < warp) ? c : 0;
+      total += c;
+    }
+    if (full) list[base + before + __popc(m & lanemask_lt())] = r;
+    __syncthreads();
+    if (tid == 0) base += total;
+    __syncthreads();
+  }
+  if (tid == 0) *count = base;
+}
+
+cudaError_t launch_classify(const BatchArgs& a, int* list, int* count, cudaStream_t stream) {
+  classify_full_rows<<<1, 1024, 0, stream>>>(a, list, count);
+  return cudaGetLastError();
 }
 
 static std::atomic<int> g_full_smem_set[kMaxDevicesAttr];

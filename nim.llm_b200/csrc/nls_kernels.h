@@ -24,6 +24,10 @@ size_t full_smem_bytes(int V);
 cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slots,
                         cudaStream_t stream, bool after_light = false);
 
+// The rows whose parameters select the full path, ascending, into
+// list[0 .. *count): what a row-claiming full-sort launch claims from.
+cudaError_t launch_classify(const BatchArgs& a, int* list, int* count, cudaStream_t stream);
+
 // topTokens: one CTA per row (up to `slots`), scratch slots as launch_full.
 size_t top_smem_bytes();
 cudaError_t launch_top(const float* logits, int64_t ld, int rows, int V, int n, int64_t* out_ids,

@@ -2,7 +2,7 @@
 //
 // One thread-block cluster per row (cluster size C = 1..16). CTA c owns the
 // chunk [c*chunk, (c+1)*chunk) of the row and reads it from HBM exactly once:
-// one thread issues bulk copies (cp.async.bulk, 16 KB stages, LT_NSTAGE in
+// one thread issues bulk copies (cp.async.bulk, 32 KB stages, LT_NSTAGE in
 // flight, mbarrier completion) into a shared-memory ring while the block
 // consumes earlier stages. On the fly it applies the row's penalties and bias
 // (a bitmap marks the patched float4 groups) and the temperature
@@ -38,12 +38,19 @@ namespace cg = cooperative_groups;
 namespace nls {
 
 constexpr int LT_THREADS = 256;
-constexpr int LT_STAGE = 4096;                        // floats per bulk-copy stage (16 KB)
-constexpr int LT_NSTAGE = 4;                          // stages in flight
+// Two 32 KB stages: per-stage costs (the mbarrier wait, the block barrier,
+// the refill) are paid per 8192 logits; measured on config 4 against 4 x 16 KB
+// (2.62 TB/s), 6 x 12 KB (2.30), 3 x 24 KB (3.12) and 3 x 32 KB at one CTA per
+// SM (2.12): 3.46 TB/s.
+constexpr int LT_STAGE = 8192;                        // floats per bulk-copy stage (32 KB)
+constexpr int LT_NSTAGE = 2;                          // stages in flight
 // optimistic threshold: at least this many of stage 0's elements above it,
 // and about this many of the whole chunk's expected above it
-constexpr int LT_MFLOOR = 8;
-constexpr int LT_CHUNK_FLOOR = 64;
+// (a threshold above the row's k-th value sends the row to the full-sort
+// kernel, which costs about 1 ms at V = 151936: with an 8192-logit stage 0,
+// floors of 8 and 64 let one config-4 row in 8192 through)
+constexpr int LT_MFLOOR = 16;
+constexpr int LT_CHUNK_FLOOR = 128;
 constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per thread per stage
 constexpr int LT_CAP = 2048;                          // candidate buffer
 constexpr int LT_LIMIT = LT_CAP / 2;                  // compact above this after a stage
