@@ -2,7 +2,7 @@
 //
 // One thread-block cluster per row (cluster size C = 1..16). CTA c owns the
 // chunk [c*chunk, (c+1)*chunk) of the row and reads it from HBM exactly once:
-// one thread issues bulk copies (cp.async.bulk, 32 KB stages, LT_NSTAGE in
+// one thread issues bulk copies (cp.async.bulk, 16 or 32 KB stages, a few in
 // flight, mbarrier completion) into a shared-memory ring while the block
 // consumes earlier stages. On the fly it applies the row's penalties and bias
 // (a bitmap marks the patched float4 groups) and the temperature
@@ -38,12 +38,16 @@ namespace cg = cooperative_groups;
 namespace nls {
 
 constexpr int LT_THREADS = 256;
-// Two 32 KB stages: per-stage costs (the mbarrier wait, the block barrier,
-// the refill) are paid per 8192 logits; measured on config 4 against 4 x 16 KB
-// (2.62 TB/s), 6 x 12 KB (2.30), 3 x 24 KB (3.12) and 3 x 32 KB at one CTA per
-// SM (2.12): 3.46 TB/s.
-constexpr int LT_STAGE = 8192;                        // floats per bulk-copy stage (32 KB)
-constexpr int LT_NSTAGE = 2;                          // stages in flight
+// Bulk-copy ring shapes (floats per stage, stages in flight); the kernel is
+// instantiated for both. A CTA that streams a whole row (one CTA per row,
+// batches of many rows) uses two 32 KB stages: per-stage costs (the mbarrier
+// wait, the block barrier, the refill) are then paid per 8192 logits;
+// measured on config 4 against 4 x 16 KB (2.62 TB/s), 6 x 12 KB (2.30),
+// 3 x 24 KB (3.12) and 3 x 32 KB at one CTA per SM (2.12): 3.46 TB/s. A row
+// split over a cluster (a few rows: each CTA holds a few thousand logits)
+// uses four 16 KB stages, so its copies and its compute overlap.
+constexpr int LT_STAGE_ROW = 8192, LT_NSTAGE_ROW = 2;
+constexpr int LT_STAGE_SPLIT = 4096, LT_NSTAGE_SPLIT = 4;
 // optimistic threshold: at least this many of stage 0's elements above it,
 // and about this many of the whole chunk's expected above it
 // (a threshold above the row's k-th value sends the row to the full-sort
@@ -51,7 +55,6 @@ constexpr int LT_NSTAGE = 2;                          // stages in flight
 // floors of 8 and 64 let one config-4 row in 8192 through)
 constexpr int LT_MFLOOR = 16;
 constexpr int LT_CHUNK_FLOOR = 128;
-constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per thread per stage
 constexpr int LT_CAP = 2048;                          // candidate buffer
 constexpr int LT_LIMIT = LT_CAP / 2;                  // compact above this after a stage
 constexpr int LT_SLOT = LT_LIMIT;                     // candidates a CTA hands to the merge
@@ -61,9 +64,9 @@ __host__ __device__ constexpr int lt_slot(int C) { return C > 8 ? LT_SLOT / 2 : 
 constexpr int LT_HASH_LOG2 = 10;
 constexpr int LT_PER_THREAD = LT_CAP / LT_THREADS;
 constexpr int LT_GSHIFT = 2;                          // one patch bit per float4 group
-static_assert(LT_STAGE % (4 * LT_THREADS) == 0, "a stage splits into whole float4 groups");
-
+template <int LT_STAGE, int LT_NSTAGE>
 struct LightShared {
+  static_assert(LT_STAGE % (4 * LT_THREADS) == 0, "a stage splits into whole float4 groups");
   float ring[LT_NSTAGE][LT_STAGE];
   uint64_t full_bar[LT_NSTAGE];
   uint32_t cand_key[LT_CAP];
@@ -109,8 +112,9 @@ static int bitmap_words_host(int chunk) {
   return (w + 3) & ~3;
 }
 
-size_t light_smem_bytes(int C, int chunk) {
-  size_t base = (sizeof(LightShared) + 15) & ~(size_t)15;
+template <int LT_STAGE, int LT_NSTAGE>
+size_t light_smem_bytes_t(int C, int chunk) {
+  size_t base = (sizeof(LightShared<LT_STAGE, LT_NSTAGE>) + 15) & ~(size_t)15;
   size_t merge = (C > 1) ? (size_t)C * lt_slot(C) * (sizeof(uint32_t) + sizeof(int)) : 0;
   return base + (size_t)bitmap_words_host(chunk) * 4 + merge;
 }
@@ -118,7 +122,8 @@ size_t light_smem_bytes(int C, int chunk) {
 // Keep the candidates whose key is at least a lower bound of the K-th largest
 // (its top 16 bits, or all 32 when that leaves too many); raises S.thr.
 // Returns the new candidate count (the same value in every thread).
-__device__ int light_compact(LightShared& S, uint32_t K) {
+template <class SharedT>
+__device__ int light_compact(SharedT& S, uint32_t K) {
   const int tid = threadIdx.x;
   const int n = S.ncand;
   auto get = [&](int i, uint32_t* k) { *k = S.cand_key[i]; return S.cand_idx[i] >= 0; };
@@ -158,8 +163,11 @@ __device__ int light_compact(LightShared& S, uint32_t K) {
   return nnew;
 }
 
+template <int LT_STAGE, int LT_NSTAGE>
 __global__ void __launch_bounds__(LT_THREADS, 2)
 light_kernel(BatchArgs a, int C, int chunk) {
+  using LightShared = nls::LightShared<LT_STAGE, LT_NSTAGE>;
+  constexpr int LT_GROUPS = LT_STAGE / 4 / LT_THREADS;  // float4 groups per thread per stage
   // a full-sort launch that depends on this grid may be scheduled now; it
   // waits (griddepcontrol.wait) for this grid's completion before reading
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -710,7 +718,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
     // not wait); after the barrier every CTA knows all counts locally.
     if (tid < C) {
       LightShared* R = cluster.map_shared_rank(&S, tid);
-      LightShared::MergeRec m;
+      typename LightShared::MergeRec m;
       m.ncand = S.ncand;
       m.flags = (S.nan ? 1 : 0) | (S.overflow ? 2 : 0) | (S.failed ? 4 : 0) | (S.nan0 ? 8 : 0);
       m.thr = S.thr_pub;
@@ -721,7 +729,7 @@ light_kernel(BatchArgs a, int C, int chunk) {
     cluster.sync();
     int offs = 0, myoff = 0;
     for (int r = 0; r < C; ++r) {
-      const LightShared::MergeRec m = S.rec[r];
+      const typename LightShared::MergeRec m = S.rec[r];
       any_nan |= m.flags & 1;
       any_over |= (m.flags >> 1) & 1;
       any_fail |= (m.flags >> 2) & 1;
@@ -975,7 +983,15 @@ light_kernel(BatchArgs a, int C, int chunk) {
   }
 }
 
-static std::atomic<int> g_light_smem_set[kMaxDevicesAttr];
+static std::atomic<int> g_light_smem_set_row[kMaxDevicesAttr];
+static std::atomic<int> g_light_smem_set_split[kMaxDevicesAttr];
+
+// one CTA per row: the whole-row ring shape; a row split over a cluster: the
+// split shape
+size_t light_smem_bytes(int C, int chunk) {
+  return C == 1 ? light_smem_bytes_t<LT_STAGE_ROW, LT_NSTAGE_ROW>(C, chunk)
+                : light_smem_bytes_t<LT_STAGE_SPLIT, LT_NSTAGE_SPLIT>(C, chunk);
+}
 
 static std::atomic<int> g_light_big_cluster[kMaxDevicesAttr];  // 0 unknown, 1 no, 2 yes
 
@@ -989,10 +1005,9 @@ int light_max_cluster(int V) {
   int ok = 1;
   const int chunk = ((V + LT_CMAX - 1) / LT_CMAX + 3) & ~3;
   const size_t smem = light_smem_bytes(LT_CMAX, chunk);
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(light_kernel),
-                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
-      ensure_smem_attr(reinterpret_cast<const void*>(light_kernel), (int)smem, g_light_smem_set) ==
-          cudaSuccess) {
+  const void* fn = reinterpret_cast<const void*>(light_kernel<LT_STAGE_SPLIT, LT_NSTAGE_SPLIT>);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+      ensure_smem_attr(fn, (int)smem, g_light_smem_set_split) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(LT_CMAX, 1, 1);
     cfg.blockDim = dim3(LT_THREADS, 1, 1);
@@ -1005,8 +1020,7 @@ int light_max_cluster(int V) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(light_kernel), &cfg) ==
-            cudaSuccess &&
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess &&
         n >= 1)
       ok = 2;
   }
@@ -1017,7 +1031,9 @@ int light_max_cluster(int V) {
 
 cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stream) {
   const size_t smem = light_smem_bytes(C, chunk);
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(light_kernel), (int)smem, g_light_smem_set);
+  const void* fn = C == 1 ? reinterpret_cast<const void*>(light_kernel<LT_STAGE_ROW, LT_NSTAGE_ROW>)
+                          : reinterpret_cast<const void*>(light_kernel<LT_STAGE_SPLIT, LT_NSTAGE_SPLIT>);
+  cudaError_t e = ensure_smem_attr(fn, (int)smem, C == 1 ? g_light_smem_set_row : g_light_smem_set_split);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.rows * C), 1, 1);
@@ -1031,7 +1047,8 @@ cudaError_t launch_light(const BatchArgs& a, int C, int chunk, cudaStream_t stre
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, light_kernel, a, C, chunk);
+  if (C == 1) return cudaLaunchKernelEx(&cfg, light_kernel<LT_STAGE_ROW, LT_NSTAGE_ROW>, a, C, chunk);
+  return cudaLaunchKernelEx(&cfg, light_kernel<LT_STAGE_SPLIT, LT_NSTAGE_SPLIT>, a, C, chunk);
 }
 
 }  // namespace nls
