@@ -972,7 +972,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": B * world / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "latency_b1": latency,
             "clocks": clk,
             "vocab_sharded": vsh,

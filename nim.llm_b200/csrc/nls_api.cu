@@ -205,13 +205,17 @@ nls_status run_batch(nls_handle* h, const nls::BatchArgs& a_in, uint32_t flags, 
   } else {
     nls::BatchArgs af = a;
     af.row_claim = h->d_work + 2;
-    af.claim_count = h->d_work + 3;
-    af.claim_list = h->d_work + 4 + h->max_rows;
-    // the full-path rows, listed first: each claim is then one atomic. The
-    // streaming kernel forks only after this, so that the full-sort kernel,
+    if (a.rows > 4 * h->sm_count) {
+      // many rows: the full-path rows are listed first, so that each claim
+      // is one atomic (walking thousands of rows per claim held every SM
+      // for ~0.1 ms on config 4); a few hundred rows are walked directly
+      af.claim_count = h->d_work + 3;
+      af.claim_list = h->d_work + 4 + h->max_rows;
+      NLS_CUDA(h, nls::launch_classify(af, h->d_work + 4 + h->max_rows, h->d_work + 3, st));
+    }
+    // The streaming kernel forks only now, so that the full-sort kernel,
     // whose slowest row sets the call's time, is dispatched onto the SMs
     // first (its CTAs cannot share an SM with streaming CTAs).
-    NLS_CUDA(h, nls::launch_classify(af, h->d_work + 4 + h->max_rows, h->d_work + 3, st));
     NLS_CUDA(h, cudaEventRecord(h->fork, st));
     NLS_CUDA(h, cudaStreamWaitEvent(h->side, h->fork, 0));
     NLS_CUDA(h, nls::launch_full(af, h->d_scratch, h->vpad, h->slots, st));

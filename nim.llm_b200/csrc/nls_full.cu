@@ -549,6 +549,24 @@ __device__ void nan_heap_row(const BatchArgs& a, int row, const nls_row_params& 
   __syncwarp();
 }
 
+// The next row whose parameters select the full path, for a row-claiming
+// launch (a.rows when none is left): from the classification's list (one
+// atomic) when there is one, else by walking the rows from the shared
+// counter (batches of a few hundred rows, where listing them first would
+// only delay the claims).
+__device__ __forceinline__ int claim_row(const BatchArgs& a, int V) {
+  if (a.claim_list != nullptr) {
+    const int i = atomicAdd(a.row_claim, 1);
+    return (i < *a.claim_count) ? a.claim_list[i] : a.rows;
+  }
+  int r;
+  while ((r = atomicAdd(a.row_claim, 1)) < a.rows) {
+    int64_t kk;
+    if (row_mode(a.params[r], V, &kk) == kModeFull) break;
+  }
+  return r;
+}
+
 // PAIR: launched as clusters of two CTAs (row-claiming launches of batches
 // larger than the GPU). The pair shares the first phase of the first row it
 // claims -- transform, histogram and scatter, each CTA taking one half of the
@@ -589,8 +607,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     int row;
     if (PAIR && pair) {  // CTA 0 claims for both
       if (crank_now() == 0 && tid == 0) {
-        const int i = atomicAdd(a.row_claim, 1);
-        const int r = (i < *a.claim_count) ? a.claim_list[i] : a.rows;
+        const int r = claim_row(a, V);
         S.ibuf[0] = r;
         partner()->x_row = r;
       }
@@ -598,10 +615,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       row = (crank_now() == 0) ? S.ibuf[0] : S.x_row;
       if (row >= a.rows) break;
     } else if (claim) {  // next row whose parameters select the full path
-      if (tid == 0) {
-        const int i = atomicAdd(a.row_claim, 1);
-        S.ibuf[0] = (i < *a.claim_count) ? a.claim_list[i] : a.rows;
-      }
+      if (tid == 0) S.ibuf[0] = claim_row(a, V);
       __syncthreads();
       row = S.ibuf[0];
       __syncthreads();
