@@ -429,6 +429,8 @@ def c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak):
     ms_max = reduce_max(dist, mean_ms, dev)
     light_max = reduce_max(dist, light_ms, dev)
     algo = int(nb) * (V * 4 + 64 + 8 + 12 + 512 * 8 + 8)  # per rank: logits, params, uniform, out, history
+    per1024 = ncu_traffic().get("light_kernel_c4_per_1024_rows")
+    traffic = int(per1024 * nb / 1024) if per1024 else None
     ach = algo / (light_max / 1e3) / 1e9
     return {"config": f"{name}: B={B} rows of V={V} fp32 (N(0,3) with a Student-t(3) mixture on 1% "
                       f"of entries), T 1.0, top-k 50, top-p 0.95, min-p 0.02, freq/pres 0.2/0.2 over "
@@ -438,7 +440,9 @@ def c4_bench(pkg, dist, world, rank, local, dev, stream, args, peak):
             "scaling": "strong",
             "roofline": {"bound": "hbm", "kernel": "light_kernel", "achieved": ach, "peak": peak,
                          "unit": "GB/s", "frac": ach / peak, "algorithmic_bytes_per_rank": algo,
-                         "ms": light_max},
+                         "ms": light_max, "traffic": traffic,
+                         "traffic_source": "ncu capture of 1024 rows (profiles/light_kernel_c4.md), "
+                                           "scaled by the rank's rows / 1024"},
             "parity_ok": bool(ok), "parity_rows_checked": 8 * world, "per_rank": allp}
 
 
