@@ -433,6 +433,29 @@ def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     assert np.array_equal(ids2[keep], ids[keep])
 
 
+def test_many_rows_claimed_from_the_classified_list(pkg, oracle_mod):
+    """Batches of more than 4 x SMs rows: a classification kernel lists the
+    full-path rows first and the full-sort CTAs claim from that list (cluster
+    pairs), beside the streaming kernel; mixed row kinds, including top-k
+    above 256 (heap rows on the full-sort path) and greedy rows."""
+    B, V = 700, 6000
+    w = pkg.workloads.make("c3_batched_hetero", seed=71, rows=np.arange(B), V=V)
+    a = as_args(w)
+    P = a["params"].copy()
+    P["top_k"][::11] = 300
+    P["temperature"][::13] = 0.0
+    a["params"] = P
+    eng = pkg.Engine(0, max_rows=B, max_vocab=V)
+    try:
+        ids, probs, st, ref, dg = run_both(eng, oracle_mod, a, threads=16)
+        assert st == 0
+        compare(ids, probs, ref, dg, P, "B=700")
+        ids2, probs2, st2 = eng.sample_batch(**a, want_probs=True)  # the list is rebuilt per call
+        assert st2 == 0 and np.array_equal(ids2, ids) and np.array_equal(probs2.view(np.uint32), probs.view(np.uint32))
+    finally:
+        eng.close()
+
+
 @pytest.mark.parametrize("seed", range(100, 108))
 def test_seed_sweep(pkg, big_engine, oracle_mod, seed):
     """Fresh seeds over three launch shapes: config 3 as benched (claiming
