@@ -825,27 +825,78 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       bk.scale = (span > 0.0f && isfinite(mx)) ? (float)(FT_NB - 1) / span : 0.0f;
       if (!isfinite(mx)) bk.dcut = INFINITY;
     }
-    for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] = 0u;
-    __syncthreads();
-    {
-      // this CTA's positions [e0, e1); e0 is a multiple of 4, KY 16-byte aligned
-      const int gk1 = PAIR ? e1 >> 2 : V >> 2;
-      for (int g = (PAIR ? (e0 >> 2) : 0) + tid; g < gk1; g += FT_THREADS) {
-        const uint4 k = reinterpret_cast<const uint4*>(KYp)[g];
-        atomicAdd(&S.h1[bk(k.x)], 1u);
-        atomicAdd(&S.h1[bk(k.y)], 1u);
-        atomicAdd(&S.h1[bk(k.z)], 1u);
-        atomicAdd(&S.h1[bk(k.w)], 1u);
+    // the row's coarse histogram (a pair: the totals of both halves in both
+    // CTAs, each holding the other's counts in x_h1)
+    auto histogram = [&]() {
+      for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] = 0u;
+      __syncthreads();
+      {
+        // this CTA's positions [e0, e1); e0 is a multiple of 4, KY 16-byte aligned
+        const int gk1 = PAIR ? e1 >> 2 : V >> 2;
+        for (int g = (PAIR ? (e0 >> 2) : 0) + tid; g < gk1; g += FT_THREADS) {
+          const uint4 k = reinterpret_cast<const uint4*>(KYp)[g];
+          atomicAdd(&S.h1[bk(k.x)], 1u);
+          atomicAdd(&S.h1[bk(k.y)], 1u);
+          atomicAdd(&S.h1[bk(k.z)], 1u);
+          atomicAdd(&S.h1[bk(k.w)], 1u);
+        }
+        for (int i = (PAIR ? max(e0, 4 * gk1) : 4 * gk1) + tid; i < e1; i += FT_THREADS) atomicAdd(&S.h1[bk(KYp[i])], 1u);
       }
-      for (int i = (PAIR ? max(e0, 4 * gk1) : 4 * gk1) + tid; i < e1; i += FT_THREADS) atomicAdd(&S.h1[bk(KYp[i])], 1u);
-    }
-    __syncthreads();
-    if constexpr (PAIR) {
-      if (pair) {  // totals; CTA 1 writes each bucket's run after CTA 0's
-        for (int b = tid; b < FT_NB; b += FT_THREADS) partner()->x_h1[b] = S.h1[b];
-        cluster_sync();
-        for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] += S.x_h1[b];
+      __syncthreads();
+      if constexpr (PAIR) {
+        if (pair) {  // totals; CTA 1 writes each bucket's run after CTA 0's
+          for (int b = tid; b < FT_NB; b += FT_THREADS) partner()->x_h1[b] = S.h1[b];
+          cluster_sync();
+          for (int b = tid; b < FT_NB; b += FT_THREADS) S.h1[b] += S.x_h1[b];
+          __syncthreads();
+        }
+      }
+    };
+    histogram();
+    {
+      // A few far outliers -- a banned token (-inf bias), a heavy tail --
+      // stretch the value-linear buckets until the bulk of the row shares a
+      // few of them, more than a window holds. Then the span is narrowed to
+      // leave at most FT_BUCKET_MAX logits beyond it (they share the last
+      // bucket, which a window sorts as one block) and the row is counted
+      // again; only repeated values still take the radix-sort fallback.
+      int bm = 0;
+      for (int b = tid; b < FT_NB; b += FT_THREADS) bm = max(bm, (int)S.h1[b]);
+      bm = block_max_int(bm, S);  // (its barriers order the reads of h1 below)
+      if (bm > FT_BUCKET_MAX && isfinite(mx) && bk.scale > 0.0f) {
+        if (warp == 0) {
+          // the smallest b* whose suffix sum_{b >= b*} h1[b] is at most
+          // FT_BUCKET_MAX (lane l holds buckets 8l .. 8l+7)
+          uint32_t loc[FT_NB / 32], sum = 0;
+#pragma unroll
+          for (int r = 0; r < FT_NB / 32; ++r) { loc[r] = S.h1[lane * (FT_NB / 32) + r]; sum += loc[r]; }
+          uint32_t suf = sum;  // inclusive suffix over lanes >= this one
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+            if (lane + o < 32) suf += v;
+          }
+          uint32_t after = suf - sum;  // buckets of the lanes above
+          int bs = FT_NB;
+#pragma unroll
+          for (int r = FT_NB / 32 - 1; r >= 0; --r) {
+            after += loc[r];
+            if (after <= (uint32_t)FT_BUCKET_MAX) bs = lane * (FT_NB / 32) + r;
+          }
+          bs = __reduce_min_sync(0xffffffffu, bs);
+          if (lane == 0) S.ibuf[4] = bs;
+        }
         __syncthreads();
+        const int bstar = S.ibuf[4];
+        __syncthreads();
+        if (bstar >= 2 && bstar < FT_NB) {
+          const float D = __fdiv_rn((float)bstar, bk.scale);  // d at bucket b*'s lower edge
+          if (D > 0.0f) {
+            bk.dcut = D;
+            bk.scale = (float)(FT_NB - 1) / D;
+            histogram();
+          }
+        }
       }
     }
     if (warp == 0) {  // exclusive scan of the 256 coarse counts (8 per lane)

@@ -433,6 +433,48 @@ def test_batch_larger_than_the_gpu(pkg, big_engine, oracle_mod):
     assert np.array_equal(ids2[keep], ids[keep])
 
 
+@pytest.mark.parametrize("B", [6, 200])  # single-CTA rows; more rows than SMs (cluster pairs)
+def test_full_rows_with_far_outliers(pkg, oracle_mod, B):
+    """Full-sort rows whose value range is stretched by a few far outliers --
+    banned tokens (a -inf bias), a heavy Student-t tail, more than 4096 -inf
+    logits -- so that value-linear buckets would squeeze the bulk of the row
+    into a few of them: the bucket span is narrowed (the radix-sort fallback
+    remains only for the last kind)."""
+    rng = np.random.default_rng(90 + B)
+    V = 40000
+    w = pkg.workloads.make("c3_batched_hetero", seed=91, rows=np.arange(B), V=V)
+    a = as_args(w)
+    P = a["params"].copy()
+    P["top_k"][:] = 0
+    a["params"] = P
+    x = a["logits"].copy()
+    bias_ids, bias_vals, boff = [], [], [0]
+    for r in range(B):
+        kind = r % 3
+        if kind == 1:  # heavy tail: 1 % of entries from a Student-t(3) x 6
+            m = rng.random(V) < 0.01
+            x[r, m] = (rng.standard_t(3.0, int(m.sum())) * 6.0).astype(np.float32)
+        elif kind == 2 and r % 2 == 0:  # more -inf logits than a bucket holds
+            x[r, rng.choice(V, 6000, replace=False)] = -np.inf
+        ids = rng.choice(V, 4 if kind == 0 else 1, replace=False)  # banned tokens
+        bias_ids += [int(i) for i in ids]
+        bias_vals += [float("-inf")] * len(ids)
+        boff.append(len(bias_ids))
+    a["logits"] = x
+    a["bias_ids"] = np.array(bias_ids, np.int64)
+    a["bias_vals"] = np.array(bias_vals, np.float64)
+    a["bias_off"] = np.array(boff, np.int64)
+    eng = pkg.Engine(0, max_rows=max(B, 8), max_vocab=V)
+    try:
+        ids, probs, st, ref, dg = run_both(eng, oracle_mod, a, threads=16)
+        assert st == 0
+        compare(ids, probs, ref, dg, P, f"outliers B={B}")
+        banned = {(r, i) for r in range(B) for i in a["bias_ids"][boff[r]:boff[r + 1]]}
+        assert all((r, int(ids[r])) not in banned for r in range(B))
+    finally:
+        eng.close()
+
+
 def test_many_rows_claimed_from_the_classified_list(pkg, oracle_mod):
     """Batches of more than 4 x SMs rows: a classification kernel lists the
     full-path rows first and the full-sort CTAs claim from that list (cluster
