@@ -60,8 +60,8 @@ enum {
                               is not an order, and its output depends on the sort's
                               internals). Top-k rows with NaN return the
                               reference's own answer (see nls_sample_batch). */
-  NLS_ERR_CAPACITY = 6,    /* rows/vocab beyond the handle's limits, or a row whose
-                              penalty window holds more distinct ids than supported */
+  NLS_ERR_CAPACITY = 6,    /* rows/vocab beyond the handle's limits (a penalty window
+                              or bias list of any length is supported) */
   NLS_ERR_NO_DEVICE = 7    /* no usable CUDA device */
 };
 
@@ -174,9 +174,9 @@ NLS_API nls_status nls_sample_batch_noalloc(const float* logits, int64_t ld, int
                                             int64_t* out_ids, float* out_probs, void* stream);
 
 /* Kernel-side status of the last nls_sample_batch_noalloc call on the current
- * device (NLS_ERR_NAN_LOGITS, NLS_ERR_TIMEOUT, NLS_ERR_INVALID_ARG for a bad
- * history offset, NLS_ERR_CAPACITY for an overfull penalty window; NLS_OK if
- * none), copied from the library's status word in stream order. With
+ * device (NLS_ERR_NAN_LOGITS, NLS_ERR_TIMEOUT, NLS_ERR_INVALID_ARG for a
+ * duplicate bias id or a sampling row without uniforms; NLS_OK if none),
+ * copied from the library's status word in stream order. With
  * NLS_DEVICE_OUTPUTS, `out` is device memory and the copy is asynchronous;
  * otherwise `out` is host memory and the call waits for `stream`. Allocates
  * nothing. No counterpart in the reference. */

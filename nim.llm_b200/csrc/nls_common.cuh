@@ -240,12 +240,11 @@ __device__ __forceinline__ int patch_find(const PatchTable& T, int tok) {
   return -1;
 }
 
-// Penalties then bias for one logit (sampler.nim:71-76). The count is > 0
-// only when the penalty block is active for the row.
-__device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int slot,
-                                             const nls_row_params& p) {
-  const int word = T.cnt[slot];
-  const int cnt = word & kPatchCountMask;
+// Penalties then bias for one logit (sampler.nim:71-76): `cnt` occurrences
+// in the penalty window (> 0 only when the penalty block is active for the
+// row), then the bias b.float32 when the id has one.
+__device__ __forceinline__ float penalise(float x, int cnt, bool has_bias, float b,
+                                          const nls_row_params& p) {
   if (cnt > 0) {
     if (p.repeat_penalty != 1.0) {
       float rp = __double2float_rn(p.repeat_penalty);
@@ -254,8 +253,32 @@ __device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int s
     double d = __dadd_rn(__dmul_rn((double)cnt, p.frequency_penalty), p.presence_penalty);
     x = __fsub_rn(x, __double2float_rn(d));
   }
-  if (word & kPatchHasBias) x = __fadd_rn(x, __int_as_float(T.flag[slot]));
+  if (has_bias) x = __fadd_rn(x, b);
   return x;
+}
+__device__ __forceinline__ float patch_apply(float x, const PatchTable& T, int slot,
+                                             const nls_row_params& p) {
+  const int word = T.cnt[slot];
+  return penalise(x, word & kPatchCountMask, (word & kPatchHasBias) != 0,
+                  __int_as_float(T.flag[slot]), p);
+}
+
+// The row's penalty window [h0, h1) in hist_ids (empty when the penalty block
+// is inactive; the last repeat_last_n ids when that is > 0, sampler.nim:67)
+// and its bias list [b0, b1).
+__device__ __forceinline__ void patch_lists(const BatchArgs& a, int row, const nls_row_params& p,
+                                            int64_t* h0, int64_t* h1, int64_t* b0, int64_t* b1) {
+  *h0 = *h1 = *b0 = *b1 = 0;
+  if (a.hist_ids != nullptr) {
+    *h0 = a.hist_off[row];
+    *h1 = a.hist_off[row + 1];
+    if (!penalties_active(p, *h1 - *h0)) *h1 = *h0;
+    else if (p.repeat_last_n > 0 && *h1 - *h0 > p.repeat_last_n) *h0 = *h1 - p.repeat_last_n;
+  }
+  if (a.bias_ids != nullptr) {
+    *b0 = a.bias_off[row];
+    *b1 = a.bias_off[row + 1];
+  }
 }
 
 // Replace each slot's logit by the final patched logit of its position.
@@ -284,17 +307,8 @@ __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_p
   const int hs = 1 << T.log2size;
   constexpr int U = 4;
   // the ids of the penalty window and of the bias list, and their logits
-  int64_t h0 = 0, h1 = 0, b0 = 0, b1 = 0;
-  if (a.hist_ids != nullptr) {
-    h0 = a.hist_off[row];
-    h1 = a.hist_off[row + 1];
-    if (!penalties_active(p, h1 - h0)) h1 = h0;
-    else if (p.repeat_last_n > 0 && h1 - h0 > p.repeat_last_n) h0 = h1 - p.repeat_last_n;  // :67
-  }
-  if (a.bias_ids != nullptr) {
-    b0 = a.bias_off[row];
-    b1 = a.bias_off[row + 1];
-  }
+  int64_t h0, h1, b0, b1;
+  patch_lists(a, row, p, &h0, &h1, &b0, &b1);
   const int64_t nh = h1 - h0, ntot = nh + (b1 - b0);
   for (int i = tid; i < hs; i += nt) { T.key[i] = -1; T.cnt[i] = 0; }
   const int nwords = patch_bitmap_words(T.hi - T.lo, T.gshift);

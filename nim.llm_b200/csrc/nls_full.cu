@@ -3,7 +3,8 @@
 // 256 < top_k < vocab (the heap path with a large k, sampler.nim:86-95), and
 // rows the streaming kernel handed over (candidate buffers overflowed, an
 // optimistic threshold that proved too high, or a penalty window with too
-// many distinct ids for its table).
+// many distinct ids for its table). A row whose window and bias list exceed
+// this kernel's own table too is patched whole in the row's scratch slot.
 //
 // One 1024-thread CTA per row, persistent over its work (rows claimed from
 // the batch, or the list the streaming kernel handed over), with its own
@@ -567,6 +568,50 @@ __device__ __forceinline__ int claim_row(const BatchArgs& a, int V) {
   return r;
 }
 
+// A row whose penalty window and bias list hold more distinct ids than the
+// shared patch table: the patched row is written whole to `out` (the CTA's
+// TT slot, unused until the scans), the window counted in `cnt` and each
+// bias entry marked in `bmark` (its index in the list + 1), both dense over
+// the vocabulary (the KY and SK slots, unused until the transform).
+// Block-wide; returns false (block-uniform) on a duplicate bias id.
+__device__ bool dense_patch_row(const BatchArgs& a, int row, const nls_row_params& p,
+                                const float* rowp, int V, int* cnt, int* bmark, float* out,
+                                int* s_dup) {
+  const int tid = threadIdx.x;
+  int64_t h0, h1, b0, b1;
+  patch_lists(a, row, p, &h0, &h1, &b0, &b1);
+  const int64_t nh = h1 - h0, ntot = nh + (b1 - b0);
+  for (int i = tid; i < V; i += FT_THREADS) {
+    cnt[i] = 0;
+    bmark[i] = 0;
+    out[i] = __ldcs(rowp + i);
+  }
+  if (tid == 0) *s_dup = 0;
+  __syncthreads();
+  for (int64_t j = tid; j < ntot; j += FT_THREADS) {
+    if (j < nh) {
+      const int64_t t = a.hist_ids[h0 + j];
+      if (t >= 0 && t < V) atomicAdd(&cnt[t], 1);
+    } else {
+      const int64_t t = a.bias_ids[b0 + (j - nh)];
+      if (t >= 0 && t < V && atomicExch(&bmark[t], (int)(j - nh) + 1) != 0) atomicExch(s_dup, 1);
+    }
+  }
+  __syncthreads();
+  if (*s_dup) return false;
+  // each listed id gets its patched logit (an id listed twice writes the same
+  // value twice)
+  for (int64_t j = tid; j < ntot; j += FT_THREADS) {
+    const int64_t t = (j < nh) ? a.hist_ids[h0 + j] : a.bias_ids[b0 + (j - nh)];
+    if (t < 0 || t >= V) continue;
+    const int m = bmark[t];
+    const float b = m ? __double2float_rn(a.bias_vals[b0 + (m - 1)]) : 0.0f;  // b.float32 (:76)
+    out[t] = penalise(rowp[t], cnt[t], m != 0, b, p);
+  }
+  __syncthreads();
+  return true;
+}
+
 // PAIR: launched as clusters of two CTAs (row-claiming launches of batches
 // larger than the GPU). The pair shares the first phase of the first row it
 // claims -- transform, histogram and scatter, each CTA taking one half of the
@@ -642,11 +687,26 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     const float* rowp = a.logits + (int64_t)row * a.ld;
 
     PatchTable T{S.ph.pt.hkey, S.ph.pt.hcnt, S.ph.pt.hbias, S.ph.pt.hflag, bitmap, FT_HASH_LOG2, 0, V, FT_GSHIFT};
-    const int npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup);
-    if (S.patch_overflow || S.dup) {
+    int npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup);
+    if (S.patch_overflow && !S.dup) {
+      // More distinct ids than the table holds: the row is patched whole in
+      // this CTA's TT slot and read from there; CTA 0 of a pair takes the
+      // row alone.
+      __syncthreads();
+      if (PAIR && pair) {
+        pair = false;
+        if (crank_now() == 1) continue;
+      }
+      if (dense_patch_row(a, row, p, rowp, V, reinterpret_cast<int*>(KY), reinterpret_cast<int*>(LA),
+                          TT, &S.dup)) {
+        rowp = TT;
+        npatch = 0;
+      }
+    }
+    if (S.dup) {
       if (tid == 0 && lead) {
         a.out_ids[row] = -1;
-        record_status(a.status, S.dup ? NLS_ERR_INVALID_ARG : NLS_ERR_CAPACITY);
+        record_status(a.status, NLS_ERR_INVALID_ARG);
       }
       __syncthreads();
       if (PAIR) pair = false;

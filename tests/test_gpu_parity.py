@@ -475,6 +475,56 @@ def test_full_rows_with_far_outliers(pkg, oracle_mod, B):
         eng.close()
 
 
+@pytest.mark.parametrize("B", [8, 200])  # single-CTA rows; more rows than SMs (cluster pairs)
+def test_penalty_window_beyond_the_patch_table(pkg, oracle_mod, B):
+    """Penalty windows and bias lists with more distinct ids than the
+    kernels' shared-memory tables hold (1024 per streaming CTA, 4096 per
+    full-sort row): a long chat with repeat_last_n <= 0 penalises the whole
+    history. Streaming rows hand such a row over; the full-sort kernel then
+    patches the row whole in its scratch slot. Every row kind: full sort,
+    heap with k > 256, small top-k, greedy; one row with a duplicate bias id
+    among thousands still reports invalid input, alone."""
+    from oracle.oracle import PARAMS_DTYPE
+    rng = np.random.default_rng(300 + B)
+    V = 40000
+    x = rng.normal(0, 2.5, (B, V)).astype(np.float32)
+    P = np.zeros(B, PARAMS_DTYPE)
+    P["temperature"] = 0.9
+    P["top_p"] = 0.95
+    P["repeat_penalty"] = 1.1
+    P["presence_penalty"] = 0.2
+    P["frequency_penalty"] = 0.05
+    P["top_k"] = np.array([0, 1000, 40, 0])[np.arange(B) % 4]
+    P["temperature"][3::4] = 0.0  # greedy
+    P["repeat_last_n"] = np.where(np.arange(B) % 2 == 0, 0, -1)
+    hist, hoff, bids, bvals, boff = [], [0], [], [], [0]
+    for r in range(B):
+        pool = rng.choice(V, 3000 + 1500 * (r % 3), replace=False)
+        hist += rng.choice(pool, 9000).tolist()  # repeats: counts above 1
+        hoff.append(len(hist))
+        nb = 5000 if r % 5 else 300
+        ids = rng.choice(V, nb, replace=False)
+        vals = rng.normal(0, 1.0, nb)
+        vals[:: 17] = -np.inf
+        bids += ids.tolist()
+        bvals += vals.tolist()
+        boff.append(len(bids))
+    dup_row = B - 1
+    j0 = boff[dup_row]
+    bids[j0 + 1] = bids[j0 + 4000 if boff[dup_row + 1] - j0 > 4000 else j0]
+    a = dict(logits=x, params=P, hist_ids=np.array(hist, np.int64), hist_off=np.array(hoff, np.int64),
+             bias_ids=np.array(bids, np.int64), bias_vals=np.array(bvals, np.float64),
+             bias_off=np.array(boff, np.int64), uniforms=rng.random(B))
+    eng = pkg.Engine(0, max_rows=max(B, 8), max_vocab=V)
+    try:
+        ids, probs, st, ref, dg = run_both(eng, oracle_mod, a, threads=16)
+        assert st == 1 and ids[dup_row] == -1
+        keep = np.arange(B) != dup_row
+        compare(ids[keep], probs[keep], ref[keep], dg[keep], P[keep], f"wide windows B={B}")
+    finally:
+        eng.close()
+
+
 def test_many_rows_claimed_from_the_classified_list(pkg, oracle_mod):
     """Batches of more than 4 x SMs rows: a classification kernel lists the
     full-path rows first and the full-sort CTAs claim from that list (cluster
