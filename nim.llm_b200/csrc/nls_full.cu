@@ -12,7 +12,8 @@
 //   KY[i]  order key of logit i (index order),
 //   SK[j]  (key << 32 | index) grouped by value bucket, candidate order
 //          between windows, sorted inside a window once a scan needs it,
-//   TT[j]  exact expf(y_j - max) of the positions of sorted windows.
+//   TT[j]  x_j = y_j - max (written with SK) until its window is sorted,
+//          then t_j = expf(x_j) exactly.
 // Steps:
 //   1. transform: penalties and bias (precomputed per patched position),
 //      temperature; KY gets each logit's key, whose ascending order is the
@@ -57,6 +58,7 @@ constexpr int FT_THREADS = 1024;
 constexpr int FT_EPT = 4;
 constexpr int FT_TILE = FT_THREADS * FT_EPT;
 constexpr int FT_WARPS = FT_THREADS / 32;
+static_assert(FT_WARPS == 32, "a warp reduces one per-warp partial per lane");
 static_assert(FT_WARPS <= 32, "block reductions keep one warp partial per lane");
 constexpr int FT_HASH_LOG2 = 12;
 constexpr int FT_GSHIFT = 2;
@@ -101,6 +103,9 @@ struct FullShared {
   float fred[FT_WARPS];
   uint32_t ured[FT_WARPS];
   uint32_t ured2[FT_WARPS];
+  // an order-independent pass's per-warp partials (sum, largest term's
+  // bits, tie), two sets used alternately
+  uint32_t pp[2][3][FT_WARPS];
   int ibuf[8];
   float fbuf[8];
   int biglist[FT_BIGLIST];
@@ -769,6 +774,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
     const int e1 = (PAIR && pair && crank_now() == 0) ? half : V;
     uint32_t* const KYp = PAIR ? KY - (pair ? (size_t)crank_now() * 4 * (size_t)vpad : 0) : KY;
     unsigned long long* const SKp = PAIR ? reinterpret_cast<unsigned long long*>(KYp + vpad) : SK;
+    float* const TTp = PAIR ? reinterpret_cast<float*>(KYp + 3 * (size_t)vpad) : TT;
     auto transform4 = [&](int g, const float4 q) {
       float x[4] = {q.x, q.y, q.z, q.w};
       if (npatch > 0 && patch_bit(T, 4 * g)) {
@@ -1177,8 +1183,11 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         // (the next tile touches lo1/gb1/stage only after its first barrier)
         for (int q = tid; q < nt; q += FT_THREADS) {
           const unsigned long long v = stage[q];
-          const int b = bk((uint32_t)(v >> 32));
-          SKp[S.gb1[b] + ((uint32_t)q - S.lo1[b])] = v;
+          const uint32_t kdv = (uint32_t)(v >> 32);
+          const int b = bk(kdv);
+          const uint32_t j = S.gb1[b] + ((uint32_t)q - S.lo1[b]);
+          SKp[j] = v;
+          TTp[j] = __fsub_rn(desc_key_value(kdv), mx);  // x = y - max, for the passes
         }
       }
       __syncthreads();
@@ -1409,6 +1418,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         }
         return ScanResult{v, -1};
       };
+      // the set of pass partials the next order-independent pass writes
+      // (alternating across all the row's scans)
+      int pset = 0;
       auto run_scan = [&](auto decc, int j1, float v0, auto fromt, auto stop, bool has_stop,
                           bool absorb) -> ScanResult {
         constexpr bool DEC = decltype(decc)::value;
@@ -1418,7 +1430,6 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
                                                           S.scan, S.fscan, prep);
         float v = v0;
         constexpr int WPT = FT_BIG / FT_THREADS;  // a pass covers at most FT_BIG positions
-        const uint32_t* SKw = reinterpret_cast<const uint32_t*>(SK);
         // The last window the order-independent pass settled: its grid, grid
         // units and size predict whether the next two windows fit one pass.
         int last_ue = INT_MIN, last_n = 1;
@@ -1433,12 +1444,19 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const int st = S.wstate[c];
           if (st != 2 && we == we0) {
             // Order-independent pass. An element's grid units follow from the
-            // estimate texp_estimate(x) unless a rounding boundary lies
-            // within the estimate's error; then ref_expf is evaluated.
+            // estimate texp_estimate(x) of its term (x from TT) unless a
+            // rounding boundary lies within the estimate's error; then
+            // ref_expf is evaluated.
+            // v's binade, its grid 2^ue and v on that grid (from v's bits:
+            // the significand with its hidden bit; denormals share E = -126)
+            const uint32_t vb = __float_as_uint(v) & 0x7fffffffu;
             const int E = binade_exp(v);
             const int ue = E - 23;
-            long long S0 = (long long)ldexp((double)v, -ue);
+            long long S0 = (vb >> 23) ? (long long)((vb & 0x7fffffu) | 0x800000u) : (long long)vb;
             if (DEC) S0 = -S0;
+            // a grid value S * 2^ue as a float (|S| <= 2^24: exact)
+            const float gunit = (ue >= -126) ? __int_as_float((ue + 127) << 23) : __int_as_float(1 << (ue + 149));
+            auto gval = [&](long long Sv) { return __fmul_rn((float)(DEC ? -Sv : Sv), gunit); };
             // Windows c and c+1 in one pass when the last settled window, on
             // this grid, predicts (terms do not grow along the sorted order)
             // that the running value stays inside its binade and short of the
@@ -1448,10 +1466,10 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             if (c != alone && last_ue == ue && c + 1 < nwin && S.wstate[c + 1] != 2) {
               const int we2 = S.wstart[c + 2];
               if (we2 > we && we2 <= j1 && we2 - ws <= FT_BIG) {
-                const double pred = 1.25 * (double)last_units * (double)(we2 - ws) / (double)last_n;
-                const double sp = (double)S0 + pred;
-                bool two = !DEC ? sp < 0x1p24 : (E != -126 && sp < -0x1p23);
-                if (two && has_stop) two = !stop(grid_value(DEC ? -(long long)sp : (long long)sp, ue));
+                const float pred = 1.25f * (float)last_units * (float)(we2 - ws) / (float)last_n;
+                const float sp = (float)S0 + pred;
+                bool two = !DEC ? sp < 0x1p24f : (E != -126 && sp < -0x1p23f);
+                if (two && has_stop) two = !stop(gval((long long)sp));
                 if (two) wend = we2;
               }
             }
@@ -1459,14 +1477,20 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             const bool scale_ok = (ue >= -120 && ue <= 126);  // terms near a grid step stay normal
             const float gscale = scale_ok ? __int_as_float((127 - ue) << 23) : 0.0f;
             const int rounds = (wend - ws + FT_THREADS - 1) / FT_THREADS;  // same in every thread
-            uint32_t raw[WPT];  // all loads first: one memory latency per pass
+            float xv[WPT];  // x = y - max per position, all loads first: one memory latency per pass
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
               const int j = ws + tid + r * FT_THREADS;
-              raw[r] = (j < wend) ? SKw[2 * j + 1] : 0u;
+              xv[r] = (j < wend) ? TT[j] : 0.0f;
             }
-            long long sum = 0;
+            // the next pass most likely starts at wend: its estimates into L1
+#pragma unroll
+            for (int r = 0; r < WPT; ++r) {
+              const int j = wend + tid + r * FT_THREADS;
+              if (j < j1) asm volatile("prefetch.global.L1 [%0];" ::"l"(TT + j));
+            }
             float sumf = 0.0f;  // settled units, each < 2^18: at most 2^21, exact in fp32
+            uint32_t usum = 0u;  // units of the elements redone exactly (saturated)
             bool tie = false;
             float amax = 0.0f;
             unsigned pending = 0u;  // elements the estimate does not settle
@@ -1478,8 +1502,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             for (int r = 0; r < WPT; ++r) {
               if (r >= rounds) break;
               const bool valid = ws + tid + r * FT_THREADS < wend;
-              const float x = __fsub_rn(desc_key_value(raw[r]), mx);
-              const float a = texp_estimate(x);
+              const float a = texp_estimate(xv[r]);
               const float emid = fromt.mid(a);
               const float q = __fmul_rn(emid, gscale);
               const float k = rintf(q);
@@ -1492,34 +1515,34 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
 #pragma unroll
             for (int r = 0; r < WPT; ++r) {
               if (!(pending & (1u << r))) continue;
-              const float x = __fsub_rn(desc_key_value(raw[r]), mx);
-              const float e = fromt.exact(ref_expf(x));
+              const float e = fromt.exact(ref_expf(xv[r]));
               bool tj;
-              sum += grid_units(e, ue, &tj);
+              const long long gu = grid_units(e, ue, &tj);
+              usum = min(usum + (uint32_t)min(gu, 1LL << 24), 1u << 24);
               tie |= tj;
               amax = fmaxf(amax, e);
             }
-            sum += (long long)sumf;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              sum += __shfl_xor_sync(0xffffffffu, sum, o);
-              amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            }
+            // Sums saturate at 2^24 units: a pass that reaches them leaves the
+            // binade anyway (|S0| < 2^24 on the same side), so the checks
+            // below still fail it; below that every sum is exact in 32 bits
+            // (32 x 2^24 < 2^32).
+            usum = min(usum + (uint32_t)sumf, 1u << 24);
+            const uint32_t wsum = min(__reduce_add_sync(0xffffffffu, usum), 1u << 24);
+            const uint32_t wmaxb = __reduce_max_sync(0xffffffffu, __float_as_uint(amax));  // amax >= 0
             const unsigned anytie = __ballot_sync(0xffffffffu, tie);
-            if (lane == 0) { S.fscan.red[warp] = sum; S.fscan.flag[warp] = anytie != 0u; S.fred[warp] = amax; }
+            // (set `pset` of the partials: the previous pass read the other
+            // one, so one barrier per pass suffices)
+            uint32_t(*const pp)[FT_WARPS] = S.pp[pset];
+            pset ^= 1;
+            if (lane == 0) { pp[0][warp] = wsum; pp[1][warp] = wmaxb; pp[2][warp] = anytie != 0u; }
             __syncthreads();
-            long long tot = lane < FT_WARPS ? S.fscan.red[lane] : 0;  // one partial per lane
-            float wmax = lane < FT_WARPS ? S.fred[lane] : 0.0f;
-            const int any = __any_sync(0xffffffffu, lane < FT_WARPS && S.fscan.flag[lane]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              tot += __shfl_xor_sync(0xffffffffu, tot, o);
-              wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
-            }
-            __syncthreads();
+            const long long tot = (long long)__reduce_add_sync(0xffffffffu, pp[0][lane]);
+            const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, pp[1][lane]));
+            const int any = __any_sync(0xffffffffu, pp[2][lane] != 0u);
             // every later term is at most this pass's largest
-            // (wmax estimates the largest term within 2^-18; 2^-12 covers it)
-            if (!DEC && absorb && (double)wmax * (1.0 + 0x1p-12) < ldexp(1.0, ue - 1))
+            // (wmax estimates the largest term within 2^-18; 2^-12 covers it;
+            // half a grid step below the float range reads 0: no early end)
+            if (!DEC && absorb && __fmul_rn(wmax, 1.0f + 0x1p-12f) < __fmul_rn(gunit, 0.5f))
               return ScanResult{v, -1};
             const long long Se = S0 + tot;
             bool fast = !any;
@@ -1527,9 +1550,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
               if (!DEC) fast = Se < (1LL << 24);
               else fast = (E == -126) ? (Se < 0) : (Se < -(1LL << 23));
             }
-            if (fast && has_stop) fast = !stop(grid_value(DEC ? -Se : Se, ue));
+            if (fast && has_stop) fast = !stop(gval(Se));
             if (fast) {
-              v = grid_value(DEC ? -Se : Se, ue);
+              v = gval(Se);
               last_ue = ue;  // v stayed in its binade
               last_units = tot;
               last_n = wend - ws;
