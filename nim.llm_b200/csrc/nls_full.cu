@@ -73,6 +73,14 @@ constexpr int FT_BIGLIST = 64;
 constexpr int FT_MAXWIN = kMaxVocab / FT_WIN;  // windows of the largest vocabulary
 constexpr float FT_DCAP = 110.0f;  // expf(-110) is 0: beyond this t_j is 0
 
+// one replay iteration's outcome, from warp 0
+struct ReplayShared {
+  float v;    // the running value after the iteration
+  int j;      // the next position
+  int stop;   // the position where the stop fired, or -1
+  int event;  // whether a group held an event (else the span grows)
+};
+
 struct FullShared {
   union {  // the patch table is dead once the row is transformed
     struct {
@@ -117,9 +125,11 @@ struct FullShared {
   int wbkt[FT_MAXWIN + 1];
   int wstate[FT_MAXWIN];
   int cwin;  // window whose exact t values sit in u.big (as floats), or -1
-  // replay of a sorted window: grid-unit sums of its 32-position groups
-  long long gsum[FT_BIG / 32];
-  int gtie[FT_BIG / 32];
+  // replay of a sorted window: grid-unit sums of its 32-position groups and
+  // their ties, two sets used alternately
+  uint32_t gsum[2][FT_BIG / 32];
+  int gtie[2][FT_BIG / 32];
+  ReplayShared rpl[2];
   long long gS;
   int gev;
   // a cluster pair's first row: values pushed here by the partner CTA
@@ -1301,6 +1311,9 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
       // warp 0 finds the first group where a tie, a binade change or the stop
       // happens, everything before it is taken at once, and one warp replays
       // from that group; then again with the new grid.
+      // the set of group sums the next replay iteration writes (alternating
+      // across all the row's replays)
+      int rset = 0;
       auto window_replay = [&](auto decc, int j0, int j1, float v0, auto elem, auto stop,
                                bool has_stop, bool absorb) -> ScanResult {
         constexpr bool DEC = decltype(decc)::value;
@@ -1316,38 +1329,50 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
         auto first_span = [&](int jj, float vv) -> int {
           const float tj = elem(jj);
           const int E = binade_exp(vv);
-          const double room = DEC ? (double)vv - ldexp(1.0, E) : ldexp(1.0, E + 1) - (double)vv;
-          return (tj > 0.0f && room < (double)tj * (32 * FT_WARPS)) ? 32 * FT_WARPS : FT_BIG;
+          // (exact: v and the binade's edge are within a factor of two)
+          const float edge = (E >= -126) ? __int_as_float((E + 127 + (DEC ? 0 : 1)) << 23) : 0.0f;
+          const float room = DEC ? __fsub_rn(vv, edge) : __fsub_rn(edge, vv);
+          return (tj > 0.0f && room < tj * (float)(32 * FT_WARPS)) ? 32 * FT_WARPS : FT_BIG;
         };
         int span = first_span(j, v);
         while (j < j1) {
           const int E = binade_exp(v);
           const int ue = E - 23;
-          if (!DEC && absorb && (double)elem(j) < ldexp(1.0, ue - 1)) break;
-          long long S0 = (long long)ldexp((double)v, -ue);
+          if (!DEC && absorb && elem(j) < half_grid(ue)) break;
+          long long S0 = grid_S(v);
           if (DEC) S0 = -S0;
           const int jend = (j1 - j > span) ? j + span : j1;
           const int ng = (jend - j + 31) >> 5;  // <= FT_BIG / 32
+          // (set `rset` of the group sums and of the results below: the
+          // next iteration writes the other set, so readers need no second
+          // barrier)
+          uint32_t* const gsum = S.gsum[rset];
+          int* const gtie = S.gtie[rset];
+          ReplayShared& rs = S.rpl[rset];
+          rset ^= 1;
           for (int g = warp; g < ng; g += FT_WARPS) {
             const int jj = j + 32 * g + lane;
             long long u = 0;
             bool tie = false;
             if (jj < jend) u = grid_units(elem(jj), ue, &tie);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
-            const unsigned tb = __ballot_sync(0xffffffffu, tie);
+            // units clamped at 2^25: such an element leaves the binade by
+            // itself, so the first event and the sums before it are exact
+            const uint32_t gs = __reduce_add_sync(0xffffffffu, (uint32_t)min(u, 1LL << 25));
+            const bool gt = __any_sync(0xffffffffu, tie);
             if (lane == 0) {
-              S.gsum[g] = u;
-              S.gtie[g] = tb != 0u;
+              gsum[g] = gs;
+              gtie[g] = gt;
             }
           }
           __syncthreads();
+          // warp 0: the first group holding a tie, a binade change or the
+          // stop (lane l scans groups l*per .. l*per+per-1)
           if (warp == 0) {
             const int per = (ng + 31) >> 5;  // groups per lane, <= 8
             long long loc = 0;
             for (int r = 0; r < per; ++r) {
               const int g = lane * per + r;
-              if (g < ng) loc += S.gsum[g];
+              if (g < ng) loc += gsum[g];
             }
             long long incl = loc;
 #pragma unroll
@@ -1361,8 +1386,8 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
             for (int r = 0; r < per; ++r) {
               const int g = lane * per + r;
               if (g >= ng) break;
-              const long long after = run + S.gsum[g];
-              bool e = S.gtie[g] != 0;
+              const long long after = run + gsum[g];
+              bool e = gtie[g] != 0;
               if (!e) {
                 if (!DEC) e = after >= (1LL << 24);
                 else e = (E == -126) ? (after >= 0) : (after >= -(1LL << 23));
@@ -1376,44 +1401,36 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
               run = after;
             }
             const unsigned eb = __ballot_sync(0xffffffffu, ev != INT_MAX);
-            const long long total = __shfl_sync(0xffffffffu, incl, 31);
             int gev = -1;
-            long long gS = S0 + total;
+            long long gS = S0 + __shfl_sync(0xffffffffu, incl, 31);
             if (eb) {
               const int L = __ffs(eb) - 1;
               gev = __shfl_sync(0xffffffffu, ev, L);
               gS = __shfl_sync(0xffffffffu, sb, L);
             }
+            float wv = grid_value(DEC ? -gS : gS, ue);
+            int wj = jend, wstop = -1;
+            if (gev >= 0) {  // replay from that group, one warp
+              const WalkResult w = warp_walk<DEC>(j + 32 * gev, j1, wv, elem, stop, has_stop, 8);
+              wv = w.v;
+              wj = w.j;
+              wstop = w.stop_j;
+            }
             if (lane == 0) {
-              S.gev = gev;
-              S.gS = gS;
+              rs.v = wv;
+              rs.j = wj;
+              rs.stop = wstop;
+              rs.event = gev >= 0;
             }
           }
           __syncthreads();
-          const int gev = S.gev;
-          const long long gS = S.gS;
-          __syncthreads();
-          v = grid_value(DEC ? -gS : gS, ue);
-          if (gev < 0) {  // no event in the span: taken in one step
-            j = jend;
+          v = rs.v;
+          j = rs.j;
+          if (rs.stop >= 0) return ScanResult{v, rs.stop};
+          if (!rs.event) {  // no event in the span: taken in one step
             span = (span < FT_BIG) ? span * 2 : span;
             continue;
           }
-          j += 32 * gev;
-          if (warp == 0) {
-            const WalkResult w = warp_walk<DEC>(j, j1, v, elem, stop, has_stop, 8);
-            if (lane == 0) {
-              S.scan.v = w.v;
-              S.scan.walk_j = w.j;
-              S.scan.walk_stop = w.stop_j;
-            }
-          }
-          __syncthreads();
-          v = S.scan.v;
-          j = S.scan.walk_j;
-          const int wstop = S.scan.walk_stop;
-          __syncthreads();
-          if (wstop >= 0) return ScanResult{v, wstop};
           if (j < j1) span = first_span(j, v);
         }
         return ScanResult{v, -1};
@@ -1572,7 +1589,7 @@ full_kernel(BatchArgs a, uint32_t* scratch, int vpad) {
           const ScanResult r = window_replay(decc, ws, we, v, elemc, stop, has_stop, absorb);
           if (r.stop_j >= 0) return r;
           v = r.v;
-          if (!DEC && absorb && (double)elemc(we - 1) < ldexp(1.0, binade_exp(v) - 24))
+          if (!DEC && absorb && elemc(we - 1) < half_grid(binade_exp(v) - 23))
             return ScanResult{v, -1};
         }
         return ScanResult{v, -1};

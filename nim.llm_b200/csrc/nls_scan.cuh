@@ -66,10 +66,31 @@ __device__ __forceinline__ Fn fn_of(float a, int ue) {
   return Fn{k, 0, 1};
 }
 
-// exact float value of S * 2^ue (|S| < 2^25 here)
-__device__ __forceinline__ float grid_value(long long S, int ue) {
-  return __double2float_rn(ldexp((double)S, ue));
+// 2^ue as a float (ue >= -149; below -126 a denormal)
+__device__ __forceinline__ float grid_unit(int ue) {
+  return ue >= -126 ? __int_as_float((ue + 127) << 23) : __int_as_float(1 << (ue + 149));
 }
+
+// fl(S * 2^ue) for |S| < 2^25 and ue >= -149: (float)S rounds once, and the
+// power-of-two scaling is exact (a product below 2^-126 is a multiple of
+// 2^-149 under 2^-126, which a denormal holds exactly), so this is the
+// correctly rounded value -- exact for |S| <= 2^24.
+__device__ __forceinline__ float grid_value(long long S, int ue) {
+  return __fmul_rn((float)S, grid_unit(ue));
+}
+
+__device__ __forceinline__ int binade_exp(float v);
+
+// v / 2^(binade_exp(v) - 23), exactly: v's significand with its hidden bit
+// (denormals and zero, on the grid 2^-149: the significand alone)
+__device__ __forceinline__ long long grid_S(float v) {
+  const uint32_t vb = __float_as_uint(v) & 0x7fffffffu;
+  return (vb >> 23) ? (long long)((vb & 0x7fffffu) | 0x800000u) : (long long)vb;
+}
+
+// half a step of the grid 2^ue as a float (0 below the denormal range: then
+// no term counts as absorbed, which only costs work)
+__device__ __forceinline__ float half_grid(int ue) { return __fmul_rn(grid_unit(ue), 0.5f); }
 
 __device__ __forceinline__ int binade_exp(float v) {
   // exponent of |v| for normals; denormals and zero share the grid of
@@ -180,7 +201,7 @@ __device__ WalkResult warp_walk(int j, int j1, float v, Elem elem, Stop stop, bo
   for (int g = 0; g < max_groups && j < j1 && quiet < 2; ++g) {
     const int E = binade_exp(v);
     const int ue = E - 23;
-    long long S0 = (long long)ldexp((double)v, -ue);
+    long long S0 = grid_S(v);
     if (DEC) S0 = -S0;
     const int jj = j + lane;
     const bool in = jj < j1;
@@ -264,11 +285,11 @@ __device__ ScanResult exact_scan(int j0, int j1, float v0, Elem elem, Stop stop,
   while (j < j1) {
     const int E = binade_exp(v);
     const int ue = E - 23;
-    long long S0 = (long long)ldexp((double)v, -ue);
+    long long S0 = grid_S(v);
     if (DEC) S0 = -S0;
     if (!DEC && absorb) {
       float a0 = elem(j);
-      if ((double)a0 < ldexp(1.0, ue - 1)) break;
+      if (a0 < half_grid(ue)) break;
     }
     const int cend = (j1 - j > CH) ? j + CH : j1;
     Fn fe[EPT];
@@ -376,13 +397,13 @@ __device__ ScanResult exact_scan_fast(int j0, int j1, float v0, Elem elem, Stop 
   while (j < j1) {
     const int E = binade_exp(v);
     const int ue = E - 23;
-    long long S0 = (long long)ldexp((double)v, -ue);
+    long long S0 = grid_S(v);
     if (DEC) S0 = -S0;
     const int cend = (j1 - j > CH) ? j + CH : j1;
     prep(j, cend);
     if (!DEC && absorb) {
       const float a0 = elem(j);
-      if ((double)a0 < ldexp(1.0, ue - 1)) break;
+      if (a0 < half_grid(ue)) break;
     }
     long long sum = 0;
     bool tie = false;
@@ -424,7 +445,7 @@ __device__ ScanResult exact_scan_fast(int j0, int j1, float v0, Elem elem, Stop 
       const int send = (cend - sj > NT) ? sj + NT : cend;
       const int E2 = binade_exp(v);
       const int ue2 = E2 - 23;
-      long long S2 = (long long)ldexp((double)v, -ue2);
+      long long S2 = grid_S(v);
       if (DEC) S2 = -S2;
       bool t2 = false;
       long long sum2 = 0;
