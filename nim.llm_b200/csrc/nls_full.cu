@@ -1796,13 +1796,12 @@ cudaError_t launch_full(const BatchArgs& a, uint32_t* scratch, int vpad, int slo
                         cudaStream_t stream, bool after_light) {
   const size_t smem = full_smem_bytes(a.V);
   int grid = (a.rows < slots) ? a.rows : slots;  // a CTA takes at most one row at a time
-  // A row-claiming launch over a batch larger than the GPU runs as cluster
-  // pairs (an even grid within the scratch slots): a pair shares its first
-  // row's first phase, and CTA 1's SM then goes to the concurrent streaming
-  // kernel, which has rows to fill it. With fewer rows than SMs there is no
-  // such work, and the single-CTA kernel is used.
-  const bool pairs = a.row_claim != nullptr && !after_light && a.rows > slots && grid >= 2;
-  if (pairs) grid &= ~1;
+  // A row-claiming launch runs as cluster pairs (an even grid within the
+  // scratch slots, two CTAs per row where the slots allow): a pair shares its
+  // first row's first phase, and CTA 1 then claims rows alone or leaves its
+  // SM to the concurrent streaming kernel.
+  const bool pairs = a.row_claim != nullptr && !after_light && slots >= 2 && a.rows >= 1;
+  if (pairs) grid = ((2 * a.rows < slots) ? 2 * a.rows : slots) & ~1;
   const void* fn = pairs ? reinterpret_cast<const void*>(full_kernel<true>)
                          : reinterpret_cast<const void*>(full_kernel<false>);
   cudaError_t e = ensure_smem_attr(fn, (int)smem, pairs ? g_full_pair_smem_set : g_full_smem_set);
