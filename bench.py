@@ -585,7 +585,8 @@ def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
         wd = W.lm_weights_device(t, rows, cols, seed=SEED, device=dev)
         wbytes = rows * W.lm_row_bytes(t, cols)
         res = {"weight_bytes": wbytes}
-        for nb in ((1, 4) if name != "f16" else (1,)):
+        # (Q6_K at 8 and 16 batch rows: the tensor-core path)
+        for nb in {"q8_0": (1, 4), "q6_k": (1, 4, 8, 16), "f16": (1,)}[name]:
             x = torch.randn((nb, cols), generator=gen, device=dev)
             y = torch.empty((nb, rows), dtype=torch.float32, device=dev)
 

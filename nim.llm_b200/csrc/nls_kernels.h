@@ -49,4 +49,11 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st);
+// Q6_K on the int8 path at more than 4 batch rows: tcgen05 int8 MMAs
+// (nls_lmhead_mma.cu), launches of up to 16 batch rows; y[b * ldy + r]
+bool lm_head_mma_path(int wtype, int cols, int nb);
+size_t lm_head_mma_smem(int cols);
+cudaError_t launch_lm_head_q6k_mma(const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x,
+                                   int nb, float* y, int64_t ldy, int* status, int sm_count,
+                                   unsigned long long wait_ns, cudaStream_t st);
 }  // namespace nls

@@ -889,6 +889,17 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
   const bool int8 = lm_head_int8_path(wtype, cols, path_nb, exact);
+  // Q6_K at 8 or more batch rows: the same exact arithmetic on the tensor
+  // cores, the weights read once per 16 batch rows (nls_lmhead_mma.cu); a
+  // tail of fewer than 8 rows takes the path below
+  int b_first = 0;
+  if (int8 && lm_head_mma_path(wtype, cols, nb)) {
+    const int tail = (nb % 16 < 8) ? nb % 16 : 0;
+    const int nm = nb - tail;
+    cudaError_t e = launch_lm_head_q6k_mma(w, rb, rows, cols, x, nm, y, rows, status, sm_count, kWaitLimitNs, st);
+    if (e != cudaSuccess || tail == 0) return e;
+    b_first = nm;
+  }
   const int bl = (wtype == 14) ? 256 : 32;
   // the int8 path's warps read consecutive blocks of one row, so its tiles
   // need no padding (one copy per tile); the float path pads rows so that
@@ -899,7 +910,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   // batch rows per launch: the int8 path keeps a block's activations of every
   // batch row in registers; the float path keeps x in shared memory
   const int nbt_max = int8 ? kLmhInt8MaxNb : std::max(1, std::min(32, (64 * 1024) / (cols * 4)));
-  for (int b0 = 0; b0 < nb; b0 += nbt_max) {
+  for (int b0 = b_first; b0 < nb; b0 += nbt_max) {
     const int nbt = std::min(nbt_max, nb - b0);
     const bool two = int8 && (nbt <= 2 || wtype != 14);
     const size_t smem_max = two ? kLmhSmemMax2 : kLmhSmemMax;

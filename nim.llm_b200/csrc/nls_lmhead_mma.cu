@@ -1,0 +1,449 @@
+// nls_lmhead_mma.cu -- the output projection for Q6_K weights at 8 to 16
+// batch rows per launch, on the 5th-generation tensor cores.
+//
+// The reference's integer path (quantizeAct quant.nim:646-662, dotQ6K
+// quant.nim:731-760, matmulTask model.nim:144-155) computes per weight row r,
+// batch row b and 256-value block ib the exact integer
+//     sumi = sum_j sc_j * s_j,   s_j = sum_{l in sub-block j} (q_l - 32) * a_l
+// (16 sub-blocks of 16 values, int8 scales sc_j), then
+//     acc += (d_a * d_w) * float(sumi)
+// block after block in fp32. The s_j are int8 x int8 -> int32 contractions
+// (|s_j| <= 16 * 32 * 127), which tcgen05.mma kind::i8 computes exactly; the
+// scale products, the float conversion and the fp32 operations are the
+// reference's, in its order, on the CUDA cores.
+//
+// One CTA of 544 threads per SM, persistent over tiles of 128 weight rows,
+// warp-specialised. Per (tile, block) step:
+//  * the 16 worker warps copy a part of the tile's raw Q6_K bytes two steps
+//    ahead into shared memory (16-byte cp.async; the bytes past the weights'
+//    last whole 16 go by plain loads);
+//  * each worker unpacks one (row, quarter) of the block -- four sub-blocks
+//    of 16 values, q - 32 as int8 -- into the A operand of its parity (one of
+//    two buffers): even sub-blocks are the first 16 values of a 32-value K
+//    step, odd ones the second, and the other half of both is one shared
+//    block of zeros that the descriptors point at (no-swizzle K-major
+//    layout; 8-row x 16-byte core matrices);
+//  * warp 0 issues 16 MMAs (M = 128 rows, N = 16 batch rows, K = 32),
+//    sub-block j into TMEM columns 16j .. 16j+15 of one of two 256-column
+//    regions, and commits them to an mbarrier, while the workers go on with
+//    the next step (operands and TMEM double-buffered);
+//  * every worker warp reads, for the 32 weight rows of its TMEM lane
+//    quarter (warp % 4) and 4 of the 16 batch rows, the previous step's 16
+//    sub-block sums and forms sumi and the fp32 term.
+// Workers synchronise among themselves with named barriers and with warp 0
+// through mbarriers. The activations are quantized once per CTA into shared
+// memory in the operand layout (batch rows past nb are zeros). Every wait is
+// bounded.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "nls_kernels.h"
+#include "nls_tma.cuh"
+
+namespace nls {
+
+namespace {
+
+constexpr int kWorkers = 512;    // warps 1-16: staging, unpacking, sums
+constexpr int kMmaThreads = 32 + kWorkers;  // warp 0: the MMA issuer
+constexpr int kMmaRows = 128;    // weight rows per tile (MMA M)
+constexpr int kMmaN = 16;        // batch rows per launch (MMA N)
+constexpr int kQ6Bytes = 210;    // a Q6_K block
+// one A buffer: even sub-blocks [0, 16 KB), a 2 KB block of zeros, odd ones
+// [18 KB, 34 KB); K step i of a parity at + 2 KB * i, row r at + 16 r
+constexpr int kAEven = 0, kAZero = 16384, kAOdd = 18432, kAStage = 34816;
+constexpr int kRawRow = 240;     // staged bytes per row: the block and its 16-byte alignment
+constexpr int kRawChunks = kRawRow / 16;
+constexpr int kRawStage = kMmaRows * kRawRow;
+constexpr int kTmemCols = 512;   // two regions of 16 sub-blocks x 16 batch columns
+constexpr int kSlots = 3;        // per-step scales: written by its unpack, read one
+                                 // iteration later (a worker may be one ahead)
+
+// offset of the 16 values of row r, sub-block j inside an A buffer
+__device__ __forceinline__ int a_off(int r, int j) { return ((j & 1) ? kAOdd : kAEven) + (j >> 1) * 2048 + r * 16; }
+// offset of byte k of batch row b inside the activation operand (K steps of
+// 32 values, 512 bytes each for 16 rows)
+__device__ __forceinline__ int b_off(int b, int k) {
+  return (k >> 5) * (kMmaN * 32) + (b >> 3) * 256 + ((k >> 4) & 1) * 128 + (b & 7) * 16 + (k & 15);
+}
+
+// shared-memory matrix descriptor: no swizzle, K-major; lbo: from a row's
+// first 16 bytes of K to its second, sbo: from 8 rows to the next 8
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version of sm_100
+  return d;
+}
+
+// instruction descriptor: s32 accumulator, s8 x s8, both K-major, N = 16, M = 128
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kMmaN >> 3) << 17) |
+                            ((uint32_t)(kMmaRows >> 4) << 24);
+
+// D = A . B^T (no accumulation into the previous contents)
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kIdesc)
+      : "memory");
+}
+
+// four consecutive TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+// 16 bytes at a 2-byte aligned shared address, as four words (reads the
+// aligned words inside [p - 2, p + 18))
+__device__ __forceinline__ void ld16s(const uint8_t* p, uint32_t (&w)[4]) {
+  const uint32_t* a = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+  const uint32_t sel = (reinterpret_cast<uintptr_t>(p) & 2) ? 0x5432u : 0x3210u;
+  uint32_t x[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) x[k] = a[k];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = __byte_perm(x[k], x[k + 1], sel);
+}
+
+struct MmaArgs {
+  const uint8_t* w;  // rows x row_bytes, 16-byte aligned
+  int64_t row_bytes;
+  int64_t total;     // rows * row_bytes
+  int rows, cols, nblk;
+  int nb;            // batch rows of this launch, <= 16
+  const float* x;    // [nb x cols]
+  float* y;          // y[b * ldy + r]
+  int64_t ldy;
+  int ntiles;
+  unsigned long long wait_ns;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wi = tid - 32;  // worker index (warp 0: negative)
+  const int kb_steps = a.cols / 32;
+  uint8_t* bop = smem;                                          // activations: kb_steps x 512 B
+  uint8_t* aop = bop + (size_t)kb_steps * (kMmaN * 32);         // 2 A buffers
+  uint8_t* raw = aop + 2 * kAStage;                             // 2 x 128 rows x 240 B
+  float* dsa = reinterpret_cast<float*>(raw + 2 * kRawStage);   // d_a [16][nblk]
+  float* dws = dsa + kMmaN * a.nblk;                            // d_w [kSlots][128]
+  uint32_t* scs = reinterpret_cast<uint32_t*>(dws + kSlots * kMmaRows);  // sc [kSlots][128][4 words]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(scs + kSlots * kMmaRows * 4) + 7) & ~uintptr_t(7));
+  uint64_t* ready = bar;     // [2] workers -> warp 0: A buffer s & 1 holds step s
+  uint64_t* done = bar + 2;  // [2] MMAs of step s completed (tcgen05.commit)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 4);
+  int* s_fail = reinterpret_cast<int*>(tmem_holder + 1);
+  int* s_last = s_fail + 1;  // the last step whose MMAs were issued
+
+  const int my_tiles = (a.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nsteps = my_tiles * a.nblk;
+  const int64_t last16 = a.total & ~int64_t(15);
+
+  // workers stage the raw bytes of step s into buffer s & 1 (one cp.async
+  // group per call, empty past the last step); worker wi's chunks
+  // i = wi + k * workers of a stage are (row i / 15, chunk i % 15)
+  constexpr int kChunksPerThread = (kMmaRows * kRawChunks + kWorkers - 1) / kWorkers;
+  int crr[kChunksPerThread], ccc[kChunksPerThread];
+#pragma unroll
+  for (int k = 0; k < kChunksPerThread; ++k) {
+    const int i = wi + k * kWorkers;
+    crr[k] = (wi >= 0 && i < kMmaRows * kRawChunks) ? i / kRawChunks : kMmaRows;
+    ccc[k] = (i >= 0) ? i % kRawChunks : 0;
+  }
+  auto stage_raw = [&](int s) {
+    if (s < nsteps) {
+      const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
+      const int kb = s % a.nblk;
+      uint8_t* dst = raw + (size_t)(s & 1) * kRawStage;
+#pragma unroll
+      for (int k = 0; k < kChunksPerThread; ++k) {
+        const int rr = crr[k], c = ccc[k];
+        if (rr >= kMmaRows) continue;
+        const int r = t * kMmaRows + rr;
+        if (r >= a.rows) continue;
+        const int64_t g = ((int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes) & ~int64_t(15);
+        const int64_t src = g + 16 * c;
+        uint8_t* d = dst + rr * kRawRow + 16 * c;
+        if (src + 16 <= last16) {
+          cp_async16(d, a.w + src);
+        } else {
+          for (int e = 0; e < 16; ++e) d[e] = (src + e < a.total) ? a.w[src + e] : 0;
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  auto worker_sync = [](int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kWorkers) : "memory"); };
+
+  if (tid == 0) {
+    for (int k = 0; k < 4; ++k) mbar_init(&bar[k], 1);
+    *s_fail = 0;
+    *s_last = -1;
+    fence_mbar_init();
+  }
+  if (wi >= 0) {
+    stage_raw(0);
+    stage_raw(1);
+  }
+  // zeros: the activation rows nb .. 15 and both A buffers (their zero blocks
+  // stay zero)
+  for (int i = tid; i < (kb_steps * (kMmaN * 32) + 2 * kAStage) / 16; i += kMmaThreads)
+    reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  // quantizeAct (quant.nim:646-662) with blocks of 256, one warp per block
+  {
+    const int nblocks = a.nb * a.nblk;
+    for (int blk = warp; blk < nblocks; blk += kMmaThreads / 32) {
+      const int b = blk / a.nblk, ib = blk % a.nblk;
+      const float* xs = a.x + (size_t)b * a.cols + (size_t)ib * 256;
+      float v[8];
+      float amax = 0.0f;
+      bool bad = false;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        v[u] = xs[u * 32 + lane];
+        bad |= !isfinite(v[u]);
+        amax = fmaxf(amax, fabsf(v[u]));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0) atomicCAS(a.status, 0, NLS_ERR_NAN_LOGITS);
+      const float d = amax / 127.0f;
+      const float id = d > 0.0f ? 1.0f / d : 0.0f;
+      if (lane == 0) dsa[b * a.nblk + ib] = d;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float q0 = v[u] * id;
+        const int q = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
+        bop[b_off(b, ib * 256 + u * 32 + lane)] = (uint8_t)(int8_t)q;
+      }
+    }
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tbase = *tmem_holder;
+  bool fail = false;
+  auto wait_bar = [&](uint64_t* b2, int s) -> bool {  // barrier b2[s & 1] completed for step s
+    return mbar_wait_bounded(&b2[s & 1], (uint32_t)((s >> 1) & 1), a.wait_ns);
+  };
+
+  if (warp == 0) {
+    // the MMA issuer: step s once its operands are ready
+    if (lane == 0) {
+      for (int s = 0; s < nsteps; ++s) {
+        if (!wait_bar(ready, s)) {
+          fail = true;
+          break;
+        }
+        if (*s_fail) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int kb = s % a.nblk;
+        const uint32_t ab = smem_u32(aop) + (uint32_t)((s & 1) * kAStage);
+        const uint32_t bb = smem_u32(bop) + (uint32_t)(kb * 8) * (kMmaN * 32);
+        const uint32_t dreg = tbase + (uint32_t)((s & 1) * 256);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint64_t db = smem_desc(bb + (uint32_t)i * (kMmaN * 32), 128, 256);
+          // even sub-block 2i: its values, then the zeros; odd 2i + 1: the
+          // zeros, then its values
+          mma_i8(dreg + 32 * i, smem_desc(ab + kAEven + 2048 * i, kAZero - kAEven - 2048 * i, 128), db);
+          mma_i8(dreg + 32 * i + 16, smem_desc(ab + kAZero, kAOdd - kAZero + 2048 * i, 128), db);
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&done[s & 1]))
+                     : "memory");
+        *s_last = s;
+      }
+      if (fail) *s_fail = 1;
+    }
+    __syncwarp();
+  } else {
+    // workers
+    const int ur = wi >> 2, uh = (wi >> 1) & 1, uhalf = wi & 1;  // unpack unit
+    // sums: weight row em of the tile (TMEM lane quarter warp % 4), batch
+    // rows eb0 .. eb0+3
+    const int em = 32 * (warp & 3) + lane, eb0 = 4 * ((warp - 1) >> 2);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int s = 0; s <= nsteps; ++s) {
+      if (s < nsteps) {
+        cp_async_wait<1>();  // this thread's copies of step s (step s + 1's may be in flight)
+        worker_sync(1);      // everyone's
+        // A buffer s & 1 was last read by the MMAs of step s - 2
+        if (s >= 2 && !fail && !wait_bar(done, s - 2)) fail = true;
+        const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
+        const int kb = s % a.nblk;
+        const int r = t * kMmaRows + ur;
+        const int64_t g = (int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes;
+        const uint8_t* blk = raw + (size_t)(s & 1) * kRawStage + ur * kRawRow + (int)(g & 15);
+        uint32_t QA[4], QB[4], QH[4];
+        ld16s(blk + 64 * uh + 16 * uhalf, QA);
+        ld16s(blk + 64 * uh + 32 + 16 * uhalf, QB);
+        ld16s(blk + 128 + 32 * uh + 16 * uhalf, QH);
+        if (uh == 0 && uhalf == 0) {
+          // this row's sub-block scales and d for the sums (rows past the
+          // matrix: zeros)
+          uint32_t sc4[4];
+          ld16s(blk + 192, sc4);
+          const bool in = r < a.rows;
+          uint32_t* sd = scs + ((size_t)(s % kSlots) * kMmaRows + ur) * 4;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sd[k] = in ? sc4[k] : 0u;
+          const uint32_t dwb = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
+          dws[(s % kSlots) * kMmaRows + ur] = in ? __half2float(__ushort_as_half((unsigned short)dwb)) : 0.0f;
+        }
+        // the four sub-blocks j = 8h + 2c + half of this quarter (dotQ6K's
+        // q1..q4, quant.nim:744-747): the 6-bit value q, then q - 32 as int8
+        // (q ^ 32 is q - 32 for q >= 32 and q + 32 below; those get bits 6, 7)
+        uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t lo4 = ((c & 1) ? QB[k] : QA[k]) >> ((c & 2) ? 4 : 0);
+            const uint32_t q6 = (lo4 & 0x0F0F0F0Fu) | (((QH[k] >> (2 * c)) << 4) & 0x30303030u);
+            const uint32_t t6 = q6 ^ 0x20202020u;
+            const uint32_t m = t6 & 0x20202020u;
+            v[k] = t6 | (m << 1) | (m << 2);
+          }
+          *reinterpret_cast<uint4*>(ab + a_off(ur, 8 * uh + 2 * c + uhalf)) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      if (fail) *s_fail = 1;
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      worker_sync(2);
+      if (*s_fail) break;  // (the same in every worker after the barrier)
+      if (s < nsteps && wi == 0) mbar_arrive(&ready[s & 1]);
+      // the raw bytes of step s are unpacked: stage step s + 2 in their place
+      stage_raw(s + 2);
+      // the previous step's sums for this warp's rows and batch rows
+      if (s >= 1) {
+        if (!fail && !wait_bar(done, s - 1)) fail = true;
+        fail = __any_sync(0xffffffffu, fail);  // (tcgen05.ld is warp-wide; a failure
+                                               // stops every worker at the next barrier)
+      }
+      if (s >= 1 && !fail) {
+        const int p = s - 1;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
+        uint32_t scw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) scw[k] = sd[k];
+        int sumi[4] = {0, 0, 0, 0};
+        const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * 256 + eb0);
+#pragma unroll
+        for (int j0 = 0; j0 < 16; j0 += 4) {
+          uint32_t d[4][4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) tmem_ld4(ta + 16 * (j0 + u), d[u]);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u;
+            const int sc = (int)(int8_t)(scw[j >> 2] >> (8 * (j & 3)));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sumi[e] += sc * (int)d[u][e];
+          }
+        }
+        const int kb = p % a.nblk;
+        const float dw = dws[(p % kSlots) * kMmaRows + em];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int b = eb0 + e;
+          if (b < a.nb)
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * a.nblk + kb], dw), __int2float_rn(sumi[e])));
+        }
+        if (kb == a.nblk - 1) {
+          const int t = (int)blockIdx.x + (p / a.nblk) * (int)gridDim.x;
+          const int r = t * kMmaRows + em;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int b = eb0 + e;
+            if (b < a.nb && r < a.rows) a.y[(size_t)b * a.ldy + r] = acc[e];
+            acc[e] = 0.0f;
+          }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      }
+    }
+    cp_async_wait<0>();  // no copy lands after the CTA ends
+  }
+  if (fail) *s_fail = 1;
+  __syncthreads();
+  if (*s_fail) {  // (uniform after the barrier)
+    if (tid == 0) {
+      atomicCAS(a.status, 0, NLS_ERR_TIMEOUT);
+      // let the last committed MMAs finish before the columns are released
+      // (bounded)
+      const int last = *s_last;
+      if (last >= 0) (void)wait_bar(done, last);
+      if (last >= 1) (void)wait_bar(done, last - 1);
+    }
+    __syncthreads();
+  }
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols) : "memory");
+}
+
+}  // namespace
+
+size_t lm_head_mma_smem(int cols) {
+  const int nblk = cols / 256;
+  return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)kAStage + 2 * (size_t)kRawStage +
+         (size_t)kMmaN * nblk * 4 + (size_t)kSlots * kMmaRows * 4 + (size_t)kSlots * kMmaRows * 16 + 8 + 32 +
+         16 + 16;
+}
+
+bool lm_head_mma_path(int wtype, int cols, int nb) {
+  return wtype == 14 && nb >= 8 && cols % 256 == 0 && cols >= 256 && lm_head_mma_smem(cols) <= (size_t)(227 * 1024);
+}
+
+cudaError_t launch_lm_head_q6k_mma(const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x,
+                                   int nb, float* y, int64_t ldy, int* status, int sm_count,
+                                   unsigned long long wait_ns, cudaStream_t st) {
+  MmaArgs a{};
+  a.w = w;
+  a.row_bytes = row_bytes;
+  a.total = (int64_t)rows * row_bytes;
+  a.rows = rows;
+  a.cols = cols;
+  a.nblk = cols / 256;
+  a.ldy = ldy;
+  a.ntiles = (rows + kMmaRows - 1) / kMmaRows;
+  a.wait_ns = wait_ns;
+  a.status = status;
+  const size_t smem = lm_head_mma_smem(cols);
+  cudaError_t e = cudaFuncSetAttribute(lmh_q6k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(a.ntiles, sm_count);
+  for (int b0 = 0; b0 < nb; b0 += kMmaN) {
+    a.nb = std::min(kMmaN, nb - b0);
+    a.x = x + (size_t)b0 * cols;
+    a.y = y + (size_t)b0 * ldy;
+    lmh_q6k_mma_kernel<<<grid, kMmaThreads, smem, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace nls

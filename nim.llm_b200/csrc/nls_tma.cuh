@@ -1,7 +1,8 @@
 // nls_tma.cuh -- bulk-copy (TMA, non-tensor) and mbarrier helpers for sm_100a.
 //
 // Only the plain `cp.async.bulk` global->shared copy is used, without
-// multicast: each CTA copies its own chunk of a row from this GPU's HBM.
+// multicast: each CTA copies its own chunk of a row from this GPU's HBM;
+// besides it, the per-thread 16-byte `cp.async`.
 // Every wait on an mbarrier is bounded by %globaltimer; a wait that runs out
 // returns false and the caller records NLS_ERR_TIMEOUT instead of hanging.
 #pragma once
@@ -14,6 +15,18 @@ constexpr unsigned long long kWaitLimitNs = 200ull * 1000ull * 1000ull;  // 200 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte asynchronous global->shared copy (cp.async, completed by
+// cp.async.wait_group: the hardware finishes it, nothing spins on a flag).
+// Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

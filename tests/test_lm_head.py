@@ -250,6 +250,51 @@ def test_special_block_scales(pkg, engine, oracle_mod, name):
         assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32)), f"{name} exact={exact}"
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("cols,rows", [(256, 1000), (4096, 3001), (8192, 515)])
+def test_q6_k_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
+    """Q6_K at 8 or more batch rows runs on the tensor cores: each block's
+    16 sub-block sums from int8 MMAs, then the reference's scale products and
+    fp32 terms in block order. Batch sizes below the switch (5), one and two
+    16-row launches, a last launch of 8 rows (24) and tails of fewer than 8
+    rows on the other path (17, 33); a partial last tile of 128 rows, one
+    block per row (cols 256) and rows too wide for the tensor-core path's
+    shared memory (cols 8192: the other path); activation blocks that are
+    zero, equal or hold rounding ties."""
+    t = TYPES["q6_k"]
+    rng = np.random.default_rng(cols + rows)
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=cols)
+    for nb in (5, 8, 16, 17, 24, 33):
+        x = _x(rng, nb, cols, edge=True)
+        _check(engine, oracle_mod, w, t, rows, cols, x, False, f"q6_k cols={cols} rows={rows} nb={nb}")
+
+
+@pytest.mark.gpu
+def test_q6_k_tensor_core_path_special_scales(pkg, engine, oracle_mod):
+    """Block scales d that are +inf, NaN, subnormal, -0 and -inf, and
+    extreme sub-block scales (-128, 127) on the tensor-core path."""
+    t = TYPES["q6_k"]
+    rows, cols = 640, 1024
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=41).copy()
+    specials = [0x7C00, 0x7E00, 0x0001, 0x8000, 0xFC00]
+    for i, h in enumerate(specials):
+        for r in range(i, rows, 37):
+            blk = (r * 7 + i) % 4
+            w[r, blk * 210 + 208] = h & 0xFF
+            w[r, blk * 210 + 209] = h >> 8
+    w[::5, 192:208] = np.array([0x80, 0x7F] * 8, np.uint8)  # sub-block scales -128, 127
+    w[::5, :128] = 0x00                                      # q = 0 (-32 after the offset)
+    w[::5, 128:192] = 0x00
+    x = np.random.default_rng(42).standard_normal((7, cols)).astype(np.float32)
+    got = engine.lm_head(_device_weights(w), t, rows, cols, x, exact=False)
+    want = oracle_mod.lm_head(w, t, rows, cols, x, exact_matmul=False, threads=16)
+    nan_g, nan_w = np.isnan(got), np.isnan(want)
+    assert np.array_equal(nan_g, nan_w)
+    assert nan_w.any()
+    ok = ~nan_w
+    assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32))
+
+
 # ---- golden fixtures (tests/golden/make_golden_lmhead.py) ---------------------
 
 def _golden_lmhead():
