@@ -300,6 +300,9 @@ NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld,
  * cols must be a whole number of blocks (32 for Q4_0/Q8_0, 256 for Q6_K) and
  * at most 16384 for F32/F16. Non-finite activations on the int8 path give
  * NLS_ERR_NAN_LOGITS (the reference's int8 conversion of them is undefined).
+ * Q6_K at 8 or more batch rows (and at most 5888 columns) runs on the tensor
+ * cores with the same results; a bounded wait there that runs out gives
+ * NLS_ERR_TIMEOUT.
  * Flags: NLS_DEVICE_INPUTS (x), NLS_DEVICE_OUTPUTS (y), NLS_EXACT_MATMUL,
  * NLS_ROWS_INDEPENDENT. */
 NLS_API nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,
