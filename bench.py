@@ -585,8 +585,9 @@ def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
         wd = W.lm_weights_device(t, rows, cols, seed=SEED, device=dev)
         wbytes = rows * W.lm_row_bytes(t, cols)
         res = {"weight_bytes": wbytes}
-        # (Q6_K at 8 and 16 batch rows: the tensor-core path)
-        for nb in {"q8_0": (1, 4), "q6_k": (1, 4, 8, 16), "f16": (1,)}[name]:
+        # (Q6_K at 8 and 16 batch rows: the tensor-core path; Q8_0 above 4
+        # rows and F16: the float path, tiled across batch rows above 1)
+        for nb in {"q8_0": (1, 4, 8, 16), "q6_k": (1, 4, 8, 16), "f16": (1, 4, 16)}[name]:
             x = torch.randn((nb, cols), generator=gen, device=dev)
             y = torch.empty((nb, rows), dtype=torch.float32, device=dev)
 

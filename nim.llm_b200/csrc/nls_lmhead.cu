@@ -10,7 +10,9 @@
 //    after block (Q6_K: (d_a * d_w) * float(sumi));
 //  * float path (exactMatmul, Q8_0 with more than 4 batch rows, F32/F16):
 //    dequantRow then dotF32 (quant.nim:362-374): eight strided fp32
-//    accumulators combined as ((s0+s1) + (s2+s3)) + (s4+s5)) + (s6+s7).
+//    accumulators combined as (((s0+s1) + (s2+s3)) + (s4+s5)) + (s6+s7).
+//    (F16 / Q8_0 / Q4_0 rows of whole 256-value chunks at more than one batch
+//    row, or Q8_0 / Q4_0 at any, take the tiled kernel of nls_lmhead_float.cu.)
 // Both are HBM-bound on the weights (one pass over rows x rowBytes per call at
 // small batch). The kernel streams row tiles of the weights through a ring of
 // shared-memory slots with cp.async.bulk (no multicast) and:
@@ -892,6 +894,10 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   // Q6_K at 8 or more batch rows: the same exact arithmetic on the tensor
   // cores, the weights read once per 16 batch rows (nls_lmhead_mma.cu); a
   // tail of fewer than 8 rows takes the path below
+  // the float path, tiled across batch rows (nls_lmhead_float.cu)
+  if (!int8 && lm_head_float_tiled(wtype, cols, rb) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (nb > 1 || wtype != 1))
+    return launch_lm_head_float(w, wtype, rb, rows, cols, x, nb, y, rows, sm_count, st);
   int b_first = 0;
   if (int8 && lm_head_mma_path(wtype, cols, nb)) {
     const int tail = (nb % 16 < 8) ? nb % 16 : 0;

@@ -270,6 +270,23 @@ def test_q6_k_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("name", ["f16", "q8_0", "q4_0"])
+def test_float_path_batch_tiles(pkg, engine, oracle_mod, name):
+    """The float path (dequantRow + dotF32) tiled across batch rows: one,
+    two and four batch rows per thread with padded batch groups (3, 7, 12),
+    several 16-row launches (21, 33) and a partial last tile of rows; both
+    the reference's own switch (Q8_0 above 4 rows) and exactMatmul."""
+    t = TYPES[name]
+    rng = np.random.default_rng(t + 7)
+    rows, cols = 1000, 1024
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=t + 3)
+    for nb in (2, 3, 7, 12, 16, 21, 33):
+        x = _x(rng, nb, cols, edge=True)
+        for exact in (False, True):
+            _check(engine, oracle_mod, w, t, rows, cols, x, exact, f"{name} nb={nb} exact={exact}")
+
+
+@pytest.mark.gpu
 def test_q6_k_tensor_core_path_special_scales(pkg, engine, oracle_mod):
     """Block scales d that are +inf, NaN, subnormal, -0 and -inf, and
     extreme sub-block scales (-128, 127) on the tensor-core path."""
