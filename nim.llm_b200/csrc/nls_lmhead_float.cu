@@ -8,7 +8,7 @@
 // (((s0 + s1) + (s2 + s3)) + (s4 + s5)) + (s6 + s7). Only each chain's own
 // order is fixed, so a thread can advance many chains at once: thread
 // (chain j, row group, batch group) holds the chains j of 4 weight rows x up
-// to 4 batch rows (16 independent dependency chains) and walks them together,
+// to 8 batch rows (up to 32 independent dependency chains) and walks them together,
 // one dequantised weight serving all its batch rows. A CTA of 256 threads
 // takes a tile of R weight rows (R = 128 / batch groups) for every batch row
 // of the launch; the tile's weights and the activations stream through
@@ -34,7 +34,7 @@ struct FloatArgs {
   const uint8_t* w;  // rows x row_bytes, 16-byte aligned, row_bytes % 16 == 0
   int64_t row_bytes;
   int rows, cols, nb;
-  int G;             // batch groups: batch rows per thread = BB, G * BB >= nb
+  int G;             // batch groups (1, 2, 4): batch rows per thread = BB, G * BB >= nb
   int R;             // weight rows per tile = 4 * (32 / G)
   int ntiles;
   int chunk_bytes;   // bytes of 256 values of one row (multiple of 16)
@@ -177,9 +177,13 @@ cudaError_t launch_bb(const FloatArgs& a, int BB, size_t smem, int grid, cudaStr
       e = cudaFuncSetAttribute(lmh_float_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) lmh_float_kernel<WT, 2><<<grid, kFThreads, smem, st>>>(a);
       break;
-    default:
+    case 4:
       e = cudaFuncSetAttribute(lmh_float_kernel<WT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) lmh_float_kernel<WT, 4><<<grid, kFThreads, smem, st>>>(a);
+      break;
+    default:
+      e = cudaFuncSetAttribute(lmh_float_kernel<WT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) lmh_float_kernel<WT, 8><<<grid, kFThreads, smem, st>>>(a);
       break;
   }
   if (e != cudaSuccess) return e;
@@ -207,7 +211,7 @@ cudaError_t launch_lm_head_float(const uint8_t* w, int wtype, int64_t row_bytes,
                                  cudaStream_t st) {
   for (int b0 = 0; b0 < nb; b0 += 16) {
     const int n = std::min(16, nb - b0);
-    const int BB = n >= 4 ? 4 : (n >= 2 ? 2 : 1);
+    const int BB = n >= 8 ? 8 : (n >= 4 ? 4 : (n >= 2 ? 2 : 1));
     FloatArgs a{};
     a.w = w;
     a.row_bytes = row_bytes;
