@@ -49,9 +49,11 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
                            cudaStream_t st);
-// Q6_K on the int8 path at more than 4 batch rows: tcgen05 int8 MMAs
-// (nls_lmhead_mma.cu), launches of up to 16 batch rows; y[b * ldy + r]
+// Q6_K / Q8_0 on the int8 path at lm_head_mma_min_rows or more batch rows:
+// tcgen05 int8 MMAs (nls_lmhead_mma.cu), launches of up to 16 batch rows;
+// y[b * ldy + r]
 bool lm_head_mma_path(int wtype, int cols, int nb);
+int lm_head_mma_min_rows(int wtype);
 // the float path (dequantRow + dotF32) for F16 / Q8_0 / Q4_0 weights whose
 // rows and 256-value chunks are 16-byte multiples (nls_lmhead_float.cu);
 // x 16-byte aligned; launches of up to 16 batch rows
@@ -59,8 +61,8 @@ bool lm_head_float_tiled(int wtype, int cols, int64_t row_bytes);
 cudaError_t launch_lm_head_float(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols,
                                  const float* x, int nb, float* y, int64_t ldy, int sm_count,
                                  cudaStream_t st);
-size_t lm_head_mma_smem(int cols);
-cudaError_t launch_lm_head_q6k_mma(const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x,
-                                   int nb, float* y, int64_t ldy, int* status, int sm_count,
-                                   unsigned long long wait_ns, cudaStream_t st);
+size_t lm_head_mma_smem(int wtype, int cols);
+cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols, const float* x,
+                               int nb, float* y, int64_t ldy, int* status, int sm_count,
+                               unsigned long long wait_ns, cudaStream_t st);
 }  // namespace nls

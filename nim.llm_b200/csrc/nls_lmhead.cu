@@ -891,18 +891,19 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
   const bool int8 = lm_head_int8_path(wtype, cols, path_nb, exact);
-  // Q6_K at 8 or more batch rows: the same exact arithmetic on the tensor
-  // cores, the weights read once per 16 batch rows (nls_lmhead_mma.cu); a
-  // tail of fewer than 8 rows takes the path below
   // the float path, tiled across batch rows (nls_lmhead_float.cu)
   if (!int8 && lm_head_float_tiled(wtype, cols, rb) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (nb > 1 || wtype != 1))
     return launch_lm_head_float(w, wtype, rb, rows, cols, x, nb, y, rows, sm_count, st);
+  // Q6_K / Q8_0 on the int8 path at 8 or more batch rows: the same exact
+  // arithmetic on the tensor cores, the weights read once per 16 batch rows
+  // (nls_lmhead_mma.cu); a tail of fewer than 8 rows takes the path below
   int b_first = 0;
   if (int8 && lm_head_mma_path(wtype, cols, nb)) {
-    const int tail = (nb % 16 < 8) ? nb % 16 : 0;
+    const int lo = lm_head_mma_min_rows(wtype);
+    const int tail = (nb % 16 < lo) ? nb % 16 : 0;
     const int nm = nb - tail;
-    cudaError_t e = launch_lm_head_q6k_mma(w, rb, rows, cols, x, nm, y, rows, status, sm_count, kWaitLimitNs, st);
+    cudaError_t e = launch_lm_head_mma(w, wtype, rb, rows, cols, x, nm, y, rows, status, sm_count, kWaitLimitNs, st);
     if (e != cudaSuccess || tail == 0) return e;
     b_first = nm;
   }

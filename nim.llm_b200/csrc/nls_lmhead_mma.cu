@@ -1,35 +1,46 @@
-// nls_lmhead_mma.cu -- the output projection for Q6_K weights at 8 to 16
-// batch rows per launch, on the 5th-generation tensor cores.
+// nls_lmhead_mma.cu -- the output projection for Q6_K, Q8_0 and Q4_0 weights at 8
+// to 16 batch rows per launch on the int8 path, on the 5th-generation
+// tensor cores.
 //
 // The reference's integer path (quantizeAct quant.nim:646-662, dotQ6K
-// quant.nim:731-760, matmulTask model.nim:144-155) computes per weight row r,
-// batch row b and 256-value block ib the exact integer
-//     sumi = sum_j sc_j * s_j,   s_j = sum_{l in sub-block j} (q_l - 32) * a_l
-// (16 sub-blocks of 16 values, int8 scales sc_j), then
-//     acc += (d_a * d_w) * float(sumi)
-// block after block in fp32. The s_j are int8 x int8 -> int32 contractions
-// (|s_j| <= 16 * 32 * 127), which tcgen05.mma kind::i8 computes exactly; the
-// scale products, the float conversion and the fp32 operations are the
-// reference's, in its order, on the CUDA cores.
+// quant.nim:731-760, dotQ8_0i quant.nim:762-772, matmulTask model.nim:144-155)
+// computes per weight row r, batch row b and weight block exact integer
+// sums of int8 x int8 products, then fp32 terms block after block:
+//  * Q6_K (256-value blocks): sumi = sum_j sc_j * s_j over 16 sub-blocks of
+//    16 values, s_j = sum (q_l - 32) * a_l, int8 scales sc_j; then
+//    acc += (d_a * d_w) * float(sumi);
+//  * Q8_0 and Q4_0 (32-value blocks, activations quantized in blocks of
+//    32): s = sum q_l * a_l (Q4_0: q_l a nibble minus 8); then
+//    acc += (d_w * d_a) * float(s).
+// The s_j and s are int8 x int8 -> int32 contractions (|s| <= 32 * 128 * 127),
+// which tcgen05.mma kind::i8 computes exactly; the scale products, the
+// float conversion and the fp32 operations are the reference's, in its
+// order, on the CUDA cores. (Q8_0 takes the int8 path at more than 4 batch
+// rows only when the rows are separate sequences, model.nim:185.)
 //
 // One CTA of 544 threads per SM, persistent over tiles of 128 weight rows,
-// warp-specialised. Per (tile, block) step:
-//  * the 16 worker warps copy a part of the tile's raw Q6_K bytes two steps
+// warp-specialised. A step covers 256 values of every row of the tile (one
+// Q6_K block, eight Q8_0 or Q4_0 blocks). Per (tile, step):
+//  * the 16 worker warps copy a part of the tile's raw bytes two steps
 //    ahead into shared memory (16-byte cp.async; the bytes past the weights'
 //    last whole 16 go by plain loads);
-//  * each worker unpacks one (row, quarter) of the block -- four sub-blocks
-//    of 16 values, q - 32 as int8 -- into the A operand of its parity (one of
-//    two buffers): even sub-blocks are the first 16 values of a 32-value K
-//    step, odd ones the second, and the other half of both is one shared
-//    block of zeros that the descriptors point at (no-swizzle K-major
-//    layout; 8-row x 16-byte core matrices);
-//  * warp 0 issues 16 MMAs (M = 128 rows, N = 16 batch rows, K = 32),
-//    sub-block j into TMEM columns 16j .. 16j+15 of one of two 256-column
-//    regions, and commits them to an mbarrier, while the workers go on with
-//    the next step (operands and TMEM double-buffered);
+//  * the workers lay the step's weights out as the A operand of its parity
+//    (one of two buffers; no-swizzle K-major layout, 8-row x 16-byte core
+//    matrices). Q6_K: each worker unpacks one (row, quarter) of the block --
+//    four sub-blocks of 16 values, q - 32 as int8 -- even sub-blocks as the
+//    first 16 values of a 32-value K step, odd ones as the second, and the
+//    other half of both is one shared block of zeros that the descriptors
+//    point at. Q8_0 / Q4_0: each worker lays out four (row, block, half)
+//    units of 16 int8 values (Q4_0: nibbles minus 8), one K step per block,
+//    and records the blocks' d;
+//  * warp 0 issues the step's MMAs (M = 128 rows, N = 16 batch rows, K = 32;
+//    16 for Q6_K, sub-block j into TMEM columns 16j .. 16j+15, 8 for the others,
+//    block i into columns 16i ..) into one of two regions and commits them to
+//    an mbarrier, while the workers go on with the next step (operands and
+//    TMEM double-buffered);
 //  * every worker warp reads, for the 32 weight rows of its TMEM lane
-//    quarter (warp % 4) and 4 of the 16 batch rows, the previous step's 16
-//    sub-block sums and forms sumi and the fp32 term.
+//    quarter (warp % 4) and 4 of the 16 batch rows, the previous step's sums
+//    and forms the fp32 terms in block order.
 // Workers synchronise among themselves with named barriers and with warp 0
 // through mbarriers. The activations are quantized once per CTA into shared
 // memory in the operand layout (batch rows past nb are zeros). Every wait is
@@ -53,10 +64,6 @@ constexpr int kQ6Bytes = 210;    // a Q6_K block
 // one A buffer: even sub-blocks [0, 16 KB), a 2 KB block of zeros, odd ones
 // [18 KB, 34 KB); K step i of a parity at + 2 KB * i, row r at + 16 r
 constexpr int kAEven = 0, kAZero = 16384, kAOdd = 18432, kAStage = 34816;
-constexpr int kRawRow = 240;     // staged bytes per row: the block and its 16-byte alignment
-constexpr int kRawChunks = kRawRow / 16;
-constexpr int kRawStage = kMmaRows * kRawRow;
-constexpr int kTmemCols = 512;   // two regions of 16 sub-blocks x 16 batch columns
 constexpr int kSlots = 3;        // per-step scales: written by its unpack, read one
                                  // iteration later (a worker may be one ahead)
 
@@ -125,19 +132,65 @@ struct MmaArgs {
   int* status;
 };
 
-__global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaArgs a) {
+template <int WT>
+struct MmaType;
+// A step covers 256 values of a weight row (one K step of 32 per MMA).
+template <>
+struct MmaType<14> {                 // Q6_K: one 210-byte block per step
+  static constexpr int kBL = 256;    // activation block (quantizeAct)
+  static constexpr int kStepBytes = kQ6Bytes;
+  static constexpr int kRawRow = 240;  // the block and its 16-byte alignment
+  static constexpr int kDw = 1;      // d per row and step
+  static constexpr int kScWords = 4; // sub-block scales per row and step
+  static constexpr int kRegion = 256;  // TMEM columns per step: 16 sub-blocks x 16
+};
+template <>
+struct MmaType<8> {                  // Q8_0: eight 34-byte blocks per step
+  static constexpr int kBL = 32;
+  static constexpr int kStepBytes = 8 * 34;
+  static constexpr int kRawRow = 8 * 34;  // 16-byte aligned (rows of whole steps)
+  static constexpr int kDw = 8;
+  static constexpr int kScWords = 0;
+  static constexpr int kRegion = 128;  // 8 blocks x 16
+  static constexpr int kBlockBytes = 34;
+};
+template <>
+struct MmaType<2> {                  // Q4_0: eight 18-byte blocks per step
+  static constexpr int kBL = 32;
+  static constexpr int kStepBytes = 8 * 18;
+  static constexpr int kRawRow = 8 * 18;  // 16-byte aligned (rows of whole steps)
+  static constexpr int kDw = 8;
+  static constexpr int kScWords = 0;
+  static constexpr int kRegion = 128;
+  static constexpr int kBlockBytes = 18;
+};
+
+template <int WT>
+__host__ __device__ constexpr size_t mma_smem(int cols) {
+  using T = MmaType<WT>;
+  return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)kAStage + 2 * (size_t)kMmaRows * T::kRawRow +
+         (size_t)kMmaN * (cols / T::kBL) * 4 + (size_t)kSlots * kMmaRows * T::kDw * 4 +
+         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 32 + 16 + 16;
+}
+
+template <int WT>
+__global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a) {
+  using T = MmaType<WT>;
+  constexpr int kRawRowT = T::kRawRow, kRawChunksT = kRawRowT / 16, kRawStageT = kMmaRows * kRawRowT;
+  constexpr int kTmemCols = 2 * T::kRegion;  // two regions: steps s and s + 1
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wi = tid - 32;  // worker index (warp 0: negative)
   const int kb_steps = a.cols / 32;
+  const int nab = a.cols / T::kBL;                              // activation blocks per row
   uint8_t* bop = smem;                                          // activations: kb_steps x 512 B
   uint8_t* aop = bop + (size_t)kb_steps * (kMmaN * 32);         // 2 A buffers
-  uint8_t* raw = aop + 2 * kAStage;                             // 2 x 128 rows x 240 B
-  float* dsa = reinterpret_cast<float*>(raw + 2 * kRawStage);   // d_a [16][nblk]
-  float* dws = dsa + kMmaN * a.nblk;                            // d_w [kSlots][128]
-  uint32_t* scs = reinterpret_cast<uint32_t*>(dws + kSlots * kMmaRows);  // sc [kSlots][128][4 words]
+  uint8_t* raw = aop + 2 * kAStage;                             // 2 x 128 rows x kRawRow B
+  float* dsa = reinterpret_cast<float*>(raw + 2 * kRawStageT);  // d_a [16][nab]
+  float* dws = dsa + kMmaN * nab;                               // d_w [kSlots][kDw][128]
+  uint32_t* scs = reinterpret_cast<uint32_t*>(dws + kSlots * kMmaRows * T::kDw);  // Q6_K sc [kSlots][128][4 words]
   uint64_t* bar = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(scs + kSlots * kMmaRows * 4) + 7) & ~uintptr_t(7));
+      (reinterpret_cast<uintptr_t>(scs + kSlots * kMmaRows * T::kScWords) + 7) & ~uintptr_t(7));
   uint64_t* ready = bar;     // [2] workers -> warp 0: A buffer s & 1 holds step s
   uint64_t* done = bar + 2;  // [2] MMAs of step s completed (tcgen05.commit)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 4);
@@ -151,28 +204,28 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
   // workers stage the raw bytes of step s into buffer s & 1 (one cp.async
   // group per call, empty past the last step); worker wi's chunks
   // i = wi + k * workers of a stage are (row i / 15, chunk i % 15)
-  constexpr int kChunksPerThread = (kMmaRows * kRawChunks + kWorkers - 1) / kWorkers;
+  constexpr int kChunksPerThread = (kMmaRows * kRawChunksT + kWorkers - 1) / kWorkers;
   int crr[kChunksPerThread], ccc[kChunksPerThread];
 #pragma unroll
   for (int k = 0; k < kChunksPerThread; ++k) {
     const int i = wi + k * kWorkers;
-    crr[k] = (wi >= 0 && i < kMmaRows * kRawChunks) ? i / kRawChunks : kMmaRows;
-    ccc[k] = (i >= 0) ? i % kRawChunks : 0;
+    crr[k] = (wi >= 0 && i < kMmaRows * kRawChunksT) ? i / kRawChunksT : kMmaRows;
+    ccc[k] = (i >= 0) ? i % kRawChunksT : 0;
   }
   auto stage_raw = [&](int s) {
     if (s < nsteps) {
       const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
       const int kb = s % a.nblk;
-      uint8_t* dst = raw + (size_t)(s & 1) * kRawStage;
+      uint8_t* dst = raw + (size_t)(s & 1) * kRawStageT;
 #pragma unroll
       for (int k = 0; k < kChunksPerThread; ++k) {
         const int rr = crr[k], c = ccc[k];
         if (rr >= kMmaRows) continue;
         const int r = t * kMmaRows + rr;
         if (r >= a.rows) continue;
-        const int64_t g = ((int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes) & ~int64_t(15);
+        const int64_t g = ((int64_t)r * a.row_bytes + (int64_t)kb * T::kStepBytes) & ~int64_t(15);
         const int64_t src = g + 16 * c;
-        uint8_t* d = dst + rr * kRawRow + 16 * c;
+        uint8_t* d = dst + rr * kRawRowT + 16 * c;
         if (src + 16 <= last16) {
           cp_async16(d, a.w + src);
         } else {
@@ -199,32 +252,60 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
   for (int i = tid; i < (kb_steps * (kMmaN * 32) + 2 * kAStage) / 16; i += kMmaThreads)
     reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
-  // quantizeAct (quant.nim:646-662) with blocks of 256, one warp per block
+  // quantizeAct (quant.nim:646-662) with the type's blocks (256 values for
+  // Q6_K, 32 for Q8_0): each thread takes 32 consecutive values, the G
+  // threads of a block (consecutive lanes) combine their maxima by shuffles
   {
-    const int nblocks = a.nb * a.nblk;
-    for (int blk = warp; blk < nblocks; blk += kMmaThreads / 32) {
-      const int b = blk / a.nblk, ib = blk % a.nblk;
-      const float* xs = a.x + (size_t)b * a.cols + (size_t)ib * 256;
-      float v[8];
+    constexpr int G = T::kBL / 32;
+    const int per_row = a.cols / 32;
+    const int units = a.nb * per_row;  // a multiple of 8: whole blocks per warp
+    for (int base = warp * 32; base < units; base += kMmaThreads) {
+      const int u = base + lane;
+      const bool act = u < units;
+      const int b = act ? u / per_row : 0, c = act ? u % per_row : 0;
+      const float* xs = a.x + (size_t)b * a.cols + (size_t)c * 32;
+      float v[32];
+      if (act && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 f = reinterpret_cast<const float4*>(xs)[k];
+          v[4 * k] = f.x;
+          v[4 * k + 1] = f.y;
+          v[4 * k + 2] = f.z;
+          v[4 * k + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = act ? xs[k] : 0.0f;
+      }
       float amax = 0.0f;
       bool bad = false;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        v[u] = xs[u * 32 + lane];
-        bad |= !isfinite(v[u]);
-        amax = fmaxf(amax, fabsf(v[u]));
+      for (int k = 0; k < 32; ++k) {
+        bad |= !isfinite(v[k]);
+        amax = fmaxf(amax, fabsf(v[k]));
       }
 #pragma unroll
-      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      for (int o = 1; o < G; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0) atomicCAS(a.status, 0, NLS_ERR_NAN_LOGITS);
-      const float d = amax / 127.0f;
-      const float id = d > 0.0f ? 1.0f / d : 0.0f;
-      if (lane == 0) dsa[b * a.nblk + ib] = d;
+      if (act) {
+        const float d = amax / 127.0f;
+        const float id = d > 0.0f ? 1.0f / d : 0.0f;
+        if (c % G == 0) dsa[b * nab + c / G] = d;
+        uint32_t qw[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float q0 = v[u] * id;
-        const int q = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
-        bop[b_off(b, ib * 256 + u * 32 + lane)] = (uint8_t)(int8_t)q;
+        for (int k = 0; k < 8; ++k) {
+          uint32_t wv = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float q0 = v[4 * k + e] * id;
+            const int q = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
+            wv |= ((uint32_t)q & 0xFFu) << (8 * e);
+          }
+          qw[k] = wv;
+        }
+        *reinterpret_cast<uint4*>(bop + b_off(b, c * 32)) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+        *reinterpret_cast<uint4*>(bop + b_off(b, c * 32 + 16)) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
       }
     }
   }
@@ -257,14 +338,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
         const int kb = s % a.nblk;
         const uint32_t ab = smem_u32(aop) + (uint32_t)((s & 1) * kAStage);
         const uint32_t bb = smem_u32(bop) + (uint32_t)(kb * 8) * (kMmaN * 32);
-        const uint32_t dreg = tbase + (uint32_t)((s & 1) * 256);
+        const uint32_t dreg = tbase + (uint32_t)((s & 1) * T::kRegion);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const uint64_t db = smem_desc(bb + (uint32_t)i * (kMmaN * 32), 128, 256);
-          // even sub-block 2i: its values, then the zeros; odd 2i + 1: the
-          // zeros, then its values
-          mma_i8(dreg + 32 * i, smem_desc(ab + kAEven + 2048 * i, kAZero - kAEven - 2048 * i, 128), db);
-          mma_i8(dreg + 32 * i + 16, smem_desc(ab + kAZero, kAOdd - kAZero + 2048 * i, 128), db);
+          if constexpr (WT == 14) {
+            // even sub-block 2i: its values, then the zeros; odd 2i + 1: the
+            // zeros, then its values
+            mma_i8(dreg + 32 * i, smem_desc(ab + kAEven + 2048 * i, kAZero - kAEven - 2048 * i, 128), db);
+            mma_i8(dreg + 32 * i + 16, smem_desc(ab + kAZero, kAOdd - kAZero + 2048 * i, 128), db);
+          } else {
+            // block i: its first 16 values of every row, then its second 16
+            mma_i8(dreg + 16 * i, smem_desc(ab + 4096 * i, 2048, 128), db);
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&done[s & 1]))
@@ -289,9 +375,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
         if (s >= 2 && !fail && !wait_bar(done, s - 2)) fail = true;
         const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
         const int kb = s % a.nblk;
+        if constexpr (WT == 14) {
         const int r = t * kMmaRows + ur;
         const int64_t g = (int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes;
-        const uint8_t* blk = raw + (size_t)(s & 1) * kRawStage + ur * kRawRow + (int)(g & 15);
+        const uint8_t* blk = raw + (size_t)(s & 1) * kRawStageT + ur * kRawRowT + (int)(g & 15);
         uint32_t QA[4], QB[4], QH[4];
         ld16s(blk + 64 * uh + 16 * uhalf, QA);
         ld16s(blk + 64 * uh + 32 + 16 * uhalf, QB);
@@ -325,6 +412,42 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
           }
           *reinterpret_cast<uint4*>(ab + a_off(ur, 8 * uh + 2 * c + uhalf)) = make_uint4(v[0], v[1], v[2], v[3]);
         }
+        } else {
+          // Q8_0 / Q4_0: four (row, block, half) units per worker, 32
+          // consecutive rows per warp; half h of block j is values
+          // 16h .. 16h+15, which go to the block's K step as int8: Q8_0's as
+          // they are, Q4_0's nibbles (low ones for h = 0, high ones for
+          // h = 1; dotQ4_0i quant.nim:774-786) minus 8 (q ^ 8 is q - 8 for
+          // q >= 8 and q + 8 below; those get bits 4-7). The half h = 0 also
+          // records d (rows past the matrix: zero).
+          const uint8_t* rs = raw + (size_t)(s & 1) * kRawStageT;
+          uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int u = wi + k * kWorkers;
+            const int rr = u & (kMmaRows - 1), jh = u >> 7, j = jh >> 1, h = jh & 1;
+            const uint8_t* blk = rs + rr * kRawRowT + T::kBlockBytes * j;
+            uint32_t q[4];
+            if constexpr (WT == 8) {
+              ld16s(blk + 2 + 16 * h, q);
+            } else {
+              ld16s(blk + 2, q);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t v = (q[e] >> (4 * h)) & 0x0F0F0F0Fu;
+                const uint32_t t = v ^ 0x08080808u;
+                const uint32_t m = ~v & 0x08080808u;
+                q[e] = t | (m << 1) | (m << 2) | (m << 3) | (m << 4);
+              }
+            }
+            *reinterpret_cast<uint4*>(ab + 4096 * j + 2048 * h + 16 * rr) = make_uint4(q[0], q[1], q[2], q[3]);
+            if (h == 0) {
+              const uint32_t dwb = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8);
+              dws[((s % kSlots) * 8 + j) * kMmaRows + rr] =
+                  (t * kMmaRows + rr < a.rows) ? __half2float(__ushort_as_half((unsigned short)dwb)) : 0.0f;
+            }
+          }
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
       if (fail) *s_fail = 1;
@@ -343,12 +466,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
       if (s >= 1 && !fail) {
         const int p = s - 1;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int kb = p % a.nblk;
+        const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * T::kRegion + eb0);
+        if constexpr (WT == 14) {
         const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
         uint32_t scw[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) scw[k] = sd[k];
         int sumi[4] = {0, 0, 0, 0};
-        const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * 256 + eb0);
 #pragma unroll
         for (int j0 = 0; j0 < 16; j0 += 4) {
           uint32_t d[4][4];
@@ -363,13 +488,31 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
             for (int e = 0; e < 4; ++e) sumi[e] += sc * (int)d[u][e];
           }
         }
-        const int kb = p % a.nblk;
         const float dw = dws[(p % kSlots) * kMmaRows + em];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int b = eb0 + e;
           if (b < a.nb)
-            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * a.nblk + kb], dw), __int2float_rn(sumi[e])));
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * nab + kb], dw), __int2float_rn(sumi[e])));
+        }
+        } else {
+          // dotQ8_0i / dotQ4_0i (quant.nim:762-786): block after block,
+          // acc += (d_w * d_a) * float(s)
+          uint32_t d[8][4];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) tmem_ld4(ta + 16 * i, d[i]);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float dw = dws[((p % kSlots) * 8 + i) * kMmaRows + em];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int b = eb0 + e;
+              if (b < a.nb)
+                acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw, dsa[b * nab + kb * 8 + i]),
+                                                     __int2float_rn((int)d[i][e])));
+            }
+          }
         }
         if (kb == a.nblk - 1) {
           const int t = (int)blockIdx.x + (p / a.nblk) * (int)gridDim.x;
@@ -406,20 +549,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_q6k_mma_kernel(const MmaAr
 
 }  // namespace
 
-size_t lm_head_mma_smem(int cols) {
-  const int nblk = cols / 256;
-  return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)kAStage + 2 * (size_t)kRawStage +
-         (size_t)kMmaN * nblk * 4 + (size_t)kSlots * kMmaRows * 4 + (size_t)kSlots * kMmaRows * 16 + 8 + 32 +
-         16 + 16;
+size_t lm_head_mma_smem(int wtype, int cols) {
+  return wtype == 14 ? mma_smem<14>(cols) : wtype == 8 ? mma_smem<8>(cols) : wtype == 2 ? mma_smem<2>(cols) : 0;
 }
+
+int lm_head_mma_min_rows(int wtype) { return wtype == 14 ? 8 : 8; }
 
 bool lm_head_mma_path(int wtype, int cols, int nb) {
-  return wtype == 14 && nb >= 8 && cols % 256 == 0 && cols >= 256 && lm_head_mma_smem(cols) <= (size_t)(227 * 1024);
+  return (wtype == 14 || wtype == 8 || wtype == 2) && nb >= lm_head_mma_min_rows(wtype) && cols % 256 == 0 &&
+         cols >= 256 && lm_head_mma_smem(wtype, cols) <= (size_t)(227 * 1024);
 }
 
-cudaError_t launch_lm_head_q6k_mma(const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x,
-                                   int nb, float* y, int64_t ldy, int* status, int sm_count,
-                                   unsigned long long wait_ns, cudaStream_t st) {
+cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols, const float* x,
+                               int nb, float* y, int64_t ldy, int* status, int sm_count,
+                               unsigned long long wait_ns, cudaStream_t st) {
+  if (wtype != 14 && wtype != 8 && wtype != 2) return cudaErrorInvalidValue;
   MmaArgs a{};
   a.w = w;
   a.row_bytes = row_bytes;
@@ -431,15 +575,16 @@ cudaError_t launch_lm_head_q6k_mma(const uint8_t* w, int64_t row_bytes, int rows
   a.ntiles = (rows + kMmaRows - 1) / kMmaRows;
   a.wait_ns = wait_ns;
   a.status = status;
-  const size_t smem = lm_head_mma_smem(cols);
-  cudaError_t e = cudaFuncSetAttribute(lmh_q6k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = lm_head_mma_smem(wtype, cols);
+  auto kern = (wtype == 14) ? lmh_mma_kernel<14> : (wtype == 8) ? lmh_mma_kernel<8> : lmh_mma_kernel<2>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::min(a.ntiles, sm_count);
   for (int b0 = 0; b0 < nb; b0 += kMmaN) {
     a.nb = std::min(kMmaN, nb - b0);
     a.x = x + (size_t)b0 * cols;
     a.y = y + (size_t)b0 * ldy;
-    lmh_q6k_mma_kernel<<<grid, kMmaThreads, smem, st>>>(a);
+    kern<<<grid, kMmaThreads, smem, st>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

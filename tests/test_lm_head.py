@@ -269,6 +269,91 @@ def test_q6_k_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
         _check(engine, oracle_mod, w, t, rows, cols, x, False, f"q6_k cols={cols} rows={rows} nb={nb}")
 
 
+def _oracle_independent(oracle_mod, w, t, rows, cols, x):
+    """Rows that are separate sequences: one-row matmuls (the int8 path for
+    Q8_0 at any count); a call of at most 4 rows takes the same path and
+    gives every row the same logits."""
+    return np.concatenate([oracle_mod.lm_head(w, t, rows, cols, x[i:i + 4], threads=16)
+                           for i in range(0, x.shape[0], 4)])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cols,rows", [(256, 1000), (4096, 3001), (4352, 300), (8192, 515)])
+def test_q8_0_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
+    """Q8_0 rows that are separate sequences (the int8 path at any count)
+    run on the tensor cores from 8 rows: each block's sum from an int8 MMA,
+    then (d_w * d_a) * float(s) in block order. Batch sizes below the switch
+    (5), one and two 16-row launches, a last launch of 8 rows (24) and tails
+    of fewer than 8 rows on the other path (17, 33); a partial last tile of
+    128 rows, one 256-value step per row (cols 256), the widest row that
+    fits the shared memory (4352) and one that does not (8192: the other
+    path); activation blocks that are zero, equal or hold rounding ties."""
+    t = TYPES["q8_0"]
+    rng = np.random.default_rng(cols + rows + 1)
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=cols + 1)
+    dw = _device_weights(w)
+    for nb in (5, 8, 16, 17, 24, 33):
+        x = _x(rng, nb, cols, edge=True)
+        got = engine.lm_head(dw, t, rows, cols, x, independent=True)
+        want = _oracle_independent(oracle_mod, w, t, rows, cols, x)
+        bad = np.nonzero(_bits(got) != _bits(want))
+        assert bad[0].size == 0, f"q8_0 cols={cols} nb={nb}: {bad[0].size} logits differ, first at " \
+            f"{bad[0][0]},{bad[1][0]}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cols,rows", [(256, 1000), (4096, 3001), (6144, 300), (8192, 515)])
+def test_q4_0_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
+    """Q4_0 (the int8 path at any batch size) on the tensor cores from 8
+    rows: nibbles minus 8 as int8 operands, one MMA per block, then
+    (d_w * d_a) * float(s) in block order; the same batch sizes and edges as
+    Q8_0, 6144 the widest row that fits the shared memory."""
+    t = TYPES["q4_0"]
+    rng = np.random.default_rng(cols + rows + 2)
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=cols + 2)
+    for nb in (5, 8, 16, 17, 24, 33):
+        x = _x(rng, nb, cols, edge=True)
+        _check(engine, oracle_mod, w, t, rows, cols, x, False, f"q4_0 cols={cols} rows={rows} nb={nb}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q4_0"])
+def test_32_value_blocks_tensor_core_path_special_scales(pkg, engine, oracle_mod, name):
+    """Block scales d that are +inf, NaN, subnormal, -0 and -inf, and
+    blocks of extreme values (Q8_0: -128 and 127; Q4_0: nibbles 0 and 15)
+    on the tensor-core path."""
+    t = TYPES[name]
+    bb = {"q8_0": 34, "q4_0": 18}[name]
+    rows, cols = 640, 1024
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=43).copy()
+    specials = [0x7C00, 0x7E00, 0x0001, 0x8000, 0xFC00]
+    for i, h in enumerate(specials):
+        for r in range(i, rows, 37):
+            blk = (r * 7 + i) % (cols // 32)
+            w[r, blk * bb] = h & 0xFF
+            w[r, blk * bb + 1] = h >> 8
+    w[::5, 2:bb] = 0x80 if name == "q8_0" else 0x00        # q = -128 / every nibble 0 (-8)
+    w[1::5, bb + 2:2 * bb] = 0x7F if name == "q8_0" else 0xFF  # q = 127 / every nibble 15 (7)
+    x = np.random.default_rng(44).standard_normal((11, cols)).astype(np.float32)
+    got = engine.lm_head(_device_weights(w), t, rows, cols, x, independent=True)
+    want = _oracle_independent(oracle_mod, w, t, rows, cols, x)
+    nan_g, nan_w = np.isnan(got), np.isnan(want)
+    assert np.array_equal(nan_g, nan_w)
+    assert nan_w.any()
+    ok = ~nan_w
+    assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32))
+    # a non-finite activation on this path is an error, as on the others
+    import ctypes
+    xb = x.copy()
+    xb[9, 700] = np.nan
+    y = np.empty((11, rows), np.float32)
+    dw = _device_weights(w)
+    st = engine._lib.nls_lm_head(engine._h, ctypes.c_void_p(dw.data_ptr()), t, rows, cols,
+                                 ctypes.c_void_p(xb.ctypes.data), 11, ctypes.c_void_p(y.ctypes.data),
+                                 8, ctypes.c_void_p(0))
+    assert st == 5
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["f16", "q8_0", "q4_0"])
 def test_float_path_batch_tiles(pkg, engine, oracle_mod, name):
