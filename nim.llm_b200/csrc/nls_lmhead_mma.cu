@@ -45,9 +45,11 @@
 // through mbarriers. The activations are quantized once per CTA into shared
 // memory in the operand layout (batch rows past nb are zeros). Every wait is
 // bounded.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "nls_kernels.h"
 #include "nls_tma.cuh"
@@ -56,18 +58,21 @@ namespace nls {
 
 namespace {
 
-constexpr int kWorkers = 512;    // warps 1-16: staging, unpacking, sums
-constexpr int kMmaThreads = 32 + kWorkers;  // warp 0: the MMA issuer
+constexpr int kWorkers = 512;    // warps 1-16: unpacking, sums
+constexpr int kMmaThreads = 32 + kWorkers;  // warp 0: staging, the MMA issuer
 constexpr int kMmaRows = 128;    // weight rows per tile (MMA M)
 constexpr int kMmaN = 16;        // batch rows per launch (MMA N)
 constexpr int kQ6Bytes = 210;    // a Q6_K block
-// one A buffer: even sub-blocks [0, 16 KB), a 2 KB block of zeros, odd ones
-// [18 KB, 34 KB); K step i of a parity at + 2 KB * i, row r at + 16 r
-constexpr int kAEven = 0, kAZero = 16384, kAOdd = 18432, kAStage = 34816;
-constexpr int kSlots = 3;        // per-step scales: written by its unpack, read one
-                                 // iteration later (a worker may be one ahead)
+// Q6_K's A buffer: even sub-blocks [0, 16 KB), a 2 KB block of zeros, odd
+// ones [18 KB, 34 KB); K step i of a parity at + 2 KB * i, row r at + 16 r
+constexpr int kAEven = 0, kAZero = 16384, kAOdd = 18432;
+// per-step scales: written by a step's unpack, read by its sums; the worker
+// warps run up to three steps apart (a warp unpacks step s only once every
+// warp has unpacked step s - 2, and a warp that has may still be summing
+// step s - 3)
+constexpr int kSlots = 4;
 
-// offset of the 16 values of row r, sub-block j inside an A buffer
+// offset of the 16 values of row r, sub-block j inside a Q6_K A buffer
 __device__ __forceinline__ int a_off(int r, int j) { return ((j & 1) ? kAOdd : kAEven) + (j >> 1) * 2048 + r * 16; }
 // offset of byte k of batch row b inside the activation operand (K steps of
 // 32 values, 512 bytes each for 16 rows)
@@ -128,9 +133,20 @@ struct MmaArgs {
   float* y;          // y[b * ldy + r]
   int64_t ldy;
   int ntiles;
+  int tiled;         // the weights have a tensor map (row_bytes % 16 == 0)
   unsigned long long wait_ns;
   int* status;
 };
+
+// 2-D tensor copy (no multicast): box {x .. , y ..} of the map into shared
+// memory, completing on the mbarrier
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 
 template <int WT>
 struct MmaType;
@@ -143,6 +159,7 @@ struct MmaType<14> {                 // Q6_K: one 210-byte block per step
   static constexpr int kDw = 1;      // d per row and step
   static constexpr int kScWords = 4; // sub-block scales per row and step
   static constexpr int kRegion = 256;  // TMEM columns per step: 16 sub-blocks x 16
+  static constexpr int kAStage = 34816;
 };
 template <>
 struct MmaType<8> {                  // Q8_0: eight 34-byte blocks per step
@@ -152,108 +169,187 @@ struct MmaType<8> {                  // Q8_0: eight 34-byte blocks per step
   static constexpr int kDw = 8;
   static constexpr int kScWords = 0;
   static constexpr int kRegion = 128;  // 8 blocks x 16
-  static constexpr int kBlockBytes = 34;
+  static constexpr int kAStage = 32768;  // block i: [its first 16 values of every row][its second 16]
 };
 template <>
 struct MmaType<2> {                  // Q4_0: eight 18-byte blocks per step
   static constexpr int kBL = 32;
   static constexpr int kStepBytes = 8 * 18;
-  static constexpr int kRawRow = 8 * 18;  // 16-byte aligned (rows of whole steps)
+  static constexpr int kRawRow = 8 * 18;
   static constexpr int kDw = 8;
   static constexpr int kScWords = 0;
   static constexpr int kRegion = 128;
-  static constexpr int kBlockBytes = 18;
+  static constexpr int kAStage = 32768;
 };
 
 template <int WT>
 __host__ __device__ constexpr size_t mma_smem(int cols) {
   using T = MmaType<WT>;
-  return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)kAStage + 2 * (size_t)kMmaRows * T::kRawRow +
+  return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)T::kAStage + 2 * (size_t)kMmaRows * T::kRawRow +
          (size_t)kMmaN * (cols / T::kBL) * 4 + (size_t)kSlots * kMmaRows * T::kDw * 4 +
-         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 32 + 16 + 16;
+         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 6 * 8 + 16 + 16;
+}
+
+// Q8_0: one thread lays out blocks 2Q and 2Q + 1 of a row from the 80 bytes
+// at 64Q of its staged step (five 16-byte words W; block j's d at byte 34j,
+// its values at 34j + 2). Q is uniform across the warp.
+template <int Q>
+__device__ __forceinline__ void q8_units(const uint32_t (&W)[20], uint8_t* ab, float* dslot, int rr, bool in) {
+  uint32_t v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = __byte_perm(W[Q + k], W[Q + k + 1], 0x5432);  // block 2Q at 4Q + 2
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q) + 16 * rr) = make_uint4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q) + 2048 + 16 * rr) = make_uint4(v[4], v[5], v[6], v[7]);
+  // block 2Q + 1 at 4Q + 36 (word aligned)
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q + 1) + 16 * rr) = make_uint4(W[Q + 9], W[Q + 10], W[Q + 11], W[Q + 12]);
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q + 1) + 2048 + 16 * rr) =
+      make_uint4(W[Q + 13], W[Q + 14], W[Q + 15], W[Q + 16]);
+  const float d0 = __half2float(__ushort_as_half((unsigned short)(W[Q] & 0xFFFFu)));
+  const float d1 = __half2float(__ushort_as_half((unsigned short)(W[Q + 8] >> 16)));
+  dslot[(2 * Q) * kMmaRows + rr] = in ? d0 : 0.0f;
+  dslot[(2 * Q + 1) * kMmaRows + rr] = in ? d1 : 0.0f;
+}
+
+// q - 8 as int8 for four packed nibbles q (q ^ 8 is q - 8 for q >= 8 and
+// q + 8 below; those get bits 4-7)
+__device__ __forceinline__ uint32_t nib_minus8(uint32_t v) {
+  const uint32_t t = v ^ 0x08080808u;
+  const uint32_t m = ~v & 0x08080808u;
+  return t | (m << 1) | (m << 2) | (m << 3) | (m << 4);
+}
+
+// Q4_0 (dotQ4_0i quant.nim:774-786: values 0-15 of a block are the low
+// nibbles of its 16 bytes, values 16-31 the high ones): blocks 2Q and 2Q + 1
+// from the 48 bytes at 32Q of the staged step (block j's d at 18j, its
+// bytes at 18j + 2).
+template <int Q>
+__device__ __forceinline__ void q4_units(const uint32_t (&W)[12], uint8_t* ab, float* dslot, int rr, bool in) {
+  uint32_t b0[4], b1[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    b0[k] = __byte_perm(W[Q + k], W[Q + k + 1], 0x5432);  // block 2Q at 4Q + 2
+    b1[k] = W[Q + 5 + k];                                   // block 2Q + 1 at 4Q + 20
+  }
+  uint32_t lo[4], hi[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    lo[k] = nib_minus8(b0[k] & 0x0F0F0F0Fu);
+    hi[k] = nib_minus8((b0[k] >> 4) & 0x0F0F0F0Fu);
+  }
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q) + 16 * rr) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q) + 2048 + 16 * rr) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    lo[k] = nib_minus8(b1[k] & 0x0F0F0F0Fu);
+    hi[k] = nib_minus8((b1[k] >> 4) & 0x0F0F0F0Fu);
+  }
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q + 1) + 16 * rr) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  *reinterpret_cast<uint4*>(ab + 4096 * (2 * Q + 1) + 2048 + 16 * rr) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  const float d0 = __half2float(__ushort_as_half((unsigned short)(W[Q] & 0xFFFFu)));
+  const float d1 = __half2float(__ushort_as_half((unsigned short)(W[Q + 4] >> 16)));
+  dslot[(2 * Q) * kMmaRows + rr] = in ? d0 : 0.0f;
+  dslot[(2 * Q + 1) * kMmaRows + rr] = in ? d1 : 0.0f;
 }
 
 template <int WT>
-__global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a) {
+__global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a,
+                                                                const __grid_constant__ CUtensorMap wmap) {
   using T = MmaType<WT>;
-  constexpr int kRawRowT = T::kRawRow, kRawChunksT = kRawRowT / 16, kRawStageT = kMmaRows * kRawRowT;
+  constexpr int kRawRow = T::kRawRow, kRawStage = kMmaRows * kRawRow, kAStage = T::kAStage;
   constexpr int kTmemCols = 2 * T::kRegion;  // two regions: steps s and s + 1
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wi = tid - 32;  // worker index (warp 0: negative)
   const int kb_steps = a.cols / 32;
   const int nab = a.cols / T::kBL;                              // activation blocks per row
   uint8_t* bop = smem;                                          // activations: kb_steps x 512 B
   uint8_t* aop = bop + (size_t)kb_steps * (kMmaN * 32);         // 2 A buffers
   uint8_t* raw = aop + 2 * kAStage;                             // 2 x 128 rows x kRawRow B
-  float* dsa = reinterpret_cast<float*>(raw + 2 * kRawStageT);  // d_a [16][nab]
+  float* dsa = reinterpret_cast<float*>(raw + 2 * kRawStage);   // d_a [16][nab]
   float* dws = dsa + kMmaN * nab;                               // d_w [kSlots][kDw][128]
   uint32_t* scs = reinterpret_cast<uint32_t*>(dws + kSlots * kMmaRows * T::kDw);  // Q6_K sc [kSlots][128][4 words]
   uint64_t* bar = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(scs + kSlots * kMmaRows * T::kScWords) + 7) & ~uintptr_t(7));
-  uint64_t* ready = bar;     // [2] workers -> warp 0: A buffer s & 1 holds step s
-  uint64_t* done = bar + 2;  // [2] MMAs of step s completed (tcgen05.commit)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 4);
+  uint64_t* full = bar;       // [2] raw buffer s & 1 holds step s (bulk copies)
+  uint64_t* ready = bar + 2;  // [2] every worker warp has unpacked step s (and summed step s - 2)
+  uint64_t* done = bar + 4;   // [2] MMAs of step s completed (tcgen05.commit)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 6);
   int* s_fail = reinterpret_cast<int*>(tmem_holder + 1);
-  int* s_last = s_fail + 1;  // the last step whose MMAs were issued
+  int* s_last = s_fail + 1;    // the last step whose MMAs were issued
+  int* s_staged = s_fail + 2;  // the last step whose copies were issued
 
   const int my_tiles = (a.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nsteps = my_tiles * a.nblk;
   const int64_t last16 = a.total & ~int64_t(15);
 
-  // workers stage the raw bytes of step s into buffer s & 1 (one cp.async
-  // group per call, empty past the last step); worker wi's chunks
-  // i = wi + k * workers of a stage are (row i / 15, chunk i % 15)
-  constexpr int kChunksPerThread = (kMmaRows * kRawChunksT + kWorkers - 1) / kWorkers;
-  int crr[kChunksPerThread], ccc[kChunksPerThread];
+  // warp 0 stages step s into raw buffer s & 1: row rr of the tile at
+  // rr * kRawRow, the step's bytes from their 16-byte boundary on. With a
+  // tensor map (the weights as rows of 8-byte elements, row_bytes apart) one
+  // copy moves the 128 x kRawRow box (rows past the matrix and bytes past a
+  // row read as zeros); otherwise one bulk copy per row, and a row whose copy
+  // would pass the weights' last whole 16 bytes goes by plain loads before
+  // the arrival.
+  auto stage = [&](int s) {
+    if (s >= nsteps) return;
+    const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
+    const int kb = s % a.nblk;
+    uint8_t* dst = raw + (size_t)(s & 1) * kRawStage;
+    if (a.tiled) {
+      if (lane == 0) {
+        const int x = ((kb * T::kStepBytes) >> 4) * 2;
+        mbar_arrive_expect_tx(&full[s & 1], kRawStage);
+        tma_load_2d(dst, &wmap, x, t * kMmaRows, &full[s & 1]);
+        *s_staged = s;
+      }
+      return;
+    }
+    int64_t g[4];
+    uint32_t bytes = 0;
+    unsigned bulk = 0;
 #pragma unroll
-  for (int k = 0; k < kChunksPerThread; ++k) {
-    const int i = wi + k * kWorkers;
-    crr[k] = (wi >= 0 && i < kMmaRows * kRawChunksT) ? i / kRawChunksT : kMmaRows;
-    ccc[k] = (i >= 0) ? i % kRawChunksT : 0;
-  }
-  auto stage_raw = [&](int s) {
-    if (s < nsteps) {
-      const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
-      const int kb = s % a.nblk;
-      uint8_t* dst = raw + (size_t)(s & 1) * kRawStageT;
-#pragma unroll
-      for (int k = 0; k < kChunksPerThread; ++k) {
-        const int rr = crr[k], c = ccc[k];
-        if (rr >= kMmaRows) continue;
-        const int r = t * kMmaRows + rr;
-        if (r >= a.rows) continue;
-        const int64_t g = ((int64_t)r * a.row_bytes + (int64_t)kb * T::kStepBytes) & ~int64_t(15);
-        const int64_t src = g + 16 * c;
-        uint8_t* d = dst + rr * kRawRowT + 16 * c;
-        if (src + 16 <= last16) {
-          cp_async16(d, a.w + src);
-        } else {
-          for (int e = 0; e < 16; ++e) d[e] = (src + e < a.total) ? a.w[src + e] : 0;
-        }
+    for (int k = 0; k < 4; ++k) {
+      const int rr = lane + 32 * k;
+      const int r = t * kMmaRows + rr;
+      g[k] = ((int64_t)r * a.row_bytes + (int64_t)kb * T::kStepBytes) & ~int64_t(15);
+      if (r >= a.rows) continue;
+      if (g[k] + kRawRow <= last16) {
+        bulk |= 1u << k;
+        bytes += kRawRow;
+      } else {
+        uint8_t* d = dst + rr * kRawRow;
+        for (int e = 0; e < kRawRow; ++e) d[e] = (g[k] + e < a.total) ? a.w[g[k] + e] : 0;
       }
     }
-    cp_async_commit();
+    bytes = __reduce_add_sync(0xffffffffu, bytes);
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&full[s & 1], bytes);
+      *s_staged = s;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (bulk & (1u << k)) bulk_copy_g2s(dst + (lane + 32 * k) * kRawRow, a.w + g[k], kRawRow, &full[s & 1]);
   };
-  auto worker_sync = [](int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kWorkers) : "memory"); };
 
   if (tid == 0) {
-    for (int k = 0; k < 4; ++k) mbar_init(&bar[k], 1);
+    for (int k = 0; k < 6; ++k) mbar_init(&bar[k], (k == 2 || k == 3) ? kWorkers / 32 : 1);
     *s_fail = 0;
     *s_last = -1;
+    *s_staged = -1;
     fence_mbar_init();
   }
-  if (wi >= 0) {
-    stage_raw(0);
-    stage_raw(1);
-  }
-  // zeros: the activation rows nb .. 15 and both A buffers (their zero blocks
-  // stay zero)
+  // zeros: the activation rows nb .. 15 and both A buffers (Q6_K's zero
+  // blocks stay zero)
   for (int i = tid; i < (kb_steps * (kMmaN * 32) + 2 * kAStage) / 16; i += kMmaThreads)
     reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
+  if (warp == 0) {
+    stage(0);
+    stage(1);
+  }
   // quantizeAct (quant.nim:646-662) with the type's blocks (256 values for
-  // Q6_K, 32 for Q8_0): each thread takes 32 consecutive values, the G
+  // Q6_K, 32 for the others): each thread takes 32 consecutive values, the G
   // threads of a block (consecutive lanes) combine their maxima by shuffles
   {
     constexpr int G = T::kBL / 32;
@@ -326,14 +422,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
   };
 
   if (warp == 0) {
-    // the MMA issuer: step s once its operands are ready
-    if (lane == 0) {
-      for (int s = 0; s < nsteps; ++s) {
-        if (!wait_bar(ready, s)) {
-          fail = true;
-          break;
-        }
-        if (*s_fail) break;
+    // staging two steps ahead, and the MMAs of step s once every worker warp
+    // has unpacked it (which also frees raw buffer s & 1 for step s + 2)
+    for (int s = 0; s < nsteps; ++s) {
+      bool ok = true;
+      if (lane == 0) ok = wait_bar(ready, s) && !*s_fail;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        fail = true;
+        break;
+      }
+      stage(s + 2);
+      if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int kb = s % a.nblk;
         const uint32_t ab = smem_u32(aop) + (uint32_t)((s & 1) * kAStage);
@@ -357,161 +457,176 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
                      : "memory");
         *s_last = s;
       }
-      if (fail) *s_fail = 1;
+      __syncwarp();
     }
-    __syncwarp();
   } else {
     // workers
-    const int ur = wi >> 2, uh = (wi >> 1) & 1, uhalf = wi & 1;  // unpack unit
+    const int ww = warp - 1;
     // sums: weight row em of the tile (TMEM lane quarter warp % 4), batch
     // rows eb0 .. eb0+3
-    const int em = 32 * (warp & 3) + lane, eb0 = 4 * ((warp - 1) >> 2);
+    const int em = 32 * (warp & 3) + lane, eb0 = 4 * (ww >> 2);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int s = 0; s <= nsteps; ++s) {
       if (s < nsteps) {
-        cp_async_wait<1>();  // this thread's copies of step s (step s + 1's may be in flight)
-        worker_sync(1);      // everyone's
-        // A buffer s & 1 was last read by the MMAs of step s - 2
-        if (s >= 2 && !fail && !wait_bar(done, s - 2)) fail = true;
+        // the step's bytes have landed; A buffer s & 1 was last read by the
+        // MMAs of step s - 2
+        bool ok = wait_bar(full, s);
+        if (ok && s >= 2) ok = wait_bar(done, s - 2);
+        if (__any_sync(0xffffffffu, !ok)) {
+          fail = true;
+          break;
+        }
         const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
         const int kb = s % a.nblk;
-        if constexpr (WT == 14) {
-        const int r = t * kMmaRows + ur;
-        const int64_t g = (int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes;
-        const uint8_t* blk = raw + (size_t)(s & 1) * kRawStageT + ur * kRawRowT + (int)(g & 15);
-        uint32_t QA[4], QB[4], QH[4];
-        ld16s(blk + 64 * uh + 16 * uhalf, QA);
-        ld16s(blk + 64 * uh + 32 + 16 * uhalf, QB);
-        ld16s(blk + 128 + 32 * uh + 16 * uhalf, QH);
-        if (uh == 0 && uhalf == 0) {
-          // this row's sub-block scales and d for the sums (rows past the
-          // matrix: zeros)
-          uint32_t sc4[4];
-          ld16s(blk + 192, sc4);
-          const bool in = r < a.rows;
-          uint32_t* sd = scs + ((size_t)(s % kSlots) * kMmaRows + ur) * 4;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) sd[k] = in ? sc4[k] : 0u;
-          const uint32_t dwb = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
-          dws[(s % kSlots) * kMmaRows + ur] = in ? __half2float(__ushort_as_half((unsigned short)dwb)) : 0.0f;
-        }
-        // the four sub-blocks j = 8h + 2c + half of this quarter (dotQ6K's
-        // q1..q4, quant.nim:744-747): the 6-bit value q, then q - 32 as int8
-        // (q ^ 32 is q - 32 for q >= 32 and q + 32 below; those get bits 6, 7)
+        const uint8_t* rs = raw + (size_t)(s & 1) * kRawStage;
         uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
+        if constexpr (WT == 14) {
+          const int wi = tid - 32;
+          const int ur = wi >> 2, uh = (wi >> 1) & 1, uhalf = wi & 1;  // (row, quarter)
+          const int r = t * kMmaRows + ur;
+          const int64_t g = (int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes;
+          const uint8_t* blk = rs + ur * kRawRow + (int)(g & 15);
+          uint32_t QA[4], QB[4], QH[4];
+          ld16s(blk + 64 * uh + 16 * uhalf, QA);
+          ld16s(blk + 64 * uh + 32 + 16 * uhalf, QB);
+          ld16s(blk + 128 + 32 * uh + 16 * uhalf, QH);
+          if (uh == 0 && uhalf == 0) {
+            // this row's sub-block scales and d for the sums (rows past the
+            // matrix: zeros)
+            uint32_t sc4[4];
+            ld16s(blk + 192, sc4);
+            const bool in = r < a.rows;
+            uint32_t* sd = scs + ((size_t)(s % kSlots) * kMmaRows + ur) * 4;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t lo4 = ((c & 1) ? QB[k] : QA[k]) >> ((c & 2) ? 4 : 0);
-            const uint32_t q6 = (lo4 & 0x0F0F0F0Fu) | (((QH[k] >> (2 * c)) << 4) & 0x30303030u);
-            const uint32_t t6 = q6 ^ 0x20202020u;
-            const uint32_t m = t6 & 0x20202020u;
-            v[k] = t6 | (m << 1) | (m << 2);
+            for (int k = 0; k < 4; ++k) sd[k] = in ? sc4[k] : 0u;
+            const uint32_t dwb = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
+            dws[(s % kSlots) * kMmaRows + ur] = in ? __half2float(__ushort_as_half((unsigned short)dwb)) : 0.0f;
           }
-          *reinterpret_cast<uint4*>(ab + a_off(ur, 8 * uh + 2 * c + uhalf)) = make_uint4(v[0], v[1], v[2], v[3]);
-        }
+          // the four sub-blocks j = 8h + 2c + half of this quarter (dotQ6K's
+          // q1..q4, quant.nim:744-747): the 6-bit value q, then q - 32 as int8
+          // (q ^ 32 is q - 32 for q >= 32 and q + 32 below; those get bits 6, 7)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t lo4 = ((c & 1) ? QB[k] : QA[k]) >> ((c & 2) ? 4 : 0);
+              const uint32_t q6 = (lo4 & 0x0F0F0F0Fu) | (((QH[k] >> (2 * c)) << 4) & 0x30303030u);
+              const uint32_t t6 = q6 ^ 0x20202020u;
+              const uint32_t m = t6 & 0x20202020u;
+              v[k] = t6 | (m << 1) | (m << 2);
+            }
+            *reinterpret_cast<uint4*>(ab + a_off(ur, 8 * uh + 2 * c + uhalf)) = make_uint4(v[0], v[1], v[2], v[3]);
+          }
         } else {
-          // Q8_0 / Q4_0: four (row, block, half) units per worker, 32
-          // consecutive rows per warp; half h of block j is values
-          // 16h .. 16h+15, which go to the block's K step as int8: Q8_0's as
-          // they are, Q4_0's nibbles (low ones for h = 0, high ones for
-          // h = 1; dotQ4_0i quant.nim:774-786) minus 8 (q ^ 8 is q - 8 for
-          // q >= 8 and q + 8 below; those get bits 4-7). The half h = 0 also
-          // records d (rows past the matrix: zero).
-          const uint8_t* rs = raw + (size_t)(s & 1) * kRawStageT;
-          uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
+          // Q8_0 / Q4_0: a thread takes blocks 2q, 2q + 1 of row rr (q
+          // uniform across the warp, 32 consecutive rows per warp, so its
+          // 16-byte loads and stores are free of bank conflicts); block j
+          // goes to K step j, values 0-15 then 16-31, as int8
+          const int q = ww & 3, rr = 32 * (ww >> 2) + lane;
+          const bool in = t * kMmaRows + rr < a.rows;
+          float* dslot = dws + (size_t)(s % kSlots) * 8 * kMmaRows;
+          if constexpr (WT == 8) {
+            const uint4* src = reinterpret_cast<const uint4*>(rs + rr * kRawRow + 64 * q);
+            uint32_t W[20];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int u = wi + k * kWorkers;
-            const int rr = u & (kMmaRows - 1), jh = u >> 7, j = jh >> 1, h = jh & 1;
-            const uint8_t* blk = rs + rr * kRawRowT + T::kBlockBytes * j;
-            uint32_t q[4];
-            if constexpr (WT == 8) {
-              ld16s(blk + 2 + 16 * h, q);
-            } else {
-              ld16s(blk + 2, q);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t v = (q[e] >> (4 * h)) & 0x0F0F0F0Fu;
-                const uint32_t t = v ^ 0x08080808u;
-                const uint32_t m = ~v & 0x08080808u;
-                q[e] = t | (m << 1) | (m << 2) | (m << 3) | (m << 4);
-              }
+            for (int k = 0; k < 5; ++k) {
+              const uint4 c4 = src[k];
+              W[4 * k] = c4.x;
+              W[4 * k + 1] = c4.y;
+              W[4 * k + 2] = c4.z;
+              W[4 * k + 3] = c4.w;
             }
-            *reinterpret_cast<uint4*>(ab + 4096 * j + 2048 * h + 16 * rr) = make_uint4(q[0], q[1], q[2], q[3]);
-            if (h == 0) {
-              const uint32_t dwb = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8);
-              dws[((s % kSlots) * 8 + j) * kMmaRows + rr] =
-                  (t * kMmaRows + rr < a.rows) ? __half2float(__ushort_as_half((unsigned short)dwb)) : 0.0f;
+            switch (q) {
+              case 0: q8_units<0>(W, ab, dslot, rr, in); break;
+              case 1: q8_units<1>(W, ab, dslot, rr, in); break;
+              case 2: q8_units<2>(W, ab, dslot, rr, in); break;
+              default: q8_units<3>(W, ab, dslot, rr, in); break;
+            }
+          } else {
+            const uint4* src = reinterpret_cast<const uint4*>(rs + rr * kRawRow + 32 * q);
+            uint32_t W[12];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+              const uint4 c4 = src[k];
+              W[4 * k] = c4.x;
+              W[4 * k + 1] = c4.y;
+              W[4 * k + 2] = c4.z;
+              W[4 * k + 3] = c4.w;
+            }
+            switch (q) {
+              case 0: q4_units<0>(W, ab, dslot, rr, in); break;
+              case 1: q4_units<1>(W, ab, dslot, rr, in); break;
+              case 2: q4_units<2>(W, ab, dslot, rr, in); break;
+              default: q4_units<3>(W, ab, dslot, rr, in); break;
             }
           }
         }
+        // this warp's operands, and its reads of the TMEM region that step
+        // s's MMAs overwrite (the sums of step s - 2), come before the arrival
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s & 1]);
       }
-      if (fail) *s_fail = 1;
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      worker_sync(2);
-      if (*s_fail) break;  // (the same in every worker after the barrier)
-      if (s < nsteps && wi == 0) mbar_arrive(&ready[s & 1]);
-      // the raw bytes of step s are unpacked: stage step s + 2 in their place
-      stage_raw(s + 2);
       // the previous step's sums for this warp's rows and batch rows
       if (s >= 1) {
-        if (!fail && !wait_bar(done, s - 1)) fail = true;
-        fail = __any_sync(0xffffffffu, fail);  // (tcgen05.ld is warp-wide; a failure
-                                               // stops every worker at the next barrier)
-      }
-      if (s >= 1 && !fail) {
+        const bool ok = wait_bar(done, s - 1);
+        if (__any_sync(0xffffffffu, !ok)) {  // (tcgen05.ld is warp-wide)
+          fail = true;
+          break;
+        }
         const int p = s - 1;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int kb = p % a.nblk;
         const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * T::kRegion + eb0);
         if constexpr (WT == 14) {
-        const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
-        uint32_t scw[4];
+          const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
+          uint32_t scw[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) scw[k] = sd[k];
-        int sumi[4] = {0, 0, 0, 0};
+          for (int k = 0; k < 4; ++k) scw[k] = sd[k];
+          int sumi[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int j0 = 0; j0 < 16; j0 += 4) {
-          uint32_t d[4][4];
+          for (int j0 = 0; j0 < 16; j0 += 4) {
+            uint32_t d[4][4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) tmem_ld4(ta + 16 * (j0 + u), d[u]);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int u = 0; u < 4; ++u) tmem_ld4(ta + 16 * (j0 + u), d[u]);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = j0 + u;
-            const int sc = (int)(int8_t)(scw[j >> 2] >> (8 * (j & 3)));
+            for (int u = 0; u < 4; ++u) {
+              const int j = j0 + u;
+              const int sc = (int)(int8_t)(scw[j >> 2] >> (8 * (j & 3)));
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sumi[e] += sc * (int)d[u][e];
+              for (int e = 0; e < 4; ++e) sumi[e] += sc * (int)d[u][e];
+            }
           }
-        }
-        const float dw = dws[(p % kSlots) * kMmaRows + em];
+          const float dw = dws[(p % kSlots) * kMmaRows + em];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int b = eb0 + e;
-          if (b < a.nb)
-            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * nab + kb], dw), __int2float_rn(sumi[e])));
-        }
+          for (int e = 0; e < 4; ++e) {
+            const int b = eb0 + e;
+            if (b < a.nb)
+              acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * nab + kb], dw), __int2float_rn(sumi[e])));
+          }
         } else {
           // dotQ8_0i / dotQ4_0i (quant.nim:762-786): block after block,
           // acc += (d_w * d_a) * float(s)
           uint32_t d[8][4];
 #pragma unroll
           for (int i = 0; i < 8; ++i) tmem_ld4(ta + 16 * i, d[i]);
+          float dw[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dw[i] = dws[((p % kSlots) * 8 + i) * kMmaRows + em];
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float dw = dws[((p % kSlots) * 8 + i) * kMmaRows + em];
+          for (int e = 0; e < 4; ++e) {
+            const int b = eb0 + e;
+            if (b >= a.nb) break;
+            const float4* dp = reinterpret_cast<const float4*>(dsa + b * nab + kb * 8);
+            const float4 da0 = dp[0], da1 = dp[1];
+            const float da[8] = {da0.x, da0.y, da0.z, da0.w, da1.x, da1.y, da1.z, da1.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int b = eb0 + e;
-              if (b < a.nb)
-                acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw, dsa[b * nab + kb * 8 + i]),
-                                                     __int2float_rn((int)d[i][e])));
-            }
+            for (int i = 0; i < 8; ++i)
+              acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[i], da[i]), __int2float_rn((int)d[i][e])));
           }
         }
         if (kb == a.nblk - 1) {
@@ -527,16 +642,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       }
     }
-    cp_async_wait<0>();  // no copy lands after the CTA ends
   }
   if (fail) *s_fail = 1;
   __syncthreads();
   if (*s_fail) {  // (uniform after the barrier)
     if (tid == 0) {
       atomicCAS(a.status, 0, NLS_ERR_TIMEOUT);
-      // let the last committed MMAs finish before the columns are released
-      // (bounded)
-      const int last = *s_last;
+      // let the copies and MMAs in flight finish before the shared memory and
+      // the columns are released (bounded)
+      const int st = *s_staged, last = *s_last;
+      if (st >= 0) (void)wait_bar(full, st);
+      if (st >= 1) (void)wait_bar(full, st - 1);
       if (last >= 0) (void)wait_bar(done, last);
       if (last >= 1) (void)wait_bar(done, last - 1);
     }
@@ -560,10 +676,49 @@ bool lm_head_mma_path(int wtype, int cols, int nb) {
          cols >= 256 && lm_head_mma_smem(wtype, cols) <= (size_t)(227 * 1024);
 }
 
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// the driver's tensor-map encoder (through the runtime, so the library needs
+// no link to the driver library); null if the driver has none
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+}  // namespace
+
 cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols, const float* x,
                                int nb, float* y, int64_t ldy, int* status, int sm_count,
                                unsigned long long wait_ns, cudaStream_t st) {
   if (wtype != 14 && wtype != 8 && wtype != 2) return cudaErrorInvalidValue;
+  const int raw_row = (wtype == 14) ? MmaType<14>::kRawRow : (wtype == 8) ? MmaType<8>::kRawRow : MmaType<2>::kRawRow;
+  // the weights as a 2-D tensor of 8-byte elements: row_bytes / 8 per row,
+  // rows rows, row_bytes apart; a box of 128 rows x one staged step
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  int tiled = 0;
+  if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+    if (EncodeTiledFn enc = encode_tiled()) {
+      const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows};
+      const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+      const cuuint32_t box[2] = {(cuuint32_t)(raw_row / 8), (cuuint32_t)kMmaRows};
+      const cuuint32_t estr[2] = {1, 1};
+      tiled = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+  }
   MmaArgs a{};
   a.w = w;
   a.row_bytes = row_bytes;
@@ -575,6 +730,7 @@ cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, i
   a.ntiles = (rows + kMmaRows - 1) / kMmaRows;
   a.wait_ns = wait_ns;
   a.status = status;
+  a.tiled = tiled;
   const size_t smem = lm_head_mma_smem(wtype, cols);
   auto kern = (wtype == 14) ? lmh_mma_kernel<14> : (wtype == 8) ? lmh_mma_kernel<8> : lmh_mma_kernel<2>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -584,7 +740,7 @@ cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, i
     a.nb = std::min(kMmaN, nb - b0);
     a.x = x + (size_t)b0 * cols;
     a.y = y + (size_t)b0 * ldy;
-    kern<<<grid, kMmaThreads, smem, st>>>(a);
+    kern<<<grid, kMmaThreads, smem, st>>>(a, map);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
