@@ -439,17 +439,24 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
         const uint32_t ab = smem_u32(aop) + (uint32_t)((s & 1) * kAStage);
         const uint32_t bb = smem_u32(bop) + (uint32_t)(kb * 8) * (kMmaN * 32);
         const uint32_t dreg = tbase + (uint32_t)((s & 1) * T::kRegion);
+        // descriptors of K step i: the first's with the start address (bits
+        // 0-13, in 16-byte units) and leading-byte offset (bits 16-29)
+        // advanced; no field overflows (shared addresses are below 256 KB)
+        const uint64_t db0 = smem_desc(bb, 128, 256);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const uint64_t db = smem_desc(bb + (uint32_t)i * (kMmaN * 32), 128, 256);
+          const uint64_t db = db0 + (uint64_t)(i * (kMmaN * 32) / 16);
           if constexpr (WT == 14) {
             // even sub-block 2i: its values, then the zeros; odd 2i + 1: the
             // zeros, then its values
-            mma_i8(dreg + 32 * i, smem_desc(ab + kAEven + 2048 * i, kAZero - kAEven - 2048 * i, 128), db);
-            mma_i8(dreg + 32 * i + 16, smem_desc(ab + kAZero, kAOdd - kAZero + 2048 * i, 128), db);
+            const uint64_t de0 = smem_desc(ab + kAEven, kAZero - kAEven, 128);
+            const uint64_t do0 = smem_desc(ab + kAZero, kAOdd - kAZero, 128);
+            mma_i8(dreg + 32 * i, de0 + (uint64_t)(2048 * i / 16) - ((uint64_t)(2048 * i / 16) << 16), db);
+            mma_i8(dreg + 32 * i + 16, do0 + ((uint64_t)(2048 * i / 16) << 16), db);
           } else {
             // block i: its first 16 values of every row, then its second 16
-            mma_i8(dreg + 16 * i, smem_desc(ab + 4096 * i, 2048, 128), db);
+            const uint64_t da0 = smem_desc(ab, 2048, 128);
+            mma_i8(dreg + 16 * i, da0 + (uint64_t)(4096 * i / 16), db);
           }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
