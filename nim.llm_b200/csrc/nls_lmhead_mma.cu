@@ -18,33 +18,33 @@
 // order, on the CUDA cores. (Q8_0 takes the int8 path at more than 4 batch
 // rows only when the rows are separate sequences, model.nim:185.)
 //
-// One CTA of 544 threads per SM, persistent over tiles of 128 weight rows,
-// warp-specialised. A step covers 256 values of every row of the tile (one
-// Q6_K block, eight Q8_0 or Q4_0 blocks). Per (tile, step):
-//  * the 16 worker warps copy a part of the tile's raw bytes two steps
-//    ahead into shared memory (16-byte cp.async; the bytes past the weights'
-//    last whole 16 go by plain loads);
-//  * the workers lay the step's weights out as the A operand of its parity
+// One CTA per SM, persistent over tiles of 128 weight rows, warp-specialised
+// (warp 0; kUnpackWarps unpackers; kSumWarps summers). A step covers 256
+// values of every row of the tile (one Q6_K block, eight Q8_0 or Q4_0
+// blocks). Per (tile, step):
+//  * warp 0 stages the tile's bytes of the step two steps ahead into shared
+//    memory: one tensor-map copy of a 128-row box (the weights seen as rows
+//    of 8-byte elements), or, where a row is not a multiple of 16 bytes, one
+//    bulk copy per row;
+//  * the unpackers lay the step's weights out as the A operand of its parity
 //    (one of two buffers; no-swizzle K-major layout, 8-row x 16-byte core
-//    matrices). Q6_K: each worker unpacks one (row, quarter) of the block --
-//    four sub-blocks of 16 values, q - 32 as int8 -- even sub-blocks as the
-//    first 16 values of a 32-value K step, odd ones as the second, and the
-//    other half of both is one shared block of zeros that the descriptors
-//    point at. Q8_0 / Q4_0: each worker lays out four (row, block, half)
-//    units of 16 int8 values (Q4_0: nibbles minus 8), one K step per block,
-//    and records the blocks' d;
+//    matrices) and record the scales. Q6_K: a thread unpacks (row, quarter)
+//    units of the block -- four sub-blocks of 16 values, q - 32 as int8 --
+//    even sub-blocks as the first 16 values of a 32-value K step, odd ones
+//    as the second, and the other half of both is one shared block of zeros
+//    that the descriptors point at. Q8_0 / Q4_0: a thread lays out two
+//    blocks of a row, 16 int8 values per half (Q4_0: nibbles minus 8), one
+//    K step per block;
 //  * warp 0 issues the step's MMAs (M = 128 rows, N = 16 batch rows, K = 32;
-//    16 for Q6_K, sub-block j into TMEM columns 16j .. 16j+15, 8 for the others,
-//    block i into columns 16i ..) into one of two regions and commits them to
-//    an mbarrier, while the workers go on with the next step (operands and
-//    TMEM double-buffered);
-//  * every worker warp reads, for the 32 weight rows of its TMEM lane
-//    quarter (warp % 4) and 4 of the 16 batch rows, the previous step's sums
-//    and forms the fp32 terms in block order.
-// Workers synchronise among themselves with named barriers and with warp 0
-// through mbarriers. The activations are quantized once per CTA into shared
-// memory in the operand layout (batch rows past nb are zeros). Every wait is
-// bounded.
+//    16 for Q6_K, sub-block j into TMEM columns 16j .. 16j+15, 8 for the
+//    others, block i into columns 16i ..) into one of two regions and
+//    commits them to an mbarrier;
+//  * the summers read, for the 32 weight rows of their TMEM lane quarter
+//    (warp % 4) and a share of the 16 batch rows, the step's sums and form
+//    the fp32 terms in block order, while the unpackers work on later steps.
+// All hand-offs are mbarriers (staging -> unpackers -> warp 0 -> summers ->
+// warp 0), every wait bounded. The activations are quantized once per CTA
+// into shared memory in the operand layout (batch rows past nb are zeros).
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -58,18 +58,16 @@ namespace nls {
 
 namespace {
 
-constexpr int kWorkers = 512;    // warps 1-16: unpacking, sums
-constexpr int kMmaThreads = 32 + kWorkers;  // warp 0: staging, the MMA issuer
 constexpr int kMmaRows = 128;    // weight rows per tile (MMA M)
 constexpr int kMmaN = 16;        // batch rows per launch (MMA N)
 constexpr int kQ6Bytes = 210;    // a Q6_K block
 // Q6_K's A buffer: even sub-blocks [0, 16 KB), a 2 KB block of zeros, odd
 // ones [18 KB, 34 KB); K step i of a parity at + 2 KB * i, row r at + 16 r
 constexpr int kAEven = 0, kAZero = 16384, kAOdd = 18432;
-// per-step scales: written by a step's unpack, read by its sums; the worker
-// warps run up to three steps apart (a warp unpacks step s only once every
-// warp has unpacked step s - 2, and a warp that has may still be summing
-// step s - 3)
+// per-step scales: written by a step's unpack, read by its sums; the
+// unpackers run up to three steps ahead of the summers (step s is unpacked
+// once the MMAs of step s - 2 have completed, which were issued once the
+// sums of step s - 4 had read their TMEM region)
 constexpr int kSlots = 4;
 
 // offset of the 16 values of row r, sub-block j inside a Q6_K A buffer
@@ -104,11 +102,19 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db
       : "memory");
 }
 
-// four consecutive TMEM columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
+// N (4 or 8) consecutive TMEM columns of this warp's 32 lanes
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  } else {
+    static_assert(N == 8, "4 or 8 columns");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  }
 }
 
 // 16 bytes at a 2-byte aligned shared address, as four words (reads the
@@ -160,6 +166,7 @@ struct MmaType<14> {                 // Q6_K: one 210-byte block per step
   static constexpr int kScWords = 4; // sub-block scales per row and step
   static constexpr int kRegion = 256;  // TMEM columns per step: 16 sub-blocks x 16
   static constexpr int kAStage = 34816;
+  static constexpr int kUnpackWarps = 8, kSumWarps = 8;  // (measured: above 4 + 8, 4 + 16, 8 + 16)
 };
 template <>
 struct MmaType<8> {                  // Q8_0: eight 34-byte blocks per step
@@ -170,6 +177,7 @@ struct MmaType<8> {                  // Q8_0: eight 34-byte blocks per step
   static constexpr int kScWords = 0;
   static constexpr int kRegion = 128;  // 8 blocks x 16
   static constexpr int kAStage = 32768;  // block i: [its first 16 values of every row][its second 16]
+  static constexpr int kUnpackWarps = 4, kSumWarps = 8;  // (measured: 4 + 8 above 8 + 8, 4 + 16, 8 + 16)
 };
 template <>
 struct MmaType<2> {                  // Q4_0: eight 18-byte blocks per step
@@ -180,6 +188,7 @@ struct MmaType<2> {                  // Q4_0: eight 18-byte blocks per step
   static constexpr int kScWords = 0;
   static constexpr int kRegion = 128;
   static constexpr int kAStage = 32768;
+  static constexpr int kUnpackWarps = 4, kSumWarps = 8;
 };
 
 template <int WT>
@@ -187,7 +196,7 @@ __host__ __device__ constexpr size_t mma_smem(int cols) {
   using T = MmaType<WT>;
   return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)T::kAStage + 2 * (size_t)kMmaRows * T::kRawRow +
          (size_t)kMmaN * (cols / T::kBL) * 4 + (size_t)kSlots * kMmaRows * T::kDw * 4 +
-         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 6 * 8 + 16 + 16;
+         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 10 * 8 + 16 + 16;
 }
 
 // Q8_0: one thread lays out blocks 2Q and 2Q + 1 of a row from the 80 bytes
@@ -210,13 +219,9 @@ __device__ __forceinline__ void q8_units(const uint32_t (&W)[20], uint8_t* ab, f
   dslot[(2 * Q + 1) * kMmaRows + rr] = in ? d1 : 0.0f;
 }
 
-// q - 8 as int8 for four packed nibbles q (q ^ 8 is q - 8 for q >= 8 and
-// q + 8 below; those get bits 4-7)
-__device__ __forceinline__ uint32_t nib_minus8(uint32_t v) {
-  const uint32_t t = v ^ 0x08080808u;
-  const uint32_t m = ~v & 0x08080808u;
-  return t | (m << 1) | (m << 2) | (m << 3) | (m << 4);
-}
+// q - 8 as int8 for four packed nibbles q (q + 120 stays below 256 in every
+// byte; its bit 7 flipped is q - 8 in two's complement)
+__device__ __forceinline__ uint32_t nib_minus8(uint32_t v) { return (v + 0x78787878u) ^ 0x80808080u; }
 
 // Q4_0 (dotQ4_0i quant.nim:774-786: values 0-15 of a block are the low
 // nibbles of its 16 bytes, values 16-31 the high ones): blocks 2Q and 2Q + 1
@@ -252,10 +257,19 @@ __device__ __forceinline__ void q4_units(const uint32_t (&W)[12], uint8_t* ab, f
 }
 
 template <int WT>
-__global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a,
+__global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<WT>::kSumWarps), 1)
+    lmh_mma_kernel(const MmaArgs a,
                                                                 const __grid_constant__ CUtensorMap wmap) {
   using T = MmaType<WT>;
   constexpr int kRawRow = T::kRawRow, kRawStage = kMmaRows * kRawRow, kAStage = T::kAStage;
+  // warp 0: staging and the MMAs; warps 1 .. kUnpackWarps: the A operands
+  // and scales of a step; the rest: the fp32 sums from TMEM
+  constexpr int kUnpackWarps = T::kUnpackWarps, kSumWarps = T::kSumWarps;
+  constexpr int kMmaThreads = 32 * (1 + kUnpackWarps + kSumWarps);
+  constexpr int kUnpackParts = 16 / kUnpackWarps;  // (row, quarter) units per unpacker thread
+  constexpr int EB = 16 / (kSumWarps / 4);          // batch rows per summer thread
+  static_assert(kUnpackWarps % 4 == 0 && 16 % kUnpackWarps == 0 && kSumWarps % 4 == 0 && 16 % (kSumWarps / 4) == 0,
+                "role split");
   constexpr int kTmemCols = 2 * T::kRegion;  // two regions: steps s and s + 1
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -270,9 +284,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
   uint64_t* bar = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(scs + kSlots * kMmaRows * T::kScWords) + 7) & ~uintptr_t(7));
   uint64_t* full = bar;       // [2] raw buffer s & 1 holds step s (bulk copies)
-  uint64_t* ready = bar + 2;  // [2] every worker warp has unpacked step s (and summed step s - 2)
-  uint64_t* done = bar + 4;   // [2] MMAs of step s completed (tcgen05.commit)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 6);
+  uint64_t* ready = bar + 2;  // [4] every unpacker has laid out step s (slot s % 4)
+  uint64_t* done = bar + 6;   // [2] MMAs of step s completed (tcgen05.commit)
+  uint64_t* tfree = bar + 8;  // [2] every summer has read TMEM region s & 1 for step s
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
   int* s_fail = reinterpret_cast<int*>(tmem_holder + 1);
   int* s_last = s_fail + 1;    // the last step whose MMAs were issued
   int* s_staged = s_fail + 2;  // the last step whose copies were issued
@@ -333,7 +348,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
   };
 
   if (tid == 0) {
-    for (int k = 0; k < 6; ++k) mbar_init(&bar[k], (k == 2 || k == 3) ? kWorkers / 32 : 1);
+    for (int k = 0; k < 10; ++k)
+      mbar_init(&bar[k], (k >= 2 && k < 6) ? kUnpackWarps : (k >= 8) ? kSumWarps : 1);
     *s_fail = 0;
     *s_last = -1;
     *s_staged = -1;
@@ -420,13 +436,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
   auto wait_bar = [&](uint64_t* b2, int s) -> bool {  // barrier b2[s & 1] completed for step s
     return mbar_wait_bounded(&b2[s & 1], (uint32_t)((s >> 1) & 1), a.wait_ns);
   };
+  auto wait4 = [&](uint64_t* b4, int s) -> bool {  // barrier b4[s % 4] completed for step s
+    return mbar_wait_bounded(&b4[s & 3], (uint32_t)((s >> 2) & 1), a.wait_ns);
+  };
 
   if (warp == 0) {
-    // staging two steps ahead, and the MMAs of step s once every worker warp
-    // has unpacked it (which also frees raw buffer s & 1 for step s + 2)
+    // staging two steps ahead, and the MMAs of step s once every unpacker
+    // has laid it out (which also frees raw buffer s & 1 for step s + 2) and
+    // the sums of step s - 2 have read TMEM region s & 1
     for (int s = 0; s < nsteps; ++s) {
       bool ok = true;
-      if (lane == 0) ok = wait_bar(ready, s) && !*s_fail;
+      if (lane == 0) ok = wait4(ready, s) && (s < 2 || wait_bar(tfree, s - 2)) && !*s_fail;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         fail = true;
@@ -466,29 +486,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
       }
       __syncwarp();
     }
-  } else {
-    // workers
-    const int ww = warp - 1;
-    // sums: weight row em of the tile (TMEM lane quarter warp % 4), batch
-    // rows eb0 .. eb0+3
-    const int em = 32 * (warp & 3) + lane, eb0 = 4 * (ww >> 2);
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int s = 0; s <= nsteps; ++s) {
-      if (s < nsteps) {
-        // the step's bytes have landed; A buffer s & 1 was last read by the
-        // MMAs of step s - 2
-        bool ok = wait_bar(full, s);
-        if (ok && s >= 2) ok = wait_bar(done, s - 2);
-        if (__any_sync(0xffffffffu, !ok)) {
-          fail = true;
-          break;
-        }
-        const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
-        const int kb = s % a.nblk;
-        const uint8_t* rs = raw + (size_t)(s & 1) * kRawStage;
-        uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
-        if constexpr (WT == 14) {
-          const int wi = tid - 32;
+  } else if (warp <= kUnpackWarps) {
+    // unpackers: step s's weights into A buffer s & 1 once they have landed
+    // and the MMAs of step s - 2 (the buffer's last readers) have completed
+    const int uw = warp - 1;
+    for (int s = 0; s < nsteps; ++s) {
+      bool ok = wait_bar(full, s);
+      if (ok && s >= 2) ok = wait_bar(done, s - 2);
+      if (__any_sync(0xffffffffu, !ok)) {
+        fail = true;
+        break;
+      }
+      const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
+      const int kb = s % a.nblk;
+      const uint8_t* rs = raw + (size_t)(s & 1) * kRawStage;
+      uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
+      if constexpr (WT == 14) {
+#pragma unroll 1
+        for (int part = 0; part < kUnpackParts; ++part) {
+          const int wi = (tid - 32) + 32 * kUnpackWarps * part;
           const int ur = wi >> 2, uh = (wi >> 1) & 1, uhalf = wi & 1;  // (row, quarter)
           const int r = t * kMmaRows + ur;
           const int64_t g = (int64_t)r * a.row_bytes + (int64_t)kb * kQ6Bytes;
@@ -511,7 +527,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
           }
           // the four sub-blocks j = 8h + 2c + half of this quarter (dotQ6K's
           // q1..q4, quant.nim:744-747): the 6-bit value q, then q - 32 as int8
-          // (q ^ 32 is q - 32 for q >= 32 and q + 32 below; those get bits 6, 7)
+          // (q + 96 stays below 256 in every byte; its bit 7 flipped is
+          // q - 32 in two's complement)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t v[4];
@@ -519,20 +536,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
             for (int k = 0; k < 4; ++k) {
               const uint32_t lo4 = ((c & 1) ? QB[k] : QA[k]) >> ((c & 2) ? 4 : 0);
               const uint32_t q6 = (lo4 & 0x0F0F0F0Fu) | (((QH[k] >> (2 * c)) << 4) & 0x30303030u);
-              const uint32_t t6 = q6 ^ 0x20202020u;
-              const uint32_t m = t6 & 0x20202020u;
-              v[k] = t6 | (m << 1) | (m << 2);
+              v[k] = (q6 + 0x60606060u) ^ 0x80808080u;
             }
             *reinterpret_cast<uint4*>(ab + a_off(ur, 8 * uh + 2 * c + uhalf)) = make_uint4(v[0], v[1], v[2], v[3]);
           }
-        } else {
-          // Q8_0 / Q4_0: a thread takes blocks 2q, 2q + 1 of row rr (q
-          // uniform across the warp, 32 consecutive rows per warp, so its
-          // 16-byte loads and stores are free of bank conflicts); block j
-          // goes to K step j, values 0-15 then 16-31, as int8
-          const int q = ww & 3, rr = 32 * (ww >> 2) + lane;
+        }
+      } else {
+        // Q8_0 / Q4_0: a thread takes blocks 2q, 2q + 1 of kUnpackParts rows
+        // (q uniform across the warp, 32 consecutive rows per warp and part,
+        // so its 16-byte loads and stores are free of bank conflicts); block
+        // j goes to K step j, values 0-15 then 16-31, as int8
+        const int q = uw & 3, g = uw >> 2;
+        float* dslot = dws + (size_t)(s % kSlots) * 8 * kMmaRows;
+#pragma unroll 1
+        for (int part = 0; part < kUnpackParts; ++part) {
+          const int rr = 32 * (g + (kUnpackWarps / 4) * part) + lane;
           const bool in = t * kMmaRows + rr < a.rows;
-          float* dslot = dws + (size_t)(s % kSlots) * 8 * kMmaRows;
           if constexpr (WT == 8) {
             const uint4* src = reinterpret_cast<const uint4*>(rs + rr * kRawRow + 64 * q);
             uint32_t W[20];
@@ -569,84 +588,97 @@ __global__ void __launch_bounds__(kMmaThreads, 1) lmh_mma_kernel(const MmaArgs a
             }
           }
         }
-        // this warp's operands, and its reads of the TMEM region that step
-        // s's MMAs overwrite (the sums of step s - 2), come before the arrival
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[s & 1]);
       }
-      // the previous step's sums for this warp's rows and batch rows
-      if (s >= 1) {
-        const bool ok = wait_bar(done, s - 1);
-        if (__any_sync(0xffffffffu, !ok)) {  // (tcgen05.ld is warp-wide)
-          fail = true;
-          break;
-        }
-        const int p = s - 1;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int kb = p % a.nblk;
-        const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * T::kRegion + eb0);
-        if constexpr (WT == 14) {
-          const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
-          uint32_t scw[4];
+      // the operands (async proxy: the MMAs) and the step's scales (the
+      // summers, which also wait on this barrier) before the arrival
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[s % 4]);
+    }
+  } else {
+    // summers: the sums of step p once its MMAs have completed; weight row em
+    // of the tile (TMEM lane quarter warp % 4), batch rows eb0 .. eb0+EB-1
+    const int sw = warp - 1 - kUnpackWarps;
+    const int em = 32 * (warp & 3) + lane, eb0 = EB * (sw >> 2);
+    float acc[EB];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) scw[k] = sd[k];
-          int sumi[4] = {0, 0, 0, 0};
+    for (int e = 0; e < EB; ++e) acc[e] = 0.0f;
+    for (int p = 0; p < nsteps; ++p) {
+      bool ok = wait_bar(done, p);
+      if (ok) ok = wait4(ready, p);  // (complete since the MMAs were issued: orders the scales)
+      if (__any_sync(0xffffffffu, !ok)) {  // (tcgen05.ld is warp-wide)
+        fail = true;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int kb = p % a.nblk;
+      const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * T::kRegion + eb0);
+      if constexpr (WT == 14) {
+        const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
+        uint32_t scw[4];
 #pragma unroll
-          for (int j0 = 0; j0 < 16; j0 += 4) {
-            uint32_t d[4][4];
+        for (int k = 0; k < 4; ++k) scw[k] = sd[k];
+        int sumi[EB];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) tmem_ld4(ta + 16 * (j0 + u), d[u]);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        for (int e = 0; e < EB; ++e) sumi[e] = 0;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int j = j0 + u;
-              const int sc = (int)(int8_t)(scw[j >> 2] >> (8 * (j & 3)));
+        for (int j0 = 0; j0 < 16; j0 += 4) {
+          uint32_t d[4][EB];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) sumi[e] += sc * (int)d[u][e];
-            }
-          }
-          const float dw = dws[(p % kSlots) * kMmaRows + em];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int b = eb0 + e;
-            if (b < a.nb)
-              acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * nab + kb], dw), __int2float_rn(sumi[e])));
-          }
-        } else {
-          // dotQ8_0i / dotQ4_0i (quant.nim:762-786): block after block,
-          // acc += (d_w * d_a) * float(s)
-          uint32_t d[8][4];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) tmem_ld4(ta + 16 * i, d[i]);
-          float dw[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dw[i] = dws[((p % kSlots) * 8 + i) * kMmaRows + em];
+          for (int u = 0; u < 4; ++u) tmem_ld<EB>(ta + 16 * (j0 + u), d[u]);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u;
+            const int sc = (int)(int8_t)(scw[j >> 2] >> (8 * (j & 3)));
+#pragma unroll
+            for (int e = 0; e < EB; ++e) sumi[e] += sc * (int)d[u][e];
+          }
+        }
+        const float dw = dws[(p % kSlots) * kMmaRows + em];
+#pragma unroll
+        for (int e = 0; e < EB; ++e) {
+          const int b = eb0 + e;
+          if (b < a.nb)
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dsa[b * nab + kb], dw), __int2float_rn(sumi[e])));
+        }
+      } else {
+        // dotQ8_0i / dotQ4_0i (quant.nim:762-786): block after block,
+        // acc += (d_w * d_a) * float(s); blocks 0-3, then 4-7
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t d[4][EB];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tmem_ld<EB>(ta + 16 * (4 * h + i), d[i]);
+          float dw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dw[i] = dws[((p % kSlots) * 8 + 4 * h + i) * kMmaRows + em];
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int e = 0; e < EB; ++e) {
             const int b = eb0 + e;
             if (b >= a.nb) break;
-            const float4* dp = reinterpret_cast<const float4*>(dsa + b * nab + kb * 8);
-            const float4 da0 = dp[0], da1 = dp[1];
-            const float da[8] = {da0.x, da0.y, da0.z, da0.w, da1.x, da1.y, da1.z, da1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[i], da[i]), __int2float_rn((int)d[i][e])));
+            const float4 da = *reinterpret_cast<const float4*>(dsa + b * nab + kb * 8 + 4 * h);
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[0], da.x), __int2float_rn((int)d[0][e])));
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[1], da.y), __int2float_rn((int)d[1][e])));
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[2], da.z), __int2float_rn((int)d[2][e])));
+            acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(dw[3], da.w), __int2float_rn((int)d[3][e])));
           }
         }
-        if (kb == a.nblk - 1) {
-          const int t = (int)blockIdx.x + (p / a.nblk) * (int)gridDim.x;
-          const int r = t * kMmaRows + em;
+      }
+      // TMEM region p & 1 read: the MMAs of step p + 2 may overwrite it
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[p & 1]);
+      if (kb == a.nblk - 1) {
+        const int t = (int)blockIdx.x + (p / a.nblk) * (int)gridDim.x;
+        const int r = t * kMmaRows + em;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int b = eb0 + e;
-            if (b < a.nb && r < a.rows) a.y[(size_t)b * a.ldy + r] = acc[e];
-            acc[e] = 0.0f;
-          }
+        for (int e = 0; e < EB; ++e) {
+          const int b = eb0 + e;
+          if (b < a.nb && r < a.rows) a.y[(size_t)b * a.ldy + r] = acc[e];
+          acc[e] = 0.0f;
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       }
     }
   }
@@ -740,6 +772,8 @@ cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, i
   a.tiled = tiled;
   const size_t smem = lm_head_mma_smem(wtype, cols);
   auto kern = (wtype == 14) ? lmh_mma_kernel<14> : (wtype == 8) ? lmh_mma_kernel<8> : lmh_mma_kernel<2>;
+  auto roles = [](auto t) { return 32 * (1 + decltype(t)::kUnpackWarps + decltype(t)::kSumWarps); };
+  const int threads = (wtype == 14) ? roles(MmaType<14>{}) : (wtype == 8) ? roles(MmaType<8>{}) : roles(MmaType<2>{});
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::min(a.ntiles, sm_count);
@@ -747,7 +781,7 @@ cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, i
     a.nb = std::min(kMmaN, nb - b0);
     a.x = x + (size_t)b0 * cols;
     a.y = y + (size_t)b0 * ldy;
-    kern<<<grid, kMmaThreads, smem, st>>>(a, map);
+    kern<<<grid, threads, smem, st>>>(a, map);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
