@@ -574,27 +574,34 @@ def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
     L = eng._lib
     W = pkg.workloads
     out = {"config": "nls_lm_head: rows=128256 (vocab) x cols=4096 (Llama-3 8B output layer), "
-                     "ggml-layout synthetic weights resident on the device (Q8_0, Q6_K: int8 path; "
-                     "F16: float path), fp32 activations on the device; weights 3-8x the L2, no flush "
-                     "between calls",
+                     "ggml-layout synthetic weights resident on the device (Q8_0 at 1-4 rows or rows "
+                     "that are separate sequences, Q6_K, Q4_0: int8 path, on the tensor cores from 8 "
+                     "rows; Q8_0 above 4 rows of one sequence, F16: float path), fp32 activations on "
+                     "the device; weights 3-8x the L2, no flush between calls",
            "peak_gbs": peak}
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED)
-    for name in ("q8_0", "q6_k", "f16"):
+    for name in ("q8_0", "q6_k", "q4_0", "f16"):
         t = W.LM_TYPES[name]
         wd = W.lm_weights_device(t, rows, cols, seed=SEED, device=dev)
         wbytes = rows * W.lm_row_bytes(t, cols)
         res = {"weight_bytes": wbytes}
-        # (Q6_K at 8 and 16 batch rows: the tensor-core path; Q8_0 above 4
-        # rows and F16: the float path, tiled across batch rows above 1)
-        for nb in {"q8_0": (1, 4, 8, 16), "q6_k": (1, 4, 8, 16), "f16": (1, 4, 16)}[name]:
+        # (Q6_K and Q4_0 at 8 and 16 batch rows, and Q8_0 rows that are
+        # separate sequences ("_independent", NLS_ROWS_INDEPENDENT): the
+        # tensor-core path; Q8_0 above 4 rows of one sequence and F16: the
+        # float path, tiled across batch rows above 1)
+        legs = {"q8_0": ((1, 0), (4, 0), (8, 0), (16, 0), (8, 8), (16, 8)),
+                "q6_k": ((1, 0), (4, 0), (8, 0), (16, 0)),
+                "q4_0": ((1, 0), (8, 0), (16, 0)),
+                "f16": ((1, 0), (4, 0), (16, 0))}[name]
+        for nb, fl in legs:
             x = torch.randn((nb, cols), generator=gen, device=dev)
             y = torch.empty((nb, rows), dtype=torch.float32, device=dev)
 
             def call():
                 return L.nls_lm_head(eng._h, ctypes.c_void_p(wd.data_ptr()), t, rows, cols,
                                      ctypes.c_void_p(x.data_ptr()), nb, ctypes.c_void_p(y.data_ptr()),
-                                     3, ctypes.c_void_p(sptr))
+                                     3 | fl, ctypes.c_void_p(sptr))
             for _ in range(3):
                 if call() != 0:
                     raise RuntimeError("nls_lm_head failed")
@@ -614,8 +621,8 @@ def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
             # algorithmic bytes: the weights once, the activations, the logits
             algo = wbytes + nb * cols * 4 + nb * rows * 4
             gbs = algo / (m / 1e3) / 1e9
-            res[f"nb{nb}"] = {"ms": m, "algorithmic_bytes": algo, "achieved_gbs": gbs,
-                              "frac": gbs / peak}
+            res[f"nb{nb}" + ("_independent" if fl else "")] = {
+                "ms": m, "algorithmic_bytes": algo, "achieved_gbs": gbs, "frac": gbs / peak}
             if name == "q8_0" and nb == 1:
                 tr = ncu_traffic().get("lmh_kernel_q8_0_nb1")
                 out["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
@@ -654,7 +661,7 @@ def lm_head_bench(pkg, local, dev, stream, peak, with_cpu: bool):
                 raise RuntimeError("nls_lm_head_sample status")
             ms.sort()
             res["with_sampling_b1_ms"] = ms[len(ms) // 2]
-        if with_cpu and name != "f16":
+        if with_cpu and name in ("q8_0", "q6_k"):
             from oracle import oracle
             oracle.build()
             threads = os.cpu_count() or 1
