@@ -293,6 +293,18 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
   int* s_staged = s_fail + 2;  // the last step whose copies were issued
 
   const int my_tiles = (a.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  // (tile, step in the row) of this CTA's step s, advanced step by step
+  // (no division per step)
+  struct Pos {
+    int t, kb;
+  };
+  auto next = [&](Pos& q) {
+    if (++q.kb == a.nblk) {
+      q.kb = 0;
+      q.t += (int)gridDim.x;
+    }
+  };
+  const Pos first{(int)blockIdx.x, 0};
   const int nsteps = my_tiles * a.nblk;
   const int64_t last16 = a.total & ~int64_t(15);
 
@@ -303,10 +315,9 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
   // row read as zeros); otherwise one bulk copy per row, and a row whose copy
   // would pass the weights' last whole 16 bytes goes by plain loads before
   // the arrival.
-  auto stage = [&](int s) {
+  auto stage = [&](int s, Pos q) {
     if (s >= nsteps) return;
-    const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
-    const int kb = s % a.nblk;
+    const int t = q.t, kb = q.kb;
     uint8_t* dst = raw + (size_t)(s & 1) * kRawStage;
     if (a.tiled) {
       if (lane == 0) {
@@ -361,8 +372,10 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
   if (warp == 0) {
-    stage(0);
-    stage(1);
+    Pos q = first;
+    stage(0, q);
+    next(q);
+    stage(1, q);
   }
   // quantizeAct (quant.nim:646-662) with the type's blocks (256 values for
   // Q6_K, 32 for the others): each thread takes 32 consecutive values, the G
@@ -444,7 +457,10 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     // staging two steps ahead, and the MMAs of step s once every unpacker
     // has laid it out (which also frees raw buffer s & 1 for step s + 2) and
     // the sums of step s - 2 have read TMEM region s & 1
-    for (int s = 0; s < nsteps; ++s) {
+    Pos cur = first, st2 = first;
+    next(st2);
+    next(st2);
+    for (int s = 0; s < nsteps; ++s, next(cur), next(st2)) {
       bool ok = true;
       if (lane == 0) ok = wait4(ready, s) && (s < 2 || wait_bar(tfree, s - 2)) && !*s_fail;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -452,10 +468,10 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
         fail = true;
         break;
       }
-      stage(s + 2);
+      stage(s + 2, st2);
       if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int kb = s % a.nblk;
+        const int kb = cur.kb;
         const uint32_t ab = smem_u32(aop) + (uint32_t)((s & 1) * kAStage);
         const uint32_t bb = smem_u32(bop) + (uint32_t)(kb * 8) * (kMmaN * 32);
         const uint32_t dreg = tbase + (uint32_t)((s & 1) * T::kRegion);
@@ -490,15 +506,15 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     // unpackers: step s's weights into A buffer s & 1 once they have landed
     // and the MMAs of step s - 2 (the buffer's last readers) have completed
     const int uw = warp - 1;
-    for (int s = 0; s < nsteps; ++s) {
+    Pos cur = first;
+    for (int s = 0; s < nsteps; ++s, next(cur)) {
       bool ok = wait_bar(full, s);
       if (ok && s >= 2) ok = wait_bar(done, s - 2);
       if (__any_sync(0xffffffffu, !ok)) {
         fail = true;
         break;
       }
-      const int t = (int)blockIdx.x + (s / a.nblk) * (int)gridDim.x;
-      const int kb = s % a.nblk;
+      const int t = cur.t, kb = cur.kb;
       const uint8_t* rs = raw + (size_t)(s & 1) * kRawStage;
       uint8_t* ab = aop + (size_t)(s & 1) * kAStage;
       if constexpr (WT == 14) {
@@ -603,7 +619,8 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     float acc[EB];
 #pragma unroll
     for (int e = 0; e < EB; ++e) acc[e] = 0.0f;
-    for (int p = 0; p < nsteps; ++p) {
+    Pos cur = first;
+    for (int p = 0; p < nsteps; ++p, next(cur)) {
       bool ok = wait_bar(done, p);
       if (ok) ok = wait4(ready, p);  // (complete since the MMAs were issued: orders the scales)
       if (__any_sync(0xffffffffu, !ok)) {  // (tcgen05.ld is warp-wide)
@@ -611,7 +628,7 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int kb = p % a.nblk;
+      const int kb = cur.kb;
       const uint32_t ta = tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((p & 1) * T::kRegion + eb0);
       if constexpr (WT == 14) {
         const uint32_t* sd = scs + ((size_t)(p % kSlots) * kMmaRows + em) * 4;
@@ -671,8 +688,7 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree[p & 1]);
       if (kb == a.nblk - 1) {
-        const int t = (int)blockIdx.x + (p / a.nblk) * (int)gridDim.x;
-        const int r = t * kMmaRows + em;
+        const int r = cur.t * kMmaRows + em;
 #pragma unroll
         for (int e = 0; e < EB; ++e) {
           const int b = eb0 + e;
