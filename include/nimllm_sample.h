@@ -237,10 +237,12 @@ NLS_API nls_status nls_sample_batch_vocab_sharded(
     const double* uniforms, int64_t* out_ids, float* out_probs, void* stream);
 
 /* Limit, in nanoseconds, of the bounded waits in which the streaming kernel
- * (greedy and top-k <= 256 rows) waits for its bulk copies of logits
- * (default 200 ms; later calls on this handle use it). A wait that runs out
- * fails its row (id -1) with NLS_ERR_TIMEOUT, after the kernel has waited,
- * with the default limit, for the copies it has in flight. A limit of 0 is a
+ * (greedy and top-k <= 256 rows) waits for its bulk copies of logits, and
+ * in which the tensor-core path of nls_lm_head waits between its pipeline
+ * stages (default 200 ms; later calls on this handle use it). A wait that
+ * runs out fails its row (id -1) or the projection with NLS_ERR_TIMEOUT,
+ * after the kernel has waited, with the default limit, for the copies (and
+ * MMAs) it has in flight. A limit of 0 is a
  * deadline already past: every such wait gives up at once, which drives that
  * failure path on purpose (tests of the timeout handling). No counterpart in
  * the reference (its sampler runs on the host and waits for nothing). */
@@ -300,9 +302,13 @@ NLS_API nls_status nls_token_nll(nls_handle* h, const float* logits, int64_t ld,
  * cols must be a whole number of blocks (32 for Q4_0/Q8_0, 256 for Q6_K) and
  * at most 16384 for F32/F16. Non-finite activations on the int8 path give
  * NLS_ERR_NAN_LOGITS (the reference's int8 conversion of them is undefined).
- * Q6_K at 8 or more batch rows (and at most 5888 columns) runs on the tensor
- * cores with the same results; a bounded wait there that runs out gives
- * NLS_ERR_TIMEOUT.
+ * On the int8 path, Q6_K and Q4_0 at 8 or more batch rows, and Q8_0 rows
+ * that are separate sequences (NLS_ROWS_INDEPENDENT) at 8 or more, run on
+ * the tensor cores with the same results (up to 5376, 4352 and 6144 columns
+ * for Q6_K, Q8_0 and Q4_0); a wait of that pipeline that runs out
+ * (nls_set_wait_limit) gives NLS_ERR_TIMEOUT, after the copies and MMAs in
+ * flight have finished under the default limit, and leaves the logits
+ * undefined.
  * Flags: NLS_DEVICE_INPUTS (x), NLS_DEVICE_OUTPUTS (y), NLS_EXACT_MATMUL,
  * NLS_ROWS_INDEPENDENT. */
 NLS_API nls_status nls_lm_head(nls_handle* h, const void* weights, int32_t wtype, int32_t rows,

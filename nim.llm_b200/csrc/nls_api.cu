@@ -52,7 +52,8 @@ struct nls_handle {
   // done, [3] fallback launch done
   int profiling = 0;
   int profiled = 0;
-  // limit of the streaming kernel's bulk-copy waits (nls_set_wait_limit)
+  // limit of the streaming kernel's bulk-copy waits and of the tensor-core
+  // output projection's pipeline waits (nls_set_wait_limit)
   unsigned long long wait_ns = 200ull * 1000ull * 1000ull;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
   // vocab-sharded calls: packed shard, received shards, gathered ids/probs
@@ -467,7 +468,7 @@ nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32
     dx = h->d_lmx;
   }
   NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb,
-                                  path_nb, dy, exact, h->d_work, h->sm_count, st));
+                                  path_nb, dy, exact, h->d_work, h->sm_count, h->wait_ns, st));
   return NLS_OK;
 }
 

@@ -48,7 +48,7 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
 // path_nb: the batch size the path choice sees (nb, or 1 for independent rows)
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
-                           cudaStream_t st);
+                           unsigned long long wait_ns, cudaStream_t st);
 // Q6_K / Q8_0 on the int8 path at lm_head_mma_min_rows or more batch rows:
 // tcgen05 int8 MMAs (nls_lmhead_mma.cu), launches of up to 16 batch rows;
 // y[b * ldy + r]

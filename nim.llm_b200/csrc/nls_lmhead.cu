@@ -887,7 +887,7 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact) {
 
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
-                           cudaStream_t st) {
+                           unsigned long long wait_ns, cudaStream_t st) {
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
   const bool int8 = lm_head_int8_path(wtype, cols, path_nb, exact);
@@ -903,7 +903,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
     const int lo = lm_head_mma_min_rows(wtype);
     const int tail = (nb % 16 < lo) ? nb % 16 : 0;
     const int nm = nb - tail;
-    cudaError_t e = launch_lm_head_mma(w, wtype, rb, rows, cols, x, nm, y, rows, status, sm_count, kWaitLimitNs, st);
+    cudaError_t e = launch_lm_head_mma(w, wtype, rb, rows, cols, x, nm, y, rows, status, sm_count, wait_ns, st);
     if (e != cudaSuccess || tail == 0) return e;
     b_first = nm;
   }

@@ -704,12 +704,18 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     if (tid == 0) {
       atomicCAS(a.status, 0, NLS_ERR_TIMEOUT);
       // let the copies and MMAs in flight finish before the shared memory and
-      // the columns are released (bounded)
+      // the columns are released, under the default limit whatever the
+      // call's (they are real and land); only the last two of each can be
+      // in flight (a step is staged, or its MMAs issued, once the one two
+      // steps before it has been waited for)
+      auto drain = [&](uint64_t* b2, int s) {
+        (void)mbar_wait_bounded(&b2[s & 1], (uint32_t)((s >> 1) & 1), kWaitLimitNs);
+      };
       const int st = *s_staged, last = *s_last;
-      if (st >= 0) (void)wait_bar(full, st);
-      if (st >= 1) (void)wait_bar(full, st - 1);
-      if (last >= 0) (void)wait_bar(done, last);
-      if (last >= 1) (void)wait_bar(done, last - 1);
+      if (st >= 0) drain(full, st);
+      if (st >= 1) drain(full, st - 1);
+      if (last >= 0) drain(done, last);
+      if (last >= 1) drain(done, last - 1);
     }
     __syncthreads();
   }

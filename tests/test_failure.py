@@ -128,3 +128,34 @@ def test_rank_that_stops_taking_part_ends_in_timeout(tmp_path):
     assert int(r0[1]) == pkg._abi.NLS_ERR_TIMEOUT  # the second ended in the deadline
     assert 2.5 <= r0[2] <= 20.0
     assert int(r0[3]) == pkg._abi.NLS_ERR_NCCL     # the aborted communicator refuses more calls
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q6_k", "q4_0"])
+def test_lm_head_tensor_core_wait_limit_zero(pkg, oracle_mod, name):
+    """The tensor-core output projection's pipeline waits are bounded too: at
+    a wait limit of 0 every wait gives up at once, the call returns
+    NLS_ERR_TIMEOUT after the kernel has let its copies in flight land, and
+    once the limit is restored the same handle gives the oracle's logits."""
+    import ctypes
+    import torch
+    t = {"q6_k": 14, "q4_0": 2}[name]
+    rows, cols, nb = 1000, 1024, 9
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=71)
+    x = np.random.default_rng(72).standard_normal((nb, cols)).astype(np.float32)
+    want = oracle_mod.lm_head(w, t, rows, cols, x, threads=8)
+    dw = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+    eng = pkg.Engine(0, max_rows=16, max_vocab=rows)
+    try:
+        y = np.empty((nb, rows), np.float32)
+        eng.set_wait_limit(0)
+        st = eng._lib.nls_lm_head(eng._h, ctypes.c_void_p(dw.data_ptr()), t, rows, cols,
+                                  ctypes.c_void_p(x.ctypes.data), nb, ctypes.c_void_p(y.ctypes.data), 0,
+                                  ctypes.c_void_p(0))
+        assert st == pkg._abi.NLS_ERR_TIMEOUT
+        eng.set_wait_limit(200 * 1000 * 1000)
+        for _ in range(2):
+            got = eng.lm_head(dw, t, rows, cols, x)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        eng.close()
