@@ -78,6 +78,8 @@ struct nls_handle {
   // output projection: staged activations, host-output logits
   float* d_lmx = nullptr;
   size_t lmx_cap = 0;
+  uint8_t* d_lmq = nullptr;  // the tensor-core projection's quantized activations
+  size_t lmq_cap = 0;
   float* d_lmy = nullptr;
   size_t lmy_cap = 0;
   char last_err[256] = {0};
@@ -294,6 +296,7 @@ void nls_destroy(nls_handle* h) {
     cudaFree(h->d_tgt);
     cudaFree(h->d_nll);
     cudaFree(h->d_lmx);
+    cudaFree(h->d_lmq);
     cudaFree(h->d_lmy);
     if (h->fork) cudaEventDestroy(h->fork);
     if (h->join) cudaEventDestroy(h->join);
@@ -467,8 +470,11 @@ nls_status lm_head_impl(nls_handle* h, const void* weights, int32_t wtype, int32
     NLS_CUDA(h, cudaMemcpyAsync(h->d_lmx, x, sizeof(float) * (size_t)nb * cols, cudaMemcpyHostToDevice, st));
     dx = h->d_lmx;
   }
+  // the tensor-core path (8 or more batch rows) quantizes the activations
+  // once per launch into this scratch
+  if (nb >= 8 && (s = grow(h, &h->d_lmq, &h->lmq_cap, nls::lm_head_act_scratch_bytes(cols))) != NLS_OK) return s;
   NLS_CUDA(h, nls::launch_lm_head(static_cast<const uint8_t*>(weights), wtype, rows, cols, dx, nb,
-                                  path_nb, dy, exact, h->d_work, h->sm_count, h->wait_ns, st));
+                                  path_nb, dy, exact, h->d_work, h->sm_count, h->wait_ns, h->d_lmq, st));
   return NLS_OK;
 }
 

@@ -48,7 +48,7 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
 // path_nb: the batch size the path choice sees (nb, or 1 for independent rows)
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
-                           unsigned long long wait_ns, cudaStream_t st);
+                           unsigned long long wait_ns, uint8_t* act_scratch, cudaStream_t st);
 // Q6_K / Q8_0 on the int8 path at lm_head_mma_min_rows or more batch rows:
 // tcgen05 int8 MMAs (nls_lmhead_mma.cu), launches of up to 16 batch rows;
 // y[b * ldy + r]
@@ -62,7 +62,10 @@ cudaError_t launch_lm_head_float(const uint8_t* w, int wtype, int64_t row_bytes,
                                  const float* x, int nb, float* y, int64_t ldy, int sm_count,
                                  cudaStream_t st);
 size_t lm_head_mma_smem(int wtype, int cols);
+// device scratch of the tensor-core path: the quantized activations of one
+// launch (16-byte aligned)
+size_t lm_head_act_scratch_bytes(int cols);
 cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols, const float* x,
                                int nb, float* y, int64_t ldy, int* status, int sm_count,
-                               unsigned long long wait_ns, cudaStream_t st);
+                               unsigned long long wait_ns, uint8_t* act_scratch, cudaStream_t st);
 }  // namespace nls

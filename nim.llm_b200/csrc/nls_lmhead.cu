@@ -887,7 +887,7 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact) {
 
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
-                           unsigned long long wait_ns, cudaStream_t st) {
+                           unsigned long long wait_ns, uint8_t* act_scratch, cudaStream_t st) {
   int64_t rb = 0;
   if (!lm_head_row_bytes(wtype, cols, &rb) || rows < 1 || nb < 1) return cudaErrorInvalidValue;
   const bool int8 = lm_head_int8_path(wtype, cols, path_nb, exact);
@@ -899,11 +899,11 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   // arithmetic on the tensor cores, the weights read once per 16 batch rows
   // (nls_lmhead_mma.cu); a tail of fewer than 8 rows takes the path below
   int b_first = 0;
-  if (int8 && lm_head_mma_path(wtype, cols, nb)) {
+  if (int8 && act_scratch && lm_head_mma_path(wtype, cols, nb)) {
     const int lo = lm_head_mma_min_rows(wtype);
     const int tail = (nb % 16 < lo) ? nb % 16 : 0;
     const int nm = nb - tail;
-    cudaError_t e = launch_lm_head_mma(w, wtype, rb, rows, cols, x, nm, y, rows, status, sm_count, wait_ns, st);
+    cudaError_t e = launch_lm_head_mma(w, wtype, rb, rows, cols, x, nm, y, rows, status, sm_count, wait_ns, act_scratch, st);
     if (e != cudaSuccess || tail == 0) return e;
     b_first = nm;
   }

@@ -43,8 +43,11 @@
 //    (warp % 4) and a share of the 16 batch rows, the step's sums and form
 //    the fp32 terms in block order, while the unpackers work on later steps.
 // All hand-offs are mbarriers (staging -> unpackers -> warp 0 -> summers ->
-// warp 0), every wait bounded. The activations are quantized once per CTA
-// into shared memory in the operand layout (batch rows past nb are zeros).
+// warp 0), every wait bounded. The activations are quantized once per launch
+// by a small kernel before it (lmh_mma_quant_kernel, into device scratch in
+// the operand layout; batch rows past nb are zeros) whose programmatic
+// dependent this kernel is: its set-up and first weight copies run while
+// that kernel does, then one bulk copy brings the operand and the scales.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -135,7 +138,8 @@ struct MmaArgs {
   int64_t total;     // rows * row_bytes
   int rows, cols, nblk;
   int nb;            // batch rows of this launch, <= 16
-  const float* x;    // [nb x cols]
+  const uint8_t* q;  // the quantized activations in the B operand layout (16 x cols bytes)
+  const float* dq;   // their block scales d_a [16][cols / block]
   float* y;          // y[b * ldy + r]
   int64_t ldy;
   int ntiles;
@@ -196,7 +200,7 @@ __host__ __device__ constexpr size_t mma_smem(int cols) {
   using T = MmaType<WT>;
   return (size_t)(cols / 32) * (kMmaN * 32) + 2 * (size_t)T::kAStage + 2 * (size_t)kMmaRows * T::kRawRow +
          (size_t)kMmaN * (cols / T::kBL) * 4 + (size_t)kSlots * kMmaRows * T::kDw * 4 +
-         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 10 * 8 + 16 + 16;
+         (size_t)kSlots * kMmaRows * T::kScWords * 4 + 8 + 11 * 8 + 16 + 16;
 }
 
 // Q8_0: one thread lays out blocks 2Q and 2Q + 1 of a row from the 80 bytes
@@ -256,6 +260,75 @@ __device__ __forceinline__ void q4_units(const uint32_t (&W)[12], uint8_t* ab, f
   dslot[(2 * Q + 1) * kMmaRows + rr] = in ? d1 : 0.0f;
 }
 
+// quantizeAct (quant.nim:646-662) once per launch of 16 batch rows, with the
+// type's blocks (256 values for Q6_K, 32 for the others), into the B operand
+// layout in global memory (rows nb .. 15 zeros) and the block scales d_a:
+// each thread takes 32 consecutive values, the G threads of a block
+// (consecutive lanes) combine their maxima by shuffles. The projection
+// kernel is its programmatic dependent: it is released at once and sets
+// itself up while this grid runs.
+template <int WT>
+__global__ void __launch_bounds__(256) lmh_mma_quant_kernel(const float* x, int nb, int cols, uint8_t* q,
+                                                            float* dq, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  using T = MmaType<WT>;
+  constexpr int G = T::kBL / 32;
+  const int lane = threadIdx.x & 31;
+  const int per_row = cols / 32, nab = cols / T::kBL;
+  const int units = kMmaN * per_row;  // a multiple of 8: whole blocks per warp
+  const int nthreads = (int)(gridDim.x * blockDim.x);
+  for (int base = (int)(blockIdx.x * blockDim.x + threadIdx.x) - lane; base < units; base += nthreads) {
+    const int u = base + lane;
+    const bool act = u < units;
+    const int b = act ? u / per_row : 0, c = act ? u % per_row : 0;
+    const bool real = act && b < nb;
+    const float* xs = x + (size_t)b * cols + (size_t)c * 32;
+    float v[32];
+    if (real && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 f = reinterpret_cast<const float4*>(xs)[k];
+        v[4 * k] = f.x;
+        v[4 * k + 1] = f.y;
+        v[4 * k + 2] = f.z;
+        v[4 * k + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = real ? xs[k] : 0.0f;
+    }
+    float amax = 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      bad |= !isfinite(v[k]);
+      amax = fmaxf(amax, fabsf(v[k]));
+    }
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicCAS(status, 0, NLS_ERR_NAN_LOGITS);
+    if (act) {
+      const float d = amax / 127.0f;
+      const float id = d > 0.0f ? 1.0f / d : 0.0f;
+      if (c % G == 0) dq[b * nab + c / G] = d;
+      uint32_t qw[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        uint32_t wv = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float q0 = v[4 * k + e] * id;
+          const int qi = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
+          wv |= ((uint32_t)qi & 0xFFu) << (8 * e);
+        }
+        qw[k] = wv;
+      }
+      *reinterpret_cast<uint4*>(q + b_off(b, c * 32)) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+      *reinterpret_cast<uint4*>(q + b_off(b, c * 32 + 16)) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+    }
+  }
+}
+
 template <int WT>
 __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<WT>::kSumWarps), 1)
     lmh_mma_kernel(const MmaArgs a,
@@ -287,7 +360,8 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
   uint64_t* ready = bar + 2;  // [4] every unpacker has laid out step s (slot s % 4)
   uint64_t* done = bar + 6;   // [2] MMAs of step s completed (tcgen05.commit)
   uint64_t* tfree = bar + 8;  // [2] every summer has read TMEM region s & 1 for step s
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* actbar = bar + 10;  // the activation operand and scales (bulk copies)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 11);
   int* s_fail = reinterpret_cast<int*>(tmem_holder + 1);
   int* s_last = s_fail + 1;    // the last step whose MMAs were issued
   int* s_staged = s_fail + 2;  // the last step whose copies were issued
@@ -359,80 +433,32 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
   };
 
   if (tid == 0) {
-    for (int k = 0; k < 10; ++k)
-      mbar_init(&bar[k], (k >= 2 && k < 6) ? kUnpackWarps : (k >= 8) ? kSumWarps : 1);
+    for (int k = 0; k < 11; ++k)
+      mbar_init(&bar[k], (k >= 2 && k < 6) ? kUnpackWarps : (k >= 8 && k < 10) ? kSumWarps : 1);
     *s_fail = 0;
     *s_last = -1;
     *s_staged = -1;
     fence_mbar_init();
   }
-  // zeros: the activation rows nb .. 15 and both A buffers (Q6_K's zero
-  // blocks stay zero)
-  for (int i = tid; i < (kb_steps * (kMmaN * 32) + 2 * kAStage) / 16; i += kMmaThreads)
-    reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
+  // zeros: both A buffers (Q6_K's zero blocks stay zero)
+  for (int i = tid; i < 2 * kAStage / 16; i += kMmaThreads) reinterpret_cast<uint4*>(aop)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
   if (warp == 0) {
     Pos q = first;
     stage(0, q);
     next(q);
     stage(1, q);
-  }
-  // quantizeAct (quant.nim:646-662) with the type's blocks (256 values for
-  // Q6_K, 32 for the others): each thread takes 32 consecutive values, the G
-  // threads of a block (consecutive lanes) combine their maxima by shuffles
-  {
-    constexpr int G = T::kBL / 32;
-    const int per_row = a.cols / 32;
-    const int units = a.nb * per_row;  // a multiple of 8: whole blocks per warp
-    for (int base = warp * 32; base < units; base += kMmaThreads) {
-      const int u = base + lane;
-      const bool act = u < units;
-      const int b = act ? u / per_row : 0, c = act ? u % per_row : 0;
-      const float* xs = a.x + (size_t)b * a.cols + (size_t)c * 32;
-      float v[32];
-      if (act && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float4 f = reinterpret_cast<const float4*>(xs)[k];
-          v[4 * k] = f.x;
-          v[4 * k + 1] = f.y;
-          v[4 * k + 2] = f.z;
-          v[4 * k + 3] = f.w;
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = act ? xs[k] : 0.0f;
-      }
-      float amax = 0.0f;
-      bool bad = false;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        bad |= !isfinite(v[k]);
-        amax = fmaxf(amax, fabsf(v[k]));
-      }
-#pragma unroll
-      for (int o = 1; o < G; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0) atomicCAS(a.status, 0, NLS_ERR_NAN_LOGITS);
-      if (act) {
-        const float d = amax / 127.0f;
-        const float id = d > 0.0f ? 1.0f / d : 0.0f;
-        if (c % G == 0) dsa[b * nab + c / G] = d;
-        uint32_t qw[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          uint32_t wv = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float q0 = v[4 * k + e] * id;
-            const int q = q0 >= 0.0f ? (int)(q0 + 0.5f) : -(int)(-q0 + 0.5f);
-            wv |= ((uint32_t)q & 0xFFu) << (8 * e);
-          }
-          qw[k] = wv;
-        }
-        *reinterpret_cast<uint4*>(bop + b_off(b, c * 32)) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-        *reinterpret_cast<uint4*>(bop + b_off(b, c * 32 + 16)) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
-      }
+    // the activations, quantized by the launch this kernel depends on: wait
+    // for that grid (everything above ran while it did), then one bulk copy
+    // of the operand and one of the scales
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      const uint32_t qbytes = (uint32_t)kb_steps * (kMmaN * 32), dbytes = (uint32_t)(kMmaN * nab * 4);
+      mbar_arrive_expect_tx(actbar, qbytes + dbytes);
+      bulk_copy_g2s(bop, a.q, qbytes, actbar);
+      bulk_copy_g2s(dsa, a.dq, dbytes, actbar);
     }
+    __syncwarp();
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -445,7 +471,8 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tbase = *tmem_holder;
-  bool fail = false;
+  // the activations have landed (the default limit: the copies are real)
+  bool fail = !mbar_wait_bounded(actbar, 0u, kWaitLimitNs);
   auto wait_bar = [&](uint64_t* b2, int s) -> bool {  // barrier b2[s & 1] completed for step s
     return mbar_wait_bounded(&b2[s & 1], (uint32_t)((s >> 1) & 1), a.wait_ns);
   };
@@ -453,7 +480,10 @@ __global__ void __launch_bounds__(32 * (1 + MmaType<WT>::kUnpackWarps + MmaType<
     return mbar_wait_bounded(&b4[s & 3], (uint32_t)((s >> 2) & 1), a.wait_ns);
   };
 
-  if (warp == 0) {
+  if (fail) {
+    // (the activations never landed: no role runs; the cleanup below drains
+    // the staged copies)
+  } else if (warp == 0) {
     // staging two steps ahead, and the MMAs of step s once every unpacker
     // has laid it out (which also frees raw buffer s & 1 for step s + 2) and
     // the sums of step s - 2 have read TMEM region s & 1
@@ -759,9 +789,15 @@ EncodeTiledFn encode_tiled() {
 
 }  // namespace
 
+size_t lm_head_act_scratch_bytes(int cols) {
+  // the operand of 16 batch rows, then the scales (blocks of 32 at most)
+  return (size_t)kMmaN * cols + (size_t)kMmaN * (cols / 32) * 4;
+}
+
 cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, int rows, int cols, const float* x,
                                int nb, float* y, int64_t ldy, int* status, int sm_count,
-                               unsigned long long wait_ns, cudaStream_t st) {
+                               unsigned long long wait_ns, uint8_t* act_scratch, cudaStream_t st) {
+  if ((reinterpret_cast<uintptr_t>(act_scratch) & 15) != 0) return cudaErrorInvalidValue;
   if (wtype != 14 && wtype != 8 && wtype != 2) return cudaErrorInvalidValue;
   const int raw_row = (wtype == 14) ? MmaType<14>::kRawRow : (wtype == 8) ? MmaType<8>::kRawRow : MmaType<2>::kRawRow;
   // the weights as a 2-D tensor of 8-byte elements: row_bytes / 8 per row,
@@ -799,12 +835,32 @@ cudaError_t launch_lm_head_mma(const uint8_t* w, int wtype, int64_t row_bytes, i
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::min(a.ntiles, sm_count);
+  auto quant = (wtype == 14) ? lmh_mma_quant_kernel<14> : (wtype == 8) ? lmh_mma_quant_kernel<8>
+                                                                        : lmh_mma_quant_kernel<2>;
+  uint8_t* qs = act_scratch;
+  float* ds = reinterpret_cast<float*>(act_scratch + (size_t)kMmaN * cols);
+  a.q = qs;
+  a.dq = ds;
+  const int qgrid = (kMmaN * (cols / 32) + 255) / 256;
   for (int b0 = 0; b0 < nb; b0 += kMmaN) {
     a.nb = std::min(kMmaN, nb - b0);
-    a.x = x + (size_t)b0 * cols;
     a.y = y + (size_t)b0 * ldy;
-    kern<<<grid, threads, smem, st>>>(a, map);
+    // (the next chunk's quantization starts after this chunk's projection
+    // has finished reading the scratch: plain stream order)
+    quant<<<qgrid, 256, 0, st>>>(x + (size_t)b0 * cols, a.nb, cols, qs, ds, status);
     e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a, map);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
