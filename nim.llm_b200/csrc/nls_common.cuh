@@ -420,7 +420,10 @@ __device__ uint32_t block_select_kth_largest(int n, uint32_t K, Get get, uint32_
     __syncthreads();
     prefix |= sh[0] << shift;
     pmask |= 255u << shift;
-    __syncthreads();
+    // (within the loop the next round's first barrier already separates
+    // these reads of sh[0] from warp 0's next write of it; after the last
+    // round a barrier keeps a following call's reset of sh behind them)
+    if (shift == last_shift) __syncthreads();
   }
   return prefix;
 }
