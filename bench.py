@@ -72,14 +72,14 @@ while True:
     sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
     rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
     print("%.6f %d %d" % (time.time(), sm, rs), flush=True)
-    if select.select([sys.stdin], [], [], 0.002)[0]:
+    if select.select([sys.stdin], [], [], 0.0005)[0]:
         break
 """
 
 
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons of one GPU, polled through
-    NVML (read-only queries) every ~2 ms by a separate process, so that the
+    NVML (read-only queries) every ~0.5 ms by a separate process, so that the
     polling neither competes with the timed loop for the interpreter lock nor
     misses the short timed region. start() returns once the poller runs;
     stop() keeps the samples taken between the two calls."""
@@ -135,7 +135,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
                 "reasons": sorted(reasons), "samples": len(sm),
                 "window_ms": round((self.t1 - self.t0) * 1e3, 3),
-                "source": "NVML, polled every ~2 ms by a separate process during the timed region"}
+                "source": "NVML, polled every ~0.5 ms by a separate process during the timed region"}
 
 
 def row_is_full(params, V):
@@ -693,7 +693,7 @@ def config_dict(world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)  # (a timed region of ~0.1 s: clock samples)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
