@@ -317,6 +317,23 @@ def test_q4_0_tensor_core_path(pkg, engine, oracle_mod, cols, rows):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "q4_0", "q6_k"])
+@pytest.mark.parametrize("rows", [1, 77])
+def test_tensor_core_path_fewer_rows_than_a_tile(pkg, engine, oracle_mod, name, rows):
+    """Weight matrices smaller than one 128-row tile (a single row too): the
+    staged box reaches past the matrix (rows there read as zeros and are
+    never stored), on both staging modes (Q6_K at 768 columns: rows of 630
+    bytes, one bulk copy per row; the others: the tensor-map copy)."""
+    t = TYPES[name]
+    cols = 768
+    w = pkg.workloads.lm_weights(t, rows, cols, seed=rows + t)
+    x = _x(np.random.default_rng(rows + 3 * t), 9, cols, edge=True)
+    got = engine.lm_head(_device_weights(w), t, rows, cols, x, independent=True)
+    want = _oracle_independent(oracle_mod, w, t, rows, cols, x)
+    assert np.array_equal(_bits(got), _bits(want)), f"{name} rows={rows}"
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("name", ["q8_0", "q4_0"])
 def test_32_value_blocks_tensor_core_path_special_scales(pkg, engine, oracle_mod, name):
     """Block scales d that are +inf, NaN, subnormal, -0 and -inf, and
