@@ -49,8 +49,9 @@ bool lm_head_int8_path(int wtype, int cols, int nb, bool exact);
 cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, const float* x, int nb,
                            int path_nb, float* y, bool exact, int* status, int sm_count,
                            unsigned long long wait_ns, uint8_t* act_scratch, cudaStream_t st);
-// Q6_K / Q8_0 on the int8 path at lm_head_mma_min_rows or more batch rows:
-// tcgen05 int8 MMAs (nls_lmhead_mma.cu), launches of up to 16 batch rows;
+// Q6_K / Q8_0 / Q4_0 on the int8 path at lm_head_mma_min_rows or more batch rows:
+// tcgen05 int8 MMAs (nls_lmhead_mma.cu), launches of up to 16 batch rows (with
+// act_scratch: lm_head_act_scratch_bytes, else the CUDA-core path);
 // y[b * ldy + r]
 bool lm_head_mma_path(int wtype, int cols, int nb);
 int lm_head_mma_min_rows(int wtype);

@@ -895,7 +895,7 @@ cudaError_t launch_lm_head(const uint8_t* w, int wtype, int rows, int cols, cons
   if (!int8 && lm_head_float_tiled(wtype, cols, rb) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (nb > 1 || wtype != 1))
     return launch_lm_head_float(w, wtype, rb, rows, cols, x, nb, y, rows, sm_count, st);
-  // Q6_K / Q8_0 on the int8 path at 8 or more batch rows: the same exact
+  // Q6_K / Q8_0 / Q4_0 on the int8 path at 8 or more batch rows: the same exact
   // arithmetic on the tensor cores, the weights read once per 16 batch rows
   // (nls_lmhead_mma.cu); a tail of fewer than 8 rows takes the path below
   int b_first = 0;
