@@ -297,12 +297,14 @@ __device__ __forceinline__ float patched_value(const PatchTable& T, int slot) { 
 // Block-wide construction of the patch table for positions [lo, hi) of `row`;
 // `chunk` is the row's logits from position lo. Every id's logit is read as
 // its id is read (four ids per thread in flight), so the scattered loads
-// overlap each other and the table's initialisation. Returns the number of
-// patched positions (block-uniform). Sets *overflow / *dup (shared ints) on
-// a full table / a duplicate bias id. hs must be a multiple of blockDim.x.
+// overlap each other and the table's initialisation -- unless read_logits is
+// false: then the caller fills each slot's logit itself before
+// precompute_patches. Returns the number of patched positions
+// (block-uniform). Sets *overflow / *dup (shared ints) on a full table / a
+// duplicate bias id. hs must be a multiple of blockDim.x.
 __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_params& p,
                                     PatchTable& T, const float* chunk, int* s_counter,
-                                    int* s_overflow, int* s_dup) {
+                                    int* s_overflow, int* s_dup, bool read_logits = true) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int hs = 1 << T.log2size;
   constexpr int U = 4;
@@ -326,7 +328,7 @@ __device__ inline int build_patches(const BatchArgs& a, int row, const nls_row_p
       tok[u] = (t >= T.lo && t < T.hi) ? (int)t : -1;
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) raw[u] = tok[u] >= 0 ? __ldg(chunk + (tok[u] - T.lo)) : 0.0f;
+    for (int u = 0; u < U; ++u) raw[u] = (read_logits && tok[u] >= 0) ? __ldg(chunk + (tok[u] - T.lo)) : 0.0f;
     if (base == 0) __syncthreads();  // the table is initialised
 #pragma unroll
     for (int u = 0; u < U; ++u) {

@@ -247,32 +247,23 @@ light_kernel(BatchArgs a, int C, int chunk) {
 
   PatchTable T{S.hkey, S.hcnt, S.hbias, S.hflag, bitmap, LT_HASH_LOG2, lo, hi, LT_GSHIFT};
   int npatch = 0;
-  if (!a.argmax_only) npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup);
+  if (!a.argmax_only)
+    npatch = build_patches(a, row, p, T, rowp, &S.counter, &S.patch_overflow, &S.dup, false);
   const bool bad_patch = (!a.argmax_only) && (S.patch_overflow || S.dup);
-  // Patched positions (penalty window, bias) get their final value once, here;
-  // the streaming loops leave them out and they rejoin the candidates after.
-  if (npatch > 0 && !bad_patch) precompute_patches(T, p);
-  const float invT = (mode == kModeTopK) ? __double2float_rn(__ddiv_rn(1.0, p.temperature)) : 1.0f;
-
-  // A NaN among the row's first K positions enters the reference's heap in
-  // its first K pushes and never leaves it (sampler.nim:88-91); such a row
-  // goes to the full-sort kernel, which runs the heap as written. A NaN
-  // further on is never pushed (`x > h[0][0]` is false for it), and it never
-  // passes the threshold tests below either: it is simply left out.
-  if (mode == kModeTopK && lo < (int)K) {
-    const int e = min(hi, (int)K) - lo;
-    bool nan_here = false;
-    for (int i = tid; i < e; i += LT_THREADS) {
-      float x = rowp[i];
-      if (npatch > 0 && !bad_patch && patch_bit(T, i)) {
-        const int slot = patch_find(T, lo + i);
-        if (slot >= 0) x = patched_value(T, slot);
-      }
-      const float y = __fmul_rn(x, invT);
-      nan_here |= (y != y);
+  // Patched positions (penalty window, bias) get their final value once,
+  // after the stream: their logits come by 4-byte asynchronous copies into
+  // their slots that land while the row streams (the table's build waits
+  // for no logit); the streaming loops leave those positions out and they
+  // rejoin the candidates after.
+  if (npatch > 0 && !bad_patch) {
+    constexpr int HS = 1 << LT_HASH_LOG2;
+    for (int i = tid; i < HS; i += LT_THREADS) {
+      const int k = T.key[i];
+      if (k >= 0) cp_async4(&T.bias[i], rowp + (k - lo));
     }
-    if (__syncthreads_or(nan_here) && tid == 0) S.nan = 1;
+    cp_async_commit();
   }
+  const float invT = (mode == kModeTopK) ? __double2float_rn(__ddiv_rn(1.0, p.temperature)) : 1.0f;
 
   float gb = 0.0f;
   int gi = INT_MAX;        // greedy: best non-NaN value and its first index
@@ -553,16 +544,13 @@ light_kernel(BatchArgs a, int C, int chunk) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int slot = valid[e] ? patch_find(T, lo + off + e) : -1;
-            if (slot >= 0) {
-              if (mode == kModeGreedy) x[e] = patched_value(T, slot);
-              else excl[e] = true;
-            }
+            if (slot >= 0) excl[e] = true;  // (a greedy row's too: it competes after the stream)
           }
         }
         if (mode == kModeGreedy) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            if (valid[e]) {
+            if (valid[e] && !excl[e]) {
               if (lo + off + e == 0 && x[e] != x[e]) S.nan0 = 1;
               if (!(x[e] != x[e]) && (gi == INT_MAX || x[e] > gb)) { gb = x[e]; gi = lo + off + e; }
             }
@@ -621,6 +609,33 @@ light_kernel(BatchArgs a, int C, int chunk) {
     }
   }
   __syncthreads();
+
+  // The patched positions' logits have landed: their final values.
+  if (npatch > 0 && !bad_patch) {
+    cp_async_wait<0>();
+    __syncthreads();
+    precompute_patches(T, p);
+  }
+
+  // A NaN among the row's first K positions enters the reference's heap in
+  // its first K pushes and never leaves it (sampler.nim:88-91); such a row
+  // goes to the full-sort kernel, which runs the heap as written. A NaN
+  // further on is never pushed (`x > h[0][0]` is false for it), and it never
+  // passes the threshold tests either: it is simply left out.
+  if (mode == kModeTopK && lo < (int)K) {
+    const int e = min(hi, (int)K) - lo;
+    bool nan_here = false;
+    for (int i = tid; i < e; i += LT_THREADS) {
+      float x = rowp[i];
+      if (npatch > 0 && !bad_patch && patch_bit(T, i)) {
+        const int slot = patch_find(T, lo + i);
+        if (slot >= 0) x = patched_value(T, slot);
+      }
+      const float y = __fmul_rn(x, invT);
+      nan_here |= (y != y);
+    }
+    if (__syncthreads_or(nan_here) && tid == 0) S.nan = 1;
+  }
 
   // Patched positions rejoin the top-k candidates with their patched values.
   if (mode == kModeTopK && npatch > 0 && !bad_patch && !overflow && !S.failed) {
